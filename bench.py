@@ -1,0 +1,397 @@
+"""Benchmark of the mm3fa attention hot path (GGML_OP_FLASH_ATTN_EXT) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mm3fa|reference]
+
+Workload (BASELINE config 2 at the metric's point "CFG B=2, KV 8K"): one step is the
+decode attention of all 36 layers of the Qwen3 LM for one token, each layer with its own
+F16 KV cache laid out as the reference lays it out ([128, max_seq=10240, 8, n_seq],
+viewed at n_kv = 8192, src/qwen3-lm.h:810-813), 32 query heads over 8 kv heads, D=128,
+F32 Q, zero F16 mask, scale 1/sqrt(128).  Synthetic seeded data; K/V ~ N(0, 0.5^2).
+Inputs are larger than L2 (36 x 84 MB of cache), so no L2 flush is needed.
+
+N GPUs: KV-head sharding, weak scaling.  Rank r holds kv heads [8r/N, 8(r+1)/N) of the
+caches of 2N sequences (N CFG pairs), i.e. the same bytes per GPU as N=1; after the 36
+layers one NCCL all-gather moves every rank's head slices and mm3fa_assemble_heads
+rebuilds the ggml [128, 32, 1, 2N] outputs.
+
+Printed JSON: value = whole-job algorithmic GB/s of the timed steps (device time, max over
+ranks); e2e = the same through the C ABI with Q/mask copied from pinned host memory and the
+outputs read back every step; roofline = the decode kernel's achieved GB/s vs the measured
+HBM copy bandwidth; cpu_baseline = the CPU oracle (ggml convention) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "minimaxmusic.cpp_b200"))
+
+METRIC = "decode attn GB/s & µs/layer (CFG B=2, KV 8K); DiT attn TFLOPS; % roofline"
+N_LAYERS = 36
+N_HEAD, N_HEAD_KV, D = 32, 8, 128
+N_KV, MAX_SEQ = 8192, 10240
+FALLBACK_HBM_GBS = 6650.0
+
+# dram__bytes_read.sum + dram__bytes_write.sum per decode launch at this workload, from the
+# ncu capture summarised in profiles/fa_decode_kernel_cfg2_b2_kv8192.md (None until captured)
+NCU_TRAFFIC_BYTES = None
+
+
+def layer_bytes(n_seq: int, n_head_kv: int, n_head: int) -> int:
+    """Algorithmic bytes of one decode-attention call: K+V once, Q, mask, out."""
+    kv = 2 * n_seq * n_head_kv * N_KV * D * 2
+    q = n_seq * n_head * D * 4
+    out = n_seq * n_head * D * 4
+    mask = n_seq * N_KV * 2
+    return kv + q + out + mask
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        except Exception:
+            pass
+        finally:
+            if self.path and os.path.exists(self.path):
+                os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_baseline(seconds: float = 10.0) -> dict:
+    """The CPU oracle (ggml convention: Q rounded to F16, F32 online softmax) on all host cores,
+    over distinct layers of the same shape, for about `seconds`."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # test infrastructure: the timed CPU baseline only
+    from mm3fa import workloads
+
+    threads = os.cpu_count() or 1
+    n_distinct = 2
+    cases = [workloads.decode_case(n_seq=2, n_kv=N_KV, max_seq=N_KV, kv_std=0.5, seed=1000 + i)
+             for i in range(n_distinct)]
+    descs = [(c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), c.mask.host_desc(), c.scale) for c in cases]
+    oracle.flash_attn_ext(*descs[0], mode=oracle.MODE_GGML, threads=threads)  # warm
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        oracle.flash_attn_ext(*descs[n % n_distinct], mode=oracle.MODE_GGML, threads=threads)
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    b = layer_bytes(2, N_HEAD_KV, N_HEAD)
+    return {"value": round(b * n / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} decode-attention layers (B=2, KV 8192, 32q/8kv, D=128, F16 K/V) cycling over "
+                      f"{n_distinct} distinct caches, {dt:.1f} s, oracle ggml-convention mode",
+            "us_per_layer": round(dt / n * 1e6, 1)}
+
+
+def run_reference(args) -> None:
+    """--impl reference: the reference's CPU implementation of the path.  ggml (the
+    reference's implementation) is absent from its tree, so this times the CPU oracle port
+    on the same workload, all host threads, rank 0 only."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    from mm3fa import workloads
+
+    threads = os.cpu_count() or 1
+    n_layers_per_step = 4  # a bounded sample of the 36-layer step
+    cases = [workloads.decode_case(n_seq=2, n_kv=N_KV, max_seq=N_KV, kv_std=0.5, seed=2000 + i)
+             for i in range(n_layers_per_step)]
+    descs = [(c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), c.mask.host_desc(), c.scale) for c in cases]
+
+    def step():
+        for d in descs:
+            oracle.flash_attn_ext(*d, mode=oracle.MODE_GGML, threads=threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    b = layer_bytes(2, N_HEAD_KV, N_HEAD) * n_layers_per_step * args.steps
+    gbs = b / dt / 1e9
+    us_layer = dt / (args.steps * n_layers_per_step) * 1e6
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16/f32",
+        "data": "synthetic (seeded, BASELINE config 2 shapes)",
+        "config": {"workload": "decode attention, 36-layer Qwen3 LM step at CFG B=2, KV 8192 "
+                               f"(bounded sample: {n_layers_per_step} layers per step)",
+                   "n_seq": 2, "n_kv": N_KV, "n_head": N_HEAD, "n_head_kv": N_HEAD_KV, "head_dim": D,
+                   "kv_type": "f16", "us_per_layer": round(us_layer, 1)},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{n_layers_per_step} distinct layers per step, oracle ggml-convention mode "
+                                   "(ggml, the reference's implementation, is absent from the reference tree)"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="mm3fa", choices=["mm3fa", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import mm3fa
+    from mm3fa import ggml
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if N_HEAD_KV % world:
+        raise SystemExit(f"{N_HEAD_KV} kv heads do not shard over {world} GPUs")
+
+    n_seq = 2 * world                 # N CFG pairs
+    hkv = N_HEAD_KV // world          # kv heads held by this rank
+    hq = N_HEAD // world              # query heads computed by this rank
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+
+    # ---- per-layer operands (device resident), in the reference's layouts
+    caches, qs, outs = [], [], []
+    for _ in range(N_LAYERS):
+        kc = (torch.randn(n_seq, hkv, MAX_SEQ, D, generator=g, device=dev) * 0.5).half()
+        vc = (torch.randn(n_seq, hkv, MAX_SEQ, D, generator=g, device=dev) * 0.5).half()
+        caches.append((kc, vc))
+        qs.append(torch.randn(n_seq, hq, 1, D, generator=g, device=dev))
+    mask = torch.zeros(n_seq, 1, 1, N_KV, dtype=torch.float16, device=dev)
+    outs = torch.empty(N_LAYERS, n_seq, 1, hq, D, device=dev)
+    rb = 2 * D
+    kv_nb = [2, rb, rb * MAX_SEQ, rb * MAX_SEQ * hkv]
+    descs = []
+    for l in range(N_LAYERS):
+        kc, vc = caches[l]
+        qd = ggml.make(ggml.GGML_TYPE_F32, [D, 1, hq, n_seq], qs[l].data_ptr())
+        kd = ggml.make(ggml.GGML_TYPE_F16, [D, N_KV, hkv, n_seq], kc.data_ptr(), kv_nb)
+        vd = ggml.make(ggml.GGML_TYPE_F16, [D, N_KV, hkv, n_seq], vc.data_ptr(), kv_nb)
+        md = ggml.make(ggml.GGML_TYPE_F16, [N_KV, 1, 1, n_seq], mask.data_ptr())
+        dd = ggml.make(ggml.GGML_TYPE_F32, [D, hq, 1, n_seq], outs[l].data_ptr())
+        descs.append((qd, kd, vd, md, dd))
+    scale = 1.0 / math.sqrt(D)
+    ws_bytes = mm3fa.workspace_size(*descs[0][:4], descs[0][4])
+    ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    gathered = torch.empty(world, N_LAYERS, n_seq, 1, hq, D, device=dev) if world > 1 else None
+    final = torch.empty(N_LAYERS * n_seq, 1, N_HEAD, D, device=dev) if world > 1 else None
+
+    stream = torch.cuda.Stream(device=dev)
+    ev_k0, ev_k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def attention_layers(s):
+        for (qd, kd, vd, md, dd) in descs:
+            mm3fa.flash_attn_ext(qd, kd, vd, md, scale, 0.0, 0.0, dd, ws.data_ptr(), ws.numel(), s.cuda_stream)
+
+    def exchange(s):
+        if world > 1:
+            dist.all_gather_into_tensor(gathered.view(-1), outs.view(-1))
+            mm3fa.assemble_heads(gathered.data_ptr(), final.data_ptr(), D, N_HEAD, 1, N_LAYERS * n_seq, world,
+                                 s.cuda_stream)
+
+    # capture the 36 attention launches once: the reference replays its decode graph the same way
+    with torch.cuda.stream(stream):
+        attention_layers(stream)  # first call sets kernel attributes outside capture
+        exchange(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        attention_layers(stream)
+    launches_per_step = N_LAYERS + (1 if world > 1 else 0)
+
+    def step():
+        with torch.cuda.stream(stream):
+            graph.replay()
+            exchange(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- timed region (device time, CUDA events on the launching stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kern_ms = []
+    with ClockSampler(local) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        stream.record_event(e0)
+        for _ in range(args.steps):
+            stream.record_event(ev_k0)
+            with torch.cuda.stream(stream):
+                graph.replay()
+            stream.record_event(ev_k1)
+            with torch.cuda.stream(stream):
+                exchange(stream)
+            ev_k1.synchronize()
+            kern_ms.append(ev_k0.elapsed_time(ev_k1))
+        stream.record_event(e1)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    clocks = clk.summary()
+    t_ms = e0.elapsed_time(e1)
+    t = torch.tensor([t_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t_ms = float(t.item())
+    ms_per_step = t_ms / args.steps
+    per_rank_bytes = layer_bytes(n_seq, hkv, hq) * N_LAYERS
+    job_bytes = per_rank_bytes * world
+    value = job_bytes * args.steps / (t_ms * 1e-3) / 1e9
+
+    # ---- roofline of the decode kernel (average launch inside the captured step)
+    avg_launch_us = statistics.median(kern_ms) * 1e3 / N_LAYERS
+    peak, peak_src = measured_peaks()
+    achieved = layer_bytes(n_seq, hkv, hq) / (avg_launch_us * 1e-6) / 1e9
+
+    # ---- end to end through the C ABI: Q/mask from pinned host memory, outputs back to host
+    q_host = [q.cpu().pin_memory() for q in qs]
+    mask_host = mask.cpu().pin_memory()
+    out_host = torch.empty(outs.shape, dtype=torch.float32).pin_memory()
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2, stream=stream):
+        mask.copy_(mask_host, non_blocking=True)
+        for l in range(N_LAYERS):
+            qs[l].copy_(q_host[l], non_blocking=True)
+        attention_layers(stream)
+        out_host.copy_(outs, non_blocking=True)
+    h2d = sum(q.numel() * 4 for q in q_host) + mask_host.numel() * 2
+    d2h = out_host.numel() * 4
+    for _ in range(args.warmup):
+        g2.replay()
+        exchange(stream)
+        stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream.record_event(f0)
+    for _ in range(args.steps):
+        with torch.cuda.stream(stream):
+            g2.replay()
+            exchange(stream)
+        stream.synchronize()  # the step's result is read on the host every step
+    stream.record_event(f1)
+    torch.cuda.synchronize()
+    te = torch.tensor([f0.elapsed_time(f1)], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = job_bytes * args.steps / (float(te.item()) * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 (K/V) / f32 (Q, accum, out)",
+            "data": "synthetic (seeded, BASELINE config 2 shapes; inputs larger than L2, no flush)",
+            "config": {"workload": "decode attention, 36-layer Qwen3 LM step at CFG B=2 per GPU, KV 8192 "
+                                   "(F16 cache views [128, 8192, 8, B] of [128, 10240, 8, B])",
+                       "global_batch": n_seq, "n_kv": N_KV, "n_layers": N_LAYERS, "n_head": N_HEAD,
+                       "n_head_kv": N_HEAD_KV, "head_dim": D, "parallelism": f"kv-head shard x{world}",
+                       "l2": "inputs > L2 (36 x 84 MB caches)",
+                       "us_per_layer": round(ms_per_step * 1e3 / N_LAYERS, 3),
+                       "bytes_per_layer_per_gpu": layer_bytes(n_seq, hkv, hq)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                         "traffic": NCU_TRAFFIC_BYTES, "kernel": "fa_decode_kernel<128,F16,64,4,bulk>",
+                         "avg_launch_us": round(avg_launch_us, 3)},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+    del graph, g2
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

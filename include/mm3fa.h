@@ -1,0 +1,165 @@
+/*
+ * mm3fa.h - C ABI of the B200 (sm_100a) flash-attention operator for minimaxmusic.cpp.
+ *
+ * The operator is ggml's GGML_OP_FLASH_ATTN_EXT as the reference builds it with
+ *     ggml_flash_attn_ext(ctx, q, k, v, mask, scale, max_bias, logit_softcap)
+ *     ggml_flash_attn_ext_set_prec(result, GGML_PREC_F32)
+ * at src/qwen3-lm.h:432-436 (prefill), src/qwen3-lm.h:816-820 (batched CFG decode) and
+ * src/dit.h:218-222 (DiT).  Those three graph nodes are computed by whichever ggml backend
+ * src/static-graph.h:54-57 dispatches to (ggml_backend_graph_compute or the scheduler);
+ * this library replaces the device computation of that node.
+ *
+ * Tensor convention (ggml): ne[0] is the innermost (contiguous-element) dimension and nb[i]
+ * is the byte stride of dimension i.  For Q8_0, ne[0] counts elements and nb[1] is the byte
+ * size of one row of ne[0]/32 blocks of 34 bytes.
+ *
+ *   q    [D,  n_q,  n_head,    n_seq ]   F32 (F16/BF16 accepted)
+ *   k    [D,  n_kv, n_head_kv, n_seq_k]  F16, BF16 or Q8_0 (may be a strided view of a cache)
+ *   v    [Dv, n_kv, n_head_kv, n_seq_k]  same type family as k
+ *   mask [n_kv, >=n_q, m2, m3] F16 or NULL; broadcast over heads (h % m2) and sequences (s % m3)
+ *   dst  [Dv, n_head, n_q, n_seq] F32 -- heads BEFORE query rows, exactly as ggml's result
+ *
+ * GQA: query head h reads kv head h / (n_head / n_head_kv); query sequence s reads kv
+ * sequence s / (n_seq / n_seq_k).
+ *
+ * All entry points are host functions.  None of them allocates device memory or
+ * synchronises the host with the device; work is enqueued on the caller's stream,
+ * so a call can be captured into a CUDA graph once its shape is fixed.
+ */
+#ifndef MM3FA_H
+#define MM3FA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32)
+#    define MM3FA_API __declspec(dllexport)
+#else
+#    define MM3FA_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml_type enum values used by the operator (ggml.h numbering). */
+enum mm3fa_type {
+    MM3FA_TYPE_F32  = 0,
+    MM3FA_TYPE_F16  = 1,
+    MM3FA_TYPE_Q8_0 = 8,
+    MM3FA_TYPE_BF16 = 30,
+};
+
+/* ggml_prec values accepted by the prec argument (ggml_flash_attn_ext_set_prec). */
+enum mm3fa_prec {
+    MM3FA_PREC_DEFAULT = 0,
+    MM3FA_PREC_F32     = 10,
+};
+
+/* Status codes.  The reference ignores ggml_status (src/qwen3-lm.h:620,921; src/dit.h:385);
+ * this ABI reports every rejected input instead of asserting. */
+enum mm3fa_status {
+    MM3FA_OK              = 0,
+    MM3FA_ERR_NULL        = 1,  /* a required tensor or data pointer is NULL           */
+    MM3FA_ERR_TYPE        = 2,  /* unsupported tensor type                               */
+    MM3FA_ERR_SHAPE       = 3,  /* shapes are inconsistent with the operator contract    */
+    MM3FA_ERR_STRIDE      = 4,  /* a stride is not a multiple of the element/row size    */
+    MM3FA_ERR_ALIGN       = 5,  /* data pointer not aligned to its element size          */
+    MM3FA_ERR_WORKSPACE   = 6,  /* workspace missing or smaller than mm3fa_workspace_size */
+    MM3FA_ERR_CUDA        = 7,  /* a CUDA launch failed (see mm3fa_last_cuda_error)       */
+    MM3FA_ERR_UNSUPPORTED = 8,  /* valid op, but no kernel here handles this shape       */
+    MM3FA_ERR_TIMEOUT     = 9,  /* a bounded device-side wait expired                     */
+    MM3FA_ERR_DEVICE      = 10, /* current device is not an sm_100 part                   */
+};
+
+/* One ggml tensor as the operator sees it (a plain view of struct ggml_tensor's
+ * type / ne / nb / data fields). */
+typedef struct mm3fa_tensor {
+    int32_t  type;  /* enum mm3fa_type */
+    int32_t  reserved;
+    int64_t  ne[4];
+    uint64_t nb[4]; /* bytes */
+    void *   data;  /* device pointer */
+} mm3fa_tensor;
+
+/*
+ * Computes dst = softmax(scale * q k^T [softcap] + slope_h * mask) v for every query row.
+ *   scale          softmax scale (the reference passes 1/sqrt(D))
+ *   max_bias       ALiBi maximum bias; 0 disables ALiBi (slope 1)
+ *   logit_softcap  0 disables; otherwise s <- softcap * tanh(s / softcap) before the mask
+ *   prec           MM3FA_PREC_DEFAULT or MM3FA_PREC_F32; accumulation is always F32
+ *   workspace      device scratch of at least mm3fa_workspace_size(...) bytes, or NULL when
+ *                  that size is 0.  Zero-fill it once after allocating it (cudaMemset); every
+ *                  successful call leaves its status word and arrival counters zero again, so
+ *                  the workspace can be reused and graph-replayed.  Calls that may run
+ *                  concurrently (different streams) need different workspaces.
+ *   stream         cudaStream_t (NULL = legacy default stream)
+ * Rows whose every score is -inf produce zeros.
+ * Replaces: the ggml-cuda compute of GGML_OP_FLASH_ATTN_EXT reached from
+ *           src/static-graph.h:54-57 for the nodes built at src/qwen3-lm.h:432, :817 and
+ *           src/dit.h:221.
+ */
+MM3FA_API int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                         const mm3fa_tensor * mask, float scale, float max_bias, float logit_softcap, int prec,
+                         mm3fa_tensor * dst, void * workspace, size_t workspace_bytes, void * stream);
+
+/*
+ * Bytes of device workspace mm3fa_flash_attn_ext needs for these operands on the current
+ * device (0 if none).  Depends on shapes and types only, never on data pointers.
+ * Replaces: the compute-buffer sizing ggml_gallocr / ggml_backend_sched do for the node
+ *           (src/static-graph.h:31-52).
+ */
+MM3FA_API size_t mm3fa_workspace_size(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                            const mm3fa_tensor * mask, const mm3fa_tensor * dst);
+
+/*
+ * Returns MM3FA_OK when mm3fa_flash_attn_ext would accept these operands, otherwise the
+ * status it would return.  Pure host check; data pointers are not dereferenced.
+ * Replaces: ggml_backend_supports_op for the node (src/static-graph.h:12-19).
+ */
+MM3FA_API int mm3fa_supports(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                   const mm3fa_tensor * mask, float max_bias, float logit_softcap, const mm3fa_tensor * dst);
+
+/*
+ * Reads (and clears) the device status word of a workspace: MM3FA_OK, or MM3FA_ERR_TIMEOUT
+ * when a bounded device-side wait of an earlier call on it expired (*status_out gets the raw
+ * bits).  After a timeout the workspace must be zero-filled again before reuse.  This call
+ * synchronises `stream`.
+ * Replaces: the ggml_status the reference ignores (src/qwen3-lm.h:620,921; src/dit.h:385).
+ */
+MM3FA_API int mm3fa_workspace_status(void * workspace, void * stream, uint32_t * status_out);
+
+/*
+ * Diagnostics: launches one CTA that waits on an mbarrier nothing arrives on, bounded by
+ * timeout_us, and records the expiry in the workspace status word exactly as the attention
+ * kernels do.  Lets tests check the timeout path without faulting or hanging the GPU.
+ * Replaces: nothing in the reference (it has no device-side failure detection).
+ */
+MM3FA_API int mm3fa_selftest_bounded_wait(void * workspace, uint32_t timeout_us, void * stream);
+
+/* Human-readable name of a status code (static storage). */
+MM3FA_API const char * mm3fa_status_string(int status);
+
+/* Message of the last CUDA error seen by this thread's calls ("" if none). */
+MM3FA_API const char * mm3fa_last_cuda_error(void);
+
+/* ABI version: (major << 16) | minor. */
+MM3FA_API int mm3fa_version(void);
+
+/*
+ * Multi-GPU output assembly.  With the kv heads partitioned over G ranks, rank r computes
+ * dst_r [Dv, n_head/G, n_q, n_seq] for query heads [r*n_head/G, (r+1)*n_head/G).  After an
+ * all-gather (NCCL, by the caller) the blocks sit rank-major as gathered[G][n_seq][n_q]
+ * [n_head/G][Dv]; this kernel permutes them into the ggml result [Dv, n_head, n_q, n_seq].
+ * Both buffers are contiguous F32 device memory and must not overlap.
+ * Replaces: nothing in the reference (single device); it is the exchange step of the
+ *           head-sharded layout fed to the o_proj at src/qwen3-lm.h:823-827.
+ */
+MM3FA_API int mm3fa_assemble_heads(const float * gathered, float * dst, int64_t dv, int64_t n_head, int64_t n_q,
+                         int64_t n_seq, int n_ranks, void * stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MM3FA_H */

@@ -1,0 +1,467 @@
+// mm3fa_abi.cu - the C ABI declared in include/mm3fa.h.
+//
+// Validates ggml tensor descriptors against the GGML_OP_FLASH_ATTN_EXT contract, sizes the
+// caller-owned workspace, and enqueues the kernels on the caller's stream.  Nothing here
+// allocates device memory or synchronises the host, except mm3fa_workspace_status, which
+// reads the status word back by design.
+#include "../../include/mm3fa.h"
+#include "fa_common.cuh"
+#include "fa_decode.cuh"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+using namespace mm3fa;
+
+namespace {
+
+thread_local char g_last_cuda_error[256] = "";
+
+int record_cuda(cudaError_t e) {
+    if (e == cudaSuccess) {
+        return MM3FA_OK;
+    }
+    std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s: %s", cudaGetErrorName(e),
+                  cudaGetErrorString(e));
+    return MM3FA_ERR_CUDA;
+}
+
+int64_t type_unit_bytes(int t) {
+    switch (t) {
+        case MM3FA_TYPE_F32:
+            return 4;
+        case MM3FA_TYPE_F16:
+        case MM3FA_TYPE_BF16:
+            return 2;
+        case MM3FA_TYPE_Q8_0:
+            return Q8_0_BLOCK;
+        default:
+            return 0;
+    }
+}
+
+int64_t row_bytes(int t, int64_t n) {
+    if (t == MM3FA_TYPE_Q8_0) {
+        return n / QK8_0 * Q8_0_BLOCK;
+    }
+    return type_unit_bytes(t) * n;
+}
+
+// Per-device facts cached once: SM count, compute capability.
+struct DeviceInfo {
+    int sms   = 0;
+    int major = 0;
+    int minor = 0;
+};
+
+DeviceInfo device_info() {
+    static std::mutex mu;
+    static DeviceInfo cache[64];
+    int               dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return DeviceInfo{};
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (cache[dev].sms == 0) {
+        cudaDeviceGetAttribute(&cache[dev].sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaDeviceGetAttribute(&cache[dev].major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&cache[dev].minor, cudaDevAttrComputeCapabilityMinor, dev);
+        cudaGetLastError();
+    }
+    return cache[dev];
+}
+
+int ctas_per_sm_cached(int D, int kvt, bool bulk) {
+    static std::mutex mu;
+    static int        cache[64][2][3][2];  // [dev][D==128][type idx][bulk]
+    int               dev = 0;
+    cudaGetDevice(&dev);
+    const int ti = kvt == MM3FA_TYPE_F16 ? 0 : (kvt == MM3FA_TYPE_BF16 ? 1 : 2);
+    std::lock_guard<std::mutex> lock(mu);
+    int & c = cache[dev & 63][D == 128][ti][bulk];
+    if (c == 0) {
+        c = decode_ctas_per_sm(D, kvt, bulk);
+    }
+    return c;
+}
+
+uint64_t wait_timeout_ns() {
+    static uint64_t ns = [] {
+        const char * e = std::getenv("MM3FA_WAIT_TIMEOUT_MS");
+        double       ms = e ? std::atof(e) : 2000.0;
+        if (!(ms > 0.0)) {
+            ms = 2000.0;
+        }
+        return (uint64_t) (ms * 1e6);
+    }();
+    return ns;
+}
+
+// Everything the dispatcher derives from the descriptors.
+struct OpShape {
+    int64_t D, DV, n_q, n_head, n_seq, n_kv, n_head_kv, n_seq_k;
+    int     ratio, rk3;
+    int     kvt;
+    int     key_align;  // key granularity that keeps 1-D bulk copies 16-byte aligned
+    bool    bulk;
+};
+
+bool aligned(const void * p, uintptr_t a) {
+    return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
+// Host-side contract check.  check_data: also validate data pointers.
+int check_op(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v, const mm3fa_tensor * mask,
+             float max_bias, float softcap, const mm3fa_tensor * dst, bool check_data, OpShape & s) {
+    if (!q || !k || !v || !dst) {
+        return MM3FA_ERR_NULL;
+    }
+    if (check_data && (!q->data || !k->data || !v->data || !dst->data || (mask && !mask->data))) {
+        return MM3FA_ERR_NULL;
+    }
+    // types
+    if (q->type != MM3FA_TYPE_F32 && q->type != MM3FA_TYPE_F16 && q->type != MM3FA_TYPE_BF16) {
+        return MM3FA_ERR_TYPE;
+    }
+    if (k->type != MM3FA_TYPE_F16 && k->type != MM3FA_TYPE_BF16 && k->type != MM3FA_TYPE_Q8_0) {
+        return MM3FA_ERR_TYPE;
+    }
+    if (v->type != k->type || dst->type != MM3FA_TYPE_F32 || (mask && mask->type != MM3FA_TYPE_F16)) {
+        return MM3FA_ERR_TYPE;
+    }
+    for (const mm3fa_tensor * t : { q, k, v, dst }) {
+        for (int i = 0; i < 4; i++) {
+            if (t->ne[i] < 0) {
+                return MM3FA_ERR_SHAPE;
+            }
+        }
+    }
+    // shapes (ggml_flash_attn_ext's contract)
+    s.D         = q->ne[0];
+    s.n_q       = q->ne[1];
+    s.n_head    = q->ne[2];
+    s.n_seq     = q->ne[3];
+    s.DV        = v->ne[0];
+    s.n_kv      = k->ne[1];
+    s.n_head_kv = k->ne[2];
+    s.n_seq_k   = k->ne[3];
+    s.kvt       = k->type;
+    if (k->ne[0] != s.D || v->ne[1] != s.n_kv || v->ne[2] != s.n_head_kv || v->ne[3] != s.n_seq_k) {
+        return MM3FA_ERR_SHAPE;
+    }
+    if (s.n_head_kv == 0 || s.n_seq_k == 0 || s.n_head % s.n_head_kv != 0 || s.n_seq % s.n_seq_k != 0) {
+        return MM3FA_ERR_SHAPE;
+    }
+    if (dst->ne[0] != s.DV || dst->ne[1] != s.n_head || dst->ne[2] != s.n_q || dst->ne[3] != s.n_seq) {
+        return MM3FA_ERR_SHAPE;
+    }
+    if (mask) {
+        if (mask->ne[0] != s.n_kv || mask->ne[1] < s.n_q || mask->ne[2] < 1 || mask->ne[3] < 1 ||
+            s.n_head % mask->ne[2] != 0 || s.n_seq % mask->ne[3] != 0) {
+            return MM3FA_ERR_SHAPE;
+        }
+    }
+    if (s.kvt == MM3FA_TYPE_Q8_0 && s.D % QK8_0 != 0) {
+        return MM3FA_ERR_SHAPE;
+    }
+    if (!std::isfinite(max_bias) || !std::isfinite(softcap) || max_bias < 0.0f) {
+        return MM3FA_ERR_SHAPE;
+    }
+    // strides: innermost dims packed, the rest multiples of the element (block) size
+    const int64_t qe = type_unit_bytes(q->type), ke = type_unit_bytes(k->type);
+    if ((int64_t) q->nb[0] != qe || (int64_t) k->nb[0] != ke || (int64_t) v->nb[0] != ke ||
+        (int64_t) dst->nb[0] != 4 || (mask && mask->nb[0] != 2)) {
+        return MM3FA_ERR_STRIDE;
+    }
+    for (int i = 1; i < 4; i++) {
+        if (q->nb[i] % (uint64_t) qe || k->nb[i] % 2 || v->nb[i] % 2 || dst->nb[i] % 4 || (mask && mask->nb[i] % 2)) {
+            return MM3FA_ERR_STRIDE;
+        }
+    }
+    if ((int64_t) k->nb[1] < row_bytes(k->type, s.D) || (int64_t) v->nb[1] < row_bytes(v->type, s.DV) ||
+        (int64_t) dst->nb[1] < 4 * s.DV) {
+        return MM3FA_ERR_STRIDE;
+    }
+    if (check_data) {
+        if (!aligned(q->data, (uintptr_t) qe) || !aligned(k->data, 2) || !aligned(v->data, 2) ||
+            !aligned(dst->data, 4) || (mask && !aligned(mask->data, 2))) {
+            return MM3FA_ERR_ALIGN;
+        }
+    }
+    // what the kernels here implement
+    if (s.DV != s.D || (s.D != 64 && s.D != 128)) {
+        return MM3FA_ERR_UNSUPPORTED;
+    }
+    if (s.n_kv > (int64_t) 0x7fffffff || s.n_q > 65535 || s.n_head > 65535) {
+        return MM3FA_ERR_UNSUPPORTED;
+    }
+    s.ratio = (int) (s.n_head / s.n_head_kv);
+    s.rk3   = (int) (s.n_seq / s.n_seq_k);
+    // bulk (TMA engine) copies need 16-byte aligned starts and sizes for every chunk
+    const int64_t rb = row_bytes(s.kvt, s.D);
+    int           u  = 1;
+    while ((rb * u) % 16 != 0) {
+        u *= 2;
+    }
+    s.key_align = u;
+    bool bulk   = (int64_t) k->nb[1] == rb && (int64_t) v->nb[1] == rb && s.n_kv % u == 0;
+    for (const mm3fa_tensor * t : { k, v }) {
+        if (t->ne[2] > 1 && t->nb[2] % 16) {
+            bulk = false;
+        }
+        if (t->ne[3] > 1 && t->nb[3] % 16) {
+            bulk = false;
+        }
+        if (check_data && !aligned(t->data, 16)) {
+            bulk = false;
+        }
+    }
+    s.bulk = bulk;
+    return MM3FA_OK;
+}
+
+DecodeGeometry geometry_for(const OpShape & s) {
+    const DeviceInfo di = device_info();
+    const int        cps = ctas_per_sm_cached((int) s.D, s.kvt, s.bulk);
+    return decode_geometry((int) s.n_seq, (int) s.n_head_kv, s.ratio, (int) s.n_q, (int) s.n_kv, s.key_align,
+                           di.sms, cps);
+}
+
+__global__ void zero_rows_kernel(char * dst, int64_t dv, int64_t n1, int64_t n2, int64_t n3, int64_t nb1,
+                                 int64_t nb2, int64_t nb3) {
+    const int64_t total = dv * n1 * n2 * n3;
+    for (int64_t i = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; i < total; i += (int64_t) gridDim.x * blockDim.x) {
+        const int64_t d = i % dv, a = (i / dv) % n1, b = (i / (dv * n1)) % n2, c = i / (dv * n1 * n2);
+        reinterpret_cast<float *>(dst + a * nb1 + b * nb2 + c * nb3)[d] = 0.0f;
+    }
+}
+
+__global__ void assemble_heads_kernel(const float * __restrict__ gathered, float * __restrict__ dst, int64_t dv,
+                                      int64_t n_head, int64_t n_q, int64_t n_seq, int n_ranks) {
+    const int64_t hl    = n_head / n_ranks;
+    const int64_t total = dv * n_head * n_q * n_seq;
+    for (int64_t o = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; o < total; o += (int64_t) gridDim.x * blockDim.x) {
+        const int64_t d = o % dv;
+        const int64_t h = (o / dv) % n_head;
+        const int64_t i = (o / (dv * n_head)) % n_q;
+        const int64_t s = o / (dv * n_head * n_q);
+        const int64_t r = h / hl;
+        dst[o]          = gathered[(((r * n_seq + s) * n_q + i) * hl + (h % hl)) * dv + d];
+    }
+}
+
+// Status self-test: one CTA waits on an mbarrier that nothing ever arrives on, bounded by
+// timeout_ns, then reports the expiry through the workspace status word.
+__global__ void bounded_wait_selftest_kernel(uint32_t * status, uint64_t timeout_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const bool ok = mbar_wait_bounded(&bar, 0, global_timer_ns() + timeout_ns);
+    if (!ok && threadIdx.x == 0) {
+        atomicOr(&status[0], ST_TIMEOUT);
+        atomicExch(&status[1], 0xffffffffu);
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int mm3fa_version(void) {
+    return (1 << 16) | 0;
+}
+
+const char * mm3fa_status_string(int st) {
+    switch (st) {
+        case MM3FA_OK:
+            return "ok";
+        case MM3FA_ERR_NULL:
+            return "null tensor or data pointer";
+        case MM3FA_ERR_TYPE:
+            return "unsupported tensor type";
+        case MM3FA_ERR_SHAPE:
+            return "inconsistent shapes";
+        case MM3FA_ERR_STRIDE:
+            return "unsupported strides";
+        case MM3FA_ERR_ALIGN:
+            return "misaligned data pointer";
+        case MM3FA_ERR_WORKSPACE:
+            return "workspace missing or too small";
+        case MM3FA_ERR_CUDA:
+            return "CUDA error";
+        case MM3FA_ERR_UNSUPPORTED:
+            return "shape not handled by these kernels";
+        case MM3FA_ERR_TIMEOUT:
+            return "a bounded device wait expired";
+        case MM3FA_ERR_DEVICE:
+            return "device is not sm_100";
+        default:
+            return "unknown status";
+    }
+}
+
+const char * mm3fa_last_cuda_error(void) {
+    return g_last_cuda_error;
+}
+
+int mm3fa_supports(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                   const mm3fa_tensor * mask, float max_bias, float logit_softcap, const mm3fa_tensor * dst) {
+    OpShape s{};
+    return check_op(q, k, v, mask, max_bias, logit_softcap, dst, false, s);
+}
+
+size_t mm3fa_workspace_size(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                            const mm3fa_tensor * mask, const mm3fa_tensor * dst) {
+    OpShape s{};
+    if (check_op(q, k, v, mask, 0.0f, 0.0f, dst, false, s) != MM3FA_OK) {
+        return 0;
+    }
+    if (s.n_kv == 0 || s.n_q == 0 || s.n_head == 0 || s.n_seq == 0) {
+        return 0;
+    }
+    // size for the bulk and the element-copy variant alike (they can differ in occupancy)
+    OpShape a = s, b = s;
+    a.bulk    = true;
+    b.bulk    = false;
+    const size_t wa = decode_workspace_bytes(geometry_for(a), (int) s.DV);
+    const size_t wb = decode_workspace_bytes(geometry_for(b), (int) s.DV);
+    return wa > wb ? wa : wb;
+}
+
+int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                         const mm3fa_tensor * mask, float scale, float max_bias, float logit_softcap, int prec,
+                         mm3fa_tensor * dst, void * workspace, size_t workspace_bytes, void * stream) {
+    if (prec != MM3FA_PREC_DEFAULT && prec != MM3FA_PREC_F32) {
+        return MM3FA_ERR_UNSUPPORTED;
+    }
+    OpShape s{};
+    int     st = check_op(q, k, v, mask, max_bias, logit_softcap, dst, true, s);
+    if (st != MM3FA_OK) {
+        return st;
+    }
+    const DeviceInfo di = device_info();
+    if (di.major != 10) {
+        return MM3FA_ERR_DEVICE;
+    }
+    cudaStream_t cs = static_cast<cudaStream_t>(stream);
+    if (s.n_q == 0 || s.n_head == 0 || s.n_seq == 0 || s.DV == 0) {
+        return MM3FA_OK;
+    }
+    if (s.n_kv == 0) {  // no keys: every row is empty
+        zero_rows_kernel<<<148, 256, 0, cs>>>(static_cast<char *>(dst->data), s.DV, s.n_head, s.n_q, s.n_seq,
+                                              (int64_t) dst->nb[1], (int64_t) dst->nb[2], (int64_t) dst->nb[3]);
+        return record_cuda(cudaGetLastError());
+    }
+    const DecodeGeometry g = geometry_for(s);
+    if (!workspace || workspace_bytes < decode_workspace_bytes(g, (int) s.DV)) {
+        return MM3FA_ERR_WORKSPACE;
+    }
+    DecodeParams p{};
+    p.q         = static_cast<const char *>(q->data);
+    p.k         = static_cast<const char *>(k->data);
+    p.v         = static_cast<const char *>(v->data);
+    p.mask      = mask ? static_cast<const char *>(mask->data) : nullptr;
+    p.dst       = static_cast<char *>(dst->data);
+    p.q_nb1     = (int64_t) q->nb[1];
+    p.q_nb2     = (int64_t) q->nb[2];
+    p.q_nb3     = (int64_t) q->nb[3];
+    p.k_nb1     = (int64_t) k->nb[1];
+    p.k_nb2     = (int64_t) k->nb[2];
+    p.k_nb3     = (int64_t) k->nb[3];
+    p.v_nb1     = (int64_t) v->nb[1];
+    p.v_nb2     = (int64_t) v->nb[2];
+    p.v_nb3     = (int64_t) v->nb[3];
+    p.m_nb1     = mask ? (int64_t) mask->nb[1] : 0;
+    p.m_nb2     = mask ? (int64_t) mask->nb[2] : 0;
+    p.m_nb3     = mask ? (int64_t) mask->nb[3] : 0;
+    p.m_ne2     = mask ? (int) mask->ne[2] : 1;
+    p.m_ne3     = mask ? (int) mask->ne[3] : 1;
+    p.d_nb1     = (int64_t) dst->nb[1];
+    p.d_nb2     = (int64_t) dst->nb[2];
+    p.d_nb3     = (int64_t) dst->nb[3];
+    p.q_type    = q->type;
+    p.n_q       = (int) s.n_q;
+    p.n_head    = (int) s.n_head;
+    p.n_head_kv = (int) s.n_head_kv;
+    p.n_seq     = (int) s.n_seq;
+    p.ratio     = s.ratio;
+    p.rk3       = s.rk3;
+    p.n_kv      = (int) s.n_kv;
+    p.rows_per_pair = s.ratio * (int) s.n_q;
+    p.scale     = scale;
+    p.softcap   = logit_softcap;
+    p.max_bias  = max_bias;
+    const int n_head_log2 = s.n_head > 0 ? 1 << (int) std::floor(std::log2((double) s.n_head)) : 1;
+    p.n_head_log2 = n_head_log2;
+    p.m0        = std::pow(2.0f, -max_bias / (float) n_head_log2);
+    p.m1        = std::pow(2.0f, -max_bias / 2.0f / (float) n_head_log2);
+    p.timeout_ns = wait_timeout_ns();
+    return record_cuda(launch_decode(p, g, (int) s.D, s.kvt, s.bulk, workspace, cs));
+}
+
+int mm3fa_assemble_heads(const float * gathered, float * dst, int64_t dv, int64_t n_head, int64_t n_q, int64_t n_seq,
+                         int n_ranks, void * stream) {
+    if (!gathered || !dst) {
+        return MM3FA_ERR_NULL;
+    }
+    if (n_ranks < 1 || dv < 0 || n_head < 0 || n_q < 0 || n_seq < 0 || (n_head % n_ranks) != 0) {
+        return MM3FA_ERR_SHAPE;
+    }
+    const int64_t total = dv * n_head * n_q * n_seq;
+    if (total == 0) {
+        return MM3FA_OK;
+    }
+    const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 8);
+    assemble_heads_kernel<<<(unsigned) blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(gathered, dst, dv, n_head,
+                                                                                            n_q, n_seq, n_ranks);
+    return record_cuda(cudaGetLastError());
+}
+
+int mm3fa_workspace_status(void * workspace, void * stream, uint32_t * status_out) {
+    if (!workspace || !status_out) {
+        return MM3FA_ERR_NULL;
+    }
+    cudaStream_t cs = static_cast<cudaStream_t>(stream);
+    uint32_t     st[2] = { 0, 0 };
+    cudaError_t  e     = cudaMemcpyAsync(st, workspace, sizeof(st), cudaMemcpyDeviceToHost, cs);
+    if (e == cudaSuccess) {
+        e = cudaStreamSynchronize(cs);
+    }
+    if (e != cudaSuccess) {
+        return record_cuda(e);
+    }
+    *status_out = st[0];
+    if (st[0] != 0) {
+        const uint32_t zero[2] = { 0, 0 };
+        e                      = cudaMemcpyAsync(workspace, zero, sizeof(zero), cudaMemcpyHostToDevice, cs);
+        if (e == cudaSuccess) {
+            e = cudaStreamSynchronize(cs);
+        }
+        if (e != cudaSuccess) {
+            return record_cuda(e);
+        }
+        return MM3FA_ERR_TIMEOUT;
+    }
+    return MM3FA_OK;
+}
+
+int mm3fa_selftest_bounded_wait(void * workspace, uint32_t timeout_us, void * stream) {
+    if (!workspace) {
+        return MM3FA_ERR_NULL;
+    }
+    bounded_wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<uint32_t *>(workspace), (uint64_t) timeout_us * 1000ull);
+    return record_cuda(cudaGetLastError());
+}
+
+}  // extern "C"

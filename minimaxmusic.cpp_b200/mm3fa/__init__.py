@@ -1,0 +1,158 @@
+"""mm3fa: B200 (sm_100a) GGML_OP_FLASH_ATTN_EXT behind a C ABI (include/mm3fa.h).
+
+Host-side mirror of the reference's operator interface.  The reference builds the op as
+
+    attn = ggml_flash_attn_ext(ctx, q, k, v, mask, scale, max_bias, logit_softcap)
+    ggml_flash_attn_ext_set_prec(attn, GGML_PREC_F32)
+
+(src/qwen3-lm.h:432-436, :816-820; src/dit.h:221-222).  `flash_attn_ext` here takes the
+same operands - ggml tensor descriptors of device memory, see `mm3fa.ggml` - plus the
+caller-owned workspace and stream, and raises `MM3FAError` where ggml would assert.
+
+The compute always runs in libmm3fa.so (CUDA); there is no CPU path.  If the library is
+missing or fails to load, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+from . import ggml
+from .ggml import (GGML_PREC_DEFAULT, GGML_PREC_F32, GGML_TYPE_BF16, GGML_TYPE_F16, GGML_TYPE_F32,  # noqa: F401
+                   GGML_TYPE_Q8_0, Tensor)
+
+_PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(_PKG, "lib", "libmm3fa.so")
+
+OK = 0
+ERR_NULL, ERR_TYPE, ERR_SHAPE, ERR_STRIDE, ERR_ALIGN = 1, 2, 3, 4, 5
+ERR_WORKSPACE, ERR_CUDA, ERR_UNSUPPORTED, ERR_TIMEOUT, ERR_DEVICE = 6, 7, 8, 9, 10
+
+_lib = None
+
+
+class MM3FAError(RuntimeError):
+    def __init__(self, status: int, what: str = ""):
+        self.status = status
+        msg = f"mm3fa status {status}: {status_string(status)}"
+        if status == ERR_CUDA:
+            msg += f" ({lib().mm3fa_last_cuda_error().decode()})"
+        if what:
+            msg = f"{what}: {msg}"
+        super().__init__(msg)
+
+
+def lib():
+    """The loaded libmm3fa.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise OSError(f"{LIB_PATH} is missing: run python minimaxmusic.cpp_b200/build.py")
+        L = ctypes.CDLL(LIB_PATH)
+        P = ctypes.POINTER(Tensor)
+        L.mm3fa_flash_attn_ext.argtypes = [P, P, P, P, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_int,
+                                           P, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+        L.mm3fa_flash_attn_ext.restype = ctypes.c_int
+        L.mm3fa_workspace_size.argtypes = [P, P, P, P, P]
+        L.mm3fa_workspace_size.restype = ctypes.c_size_t
+        L.mm3fa_supports.argtypes = [P, P, P, P, ctypes.c_float, ctypes.c_float, P]
+        L.mm3fa_supports.restype = ctypes.c_int
+        L.mm3fa_status_string.argtypes = [ctypes.c_int]
+        L.mm3fa_status_string.restype = ctypes.c_char_p
+        L.mm3fa_last_cuda_error.argtypes = []
+        L.mm3fa_last_cuda_error.restype = ctypes.c_char_p
+        L.mm3fa_version.restype = ctypes.c_int
+        L.mm3fa_assemble_heads.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                           ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p]
+        L.mm3fa_assemble_heads.restype = ctypes.c_int
+        L.mm3fa_workspace_status.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]
+        L.mm3fa_workspace_status.restype = ctypes.c_int
+        L.mm3fa_selftest_bounded_wait.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]
+        L.mm3fa_selftest_bounded_wait.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def status_string(status: int) -> str:
+    return lib().mm3fa_status_string(status).decode()
+
+
+def version() -> tuple[int, int]:
+    v = lib().mm3fa_version()
+    return v >> 16, v & 0xFFFF
+
+
+def _ref(t):
+    return ctypes.byref(t) if t is not None else None
+
+
+def supports(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None, dst: Tensor, max_bias: float = 0.0,
+             logit_softcap: float = 0.0) -> int:
+    """Status mm3fa_flash_attn_ext would return for these descriptors (0 = accepted)."""
+    return lib().mm3fa_supports(_ref(q), _ref(k), _ref(v), _ref(mask), max_bias, logit_softcap, _ref(dst))
+
+
+def workspace_size(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None, dst: Tensor) -> int:
+    return int(lib().mm3fa_workspace_size(_ref(q), _ref(k), _ref(v), _ref(mask), _ref(dst)))
+
+
+def dst_desc(q: Tensor, v: Tensor, data_ptr: int) -> Tensor:
+    """Contiguous F32 result descriptor [Dv, n_head, n_q, n_seq] (ggml_flash_attn_ext's)."""
+    return ggml.make(GGML_TYPE_F32, [v.ne[0], q.ne[2], q.ne[1], q.ne[3]], data_ptr)
+
+
+def flash_attn_ext(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None, scale: float, max_bias: float,
+                   logit_softcap: float, dst: Tensor, workspace: int, workspace_bytes: int, stream: int = 0,
+                   prec: int = GGML_PREC_F32) -> None:
+    """Enqueues the op on `stream` (a cudaStream_t as int).  Raises MM3FAError on rejection."""
+    st = lib().mm3fa_flash_attn_ext(_ref(q), _ref(k), _ref(v), _ref(mask), scale, max_bias, logit_softcap, prec,
+                                    _ref(dst), ctypes.c_void_p(workspace or None), workspace_bytes,
+                                    ctypes.c_void_p(stream or None))
+    if st != OK:
+        raise MM3FAError(st, "mm3fa_flash_attn_ext")
+
+
+def assemble_heads(gathered_ptr: int, dst_ptr: int, dv: int, n_head: int, n_q: int, n_seq: int, n_ranks: int,
+                   stream: int = 0) -> None:
+    st = lib().mm3fa_assemble_heads(ctypes.c_void_p(gathered_ptr), ctypes.c_void_p(dst_ptr), dv, n_head, n_q, n_seq,
+                                    n_ranks, ctypes.c_void_p(stream or None))
+    if st != OK:
+        raise MM3FAError(st, "mm3fa_assemble_heads")
+
+
+def workspace_status(workspace: int, stream: int = 0) -> tuple[int, int]:
+    """(status code, raw bits) of a workspace's device status word; clears it."""
+    raw = ctypes.c_uint32(0)
+    st = lib().mm3fa_workspace_status(ctypes.c_void_p(workspace), ctypes.c_void_p(stream or None), ctypes.byref(raw))
+    return st, raw.value
+
+
+# ---------------------------------------------------------------------- torch conveniences
+
+class Workspace:
+    """A zero-filled device workspace that grows on demand (one per stream)."""
+
+    def __init__(self, device=None):
+        self.device = device
+        self.buf = None
+
+    def get(self, nbytes: int):
+        import torch
+
+        if nbytes == 0:
+            return 0, 0
+        if self.buf is None or self.buf.numel() < nbytes:
+            self.buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=self.device)
+        return self.buf.data_ptr(), self.buf.numel()
+
+
+def run(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None, dst: Tensor, scale: float, max_bias: float = 0.0,
+        logit_softcap: float = 0.0, ws: Workspace | None = None, stream=None) -> None:
+    """flash_attn_ext with a torch-allocated workspace on torch's current (or given) stream."""
+    import torch
+
+    ws = ws or Workspace(torch.device("cuda", torch.cuda.current_device()))
+    nbytes = workspace_size(q, k, v, mask, dst)
+    ptr, cap = ws.get(nbytes)
+    s = stream if stream is not None else torch.cuda.current_stream()
+    flash_attn_ext(q, k, v, mask, scale, max_bias, logit_softcap, dst, ptr, cap, s.cuda_stream)

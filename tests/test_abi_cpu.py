@@ -1,0 +1,117 @@
+"""Host-only checks of the C ABI: the library loads, exports every declared entry point,
+and its contract checks (mm3fa_supports) accept and reject descriptors as documented.
+No kernel is launched here."""
+import ctypes
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+import mm3fa
+from mm3fa import ggml, workloads
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "mm3fa.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(mm3fa_\w+)\s*\(", src)))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    for n in ("mm3fa_flash_attn_ext", "mm3fa_workspace_size", "mm3fa_supports", "mm3fa_assemble_heads",
+              "mm3fa_status_string", "mm3fa_version"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = mm3fa.lib()
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+    out = subprocess.run(["nm", "-D", "--defined-only", mm3fa.LIB_PATH], capture_output=True, text=True).stdout
+    exported = set(re.findall(r"\b(mm3fa_\w+)\b", out))
+    assert set(declared_functions()) <= exported
+    # only the C ABI is visible
+    assert all(n.startswith("mm3fa_") for n in exported)
+
+
+def test_struct_layout_matches_header():
+    assert ctypes.sizeof(ggml.Tensor) == 4 + 4 + 32 + 32 + 8
+    assert ggml.Tensor.data.offset == 72
+
+
+def test_version_and_status_strings():
+    assert mm3fa.version()[0] == 1
+    assert mm3fa.status_string(0) == "ok"
+    assert "workspace" in mm3fa.status_string(mm3fa.ERR_WORKSPACE)
+    assert mm3fa.status_string(12345) == "unknown status"
+
+
+def _decode_descs(**kw):
+    c = workloads.decode_case(**kw)
+    q, k, v, m = c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), c.mask.host_desc()
+    d = mm3fa.dst_desc(q, v, 0x1000)
+    return c, q, k, v, m, d
+
+
+def test_supports_accepts_reference_layouts():
+    _, q, k, v, m, d = _decode_descs(n_seq=2, n_kv=512, max_seq=1024)
+    assert mm3fa.supports(q, k, v, m, d) == mm3fa.OK
+    assert mm3fa.supports(q, k, v, None, d) == mm3fa.OK
+    _, q, k, v, m, d = _decode_descs(n_seq=2, n_kv=256, kv_type=ggml.GGML_TYPE_Q8_0)
+    assert mm3fa.supports(q, k, v, m, d) == mm3fa.OK
+    c = workloads.prefill_case(n_seq=1, S=16, n_head=4, n_head_kv=2, pad=32)
+    q, k, v, m = c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), c.mask.host_desc()
+    assert mm3fa.supports(q, k, v, m, mm3fa.dst_desc(q, v, 0x1000)) == mm3fa.OK
+    c = workloads.dit_case(B=2, S=20, H=4, D=64)
+    q, k, v = c.q.host_desc(), c.k.host_desc(), c.v.host_desc()
+    assert mm3fa.supports(q, k, v, None, mm3fa.dst_desc(q, v, 0x1000)) == mm3fa.OK
+
+
+def test_supports_rejections():
+    _, q, k, v, m, d = _decode_descs(n_seq=2, n_kv=128)
+    assert mm3fa.supports(None, k, v, m, d) == mm3fa.ERR_NULL
+    bad = ggml.make(ggml.GGML_TYPE_F32, list(k.ne), k.data, [4, 512, 512 * 128, 512 * 128 * 8])
+    assert mm3fa.supports(q, bad, v, m, d) == mm3fa.ERR_TYPE  # F32 K
+    assert mm3fa.supports(q, k, v, m, ggml.make(ggml.GGML_TYPE_F16, list(d.ne), 0x1000)) == mm3fa.ERR_TYPE
+    wrong_dst = ggml.make(ggml.GGML_TYPE_F32, [128, 1, 32, 2], 0x1000)  # rows before heads
+    assert mm3fa.supports(q, k, v, m, wrong_dst) == mm3fa.ERR_SHAPE
+    short_mask = ggml.make(ggml.GGML_TYPE_F16, [64, 1, 1, 2], m.data)
+    assert mm3fa.supports(q, k, v, short_mask, d) == mm3fa.ERR_SHAPE
+    q7 = ggml.make(q.type, [128, 1, 28, 2], q.data)  # 28 heads over 8 kv heads
+    assert mm3fa.supports(q7, k, v, m, mm3fa.dst_desc(q7, v, 0x1000)) == mm3fa.ERR_SHAPE
+    transposed_k = ggml.make(k.type, list(k.ne), k.data, [256, 2, 256 * 128, 256 * 128 * 8])
+    assert mm3fa.supports(q, transposed_k, v, m, d) == mm3fa.ERR_STRIDE
+    q96 = ggml.make(q.type, [96, 1, 32, 2], q.data)
+    k96 = ggml.make(k.type, [96, 128, 8, 2], k.data)
+    v96 = ggml.make(v.type, [96, 128, 8, 2], v.data)
+    assert mm3fa.supports(q96, k96, v96, m, mm3fa.dst_desc(q96, v96, 0x1000)) == mm3fa.ERR_UNSUPPORTED
+    assert mm3fa.supports(q, k, v, m, d, max_bias=-1.0) == mm3fa.ERR_SHAPE
+    assert mm3fa.supports(q, k, v, m, d, logit_softcap=float("nan")) == mm3fa.ERR_SHAPE
+
+
+def test_flash_attn_ext_rejects_before_touching_the_device():
+    _, q, k, v, m, d = _decode_descs(n_seq=2, n_kv=128)
+    with pytest.raises(mm3fa.MM3FAError) as e:
+        mm3fa.flash_attn_ext(q, k, v, m, 0.1, 0.0, 0.0, ggml.make(ggml.GGML_TYPE_F16, list(d.ne), 0x1000), 0, 0)
+    assert e.value.status == mm3fa.ERR_TYPE
+    with pytest.raises(mm3fa.MM3FAError) as e:
+        mm3fa.flash_attn_ext(q, k, v, m, 0.1, 0.0, 0.0, d, 0, 0, prec=3)
+    assert e.value.status == mm3fa.ERR_UNSUPPORTED
+    with pytest.raises(mm3fa.MM3FAError) as e:
+        mm3fa.assemble_heads(0, 0, 128, 32, 1, 2, 4)
+    assert e.value.status == mm3fa.ERR_NULL
+
+
+def test_descriptor_helpers_roundtrip():
+    a = np.zeros((3, 5, 7, 64), dtype=np.float32)
+    t = ggml.from_numpy(a)
+    assert list(t.ne) == [64, 7, 5, 3] and list(t.nb) == [4, 256, 256 * 7, 256 * 35]
+    b = np.zeros((2, 3, 136), dtype=np.uint8)
+    t = ggml.from_numpy(b, ggml.GGML_TYPE_Q8_0)
+    assert list(t.ne) == [128, 3, 2, 1] and list(t.nb) == [34, 136, 408, 816]

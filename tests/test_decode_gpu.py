@@ -1,0 +1,189 @@
+"""Parity of the CUDA decode path (through the C ABI) against the CPU oracle.
+
+Tolerance (north star, F32 output): max-abs <= 2e-3 and cosine >= 0.99999 against the
+oracle's ggml-convention mode, i.e. ggml's own CPU arithmetic.  Against the exact (float64)
+oracle the same bound holds for F16/BF16 K; for Q8_0 K the ggml convention itself quantizes
+Q to 8 bits, so the exact comparison uses max-abs <= 5e-3, cosine >= 0.9999.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import mm3fa
+import oracle
+from gpu_util import assert_close, run_gpu, run_oracle
+from mm3fa import ggml, workloads
+from test_oracle import GOLDEN_FILES, _load_golden
+
+pytestmark = pytest.mark.gpu
+
+F16, BF16, Q8 = ggml.GGML_TYPE_F16, ggml.GGML_TYPE_BF16, ggml.GGML_TYPE_Q8_0
+
+
+def check(c, dev, exact_abs=2e-3, exact_cos=0.99999):
+    got = run_gpu(c, dev)
+    assert_close(got, run_oracle(c, oracle.MODE_GGML), what=f"{c.name} vs ggml-convention oracle")
+    assert_close(got, run_oracle(c, oracle.MODE_EXACT), exact_abs, exact_cos, what=f"{c.name} vs exact oracle")
+    return got
+
+
+def test_config1_decode(cuda_device):
+    """CFG B=2, 32q/8kv, D=128, KV 2048, F16 cache view (max_seq 2560)."""
+    check(workloads.decode_case(n_seq=2, n_kv=2048, max_seq=2560, seed=1), cuda_device)
+
+
+def test_headline_decode_kv8192(cuda_device):
+    check(workloads.decode_case(n_seq=2, n_kv=8192, max_seq=10240, seed=2), cuda_device)
+
+
+def test_config3_q8_0_kv8192(cuda_device):
+    c = workloads.decode_case(n_seq=2, n_kv=8192, kv_type=Q8, seed=3)
+    check(c, cuda_device, exact_abs=5e-3, exact_cos=0.9999)
+
+
+@pytest.mark.parametrize("n_seq,n_kv", [(4, 512), (8, 2048)])
+def test_config2_sweep_points(cuda_device, n_seq, n_kv):
+    check(workloads.decode_case(n_seq=n_seq, n_kv=n_kv, kv_std=0.5, seed=40 + n_seq), cuda_device)
+
+
+def test_ragged_kv_lengths(cuda_device):
+    """Per-sequence kv_len with the reference's -inf padded tail (src/qwen3-lm.h:909-920)."""
+    check(workloads.decode_case(n_seq=4, n_kv=2304, kv_len=[1, 700, 2047, 2300], seed=5), cuda_device)
+
+
+@pytest.mark.parametrize("n_q", [2, 4, 8])
+def test_multirow_decode(cuda_device, n_q):
+    check(workloads.decode_case(n_seq=2, n_kv=1024, n_q=n_q, kv_len=[900, 1024], seed=6 + n_q), cuda_device)
+
+
+@pytest.mark.parametrize("n_kv", [1, 7, 255, 257, 1000])
+def test_odd_kv_lengths(cuda_device, n_kv):
+    check(workloads.decode_case(n_seq=2, n_kv=n_kv, seed=100 + n_kv), cuda_device)
+
+
+@pytest.mark.parametrize("n_kv", [2, 62, 258])
+def test_q8_0_small_and_odd(cuda_device, n_kv):
+    check(workloads.decode_case(n_seq=2, n_kv=n_kv, kv_type=Q8, seed=200 + n_kv), cuda_device, 5e-3, 0.9999)
+
+
+def test_q8_0_odd_length_takes_element_copy_path(cuda_device):
+    # 136-byte rows: an odd key count cannot be bulk-copied in 16-byte units
+    check(workloads.decode_case(n_seq=2, n_kv=333, kv_type=Q8, seed=7), cuda_device, 5e-3, 0.9999)
+
+
+def test_padded_rows_take_element_copy_path(cuda_device):
+    c = workloads.decode_case(n_seq=2, n_kv=300, seed=8)
+    # re-lay K/V with 8 bytes of padding after each 256-byte row (nb1 = 264)
+    for name in ("k", "v"):
+        op = getattr(c, name)
+        st = op.storage  # (s, h, j, 128) f16
+        padded = np.zeros(st.shape[:-1] + (132,), dtype=np.float16)
+        padded[..., :128] = st
+        setattr(c, name, workloads.Operand(padded, F16, op.ne, [2, 264, 264 * st.shape[2], 264 * st.shape[2] * 8]))
+    check(c, cuda_device)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("kvt", [F16, BF16, Q8])
+def test_head_dims_and_types(cuda_device, D, kvt):
+    c = workloads.decode_case(n_seq=2, n_kv=640, D=D, n_head=8, n_head_kv=2, seed=9, kv_type=kvt if kvt != BF16
+                              else F16)
+    if kvt == BF16:
+        for name in ("k", "v"):
+            op = getattr(c, name)
+            bf = torch.from_numpy(op.storage.astype(np.float32)).to(torch.bfloat16).view(torch.int16).numpy()
+            setattr(c, name, workloads.Operand(bf.view(np.uint16), BF16, op.ne, op.nb))
+    if kvt == Q8:
+        check(c, cuda_device, 5e-3, 0.9999)
+    else:
+        check(c, cuda_device)
+
+
+@pytest.mark.parametrize("ratio", [1, 2, 8, 32])
+def test_gqa_ratios(cuda_device, ratio):
+    check(workloads.decode_case(n_seq=2, n_kv=512, n_head=32, n_head_kv=32 // ratio, seed=10 + ratio), cuda_device)
+
+
+def test_softcap_and_alibi(cuda_device):
+    c = workloads.decode_case(n_seq=2, n_kv=777, n_head=8, n_head_kv=4, seed=11)
+    c.softcap, c.max_bias = 25.0, 8.0
+    check(c, cuda_device)
+
+
+def test_f16_query_and_seq_broadcast(cuda_device):
+    c = workloads.decode_case(n_seq=4, n_kv=512, seed=12)
+    # Q as F16, and 4 query sequences over 2 kv sequences (ik3 = iq3 / 2)
+    q16 = c.q.storage.astype(np.float16)
+    c.q = workloads.Operand(q16, F16, c.q.ne, [2, 256, 256, 256 * 32])
+    k = c.k
+    c.k = workloads.Operand(k.storage, F16, [128, 512, 8, 2], k.nb)
+    c.v = workloads.Operand(c.v.storage, F16, [128, 512, 8, 2], c.v.nb)
+    check(c, cuda_device)
+
+
+def test_fully_masked_sequence_gives_zeros(cuda_device):
+    c = workloads.decode_case(n_seq=2, n_kv=1024, seed=13)
+    c.mask.storage[1, 0, 0, :] = -np.inf
+    got = check(c, cuda_device)
+    assert np.all(got[1] == 0.0)
+
+
+def test_zero_kv_gives_zeros(cuda_device):
+    c = workloads.decode_case(n_seq=2, n_kv=64, seed=14)
+    for name in ("k", "v"):
+        op = getattr(c, name)
+        setattr(c, name, workloads.Operand(op.storage, op.gtype, [128, 0, 8, 2], op.nb))
+    c.mask = None
+    got = run_gpu(c, cuda_device)
+    assert np.all(got == 0.0)
+
+
+def test_prefill_and_dit_shapes(cuda_device):
+    check(workloads.prefill_case(n_seq=2, S=96, n_head=8, n_head_kv=2, kv_pos=40, pad=256, seed=15), cuda_device)
+    check(workloads.dit_case(B=2, S=130, H=4, D=64, seed=16), cuda_device)
+
+
+def test_workspace_reuse_is_stable(cuda_device):
+    """Arrival counters reset themselves: repeated calls on one workspace agree exactly."""
+    c = workloads.decode_case(n_seq=2, n_kv=4096, seed=17)
+    ws = mm3fa.Workspace(cuda_device)
+    a = run_gpu(c, cuda_device, ws)
+    b = run_gpu(c, cuda_device, ws, repeat=3)
+    assert np.array_equal(a, b)
+    st, raw = mm3fa.workspace_status(ws.buf.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert st == mm3fa.OK and raw == 0
+
+
+@pytest.mark.parametrize("path", GOLDEN_FILES, ids=[os.path.basename(p) for p in GOLDEN_FILES])
+def test_golden_fixtures_on_gpu(cuda_device, path):
+    c, z = _load_golden(path)
+    got = run_gpu(c, cuda_device)
+    assert_close(got, z["out_ggml"], what="vs golden ggml-convention")
+    loose = c.k.gtype == Q8
+    assert_close(got, z["out_exact"], 5e-3 if loose else 2e-3, 0.9999 if loose else 0.99999, what="vs golden exact")
+
+
+def test_bounded_wait_reports_timeout(cuda_device):
+    """A device wait that nothing satisfies expires after its limit and is reported through
+    the workspace status word; the context stays usable."""
+    ws = torch.zeros(4096, dtype=torch.uint8, device=cuda_device)
+    s = torch.cuda.current_stream().cuda_stream
+    assert mm3fa.lib().mm3fa_selftest_bounded_wait(ws.data_ptr(), 20000, s) == mm3fa.OK
+    st, raw = mm3fa.workspace_status(ws.data_ptr(), s)
+    assert st == mm3fa.ERR_TIMEOUT and raw & 1
+    st, raw = mm3fa.workspace_status(ws.data_ptr(), s)
+    assert st == mm3fa.OK and raw == 0
+    check(workloads.decode_case(n_seq=1, n_kv=256, n_head=8, n_head_kv=2, seed=18), cuda_device)
+
+
+def test_assemble_heads_matches_numpy(cuda_device):
+    from mm3fa.sharding import assemble_heads_np
+
+    G, n_seq, n_q, H, Dv = 4, 3, 2, 32, 128
+    g = torch.randn(G, n_seq, n_q, H // G, Dv, device=cuda_device)
+    out = torch.empty(n_seq, n_q, H, Dv, device=cuda_device)
+    mm3fa.assemble_heads(g.data_ptr(), out.data_ptr(), Dv, H, n_q, n_seq, G, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), assemble_heads_np(g.cpu().numpy(), G))
