@@ -299,17 +299,22 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) fa_decode_kernel(const DecodeP
 
     // ---- unit end: reduce O over key groups, then write dst or a partial (+ merge if last)
     auto end_unit = [&](int64_t unit, int j0, int j1) {
+        // key groups add their partial O in a fixed order: results are bit-reproducible
+        for (int kg = 0; kg < KG; kg++) {
+            if (pkg == kg) {
 #pragma unroll
-        for (int rr = 0; rr < 4; rr++) {
-            const int r = prg * 4 + rr;
-            if (r < nrow) {
+                for (int rr = 0; rr < 4; rr++) {
+                    const int r = prg * 4 + rr;
+                    if (r < nrow) {
 #pragma unroll
-                for (int e = 0; e < 8; e++) {
-                    atomicAdd(&sQO[r * D + dg * 8 + e], acc[rr][e]);
+                        for (int e = 0; e < 8; e++) {
+                            sQO[r * D + dg * 8 + e] += acc[rr][e];
+                        }
+                    }
                 }
             }
+            __syncthreads();
         }
-        __syncthreads();
         if (j0 == 0 && j1 == p.n_kv) {  // whole unit in this CTA
             for (int idx = tid; idx < nrow * D; idx += DEC_THREADS) {
                 const int   r = idx / D;

@@ -13,7 +13,7 @@ import torch
 
 import mm3fa
 import oracle
-from gpu_util import assert_close, run_gpu, run_oracle
+from gpu_util import assert_close, cosine, run_gpu, run_oracle
 from mm3fa import ggml, workloads
 from test_oracle import GOLDEN_FILES, _load_golden
 
@@ -23,9 +23,17 @@ F16, BF16, Q8 = ggml.GGML_TYPE_F16, ggml.GGML_TYPE_BF16, ggml.GGML_TYPE_Q8_0
 
 
 def check(c, dev, exact_abs=2e-3, exact_cos=0.99999):
+    """GPU vs the ggml-convention oracle at the north-star tolerance; GPU vs the exact oracle
+    at (exact_abs, exact_cos), widened to the ggml convention's own distance from exact math
+    when that is larger (Q8_0 with a handful of keys: Q's 8-bit rounding moves the weights)."""
     got = run_gpu(c, dev)
-    assert_close(got, run_oracle(c, oracle.MODE_GGML), what=f"{c.name} vs ggml-convention oracle")
-    assert_close(got, run_oracle(c, oracle.MODE_EXACT), exact_abs, exact_cos, what=f"{c.name} vs exact oracle")
+    gg = run_oracle(c, oracle.MODE_GGML)
+    ex = run_oracle(c, oracle.MODE_EXACT)
+    assert_close(got, gg, what=f"{c.name} vs ggml-convention oracle")
+    conv_abs = float(np.abs(gg - ex).max()) if ex.size else 0.0
+    conv_cos = cosine(gg, ex)
+    assert_close(got, ex, max(exact_abs, 1.25 * conv_abs), min(exact_cos, conv_cos - 1e-6),
+                 what=f"{c.name} vs exact oracle")
     return got
 
 
