@@ -198,12 +198,15 @@ def main() -> None:
     ap.add_argument("--impl", default="mm3fa", choices=["mm3fa", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--layers", type=int, default=N_LAYERS,
+                    help="layers per step (36 = the LM; fewer only for small ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
         return
+    n_layers = args.layers
 
     import torch
     import torch.distributed as dist
@@ -231,17 +234,17 @@ def main() -> None:
 
     # ---- per-layer operands (device resident), in the reference's layouts
     caches, qs, outs = [], [], []
-    for _ in range(N_LAYERS):
+    for _ in range(n_layers):
         kc = (torch.randn(n_seq, hkv, MAX_SEQ, D, generator=g, device=dev) * 0.5).half()
         vc = (torch.randn(n_seq, hkv, MAX_SEQ, D, generator=g, device=dev) * 0.5).half()
         caches.append((kc, vc))
         qs.append(torch.randn(n_seq, hq, 1, D, generator=g, device=dev))
     mask = torch.zeros(n_seq, 1, 1, N_KV, dtype=torch.float16, device=dev)
-    outs = torch.empty(N_LAYERS, n_seq, 1, hq, D, device=dev)
+    outs = torch.empty(n_layers, n_seq, 1, hq, D, device=dev)
     rb = 2 * D
     kv_nb = [2, rb, rb * MAX_SEQ, rb * MAX_SEQ * hkv]
     descs = []
-    for l in range(N_LAYERS):
+    for l in range(n_layers):
         kc, vc = caches[l]
         qd = ggml.make(ggml.GGML_TYPE_F32, [D, 1, hq, n_seq], qs[l].data_ptr())
         kd = ggml.make(ggml.GGML_TYPE_F16, [D, N_KV, hkv, n_seq], kc.data_ptr(), kv_nb)
@@ -252,8 +255,8 @@ def main() -> None:
     scale = 1.0 / math.sqrt(D)
     ws_bytes = mm3fa.workspace_size(*descs[0][:4], descs[0][4])
     ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
-    gathered = torch.empty(world, N_LAYERS, n_seq, 1, hq, D, device=dev) if world > 1 else None
-    final = torch.empty(N_LAYERS * n_seq, 1, N_HEAD, D, device=dev) if world > 1 else None
+    gathered = torch.empty(world, n_layers, n_seq, 1, hq, D, device=dev) if world > 1 else None
+    final = torch.empty(n_layers * n_seq, 1, N_HEAD, D, device=dev) if world > 1 else None
 
     stream = torch.cuda.Stream(device=dev)
     ev_k0, ev_k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -265,7 +268,7 @@ def main() -> None:
     def exchange(s):
         if world > 1:
             dist.all_gather_into_tensor(gathered.view(-1), outs.view(-1))
-            mm3fa.assemble_heads(gathered.data_ptr(), final.data_ptr(), D, N_HEAD, 1, N_LAYERS * n_seq, world,
+            mm3fa.assemble_heads(gathered.data_ptr(), final.data_ptr(), D, N_HEAD, 1, n_layers * n_seq, world,
                                  s.cuda_stream)
 
     # capture the 36 attention launches once: the reference replays its decode graph the same way
@@ -276,7 +279,7 @@ def main() -> None:
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         attention_layers(stream)
-    launches_per_step = N_LAYERS + (1 if world > 1 else 0)
+    launches_per_step = n_layers + (1 if world > 1 else 0)
 
     def step():
         with torch.cuda.stream(stream):
@@ -315,12 +318,12 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     t_ms = float(t.item())
     ms_per_step = t_ms / args.steps
-    per_rank_bytes = layer_bytes(n_seq, hkv, hq) * N_LAYERS
+    per_rank_bytes = layer_bytes(n_seq, hkv, hq) * n_layers
     job_bytes = per_rank_bytes * world
     value = job_bytes * args.steps / (t_ms * 1e-3) / 1e9
 
     # ---- roofline of the decode kernel (average launch inside the captured step)
-    avg_launch_us = statistics.median(kern_ms) * 1e3 / N_LAYERS
+    avg_launch_us = statistics.median(kern_ms) * 1e3 / n_layers
     peak, peak_src = measured_peaks()
     achieved = layer_bytes(n_seq, hkv, hq) / (avg_launch_us * 1e-6) / 1e9
 
@@ -331,7 +334,7 @@ def main() -> None:
     g2 = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g2, stream=stream):
         mask.copy_(mask_host, non_blocking=True)
-        for l in range(N_LAYERS):
+        for l in range(n_layers):
             qs[l].copy_(q_host[l], non_blocking=True)
         attention_layers(stream)
         out_host.copy_(outs, non_blocking=True)
@@ -369,10 +372,10 @@ def main() -> None:
             "data": "synthetic (seeded, BASELINE config 2 shapes; inputs larger than L2, no flush)",
             "config": {"workload": "decode attention, 36-layer Qwen3 LM step at CFG B=2 per GPU, KV 8192 "
                                    "(F16 cache views [128, 8192, 8, B] of [128, 10240, 8, B])",
-                       "global_batch": n_seq, "n_kv": N_KV, "n_layers": N_LAYERS, "n_head": N_HEAD,
+                       "global_batch": n_seq, "n_kv": N_KV, "n_layers": n_layers, "n_head": N_HEAD,
                        "n_head_kv": N_HEAD_KV, "head_dim": D, "parallelism": f"kv-head shard x{world}",
                        "l2": "inputs > L2 (36 x 84 MB caches)",
-                       "us_per_layer": round(ms_per_step * 1e3 / N_LAYERS, 3),
+                       "us_per_layer": round(ms_per_step * 1e3 / n_layers, 3),
                        "bytes_per_layer_per_gpu": layer_bytes(n_seq, hkv, hq)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
