@@ -70,7 +70,11 @@ enum mm3fa_status {
     MM3FA_ERR_UNSUPPORTED = 8,  /* valid op, but no kernel here handles this shape       */
     MM3FA_ERR_TIMEOUT     = 9,  /* a bounded device-side wait expired                     */
     MM3FA_ERR_DEVICE      = 10, /* current device is not an sm_100 part                   */
+    MM3FA_ERR_SCRATCH_LIMIT = 11, /* needs more scratch than MM3FA_NOALLOC_SCRATCH_BYTES  */
 };
+
+/* Size of the fixed device scratch buffer behind mm3fa_flash_attn_ext_noalloc (8 MiB). */
+#define MM3FA_NOALLOC_SCRATCH_BYTES (8u << 20)
 
 /* One ggml tensor as the operator sees it (a plain view of struct ggml_tensor's
  * type / ne / nb / data fields). */
@@ -102,6 +106,25 @@ typedef struct mm3fa_tensor {
 MM3FA_API int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
                          const mm3fa_tensor * mask, float scale, float max_bias, float logit_softcap, int prec,
                          mm3fa_tensor * dst, void * workspace, size_t workspace_bytes, void * stream);
+
+/*
+ * mm3fa_flash_attn_ext for callers that cannot allocate device memory: the same computation,
+ * but the split-KV scratch comes from a buffer of MM3FA_NOALLOC_SCRATCH_BYTES built into the
+ * library (one per GPU that loads it, held until the process exits) instead of a workspace
+ * argument.  For hosts that may not call cudaMalloc where attention runs - a ggml backend whose
+ * buffers were all planned ahead, a graph-recording engine, a plugin without an allocator.
+ * Inputs and outputs are still the caller's.
+ *   - Returns MM3FA_ERR_SCRATCH_LIMIT, enqueuing nothing, when the operands need more scratch
+ *     than the buffer holds (mm3fa_workspace_size > MM3FA_NOALLOC_SCRATCH_BYTES).
+ *   - The first call on a device looks up the buffer's device address (cudaGetSymbolAddress)
+ *     with that device current; make that first call before any stream capture.
+ *   - Each call clears the buffer's counters on `stream` and allocates nothing.  All calls on a
+ *     device share the buffer: calls that can overlap on the GPU (unordered streams) race.
+ * Replaces: nothing - it has no counterpart in the reference.
+ */
+MM3FA_API int mm3fa_flash_attn_ext_noalloc(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                                           const mm3fa_tensor * mask, float scale, float max_bias,
+                                           float logit_softcap, int prec, mm3fa_tensor * dst, void * stream);
 
 /*
  * Bytes of device workspace mm3fa_flash_attn_ext needs for these operands on the current

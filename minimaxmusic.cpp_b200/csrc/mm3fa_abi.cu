@@ -305,6 +305,8 @@ const char * mm3fa_status_string(int st) {
             return "a bounded device wait expired";
         case MM3FA_ERR_DEVICE:
             return "device is not sm_100";
+        case MM3FA_ERR_SCRATCH_LIMIT:
+            return "operands need more scratch than the built-in no-allocation buffer holds";
         default:
             return "unknown status";
     }

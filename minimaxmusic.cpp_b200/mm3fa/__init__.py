@@ -27,6 +27,10 @@ LIB_PATH = os.path.join(_PKG, "lib", "libmm3fa.so")
 OK = 0
 ERR_NULL, ERR_TYPE, ERR_SHAPE, ERR_STRIDE, ERR_ALIGN = 1, 2, 3, 4, 5
 ERR_WORKSPACE, ERR_CUDA, ERR_UNSUPPORTED, ERR_TIMEOUT, ERR_DEVICE = 6, 7, 8, 9, 10
+ERR_SCRATCH_LIMIT = 11
+
+# size of the fixed scratch buffer behind flash_attn_ext_noalloc (MM3FA_NOALLOC_SCRATCH_BYTES)
+NOALLOC_SCRATCH_BYTES = 8 << 20
 
 _lib = None
 
@@ -69,6 +73,9 @@ def lib():
         L.mm3fa_workspace_status.restype = ctypes.c_int
         L.mm3fa_selftest_bounded_wait.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]
         L.mm3fa_selftest_bounded_wait.restype = ctypes.c_int
+        L.mm3fa_flash_attn_ext_noalloc.argtypes = [P, P, P, P, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                                   ctypes.c_int, P, ctypes.c_void_p]
+        L.mm3fa_flash_attn_ext_noalloc.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -110,6 +117,23 @@ def flash_attn_ext(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None, scale: 
                                     ctypes.c_void_p(stream or None))
     if st != OK:
         raise MM3FAError(st, "mm3fa_flash_attn_ext")
+
+
+def flash_attn_ext_noalloc(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None, scale: float, max_bias: float,
+                           logit_softcap: float, dst: Tensor, stream: int = 0, prec: int = GGML_PREC_F32) -> None:
+    """flash_attn_ext for callers that cannot allocate device memory.
+
+    The scratch comes from a fixed 8 MiB buffer inside libmm3fa.so rather than a workspace
+    argument, for hosts that may not call cudaMalloc where attention runs (a backend whose
+    buffers were planned ahead, a graph-recording engine, a plugin without an allocator).
+    Operands needing more scratch raise MM3FAError(ERR_SCRATCH_LIMIT).  The first call on a
+    device looks the buffer up and should come before any stream capture; calls that can
+    overlap on the GPU share the buffer and race.
+    """
+    st = lib().mm3fa_flash_attn_ext_noalloc(_ref(q), _ref(k), _ref(v), _ref(mask), scale, max_bias, logit_softcap,
+                                            prec, _ref(dst), ctypes.c_void_p(stream or None))
+    if st != OK:
+        raise MM3FAError(st, "mm3fa_flash_attn_ext_noalloc")
 
 
 def assemble_heads(gathered_ptr: int, dst_ptr: int, dv: int, n_head: int, n_q: int, n_seq: int, n_ranks: int,
