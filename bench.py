@@ -41,8 +41,8 @@ N_KV, MAX_SEQ = 8192, 10240
 FALLBACK_HBM_GBS = 6650.0
 
 # dram__bytes_read.sum + dram__bytes_write.sum per decode launch at this workload, from the
-# ncu capture summarised in profiles/fa_decode_kernel_cfg2_b2_kv8192.md (None until captured)
-NCU_TRAFFIC_BYTES = None
+# ncu capture summarised in profiles/fa_decode_kernel_cfg2_b2_kv8192.md
+NCU_TRAFFIC_BYTES = 67_239_680 + 921_344
 
 
 def layer_bytes(n_seq: int, n_head_kv: int, n_head: int) -> int:
