@@ -18,7 +18,7 @@ LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libmm3fa.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["mm3fa_abi.cu", "fa_decode.cu", "mm3fa_noalloc.cu"]
+SOURCES = ["mm3fa_abi.cu", "fa_decode.cu", "fa_decode_mma.cu", "mm3fa_noalloc.cu"]
 HEADERS = ["fa_common.cuh", "fa_decode.cuh"]
 
 NVCC_FLAGS = [

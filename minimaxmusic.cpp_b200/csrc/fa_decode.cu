@@ -57,25 +57,6 @@ struct DecodeSmem {
     static constexpr int TOTAL      = OFF_FLAG + 16;
 };
 
-// Iterates the stages of one CTA's key range [pos, end): a stage never crosses a unit.
-struct StageIter {
-    int64_t pos, end;
-    int     n_kv, C;
-
-    __device__ bool has() const { return pos < end; }
-
-    __device__ void next(int64_t & unit, int & j0, int & n) {
-        unit             = pos / n_kv;
-        j0               = (int) (pos - unit * n_kv);
-        const int64_t left = end - pos;
-        n                = min(C, n_kv - j0);
-        if ((int64_t) n > left) {
-            n = (int) left;
-        }
-        pos += n;
-    }
-};
-
 // Reads 4*NW bytes starting at a 2-byte aligned shared-memory offset (rows start 4-aligned).
 template <int NW>
 __device__ __forceinline__ void lds_bytes(const char * row, int off, uint32_t (&out)[NW]) {
@@ -90,16 +71,6 @@ __device__ __forceinline__ void lds_bytes(const char * row, int off, uint32_t (&
     for (int i = 0; i < NW; i++) {
         out[i] = __byte_perm(w[i], w[i + 1], sel);
     }
-}
-
-__device__ __forceinline__ float ld_q_elem(const char * p, int type, int e) {
-    if (type == KV_F32) {
-        return reinterpret_cast<const float *>(p)[e];
-    }
-    if (type == KV_F16) {
-        return __half2float(reinterpret_cast<const __half *>(p)[e]);
-    }
-    return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[e]);
 }
 
 template <int D, int KVT, int C, int NSTAGE, bool BULK>

@@ -1,0 +1,698 @@
+// fa_decode_mma.cu - split-KV decode attention on tensor cores, TMA tensor staging (sm_100a).
+//
+// Same operator, work split and partial-merge protocol as fa_decode.cu (units of <= 32 GQA
+// rows sharing one K/V slab, a stream-K cut of all unit keys over one wave of CTAs, a last-
+// arriver merge of partials in fixed order), for F16/BF16 K/V with <= 16 rows per unit
+// (the CFG decode of src/qwen3-lm.h:784-824: 4 query heads per kv head, 1 query row).
+//
+// Pipeline per CTA (160 threads):
+//   warp 4 (producer)  - one thread issues 2-D tiled TMA loads (cp.async.bulk.tensor, 128-byte
+//                        swizzle, no multicast) of C=64 keys x D of K and V per stage into an
+//                        NSTAGE ring; full/empty mbarriers, no block-wide barrier in the loop.
+//   warps 0-3          - each owns 16 keys of every stage and keeps its own online-softmax
+//                        state; the four warp partials are merged once per unit.
+// Math per warp and stage, with keys on the MMA's M dimension so the few GQA rows fill N:
+//   S^T[16 keys x 8r rows] = K[16 x D] . Q^T        (mma.sync m16n8k16, A via ldmatrix)
+//   P^T -> P fragments by movmatrix (register transpose, no shared-memory round trip)
+//   O^T[D x 8r]           += V^T[D x 16] . P^T       (A via ldmatrix.trans)
+// Q is rounded to K's type (ggml's convention for F16/BF16 K); P is rounded to that type for
+// the PV product; accumulation, softmax and the running row sums are F32.
+#include "fa_decode.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+namespace mm3fa {
+
+constexpr int MMA_CONSUMERS = 4;                       // consumer warps
+constexpr int MMA_THREADS   = 32 * (MMA_CONSUMERS + 1);  // + producer warp
+constexpr int MMA_C         = 64;                      // keys per stage (16 per consumer warp)
+constexpr int MMA_NSTAGE    = 3;
+constexpr int MMA_RMAX      = 32;                      // rows per unit in the partial layout
+
+template <int D, int NT>
+struct MmaSmem {
+    static constexpr int HALVES     = D / 64;                 // 128-byte column blocks per row
+    static constexpr int TILE       = MMA_C * 128;            // one TMA box: 64 keys x 128 B
+    static constexpr int MAT        = HALVES * TILE;          // K or V of one stage
+    static constexpr int STAGE      = 2 * MAT;
+    static constexpr int OFF_RED_O  = MMA_NSTAGE * STAGE;     // [row][D] merged O of the 4 warps
+    static constexpr int OFF_RED_ML = OFF_RED_O + 8 * NT * D * 4;  // [warp][row][2] (m, l)
+    static constexpr int OFF_BAR    = OFF_RED_ML + MMA_CONSUMERS * 8 * NT * 2 * 4;
+    static constexpr int OFF_FLAG   = OFF_BAR + 2 * MMA_NSTAGE * 8;
+    static constexpr int TOTAL      = OFF_FLAG + 16 + 1024;   // + alignment slack for the ring
+};
+
+// ------------------------------------------------------------------ PTX helpers
+
+__device__ __forceinline__ void tma_load_4d(void * dst, const CUtensorMap * tm, int c0, int c1, int c2, int c3,
+                                            uint64_t * bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t * bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t & r0, uint32_t & r1, uint32_t & r2, uint32_t & r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t & r0, uint32_t & r1, uint32_t & r2,
+                                          uint32_t & r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+template <bool BF16>
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    if (BF16) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    }
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    if (BF16) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<uint32_t *>(&v);
+    }
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+__device__ __forceinline__ void named_barrier_consumers() {
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * MMA_CONSUMERS) : "memory");
+}
+
+// Barrier over the consumer warps that also ORs a predicate: every consumer thread gets the
+// same answer, so branches on it keep the warps' barrier sequences identical.
+__device__ __forceinline__ bool consumers_any(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pin, pout;\n\t"
+        "setp.ne.u32 pin, %1, 0;\n\t"
+        "bar.red.or.pred pout, 1, %2, pin;\n\t"
+        "selp.u32 %0, 1, 0, pout;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t) v), "n"(32 * MMA_CONSUMERS)
+        : "memory");
+    return r != 0;
+}
+
+// byte offset of (key row j, 16-byte chunk c) inside one 128-byte-swizzled TMA box
+__device__ __forceinline__ uint32_t swz(int j, int c) {
+    return (uint32_t) (j * 128 + ((c ^ (j & 7)) << 4));
+}
+
+// ------------------------------------------------------------------ kernel
+
+template <int D, bool BF16, int NT>
+__global__ void __launch_bounds__(MMA_THREADS, 2)
+    fa_decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                         const DecodeParams p) {
+    using L          = MmaSmem<D, NT>;
+    constexpr int KS = D / 16;  // k-steps of QK, m-tiles of PV
+    extern __shared__ __align__(16) char smem_raw[];
+    char * smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
+
+    float *    redO  = reinterpret_cast<float *>(smem + L::OFF_RED_O);
+    float *    redML = reinterpret_cast<float *>(smem + L::OFF_RED_ML);
+    uint64_t * full  = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
+    uint64_t * empty = full + MMA_NSTAGE;
+    int *      flag  = reinterpret_cast<int *>(smem + L::OFF_FLAG);  // [0] abort, [1] last-arriver
+
+    const int tid  = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+
+    const int64_t total = p.n_units * (int64_t) p.n_kv;
+    const int64_t g0    = (int64_t) blockIdx.x * p.keys_per_cta;
+    const int64_t g1    = min(total, g0 + p.keys_per_cta);
+    if (g0 >= g1) {
+        return;
+    }
+    if (tid == 0) {
+        for (int s = 0; s < MMA_NSTAGE; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], MMA_CONSUMERS);
+        }
+        flag[0] = 0;
+        flag[1] = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const uint64_t deadline = global_timer_ns() + p.timeout_ns;
+
+    // ================================================================ producer warp
+    if (warp == MMA_CONSUMERS) {
+        if (lane == 0) {
+            StageIter it{ g0, g1, p.n_kv, MMA_C };
+            int        s = 0;
+            bool       ok = true;
+            while (it.has()) {
+                int64_t unit;
+                int     j0, n;
+                it.next(unit, j0, n);
+                const int slot = s % MMA_NSTAGE;
+                if (s >= MMA_NSTAGE) {
+                    ok = mbar_wait_bounded(&empty[slot], (uint32_t) (((s / MMA_NSTAGE) - 1) & 1), deadline);
+                    if (!ok) {
+                        atomicExch(&flag[0], 1);
+                        break;
+                    }
+                }
+                const int64_t sg  = unit / p.groups;
+                const int     g   = (int) (sg % p.n_head_kv);
+                const int     sq  = (int) (sg / p.n_head_kv);
+                const int     ks3 = sq / p.rk3;
+                char *        dk  = smem + slot * L::STAGE;
+                char *        dv  = dk + L::MAT;
+                mbar_arrive_expect_tx(&full[slot], (uint32_t) L::STAGE);
+#pragma unroll
+                for (int h = 0; h < L::HALVES; h++) {
+                    tma_load_4d(dk + h * L::TILE, &tmk, h * 64, j0, g, ks3, &full[slot]);
+                    tma_load_4d(dv + h * L::TILE, &tmv, h * 64, j0, g, ks3, &full[slot]);
+                }
+                s++;
+            }
+            // the last loads issued must land before this CTA's shared memory is released
+            // (consumers normally wait for them too; this matters when a wait expired)
+            const uint64_t drain = global_timer_ns() + p.timeout_ns;
+            for (int t = max(0, s - MMA_NSTAGE); t < s; t++) {
+                mbar_wait_bounded(&full[t % MMA_NSTAGE], (uint32_t) ((t / MMA_NSTAGE) & 1), drain);
+            }
+        }
+        return;
+    }
+
+    // ================================================================ consumer warps
+    const int g4 = lane >> 2;  // fragment row group
+    const int q4 = lane & 3;   // fragment column pair
+
+    uint32_t qb[NT][KS][2];   // Q^T B fragments
+    float    acc[KS][NT][4];  // O^T fragments: (dim = 16*m + g4 (+8), row = 8*nt + 2*q4 (+1))
+    float    m_run[NT][2], l_run[NT][2];
+    float    slope[NT][2];
+    int64_t  moff[NT][2];
+    bool     rvalid[NT][2];
+
+    int64_t cur_unit = -1;
+    int     nrow     = 0;
+    int     seg_j0 = 0, seg_j1 = 0;
+    bool    aborted  = false;
+
+    auto begin_unit = [&](int64_t unit) {
+        const int64_t sg   = unit / p.groups;
+        const int     rgrp = (int) (unit % p.groups);
+        const int     g    = (int) (sg % p.n_head_kv);
+        const int     sq   = (int) (sg / p.n_head_kv);
+        nrow               = min(p.rows_per_unit, p.rows_per_pair - rgrp * MMA_RMAX);
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            // B fragment rows: n = g4 -> unit row 8*nt + g4
+            const int  rb = nt * 8 + g4;
+            const bool vb = rb < nrow;
+            const int  rf = rgrp * MMA_RMAX + rb;
+            const int  hb = g * p.ratio + rf / p.n_q;
+            const int  ib = rf % p.n_q;
+            const char * qrow = p.q + (int64_t) ib * p.q_nb1 + (int64_t) hb * p.q_nb2 + (int64_t) sq * p.q_nb3;
+#pragma unroll
+            for (int ks = 0; ks < KS; ks++) {
+                float x[4] = { 0.f, 0.f, 0.f, 0.f };
+                if (vb) {
+                    const int d0 = ks * 16 + 2 * q4;
+                    x[0]         = ld_q_elem(qrow, p.q_type, d0);
+                    x[1]         = ld_q_elem(qrow, p.q_type, d0 + 1);
+                    x[2]         = ld_q_elem(qrow, p.q_type, d0 + 8);
+                    x[3]         = ld_q_elem(qrow, p.q_type, d0 + 9);
+                }
+                qb[nt][ks][0] = pack2<BF16>(x[0], x[1]);
+                qb[nt][ks][1] = pack2<BF16>(x[2], x[3]);
+            }
+            // softmax state rows: 8*nt + 2*q4 + {0,1}
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int r  = nt * 8 + 2 * q4 + e;
+                const int rf2 = rgrp * MMA_RMAX + r;
+                const int h  = g * p.ratio + rf2 / p.n_q;
+                const int i  = rf2 % p.n_q;
+                rvalid[nt][e] = r < nrow;
+                m_run[nt][e]  = -INFINITY;
+                l_run[nt][e]  = 0.0f;
+                slope[nt][e]  = rvalid[nt][e] ? alibi_slope(h, p.max_bias, p.n_head_log2, p.m0, p.m1) : 1.0f;
+                moff[nt][e]   = rvalid[nt][e] ? (int64_t) i * p.m_nb1 + (int64_t) (h % p.m_ne2) * p.m_nb2 +
+                                                  (int64_t) (sq % p.m_ne3) * p.m_nb3
+                                              : 0;
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < KS; m++) {
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    acc[m][nt][e] = 0.0f;
+                }
+            }
+        }
+    };
+
+    auto end_unit = [&](int64_t unit) {
+        // each warp's (m, l) per row to shared memory, l summed over the 8 key lanes
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                float l = l_run[nt][e];
+                l += __shfl_xor_sync(0xffffffffu, l, 4);
+                l += __shfl_xor_sync(0xffffffffu, l, 8);
+                l += __shfl_xor_sync(0xffffffffu, l, 16);
+                if (g4 == 0) {
+                    const int r                        = nt * 8 + 2 * q4 + e;
+                    redML[(warp * 8 * NT + r) * 2 + 0] = m_run[nt][e];
+                    redML[(warp * 8 * NT + r) * 2 + 1] = l;
+                }
+            }
+        }
+        named_barrier_consumers();
+        // the warps add their O, rescaled to the unit's row maximum, into one buffer in warp order
+        float scl[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int r = nt * 8 + 2 * q4 + e;
+                float     M = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < MMA_CONSUMERS; w++) {
+                    M = fmaxf(M, redML[(w * 8 * NT + r) * 2]);
+                }
+                scl[nt][e] = m_run[nt][e] == -INFINITY ? 0.0f : exp2f(m_run[nt][e] - M);
+            }
+        }
+        for (int w = 0; w < MMA_CONSUMERS; w++) {
+            if (warp == w) {
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+                    for (int m = 0; m < KS; m++) {
+                        const int r   = nt * 8 + 2 * q4;
+                        const int d   = m * 16 + g4;
+                        float *   o00 = &redO[r * D + d];
+                        float *   o10 = &redO[(r + 1) * D + d];
+                        float *   o01 = &redO[r * D + d + 8];
+                        float *   o11 = &redO[(r + 1) * D + d + 8];
+                        const float v00 = scl[nt][0] * acc[m][nt][0], v10 = scl[nt][1] * acc[m][nt][1];
+                        const float v01 = scl[nt][0] * acc[m][nt][2], v11 = scl[nt][1] * acc[m][nt][3];
+                        *o00 = w == 0 ? v00 : *o00 + v00;
+                        *o10 = w == 0 ? v10 : *o10 + v10;
+                        *o01 = w == 0 ? v01 : *o01 + v01;
+                        *o11 = w == 0 ? v11 : *o11 + v11;
+                    }
+                }
+            }
+            named_barrier_consumers();
+        }
+        // flag[0] can be raised by the producer at any time: decide once, for all warps alike
+        if (!consumers_any(flag[0] != 0)) {
+            const int  nthr  = 32 * MMA_CONSUMERS;
+            const bool whole = seg_j0 == 0 && seg_j1 == p.n_kv;
+            for (int idx = tid; idx < nrow * D; idx += nthr) {
+                const int r = idx / D, d = idx % D;
+                float     M = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < MMA_CONSUMERS; w++) {
+                    M = fmaxf(M, redML[(w * 8 * NT + r) * 2]);
+                }
+                float O = 0.0f, Ls = 0.0f;
+                if (M != -INFINITY) {
+                    O = redO[r * D + d];
+#pragma unroll
+                    for (int w = 0; w < MMA_CONSUMERS; w++) {
+                        const float mw = redML[(w * 8 * NT + r) * 2];
+                        Ls += (mw == -INFINITY ? 0.0f : exp2f(mw - M)) * redML[(w * 8 * NT + r) * 2 + 1];
+                    }
+                }
+                const int64_t sg   = unit / p.groups;
+                const int     rgrp = (int) (unit % p.groups);
+                const int     g    = (int) (sg % p.n_head_kv);
+                const int     sq   = (int) (sg / p.n_head_kv);
+                const int     rf   = rgrp * MMA_RMAX + r;
+                const int     h    = g * p.ratio + rf / p.n_q;
+                const int     i    = rf % p.n_q;
+                if (whole) {
+                    float * dst = reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 + (int64_t) i * p.d_nb2 +
+                                                            (int64_t) sq * p.d_nb3);
+                    dst[d]      = Ls > 0.0f ? O / Ls : 0.0f;
+                } else {
+                    const int64_t first = unit * (int64_t) p.n_kv / p.keys_per_cta;
+                    const int64_t pbase = unit * p.max_slots + ((int64_t) blockIdx.x - first);
+                    p.part_o[pbase * MMA_RMAX * D + (int64_t) r * D + d] = O;
+                    if (d == 0) {
+                        p.part_ml[(pbase * MMA_RMAX + r) * 2 + 0] = M;
+                        p.part_ml[(pbase * MMA_RMAX + r) * 2 + 1] = Ls;
+                    }
+                }
+            }
+            if (!whole) {
+                __threadfence();
+                named_barrier_consumers();
+                if (tid == 0) {
+                    const int64_t  first = unit * (int64_t) p.n_kv / p.keys_per_cta;
+                    const int64_t  last  = (unit * (int64_t) p.n_kv + p.n_kv - 1) / p.keys_per_cta;
+                    const uint32_t old   = atomicAdd(&p.counters[unit], 1u);
+                    flag[1]              = (old == (uint32_t) (last - first)) ? 1 : 0;
+                }
+                named_barrier_consumers();
+                if (flag[1]) {
+                    __threadfence();
+                    const int64_t first = unit * (int64_t) p.n_kv / p.keys_per_cta;
+                    const int64_t last  = (unit * (int64_t) p.n_kv + p.n_kv - 1) / p.keys_per_cta;
+                    const int     nslot = (int) (last - first + 1);
+                    const int64_t b0    = unit * p.max_slots;
+                    const int64_t sg    = unit / p.groups;
+                    const int     rgrp  = (int) (unit % p.groups);
+                    const int     g     = (int) (sg % p.n_head_kv);
+                    const int     sq    = (int) (sg / p.n_head_kv);
+                    for (int idx = tid; idx < nrow * D; idx += nthr) {
+                        const int r = idx / D, d = idx % D;
+                        float     M = -INFINITY;
+                        for (int sl = 0; sl < nslot; sl++) {
+                            M = fmaxf(M, __ldcg(&p.part_ml[((b0 + sl) * MMA_RMAX + r) * 2]));
+                        }
+                        float Lsum = 0.0f, O = 0.0f;
+                        if (M != -INFINITY) {
+                            for (int sl = 0; sl < nslot; sl++) {
+                                const float w = exp2f(__ldcg(&p.part_ml[((b0 + sl) * MMA_RMAX + r) * 2]) - M);
+                                Lsum += w * __ldcg(&p.part_ml[((b0 + sl) * MMA_RMAX + r) * 2 + 1]);
+                                O += w * __ldcg(&p.part_o[(b0 + sl) * MMA_RMAX * D + (int64_t) r * D + d]);
+                            }
+                        }
+                        const int rf = rgrp * MMA_RMAX + r;
+                        const int h  = g * p.ratio + rf / p.n_q;
+                        const int i  = rf % p.n_q;
+                        float *   dst = reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 +
+                                                                (int64_t) i * p.d_nb2 + (int64_t) sq * p.d_nb3);
+                        dst[d]        = Lsum > 0.0f ? O / Lsum : 0.0f;
+                    }
+                    if (tid == 0) {
+                        p.counters[unit] = 0u;
+                    }
+                }
+            }
+        }
+        named_barrier_consumers();  // shared reduction buffers are free again
+    };
+
+    StageIter it{ g0, g1, p.n_kv, MMA_C };
+    int        s = 0;
+    while (it.has()) {
+        int64_t unit;
+        int     j0, n;
+        it.next(unit, j0, n);
+        if (unit != cur_unit) {
+            if (cur_unit >= 0) {
+                end_unit(cur_unit);
+            }
+            begin_unit(unit);
+            cur_unit = unit;
+            seg_j0   = j0;
+        }
+        seg_j1 = j0 + n;
+
+        const int slot = s % MMA_NSTAGE;
+        const int kb   = warp * 16;  // this warp's first key in the stage
+        // mask values for this warp's keys, loaded before the wait so the latency overlaps it
+        float mk[NT][2][2];  // [nt][row e][key half kh]
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+#pragma unroll
+                for (int kh = 0; kh < 2; kh++) {
+                    const int j  = kb + g4 + 8 * kh;
+                    mk[nt][e][kh] = 0.0f;
+                    if (p.mask && rvalid[nt][e] && j < n) {
+                        mk[nt][e][kh] = __half2float(
+                            *reinterpret_cast<const __half *>(p.mask + moff[nt][e] + (int64_t) (j0 + j) * 2));
+                    }
+                }
+            }
+        }
+        if (!aborted) {
+            aborted = !mbar_wait_bounded(&full[slot], (uint32_t) ((s / MMA_NSTAGE) & 1), deadline);
+            if (aborted) {
+                atomicExch(&flag[0], 1);
+            }
+        }
+        if (!aborted && kb < n) {
+            const uint32_t sk = smem_addr(smem + slot * L::STAGE);
+            const uint32_t sv = sk + L::MAT;
+            // ---- S^T = K Q^T for this warp's 16 keys
+            float sc[NT][4];
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    sc[nt][e] = 0.0f;
+                }
+            }
+            {
+                const int krow = kb + (lane & 7) + ((lane >> 3) & 1) * 8;  // A rows supplied by this lane
+#pragma unroll
+                for (int ks = 0; ks < KS; ks++) {
+                    const int dim0 = ks * 16 + (lane >> 4) * 8;
+                    uint32_t  a0, a1, a2, a3;
+                    ldsm_x4(sk + (dim0 >> 6) * L::TILE + swz(krow, (dim0 & 63) >> 3), a0, a1, a2, a3);
+#pragma unroll
+                    for (int nt = 0; nt < NT; nt++) {
+                        mma16816<BF16>(sc[nt], a0, a1, a2, a3, qb[nt][ks][0], qb[nt][ks][1]);
+                    }
+                }
+            }
+            // ---- online softmax (per warp), P^T -> P fragments
+            uint32_t pb[NT][2];
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+                float x[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int re = e & 1;       // row 2*q4 + re
+                    const int kh = e >> 1;      // key g4 + 8*kh
+                    const int j  = kb + g4 + 8 * kh;
+                    float     v  = sc[nt][e] * p.scale;
+                    if (p.softcap != 0.0f) {
+                        v = p.softcap * tanhf(v / p.softcap);
+                    }
+                    v += slope[nt][re] * mk[nt][re][kh];
+                    x[e] = j < n ? v * LOG2E : -INFINITY;
+                }
+                float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) {
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+                }
+                const float mn0 = fmaxf(m_run[nt][0], mx0);
+                const float mn1 = fmaxf(m_run[nt][1], mx1);
+                const float al0 = mn0 == -INFINITY ? 1.0f : exp2f(m_run[nt][0] - mn0);
+                const float al1 = mn1 == -INFINITY ? 1.0f : exp2f(m_run[nt][1] - mn1);
+                m_run[nt][0]    = mn0;
+                m_run[nt][1]    = mn1;
+                const float p0  = mn0 == -INFINITY ? 0.0f : exp2f(x[0] - mn0);
+                const float p1  = mn1 == -INFINITY ? 0.0f : exp2f(x[1] - mn1);
+                const float p2  = mn0 == -INFINITY ? 0.0f : exp2f(x[2] - mn0);
+                const float p3  = mn1 == -INFINITY ? 0.0f : exp2f(x[3] - mn1);
+                l_run[nt][0]    = l_run[nt][0] * al0 + p0 + p2;
+                l_run[nt][1]    = l_run[nt][1] * al1 + p1 + p3;
+#pragma unroll
+                for (int m = 0; m < KS; m++) {
+                    acc[m][nt][0] *= al0;
+                    acc[m][nt][1] *= al1;
+                    acc[m][nt][2] *= al0;
+                    acc[m][nt][3] *= al1;
+                }
+                pb[nt][0] = movmatrix_t(pack2<BF16>(p0, p1));  // keys 0-7 of the warp's 16
+                pb[nt][1] = movmatrix_t(pack2<BF16>(p2, p3));  // keys 8-15
+            }
+            // ---- O^T += V^T P^T over this warp's 16 keys
+            {
+                const int vkey = kb + (lane & 7) + ((lane >> 4) & 1) * 8;  // stored V row for ldmatrix.trans
+#pragma unroll
+                for (int m = 0; m < KS; m++) {
+                    const int dim0 = m * 16 + ((lane >> 3) & 1) * 8;
+                    uint32_t  a0, a1, a2, a3;
+                    ldsm_x4_t(sv + (dim0 >> 6) * L::TILE + swz(vkey, (dim0 & 63) >> 3), a0, a1, a2, a3);
+#pragma unroll
+                    for (int nt = 0; nt < NT; nt++) {
+                        mma16816<BF16>(acc[m][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive(&empty[slot]);  // this warp is done with the ring slot
+        }
+        s++;
+    }
+    if (cur_unit >= 0) {
+        end_unit(cur_unit);
+    }
+    if (flag[0] && tid == 0) {
+        atomicOr(&p.status[0], ST_TIMEOUT);
+        atomicExch(&p.status[1], (uint32_t) blockIdx.x);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag                     once;
+    std::call_once(once, [] {
+        void *                          ptr = nullptr;
+        cudaDriverEntryPointQueryResult q   = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+        }
+        cudaGetLastError();
+    });
+    return fn;
+}
+
+// 4-D map of a [D, n_kv, Hkv, S_k] ggml view, box = 64 elements x 64 keys, 128-byte swizzle.
+bool encode_kv_map(CUtensorMap * tm, const void * data, bool bf16, int64_t D, int64_t n_kv, int64_t hkv,
+                   int64_t sk, int64_t nb1, int64_t nb2, int64_t nb3) {
+    auto enc = tensor_map_encoder();
+    if (!enc) {
+        return false;
+    }
+    // strides of size-1 dims are never stepped; give them the natural value
+    if (hkv == 1) {
+        nb2 = nb1 * n_kv;
+    }
+    if (sk == 1) {
+        nb3 = nb2 * hkv;
+    }
+    cuuint64_t dims[4]    = { (cuuint64_t) D, (cuuint64_t) n_kv, (cuuint64_t) hkv, (cuuint64_t) sk };
+    cuuint64_t strides[3] = { (cuuint64_t) nb1, (cuuint64_t) nb2, (cuuint64_t) nb3 };
+    cuuint32_t box[4]     = { 64, (cuuint32_t) MMA_C, 1, 1 };
+    cuuint32_t estr[4]    = { 1, 1, 1, 1 };
+    CUresult   r = enc(tm, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                       const_cast<void *>(data), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int D, bool BF16, int NT>
+void * mma_kernel(int & smem) {
+    smem = MmaSmem<D, NT>::TOTAL;
+    return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT>);
+}
+
+void * select_mma_kernel(int D, bool bf16, int nt, int & smem) {
+#define MM3FA_SELM(DD, BB, NN)                      \
+    if (D == DD && bf16 == BB && nt == NN) {        \
+        return mma_kernel<DD, BB, NN>(smem);        \
+    }
+    MM3FA_SELM(128, false, 1)
+    MM3FA_SELM(128, false, 2)
+    MM3FA_SELM(128, true, 1)
+    MM3FA_SELM(128, true, 2)
+    MM3FA_SELM(64, false, 1)
+    MM3FA_SELM(64, false, 2)
+    MM3FA_SELM(64, true, 1)
+    MM3FA_SELM(64, true, 2)
+#undef MM3FA_SELM
+    return nullptr;
+}
+
+}  // namespace
+
+bool decode_mma_eligible(int D, int kvt, int rows_per_pair) {
+    return (kvt == KV_F16 || kvt == KV_BF16) && (D == 64 || D == 128) && rows_per_pair <= 16 &&
+           tensor_map_encoder() != nullptr;
+}
+
+int decode_mma_ctas_per_sm(int D, int kvt, int rows_per_pair) {
+    int    smem = 0;
+    void * fn   = select_mma_kernel(D, kvt == KV_BF16, rows_per_pair <= 8 ? 1 : 2, smem);
+    if (!fn) {
+        return 0;
+    }
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    int nb = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, MMA_THREADS, smem) != cudaSuccess || nb < 1) {
+        cudaGetLastError();
+        nb = 1;
+    }
+    return nb;
+}
+
+cudaError_t launch_decode_mma(DecodeParams p, const DecodeGeometry & g, int D, int kvt, int64_t n_head_kv,
+                              int64_t n_seq_k, void * workspace, cudaStream_t stream) {
+    const bool bf16 = kvt == KV_BF16;
+    const int  nt   = p.rows_per_pair <= 8 ? 1 : 2;
+    int        smem = 0;
+    void *     fn   = select_mma_kernel(D, bf16, nt, smem);
+    if (!fn) {
+        return cudaErrorInvalidValue;
+    }
+    alignas(64) CUtensorMap tmk, tmv;
+    if (!encode_kv_map(&tmk, p.k, bf16, D, p.n_kv, n_head_kv, n_seq_k, p.k_nb1, p.k_nb2, p.k_nb3) ||
+        !encode_kv_map(&tmv, p.v, bf16, D, p.n_kv, n_head_kv, n_seq_k, p.v_nb1, p.v_nb2, p.v_nb3)) {
+        return cudaErrorInvalidValue;
+    }
+    char *       ws   = static_cast<char *>(workspace);
+    const size_t cnt  = ((size_t) g.n_units * 4 + 255) / 256 * 256;
+    const size_t slot = (size_t) g.n_units * g.max_slots * MMA_RMAX;
+    p.status          = reinterpret_cast<uint32_t *>(ws);
+    p.counters        = reinterpret_cast<uint32_t *>(ws + WS_STATUS_BYTES);
+    p.part_ml         = reinterpret_cast<float *>(ws + WS_STATUS_BYTES + cnt);
+    p.part_o          = reinterpret_cast<float *>(ws + WS_STATUS_BYTES + cnt + slot * 2 * 4);
+    p.n_units         = g.n_units;
+    p.keys_per_cta    = g.keys_per_cta;
+    p.max_slots       = g.max_slots;
+    p.rows_per_unit   = g.rows_per_unit;
+    p.groups          = g.groups;
+    cudaError_t e     = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+        return e;
+    }
+    void * args[] = { &tmk, &tmv, &p };
+    return cudaLaunchKernel(fn, dim3((unsigned) g.n_ctas), dim3(MMA_THREADS), args, (size_t) smem, stream);
+}
+
+}  // namespace mm3fa

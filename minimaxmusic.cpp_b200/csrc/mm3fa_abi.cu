@@ -78,18 +78,35 @@ DeviceInfo device_info() {
     return cache[dev];
 }
 
-int ctas_per_sm_cached(int D, int kvt, bool bulk) {
+// Decode kernel variants: the CUDA-core kernel with bulk or element copies, and the
+// tensor-core kernel with 8 or 16 rows per unit.
+enum Variant { V_SIMT_BULK = 0, V_SIMT_COPY = 1, V_MMA_8 = 2, V_MMA_16 = 3 };
+
+int ctas_per_sm_cached(int D, int kvt, Variant var) {
     static std::mutex mu;
-    static int        cache[64][2][3][2];  // [dev][D==128][type idx][bulk]
+    static int        cache[64][2][3][4];  // [dev][D==128][type idx][variant]
     int               dev = 0;
     cudaGetDevice(&dev);
     const int ti = kvt == MM3FA_TYPE_F16 ? 0 : (kvt == MM3FA_TYPE_BF16 ? 1 : 2);
     std::lock_guard<std::mutex> lock(mu);
-    int & c = cache[dev & 63][D == 128][ti][bulk];
+    int & c = cache[dev & 63][D == 128][ti][var];
     if (c == 0) {
-        c = decode_ctas_per_sm(D, kvt, bulk);
+        c = var >= V_MMA_8 ? decode_mma_ctas_per_sm(D, kvt, var == V_MMA_8 ? 8 : 16)
+                           : decode_ctas_per_sm(D, kvt, var == V_SIMT_BULK);
     }
     return c;
+}
+
+// MM3FA_DECODE=simt|mma|auto (default auto) selects the decode kernel where both apply.
+int decode_preference() {
+    const char * e = std::getenv("MM3FA_DECODE");
+    if (e && std::strcmp(e, "simt") == 0) {
+        return 1;
+    }
+    if (e && std::strcmp(e, "mma") == 0) {
+        return 2;
+    }
+    return 0;
 }
 
 uint64_t wait_timeout_ns() {
@@ -111,6 +128,7 @@ struct OpShape {
     int     kvt;
     int     key_align;  // key granularity that keeps 1-D bulk copies 16-byte aligned
     bool    bulk;
+    bool    tma;        // strides and base addresses a TMA tensor map can express
 };
 
 bool aligned(const void * p, uintptr_t a) {
@@ -224,12 +242,34 @@ int check_op(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor 
         }
     }
     s.bulk = bulk;
+    // TMA tensor maps: 16-byte aligned base and strides (nb1 included), extents < 2^32
+    bool tma = k->nb[1] % 16 == 0 && v->nb[1] % 16 == 0 && s.n_kv > 0;
+    for (const mm3fa_tensor * t : { k, v }) {
+        if ((t->ne[2] > 1 && t->nb[2] % 16) || (t->ne[3] > 1 && t->nb[3] % 16)) {
+            tma = false;
+        }
+        if (check_data && !aligned(t->data, 16)) {
+            tma = false;
+        }
+    }
+    s.tma = tma;
     return MM3FA_OK;
 }
 
-DecodeGeometry geometry_for(const OpShape & s) {
-    const DeviceInfo di = device_info();
-    const int        cps = ctas_per_sm_cached((int) s.D, s.kvt, s.bulk);
+// The decode kernel a call with these operands runs.
+Variant variant_for(const OpShape & s) {
+    const int  pref = decode_preference();
+    const int  rows = s.ratio * (int) s.n_q;
+    const bool mma  = pref != 1 && s.tma && decode_mma_eligible((int) s.D, s.kvt, rows);
+    if (mma) {
+        return rows <= 8 ? V_MMA_8 : V_MMA_16;
+    }
+    return s.bulk ? V_SIMT_BULK : V_SIMT_COPY;
+}
+
+DecodeGeometry geometry_for(const OpShape & s, Variant var) {
+    const DeviceInfo di  = device_info();
+    const int        cps = ctas_per_sm_cached((int) s.D, s.kvt, var);
     return decode_geometry((int) s.n_seq, (int) s.n_head_kv, s.ratio, (int) s.n_q, (int) s.n_kv, s.key_align,
                            di.sms, cps);
 }
@@ -331,13 +371,19 @@ size_t mm3fa_workspace_size(const mm3fa_tensor * q, const mm3fa_tensor * k, cons
     if (s.n_kv == 0 || s.n_q == 0 || s.n_head == 0 || s.n_seq == 0) {
         return 0;
     }
-    // size for the bulk and the element-copy variant alike (they can differ in occupancy)
-    OpShape a = s, b = s;
-    a.bulk    = true;
-    b.bulk    = false;
-    const size_t wa = decode_workspace_bytes(geometry_for(a), (int) s.DV);
-    const size_t wb = decode_workspace_bytes(geometry_for(b), (int) s.DV);
-    return wa > wb ? wa : wb;
+    // data alignment is not known here: size for every variant these operands could take
+    size_t    need = 0;
+    const int rows = s.ratio * (int) s.n_q;
+    for (Variant var : { V_SIMT_BULK, V_SIMT_COPY, V_MMA_8, V_MMA_16 }) {
+        if (var == V_MMA_8 && !(rows <= 8 && decode_mma_eligible((int) s.D, s.kvt, rows))) {
+            continue;
+        }
+        if (var == V_MMA_16 && !(rows > 8 && decode_mma_eligible((int) s.D, s.kvt, rows))) {
+            continue;
+        }
+        need = std::max(need, decode_workspace_bytes(geometry_for(s, var), (int) s.DV));
+    }
+    return need;
 }
 
 int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
@@ -364,7 +410,8 @@ int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const m
                                               (int64_t) dst->nb[1], (int64_t) dst->nb[2], (int64_t) dst->nb[3]);
         return record_cuda(cudaGetLastError());
     }
-    const DecodeGeometry g = geometry_for(s);
+    const Variant        var = variant_for(s);
+    const DecodeGeometry g   = geometry_for(s, var);
     if (!workspace || workspace_bytes < decode_workspace_bytes(g, (int) s.DV)) {
         return MM3FA_ERR_WORKSPACE;
     }
@@ -408,6 +455,9 @@ int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const m
     p.m0        = std::pow(2.0f, -max_bias / (float) n_head_log2);
     p.m1        = std::pow(2.0f, -max_bias / 2.0f / (float) n_head_log2);
     p.timeout_ns = wait_timeout_ns();
+    if (var >= V_MMA_8) {
+        return record_cuda(launch_decode_mma(p, g, (int) s.D, s.kvt, s.n_head_kv, s.n_seq_k, workspace, cs));
+    }
     return record_cuda(launch_decode(p, g, (int) s.D, s.kvt, s.bulk, workspace, cs));
 }
 

@@ -22,6 +22,14 @@ pytestmark = pytest.mark.gpu
 F16, BF16, Q8 = ggml.GGML_TYPE_F16, ggml.GGML_TYPE_BF16, ggml.GGML_TYPE_Q8_0
 
 
+@pytest.fixture(params=["auto", "simt"])
+def kernel(request, monkeypatch):
+    """Runs a test on the default dispatch (the tensor-core kernel for F16/BF16 with <= 16 rows
+    per unit) and again on the CUDA-core kernel (MM3FA_DECODE=simt)."""
+    monkeypatch.setenv("MM3FA_DECODE", request.param)
+    return request.param
+
+
 def check(c, dev, exact_abs=2e-3, exact_cos=0.99999):
     """GPU vs the ggml-convention oracle at the north-star tolerance; GPU vs the exact oracle
     at (exact_abs, exact_cos), widened to the ggml convention's own distance from exact math
@@ -37,12 +45,12 @@ def check(c, dev, exact_abs=2e-3, exact_cos=0.99999):
     return got
 
 
-def test_config1_decode(cuda_device):
+def test_config1_decode(kernel, cuda_device):
     """CFG B=2, 32q/8kv, D=128, KV 2048, F16 cache view (max_seq 2560)."""
     check(workloads.decode_case(n_seq=2, n_kv=2048, max_seq=2560, seed=1), cuda_device)
 
 
-def test_headline_decode_kv8192(cuda_device):
+def test_headline_decode_kv8192(kernel, cuda_device):
     check(workloads.decode_case(n_seq=2, n_kv=8192, max_seq=10240, seed=2), cuda_device)
 
 
@@ -52,22 +60,22 @@ def test_config3_q8_0_kv8192(cuda_device):
 
 
 @pytest.mark.parametrize("n_seq,n_kv", [(4, 512), (8, 2048)])
-def test_config2_sweep_points(cuda_device, n_seq, n_kv):
+def test_config2_sweep_points(kernel, cuda_device, n_seq, n_kv):
     check(workloads.decode_case(n_seq=n_seq, n_kv=n_kv, kv_std=0.5, seed=40 + n_seq), cuda_device)
 
 
-def test_ragged_kv_lengths(cuda_device):
+def test_ragged_kv_lengths(kernel, cuda_device):
     """Per-sequence kv_len with the reference's -inf padded tail (src/qwen3-lm.h:909-920)."""
     check(workloads.decode_case(n_seq=4, n_kv=2304, kv_len=[1, 700, 2047, 2300], seed=5), cuda_device)
 
 
 @pytest.mark.parametrize("n_q", [2, 4, 8])
-def test_multirow_decode(cuda_device, n_q):
+def test_multirow_decode(kernel, cuda_device, n_q):
     check(workloads.decode_case(n_seq=2, n_kv=1024, n_q=n_q, kv_len=[900, 1024], seed=6 + n_q), cuda_device)
 
 
 @pytest.mark.parametrize("n_kv", [1, 7, 255, 257, 1000])
-def test_odd_kv_lengths(cuda_device, n_kv):
+def test_odd_kv_lengths(kernel, cuda_device, n_kv):
     check(workloads.decode_case(n_seq=2, n_kv=n_kv, seed=100 + n_kv), cuda_device)
 
 
@@ -95,7 +103,7 @@ def test_padded_rows_take_element_copy_path(cuda_device):
 
 @pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("kvt", [F16, BF16, Q8])
-def test_head_dims_and_types(cuda_device, D, kvt):
+def test_head_dims_and_types(kernel, cuda_device, D, kvt):
     c = workloads.decode_case(n_seq=2, n_kv=640, D=D, n_head=8, n_head_kv=2, seed=9, kv_type=kvt if kvt != BF16
                               else F16)
     if kvt == BF16:
@@ -110,17 +118,17 @@ def test_head_dims_and_types(cuda_device, D, kvt):
 
 
 @pytest.mark.parametrize("ratio", [1, 2, 8, 32])
-def test_gqa_ratios(cuda_device, ratio):
+def test_gqa_ratios(kernel, cuda_device, ratio):
     check(workloads.decode_case(n_seq=2, n_kv=512, n_head=32, n_head_kv=32 // ratio, seed=10 + ratio), cuda_device)
 
 
-def test_softcap_and_alibi(cuda_device):
+def test_softcap_and_alibi(kernel, cuda_device):
     c = workloads.decode_case(n_seq=2, n_kv=777, n_head=8, n_head_kv=4, seed=11)
     c.softcap, c.max_bias = 25.0, 8.0
     check(c, cuda_device)
 
 
-def test_f16_query_and_seq_broadcast(cuda_device):
+def test_f16_query_and_seq_broadcast(kernel, cuda_device):
     c = workloads.decode_case(n_seq=4, n_kv=512, seed=12)
     # Q as F16, and 4 query sequences over 2 kv sequences (ik3 = iq3 / 2)
     q16 = c.q.storage.astype(np.float16)
@@ -131,7 +139,7 @@ def test_f16_query_and_seq_broadcast(cuda_device):
     check(c, cuda_device)
 
 
-def test_fully_masked_sequence_gives_zeros(cuda_device):
+def test_fully_masked_sequence_gives_zeros(kernel, cuda_device):
     c = workloads.decode_case(n_seq=2, n_kv=1024, seed=13)
     c.mask.storage[1, 0, 0, :] = -np.inf
     got = check(c, cuda_device)
@@ -153,7 +161,7 @@ def test_prefill_and_dit_shapes(cuda_device):
     check(workloads.dit_case(B=2, S=130, H=4, D=64, seed=16), cuda_device)
 
 
-def test_workspace_reuse_is_stable(cuda_device):
+def test_workspace_reuse_is_stable(kernel, cuda_device):
     """Arrival counters reset themselves: repeated calls on one workspace agree exactly."""
     c = workloads.decode_case(n_seq=2, n_kv=4096, seed=17)
     ws = mm3fa.Workspace(cuda_device)
@@ -165,7 +173,7 @@ def test_workspace_reuse_is_stable(cuda_device):
 
 
 @pytest.mark.parametrize("path", GOLDEN_FILES, ids=[os.path.basename(p) for p in GOLDEN_FILES])
-def test_golden_fixtures_on_gpu(cuda_device, path):
+def test_golden_fixtures_on_gpu(kernel, cuda_device, path):
     c, z = _load_golden(path)
     got = run_gpu(c, cuda_device)
     assert_close(got, z["out_ggml"], what="vs golden ggml-convention")
