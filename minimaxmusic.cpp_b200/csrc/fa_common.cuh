@@ -146,6 +146,7 @@ struct DecodeParams {
     int64_t      n_units;
     int64_t      keys_per_cta;   // W
     int          max_slots;      // partial slots per unit
+    int          cluster;        // CTAs per thread-block cluster (tensor-core cluster mode)
     // workspace
     uint32_t *   status;
     uint32_t *   counters;

@@ -315,27 +315,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) fa_decode_kernel(const DecodeP
             *sFlag             = (old == (uint32_t) (nslot - 1)) ? 1 : 0;
         }
         __syncthreads();
-        if (*sFlag) {
+        if (*sFlag) {  // uniform: written by thread 0 before the barrier above
             __threadfence();
-            const int64_t b0 = unit * p.max_slots;
-            for (int idx = tid; idx < nrow * D; idx += DEC_THREADS) {
-                const int r = idx / D;
-                float     M = -INFINITY;
-                for (int sl = 0; sl < nslot; sl++) {
-                    M = fmaxf(M, __ldcg(&p.part_ml[((b0 + sl) * DEC_RMAX + r) * 2]));
-                }
-                float Lsum = 0.0f, O = 0.0f;
-                if (M != -INFINITY) {
-                    for (int sl = 0; sl < nslot; sl++) {
-                        const float m  = __ldcg(&p.part_ml[((b0 + sl) * DEC_RMAX + r) * 2]);
-                        const float w  = exp2f(m - M);
-                        Lsum += w * __ldcg(&p.part_ml[((b0 + sl) * DEC_RMAX + r) * 2 + 1]);
-                        O += w * __ldcg(&p.part_o[(b0 + sl) * DEC_RMAX * D + idx]);
-                    }
-                }
-                float * o   = reinterpret_cast<float *>(p.dst + sDoff[r]);
-                o[idx % D]  = Lsum > 0.0f ? O / Lsum : 0.0f;
-            }
+            // sQO and sM/sL/sA are free here: this CTA's partial is already in the workspace
+            merge_unit_partials<D, DEC_RMAX, DEC_RMAX, DEC_THREADS>(
+                p, unit, nslot, nrow, tid, sQO, sM, [] { __syncthreads(); },
+                [&](int r) { return reinterpret_cast<float *>(p.dst + sDoff[r]); });
             if (tid == 0) {
                 p.counters[unit] = 0u;  // ready for the next launch on this workspace
             }

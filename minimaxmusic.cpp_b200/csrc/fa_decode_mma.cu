@@ -22,26 +22,30 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <cstdlib>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 namespace mm3fa {
 
 constexpr int MMA_CONSUMERS = 4;                       // consumer warps
 constexpr int MMA_THREADS   = 32 * (MMA_CONSUMERS + 1);  // + producer warp
 constexpr int MMA_C         = 64;                      // keys per stage (16 per consumer warp)
-constexpr int MMA_NSTAGE    = 3;
 constexpr int MMA_RMAX      = 32;                      // rows per unit in the partial layout
 
-template <int D, int NT>
+template <int D, int NT, int NS>
 struct MmaSmem {
     static constexpr int HALVES     = D / 64;                 // 128-byte column blocks per row
     static constexpr int TILE       = MMA_C * 128;            // one TMA box: 64 keys x 128 B
     static constexpr int MAT        = HALVES * TILE;          // K or V of one stage
     static constexpr int STAGE      = 2 * MAT;
-    static constexpr int OFF_RED_O  = MMA_NSTAGE * STAGE;     // [row][D] merged O of the 4 warps
+    static constexpr int OFF_RED_O  = NS * STAGE;     // [row][D] merged O of the 4 warps
     static constexpr int OFF_RED_ML = OFF_RED_O + 8 * NT * D * 4;  // [warp][row][2] (m, l)
-    static constexpr int OFF_BAR    = OFF_RED_ML + MMA_CONSUMERS * 8 * NT * 2 * 4;
-    static constexpr int OFF_FLAG   = OFF_BAR + 2 * MMA_NSTAGE * 8;
+    static constexpr int OFF_CML    = OFF_RED_ML + MMA_CONSUMERS * 8 * NT * 2 * 4;  // [row][2] CTA (m, l)
+    static constexpr int OFF_BAR    = OFF_CML + 8 * NT * 2 * 4;
+    static constexpr int OFF_FLAG   = OFF_BAR + 2 * NS * 8;
     static constexpr int TOTAL      = OFF_FLAG + 16 + 1024;   // + alignment slack for the ring
 };
 
@@ -126,6 +130,31 @@ __device__ __forceinline__ bool consumers_any(bool v) {
     return r != 0;
 }
 
+// ---- thread-block cluster / distributed shared memory
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// shared-memory address of the same variable in cluster CTA `rank`
+__device__ __forceinline__ uint32_t dsmem_addr(const void * local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(local)), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ float ld_dsmem(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+// all threads of all CTAs in the cluster; release/acquire orders shared-memory writes
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // byte offset of (key row j, 16-byte chunk c) inside one 128-byte-swizzled TMA box
 __device__ __forceinline__ uint32_t swz(int j, int c) {
     return (uint32_t) (j * 128 + ((c ^ (j & 7)) << 4));
@@ -133,33 +162,48 @@ __device__ __forceinline__ uint32_t swz(int j, int c) {
 
 // ------------------------------------------------------------------ kernel
 
-template <int D, bool BF16, int NT>
-__global__ void __launch_bounds__(MMA_THREADS, 2)
+// CLUSTER = false: the stream-K split of fa_decode.cu (partials merged through the workspace).
+// CLUSTER = true : one unit per thread-block cluster of p.cluster CTAs; CTA rank r streams key
+//                  slice [r*W, (r+1)*W) of the unit, and the CTAs merge their (m, l, O) over
+//                  distributed shared memory behind a cluster barrier - no global partials,
+//                  fences or atomics; the workspace only carries the status word.
+template <int D, bool BF16, int NT, bool CLUSTER, int NS>
+__global__ void __launch_bounds__(MMA_THREADS, NS <= 3 ? 2 : 1)
     fa_decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                          const DecodeParams p) {
-    using L          = MmaSmem<D, NT>;
+    using L          = MmaSmem<D, NT, NS>;
     constexpr int KS = D / 16;  // k-steps of QK, m-tiles of PV
     extern __shared__ __align__(16) char smem_raw[];
     char * smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
 
     float *    redO  = reinterpret_cast<float *>(smem + L::OFF_RED_O);
     float *    redML = reinterpret_cast<float *>(smem + L::OFF_RED_ML);
+    float *    cml   = reinterpret_cast<float *>(smem + L::OFF_CML);
     uint64_t * full  = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
-    uint64_t * empty = full + MMA_NSTAGE;
+    uint64_t * empty = full + NS;
     int *      flag  = reinterpret_cast<int *>(smem + L::OFF_FLAG);  // [0] abort, [1] last-arriver
 
     const int tid  = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
 
-    const int64_t total = p.n_units * (int64_t) p.n_kv;
-    const int64_t g0    = (int64_t) blockIdx.x * p.keys_per_cta;
-    const int64_t g1    = min(total, g0 + p.keys_per_cta);
-    if (g0 >= g1) {
-        return;
+    int64_t g0, g1;
+    if (CLUSTER) {
+        const int64_t ubase = (int64_t) (blockIdx.x / p.cluster) * p.n_kv;
+        g0                  = min(ubase + (int64_t) (blockIdx.x % p.cluster) * p.keys_per_cta, ubase + p.n_kv);
+        g1                  = min(g0 + p.keys_per_cta, ubase + p.n_kv);  // may be empty: still joins the cluster
+    } else {
+        const int64_t total = p.n_units * (int64_t) p.n_kv;
+        g0                  = (int64_t) blockIdx.x * p.keys_per_cta;
+        g1                  = min(total, g0 + p.keys_per_cta);
+        if (g0 >= g1) {
+            return;
+        }
     }
-    if (tid == 0) {
-        for (int s = 0; s < MMA_NSTAGE; s++) {
+    if (tid == 32 * MMA_CONSUMERS) {  // the producer thread: start the descriptor fetches first
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
+        for (int s = 0; s < NS; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], MMA_CONSUMERS);
         }
@@ -180,18 +224,18 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                 int64_t unit;
                 int     j0, n;
                 it.next(unit, j0, n);
-                const int slot = s % MMA_NSTAGE;
-                if (s >= MMA_NSTAGE) {
-                    ok = mbar_wait_bounded(&empty[slot], (uint32_t) (((s / MMA_NSTAGE) - 1) & 1), deadline);
+                const int slot = s % NS;
+                if (s >= NS) {
+                    ok = mbar_wait_bounded(&empty[slot], (uint32_t) (((s / NS) - 1) & 1), deadline);
                     if (!ok) {
                         atomicExch(&flag[0], 1);
                         break;
                     }
                 }
-                const int64_t sg  = unit / p.groups;
-                const int     g   = (int) (sg % p.n_head_kv);
-                const int     sq  = (int) (sg / p.n_head_kv);
-                const int     ks3 = sq / p.rk3;
+                const int sg  = (int) unit / p.groups;  // unit < 2^31 (checked on the host)
+                const int g   = sg % p.n_head_kv;
+                const int sq  = sg / p.n_head_kv;
+                const int ks3 = sq / p.rk3;
                 char *        dk  = smem + slot * L::STAGE;
                 char *        dv  = dk + L::MAT;
                 mbar_arrive_expect_tx(&full[slot], (uint32_t) L::STAGE);
@@ -205,13 +249,14 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
             // the last loads issued must land before this CTA's shared memory is released
             // (consumers normally wait for them too; this matters when a wait expired)
             const uint64_t drain = global_timer_ns() + p.timeout_ns;
-            for (int t = max(0, s - MMA_NSTAGE); t < s; t++) {
-                mbar_wait_bounded(&full[t % MMA_NSTAGE], (uint32_t) ((t / MMA_NSTAGE) & 1), drain);
+            for (int t = max(0, s - NS); t < s; t++) {
+                mbar_wait_bounded(&full[t % NS], (uint32_t) ((t / NS) & 1), drain);
             }
         }
-        return;
-    }
-
+        if (!CLUSTER) {
+            return;
+        }
+    } else {
     // ================================================================ consumer warps
     const int g4 = lane >> 2;  // fragment row group
     const int q4 = lane & 3;   // fragment column pair
@@ -226,13 +271,46 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
     int64_t cur_unit = -1;
     int     nrow     = 0;
     int     seg_j0 = 0, seg_j1 = 0;
+    int     u_rgrp = 0, u_g = 0, u_sq = 0;  // the current unit's row group, kv head, q sequence
     bool    aborted  = false;
+
+    float mk_cur[NT][2][2], mk_nxt[NT][2][2];  // mask values [nt][row 2*q4 + e][key g4 + 8*kh]
+    bool  mk_have = false;                      // mk_cur already holds the coming stage's values
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            mk_cur[nt][e][0] = mk_cur[nt][e][1] = 0.0f;
+            mk_nxt[nt][e][0] = mk_nxt[nt][e][1] = 0.0f;
+        }
+    }
+    auto load_mask = [&](float (&mk)[NT][2][2], int j0_, int n_) {
+        const int kb_ = warp * 16;
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+#pragma unroll
+                for (int kh = 0; kh < 2; kh++) {
+                    const int j   = kb_ + g4 + 8 * kh;
+                    mk[nt][e][kh] = 0.0f;
+                    if (rvalid[nt][e] && j < n_) {
+                        mk[nt][e][kh] = __half2float(
+                            *reinterpret_cast<const __half *>(p.mask + moff[nt][e] + (int64_t) (j0_ + j) * 2));
+                    }
+                }
+            }
+        }
+    };
 
     auto begin_unit = [&](int64_t unit) {
         const int64_t sg   = unit / p.groups;
         const int     rgrp = (int) (unit % p.groups);
         const int     g    = (int) (sg % p.n_head_kv);
         const int     sq   = (int) (sg / p.n_head_kv);
+        u_rgrp             = rgrp;
+        u_g                = g;
+        u_sq               = sq;
         nrow               = min(p.rows_per_unit, p.rows_per_pair - rgrp * MMA_RMAX);
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
@@ -340,10 +418,30 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
             }
             named_barrier_consumers();
         }
+        if (CLUSTER) {
+            // this CTA's (m, l) per row; the cluster epilogue merges the CTAs over DSMEM
+            if (tid < nrow) {
+                float M = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < MMA_CONSUMERS; w++) {
+                    M = fmaxf(M, redML[(w * 8 * NT + tid) * 2]);
+                }
+                float Ls = 0.0f;
+#pragma unroll
+                for (int w = 0; w < MMA_CONSUMERS; w++) {
+                    const float mw = redML[(w * 8 * NT + tid) * 2];
+                    Ls += (mw == -INFINITY ? 0.0f : exp2f(mw - M)) * redML[(w * 8 * NT + tid) * 2 + 1];
+                }
+                cml[tid * 2]     = M;
+                cml[tid * 2 + 1] = Ls;
+            }
+            return;
+        }
         // flag[0] can be raised by the producer at any time: decide once, for all warps alike
         if (!consumers_any(flag[0] != 0)) {
-            const int  nthr  = 32 * MMA_CONSUMERS;
-            const bool whole = seg_j0 == 0 && seg_j1 == p.n_kv;
+            const int     nthr    = 32 * MMA_CONSUMERS;
+            const bool    whole   = seg_j0 == 0 && seg_j1 == p.n_kv;
+            const int64_t u_first = unit * (int64_t) p.n_kv / p.keys_per_cta;
             for (int idx = tid; idx < nrow * D; idx += nthr) {
                 const int r = idx / D, d = idx % D;
                 float     M = -INFINITY;
@@ -360,20 +458,15 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                         Ls += (mw == -INFINITY ? 0.0f : exp2f(mw - M)) * redML[(w * 8 * NT + r) * 2 + 1];
                     }
                 }
-                const int64_t sg   = unit / p.groups;
-                const int     rgrp = (int) (unit % p.groups);
-                const int     g    = (int) (sg % p.n_head_kv);
-                const int     sq   = (int) (sg / p.n_head_kv);
-                const int     rf   = rgrp * MMA_RMAX + r;
-                const int     h    = g * p.ratio + rf / p.n_q;
-                const int     i    = rf % p.n_q;
+                const int rf = u_rgrp * MMA_RMAX + r;
+                const int h  = u_g * p.ratio + rf / p.n_q;
+                const int i  = rf % p.n_q;
                 if (whole) {
                     float * dst = reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 + (int64_t) i * p.d_nb2 +
-                                                            (int64_t) sq * p.d_nb3);
+                                                            (int64_t) u_sq * p.d_nb3);
                     dst[d]      = Ls > 0.0f ? O / Ls : 0.0f;
                 } else {
-                    const int64_t first = unit * (int64_t) p.n_kv / p.keys_per_cta;
-                    const int64_t pbase = unit * p.max_slots + ((int64_t) blockIdx.x - first);
+                    const int64_t pbase = unit * p.max_slots + ((int64_t) blockIdx.x - u_first);
                     p.part_o[pbase * MMA_RMAX * D + (int64_t) r * D + d] = O;
                     if (d == 0) {
                         p.part_ml[(pbase * MMA_RMAX + r) * 2 + 0] = M;
@@ -395,33 +488,17 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                     __threadfence();
                     const int64_t first = unit * (int64_t) p.n_kv / p.keys_per_cta;
                     const int64_t last  = (unit * (int64_t) p.n_kv + p.n_kv - 1) / p.keys_per_cta;
-                    const int     nslot = (int) (last - first + 1);
-                    const int64_t b0    = unit * p.max_slots;
-                    const int64_t sg    = unit / p.groups;
-                    const int     rgrp  = (int) (unit % p.groups);
-                    const int     g     = (int) (sg % p.n_head_kv);
-                    const int     sq    = (int) (sg / p.n_head_kv);
-                    for (int idx = tid; idx < nrow * D; idx += nthr) {
-                        const int r = idx / D, d = idx % D;
-                        float     M = -INFINITY;
-                        for (int sl = 0; sl < nslot; sl++) {
-                            M = fmaxf(M, __ldcg(&p.part_ml[((b0 + sl) * MMA_RMAX + r) * 2]));
-                        }
-                        float Lsum = 0.0f, O = 0.0f;
-                        if (M != -INFINITY) {
-                            for (int sl = 0; sl < nslot; sl++) {
-                                const float w = exp2f(__ldcg(&p.part_ml[((b0 + sl) * MMA_RMAX + r) * 2]) - M);
-                                Lsum += w * __ldcg(&p.part_ml[((b0 + sl) * MMA_RMAX + r) * 2 + 1]);
-                                O += w * __ldcg(&p.part_o[(b0 + sl) * MMA_RMAX * D + (int64_t) r * D + d]);
-                            }
-                        }
-                        const int rf = rgrp * MMA_RMAX + r;
-                        const int h  = g * p.ratio + rf / p.n_q;
-                        const int i  = rf % p.n_q;
-                        float *   dst = reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 +
-                                                                (int64_t) i * p.d_nb2 + (int64_t) sq * p.d_nb3);
-                        dst[d]        = Lsum > 0.0f ? O / Lsum : 0.0f;
-                    }
+                    const int     rgrp  = u_rgrp, g = u_g, sq = u_sq;
+                    // redO / redML are free here: this CTA's own partial is already in the workspace
+                    merge_unit_partials<D, MMA_RMAX, 8 * NT, 32 * MMA_CONSUMERS>(
+                        p, unit, (int) (last - first + 1), nrow, tid, redO, redML, [] { named_barrier_consumers(); },
+                        [&](int r) {
+                            const int rf = rgrp * MMA_RMAX + r;
+                            const int h  = g * p.ratio + rf / p.n_q;
+                            const int i  = rf % p.n_q;
+                            return reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 + (int64_t) i * p.d_nb2 +
+                                                             (int64_t) sq * p.d_nb3);
+                        });
                     if (tid == 0) {
                         p.counters[unit] = 0u;
                     }
@@ -431,6 +508,11 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
         named_barrier_consumers();  // shared reduction buffers are free again
     };
 
+    if (CLUSTER) {  // the cluster's unit, even when this CTA's key slice is empty
+        cur_unit = blockIdx.x / p.cluster;
+        begin_unit(cur_unit);
+        seg_j0 = seg_j1 = (int) (g0 - cur_unit * (int64_t) p.n_kv);
+    }
     StageIter it{ g0, g1, p.n_kv, MMA_C };
     int        s = 0;
     while (it.has()) {
@@ -447,27 +529,28 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
         }
         seg_j1 = j0 + n;
 
-        const int slot = s % MMA_NSTAGE;
+        const int slot = s % NS;
         const int kb   = warp * 16;  // this warp's first key in the stage
-        // mask values for this warp's keys, loaded before the wait so the latency overlaps it
-        float mk[NT][2][2];  // [nt][row e][key half kh]
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-#pragma unroll
-                for (int kh = 0; kh < 2; kh++) {
-                    const int j  = kb + g4 + 8 * kh;
-                    mk[nt][e][kh] = 0.0f;
-                    if (p.mask && rvalid[nt][e] && j < n) {
-                        mk[nt][e][kh] = __half2float(
-                            *reinterpret_cast<const __half *>(p.mask + moff[nt][e] + (int64_t) (j0 + j) * 2));
-                    }
+        // mask values of this warp's keys: mk_cur for this stage (prefetched one stage ahead when
+        // the next stage is in the same unit), mk_nxt requested now for the next stage
+        if (p.mask) {
+            if (!mk_have) {
+                load_mask(mk_cur, j0, n);
+            }
+            StageIter pk = it;
+            mk_have      = false;
+            if (pk.has()) {
+                int64_t un;
+                int     jn, nn;
+                pk.next(un, jn, nn);
+                if (un == unit) {
+                    load_mask(mk_nxt, jn, nn);
+                    mk_have = true;
                 }
             }
         }
         if (!aborted) {
-            aborted = !mbar_wait_bounded(&full[slot], (uint32_t) ((s / MMA_NSTAGE) & 1), deadline);
+            aborted = !mbar_wait_bounded(&full[slot], (uint32_t) ((s / NS) & 1), deadline);
             if (aborted) {
                 atomicExch(&flag[0], 1);
             }
@@ -485,15 +568,37 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                 }
             }
             {
+                // all K fragments first (one shared-memory latency), then two independent
+                // accumulation chains over the even and odd k-steps
                 const int krow = kb + (lane & 7) + ((lane >> 3) & 1) * 8;  // A rows supplied by this lane
+                uint32_t  af[KS][4];
 #pragma unroll
                 for (int ks = 0; ks < KS; ks++) {
                     const int dim0 = ks * 16 + (lane >> 4) * 8;
-                    uint32_t  a0, a1, a2, a3;
-                    ldsm_x4(sk + (dim0 >> 6) * L::TILE + swz(krow, (dim0 & 63) >> 3), a0, a1, a2, a3);
+                    ldsm_x4(sk + (dim0 >> 6) * L::TILE + swz(krow, (dim0 & 63) >> 3), af[ks][0], af[ks][1],
+                            af[ks][2], af[ks][3]);
+                }
+                float sc1[NT][4];
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        sc1[nt][e] = 0.0f;
+                    }
+                }
+#pragma unroll
+                for (int ks = 0; ks < KS; ks++) {
 #pragma unroll
                     for (int nt = 0; nt < NT; nt++) {
-                        mma16816<BF16>(sc[nt], a0, a1, a2, a3, qb[nt][ks][0], qb[nt][ks][1]);
+                        mma16816<BF16>((ks & 1) ? sc1[nt] : sc[nt], af[ks][0], af[ks][1], af[ks][2], af[ks][3],
+                                       qb[nt][ks][0], qb[nt][ks][1]);
+                    }
+                }
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        sc[nt][e] += sc1[nt][e];
                     }
                 }
             }
@@ -511,7 +616,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                     if (p.softcap != 0.0f) {
                         v = p.softcap * tanhf(v / p.softcap);
                     }
-                    v += slope[nt][re] * mk[nt][re][kh];
+                    v += slope[nt][re] * mk_cur[nt][re][kh];
                     x[e] = j < n ? v * LOG2E : -INFINITY;
                 }
                 float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
@@ -545,14 +650,18 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
             // ---- O^T += V^T P^T over this warp's 16 keys
             {
                 const int vkey = kb + (lane & 7) + ((lane >> 4) & 1) * 8;  // stored V row for ldmatrix.trans
+                uint32_t  vf[KS][4];
 #pragma unroll
                 for (int m = 0; m < KS; m++) {
                     const int dim0 = m * 16 + ((lane >> 3) & 1) * 8;
-                    uint32_t  a0, a1, a2, a3;
-                    ldsm_x4_t(sv + (dim0 >> 6) * L::TILE + swz(vkey, (dim0 & 63) >> 3), a0, a1, a2, a3);
+                    ldsm_x4_t(sv + (dim0 >> 6) * L::TILE + swz(vkey, (dim0 & 63) >> 3), vf[m][0], vf[m][1],
+                              vf[m][2], vf[m][3]);
+                }
+#pragma unroll
+                for (int m = 0; m < KS; m++) {
 #pragma unroll
                     for (int nt = 0; nt < NT; nt++) {
-                        mma16816<BF16>(acc[m][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+                        mma16816<BF16>(acc[m][nt], vf[m][0], vf[m][1], vf[m][2], vf[m][3], pb[nt][0], pb[nt][1]);
                     }
                 }
             }
@@ -561,10 +670,77 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
         if (lane == 0) {
             mbar_arrive(&empty[slot]);  // this warp is done with the ring slot
         }
+        if (p.mask) {
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+#pragma unroll
+                    for (int kh = 0; kh < 2; kh++) {
+                        mk_cur[nt][e][kh] = mk_nxt[nt][e][kh];
+                    }
+                }
+            }
+        }
         s++;
     }
     if (cur_unit >= 0) {
         end_unit(cur_unit);
+    }
+    }  // consumer warps
+
+    if (CLUSTER) {
+        // every CTA's (m, l) rows and merged O are in its shared memory: CTA rank c of the
+        // cluster merges dims [c*D/CS, (c+1)*D/CS) of every row from all CS CTAs over DSMEM
+        __syncwarp();
+        cluster_sync_all();
+        const int64_t unit = blockIdx.x / p.cluster;
+        const int     rgrp = (int) (unit % p.groups);
+        const int64_t sg   = unit / p.groups;
+        const int     g    = (int) (sg % p.n_head_kv);
+        const int     sq   = (int) (sg / p.n_head_kv);
+        const int     nr   = min(p.rows_per_unit, p.rows_per_pair - rgrp * MMA_RMAX);
+        const int     CS   = p.cluster;
+        const int     rank = (int) cluster_ctarank();
+        // rank c takes the (row, dim) items c, c + CS, c + 2*CS, ... (any cluster size)
+        for (int idx = rank + tid * CS; idx < nr * D; idx += MMA_THREADS * CS) {
+            const int r = idx / D, d = idx % D;
+            // all remote loads of the item issued together (one DSMEM latency, not 3*CS)
+            float mv[16], lv[16], ov[16];
+#pragma unroll
+            for (int c = 0; c < 16; c++) {
+                mv[c] = -INFINITY;
+                lv[c] = 0.0f;
+                ov[c] = 0.0f;
+                if (c < CS) {
+                    mv[c] = ld_dsmem(dsmem_addr(&cml[r * 2], (uint32_t) c));
+                    lv[c] = ld_dsmem(dsmem_addr(&cml[r * 2 + 1], (uint32_t) c));
+                    ov[c] = ld_dsmem(dsmem_addr(&redO[r * D + d], (uint32_t) c));
+                }
+            }
+            float M = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 16; c++) {
+                M = fmaxf(M, mv[c]);
+            }
+            float O = 0.0f, Ls = 0.0f;
+            if (M != -INFINITY) {
+#pragma unroll
+                for (int c = 0; c < 16; c++) {
+                    const float w = mv[c] == -INFINITY ? 0.0f : exp2f(mv[c] - M);
+                    O += w * ov[c];
+                    Ls += w * lv[c];
+                }
+            }
+            const int rf  = rgrp * MMA_RMAX + r;
+            const int h   = g * p.ratio + rf / p.n_q;
+            const int i   = rf % p.n_q;
+            float *   out = reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 + (int64_t) i * p.d_nb2 +
+                                                    (int64_t) sq * p.d_nb3);
+            out[d]        = Ls > 0.0f ? O / Ls : 0.0f;
+        }
+        __syncwarp();
+        cluster_sync_all();  // peers may still be reading this CTA's shared memory
     }
     if (flag[0] && tid == 0) {
         atomicOr(&p.status[0], ST_TIMEOUT);
@@ -616,16 +792,30 @@ bool encode_kv_map(CUtensorMap * tm, const void * data, bool bf16, int64_t D, in
     return r == CUDA_SUCCESS;
 }
 
-template <int D, bool BF16, int NT>
-void * mma_kernel(int & smem) {
-    smem = MmaSmem<D, NT>::TOTAL;
-    return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT>);
+template <int D, bool BF16, int NT, bool CL>
+void * mma_kernel(int ns, int & smem) {
+    if (ns == 6) {
+        smem = MmaSmem<D, NT, 6>::TOTAL;
+        return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT, CL, 6>);
+    }
+    smem = MmaSmem<D, NT, 3>::TOTAL;
+    return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT, CL, 3>);
 }
 
-void * select_mma_kernel(int D, bool bf16, int nt, int & smem) {
-#define MM3FA_SELM(DD, BB, NN)                      \
-    if (D == DD && bf16 == BB && nt == NN) {        \
-        return mma_kernel<DD, BB, NN>(smem);        \
+// Ring depth: 3 stages (two CTAs per SM) or 6 (one CTA per SM); MM3FA_DECODE_NSTAGE overrides.
+int mma_nstage() {
+    static const int ns = [] {
+        const char * e = std::getenv("MM3FA_DECODE_NSTAGE");
+        return (e && std::atoi(e) == 6) ? 6 : 3;
+    }();
+    return ns;
+}
+
+void * select_mma_kernel(int D, bool bf16, int nt, bool cluster, int & smem) {
+    const int ns = mma_nstage();
+#define MM3FA_SELM(DD, BB, NN)                                                                          \
+    if (D == DD && bf16 == BB && nt == NN) {                                                            \
+        return cluster ? mma_kernel<DD, BB, NN, true>(ns, smem) : mma_kernel<DD, BB, NN, false>(ns, smem); \
     }
     MM3FA_SELM(128, false, 1)
     MM3FA_SELM(128, false, 2)
@@ -639,6 +829,33 @@ void * select_mma_kernel(int D, bool bf16, int nt, int & smem) {
     return nullptr;
 }
 
+// Clusters of `cs` CTAs the device can hold at once for this kernel (0 if it cannot).
+int max_active_clusters(void * fn, int cs, int smem) {
+    if (cs > 8) {
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+    }
+    cudaLaunchConfig_t   cfg{};
+    cudaLaunchAttribute  attr[1];
+    cfg.gridDim          = dim3((unsigned) cs);
+    cfg.blockDim         = dim3(MMA_THREADS);
+    cfg.dynamicSmemBytes = (size_t) smem;
+    attr[0].id               = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned) cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs                = attr;
+    cfg.numAttrs             = 1;
+    int n                    = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
 }  // namespace
 
 bool decode_mma_eligible(int D, int kvt, int rows_per_pair) {
@@ -648,7 +865,7 @@ bool decode_mma_eligible(int D, int kvt, int rows_per_pair) {
 
 int decode_mma_ctas_per_sm(int D, int kvt, int rows_per_pair) {
     int    smem = 0;
-    void * fn   = select_mma_kernel(D, kvt == KV_BF16, rows_per_pair <= 8 ? 1 : 2, smem);
+    void * fn   = select_mma_kernel(D, kvt == KV_BF16, rows_per_pair <= 8 ? 1 : 2, false, smem);
     if (!fn) {
         return 0;
     }
@@ -661,12 +878,48 @@ int decode_mma_ctas_per_sm(int D, int kvt, int rows_per_pair) {
     return nb;
 }
 
+// Cluster size for `n_units` units on a device with `slots` resident CTAs: the largest size
+// <= 16 with n_units * cs <= slots whose clusters all fit at once; 0 selects the stream-K split
+// (too few units to fill the GPU with clusters).  Cached per (device, kernel, units).
+int decode_mma_cluster_size(int D, int kvt, int rows_per_pair, int64_t n_units, int slots) {
+    if (n_units * 16 < slots / 2 || n_units <= 0) {
+        return 0;
+    }
+    int cs = (int) std::min<int64_t>(16, std::max<int64_t>(1, slots / n_units));
+    const int nt  = rows_per_pair <= 8 ? 1 : 2;
+    int       dev = 0;
+    cudaGetDevice(&dev);
+    static std::mutex                                   mu;
+    static std::map<std::tuple<int, int, int, int, int, int64_t>, int> cache;
+    std::lock_guard<std::mutex>                         lock(mu);
+    const auto key = std::make_tuple(dev, D, kvt, nt, slots, n_units);
+    auto       it  = cache.find(key);
+    if (it != cache.end()) {
+        return it->second;
+    }
+    int    smem = 0;
+    void * fn   = select_mma_kernel(D, kvt == KV_BF16, nt, true, smem);
+    if (!fn) {
+        return 0;
+    }
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    while (cs > 1) {
+        const int n = max_active_clusters(fn, cs, smem);
+        if ((int64_t) n >= std::min<int64_t>(n_units, (int64_t) slots / cs)) {
+            break;
+        }
+        cs--;
+    }
+    cache[key] = cs;
+    return cs;
+}
+
 cudaError_t launch_decode_mma(DecodeParams p, const DecodeGeometry & g, int D, int kvt, int64_t n_head_kv,
-                              int64_t n_seq_k, void * workspace, cudaStream_t stream) {
+                              int64_t n_seq_k, int cluster, void * workspace, cudaStream_t stream) {
     const bool bf16 = kvt == KV_BF16;
     const int  nt   = p.rows_per_pair <= 8 ? 1 : 2;
     int        smem = 0;
-    void *     fn   = select_mma_kernel(D, bf16, nt, smem);
+    void *     fn   = select_mma_kernel(D, bf16, nt, cluster > 0, smem);
     if (!fn) {
         return cudaErrorInvalidValue;
     }
@@ -687,12 +940,42 @@ cudaError_t launch_decode_mma(DecodeParams p, const DecodeGeometry & g, int D, i
     p.max_slots       = g.max_slots;
     p.rows_per_unit   = g.rows_per_unit;
     p.groups          = g.groups;
-    cudaError_t e     = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    p.cluster         = cluster;
+    unsigned grid     = (unsigned) g.n_ctas;
+    if (cluster > 0) {
+        // one unit per cluster; each CTA a slice of whole stages
+        int64_t w      = (p.n_kv + cluster - 1) / cluster;
+        w              = (w + MMA_C - 1) / MMA_C * MMA_C;
+        p.keys_per_cta = w;
+        grid           = (unsigned) (g.n_units * cluster);
+    }
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) {
         return e;
     }
+    if (cluster > 8) {
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) {
+            return e;
+        }
+    }
+    cudaLaunchConfig_t  cfg{};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim          = dim3(grid);
+    cfg.blockDim         = dim3(MMA_THREADS);
+    cfg.dynamicSmemBytes = (size_t) smem;
+    cfg.stream           = stream;
+    cfg.numAttrs         = 0;
+    if (cluster > 0) {
+        attr[0].id               = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned) cluster;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs                = attr;
+        cfg.numAttrs             = 1;
+    }
     void * args[] = { &tmk, &tmv, &p };
-    return cudaLaunchKernel(fn, dim3((unsigned) g.n_ctas), dim3(MMA_THREADS), args, (size_t) smem, stream);
+    return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 }  // namespace mm3fa

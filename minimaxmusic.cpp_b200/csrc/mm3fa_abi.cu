@@ -97,6 +97,13 @@ int ctas_per_sm_cached(int D, int kvt, Variant var) {
     return c;
 }
 
+// MM3FA_DECODE_SPLIT=streamk|auto (default auto): the tensor-core kernel's work split;
+// auto uses thread-block clusters when there are enough units to fill the GPU.
+int decode_mma_mode_preference() {
+    const char * e = std::getenv("MM3FA_DECODE_SPLIT");
+    return (e && std::strcmp(e, "streamk") == 0) ? 1 : 0;
+}
+
 // MM3FA_DECODE=simt|mma|auto (default auto) selects the decode kernel where both apply.
 int decode_preference() {
     const char * e = std::getenv("MM3FA_DECODE");
@@ -217,7 +224,9 @@ int check_op(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor 
     if (s.DV != s.D || (s.D != 64 && s.D != 128)) {
         return MM3FA_ERR_UNSUPPORTED;
     }
-    if (s.n_kv > (int64_t) 0x7fffffff || s.n_q > 65535 || s.n_head > 65535) {
+    // index math in the kernels uses 32-bit unit numbers and key counts
+    if (s.n_kv > (int64_t) 0x7fffffff || s.n_q > 65535 || s.n_head > 65535 ||
+        s.n_seq * s.n_head_kv * ((s.n_head / s.n_head_kv) * s.n_q / 32 + 1) > (int64_t) 0x7fffffff) {
         return MM3FA_ERR_UNSUPPORTED;
     }
     s.ratio = (int) (s.n_head / s.n_head_kv);
@@ -456,7 +465,12 @@ int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const m
     p.m1        = std::pow(2.0f, -max_bias / 2.0f / (float) n_head_log2);
     p.timeout_ns = wait_timeout_ns();
     if (var >= V_MMA_8) {
-        return record_cuda(launch_decode_mma(p, g, (int) s.D, s.kvt, s.n_head_kv, s.n_seq_k, workspace, cs));
+        const int slots   = device_info().sms * ctas_per_sm_cached((int) s.D, s.kvt, var);
+        const int pref    = decode_mma_mode_preference();
+        const int cluster = pref == 1 ? 0
+                                      : decode_mma_cluster_size((int) s.D, s.kvt, p.rows_per_pair, g.n_units, slots);
+        return record_cuda(
+            launch_decode_mma(p, g, (int) s.D, s.kvt, s.n_head_kv, s.n_seq_k, cluster, workspace, cs));
     }
     return record_cuda(launch_decode(p, g, (int) s.D, s.kvt, s.bulk, workspace, cs));
 }

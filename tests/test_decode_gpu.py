@@ -22,11 +22,16 @@ pytestmark = pytest.mark.gpu
 F16, BF16, Q8 = ggml.GGML_TYPE_F16, ggml.GGML_TYPE_BF16, ggml.GGML_TYPE_Q8_0
 
 
-@pytest.fixture(params=["auto", "simt"])
+@pytest.fixture(params=["auto", "simt", "mma-streamk"])
 def kernel(request, monkeypatch):
     """Runs a test on the default dispatch (the tensor-core kernel for F16/BF16 with <= 16 rows
-    per unit) and again on the CUDA-core kernel (MM3FA_DECODE=simt)."""
-    monkeypatch.setenv("MM3FA_DECODE", request.param)
+    per unit, split over thread-block clusters when there are enough units), on the CUDA-core
+    kernel (MM3FA_DECODE=simt), and on the tensor-core kernel forced onto the stream-K split."""
+    if request.param == "mma-streamk":
+        monkeypatch.setenv("MM3FA_DECODE", "mma")
+        monkeypatch.setenv("MM3FA_DECODE_SPLIT", "streamk")
+    else:
+        monkeypatch.setenv("MM3FA_DECODE", request.param)
     return request.param
 
 
