@@ -41,8 +41,9 @@ N_KV, MAX_SEQ = 8192, 10240
 FALLBACK_HBM_GBS = 6650.0
 
 # dram__bytes_read.sum + dram__bytes_write.sum per decode launch at this workload, from the
-# ncu capture summarised in profiles/fa_decode_kernel_cfg2_b2_kv8192.md
-NCU_TRAFFIC_BYTES = 67_239_680 + 921_344
+# ncu capture summarised in profiles/ (None: not yet captured for the kernel below)
+NCU_KERNEL = "fa_decode_mma_kernel<128,f16,NT=1,cluster,NS=3>"
+NCU_TRAFFIC_BYTES = None
 
 
 def layer_bytes(n_seq: int, n_head_kv: int, n_head: int) -> int:
@@ -381,7 +382,7 @@ def main() -> None:
                     "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
-                         "traffic": NCU_TRAFFIC_BYTES, "kernel": "fa_decode_kernel<128,F16,64,4,bulk>",
+                         "traffic": NCU_TRAFFIC_BYTES, "kernel": NCU_KERNEL,
                          "avg_launch_us": round(avg_launch_us, 3)},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,

@@ -9,22 +9,30 @@ namespace mm3fa {
 
 // Iterates the stages of one CTA's key range [pos, end) of the n_units * n_kv key positions;
 // a stage never crosses a unit boundary.  One division at construction, none per stage.
+// Strided form (step > 0): the chunks j = first, first + step, ... of one unit.
 struct StageIter {
     int64_t pos, end, unit;
-    int     j, n_kv, C;
+    int     j, n_kv, C, step;
 
-    __device__ StageIter(int64_t g0, int64_t g1, int n_kv_, int C_) : pos(g0), end(g1), n_kv(n_kv_), C(C_) {
+    __device__ StageIter(int64_t g0, int64_t g1, int n_kv_, int C_) : pos(g0), end(g1), n_kv(n_kv_), C(C_), step(0) {
         unit = g0 / n_kv_;
         j    = (int) (g0 - unit * n_kv_);
     }
 
-    __device__ bool has() const { return pos < end; }
+    __device__ StageIter(int64_t unit_, int first, int step_, int n_kv_, int C_)
+        : pos(0), end(0), unit(unit_), j(first), n_kv(n_kv_), C(C_), step(step_) {}
+
+    __device__ bool has() const { return step ? j < n_kv : pos < end; }
 
     __device__ void next(int64_t & u, int & j0, int & n) {
-        u                  = unit;
-        j0                 = j;
+        u  = unit;
+        j0 = j;
+        n  = min(C, n_kv - j);
+        if (step) {
+            j += step;
+            return;
+        }
         const int64_t left = end - pos;
-        n                  = min(C, n_kv - j);
         if ((int64_t) n > left) {
             n = (int) left;
         }

@@ -5,7 +5,7 @@
 // arriver merge of partials in fixed order), for F16/BF16 K/V with <= 16 rows per unit
 // (the CFG decode of src/qwen3-lm.h:784-824: 4 query heads per kv head, 1 query row).
 //
-// Pipeline per CTA (160 threads):
+// Pipeline per CTA (160 threads, two CTAs per SM at D=128):
 //   warp 4 (producer)  - one thread issues 2-D tiled TMA loads (cp.async.bulk.tensor, 128-byte
 //                        swizzle, no multicast) of C=64 keys x D of K and V per stage into an
 //                        NSTAGE ring; full/empty mbarriers, no block-wide barrier in the loop.
@@ -30,15 +30,15 @@
 
 namespace mm3fa {
 
-constexpr int MMA_CONSUMERS = 4;                       // consumer warps
+constexpr int MMA_CONSUMERS = 4;                         // consumer warps
 constexpr int MMA_THREADS   = 32 * (MMA_CONSUMERS + 1);  // + producer warp
-constexpr int MMA_C         = 64;                      // keys per stage (16 per consumer warp)
-constexpr int MMA_RMAX      = 32;                      // rows per unit in the partial layout
+constexpr int MMA_C         = 16 * MMA_CONSUMERS;        // keys per stage (16 per consumer warp)
+constexpr int MMA_RMAX      = 32;                        // rows per unit in the partial layout
 
 template <int D, int NT, int NS>
 struct MmaSmem {
     static constexpr int HALVES     = D / 64;                 // 128-byte column blocks per row
-    static constexpr int TILE       = MMA_C * 128;            // one TMA box: 64 keys x 128 B
+    static constexpr int TILE       = MMA_C * 128;            // one TMA box: MMA_C keys x 128 B
     static constexpr int MAT        = HALVES * TILE;          // K or V of one stage
     static constexpr int STAGE      = 2 * MAT;
     static constexpr int OFF_RED_O  = NS * STAGE;     // [row][D] merged O of the 4 warps
@@ -155,6 +155,17 @@ __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// ---- programmatic dependent launch: the next kernel in the stream may launch (and run up to
+// its own griddepcontrol.wait) once every CTA here has signalled; wait() returns when the
+// previous kernel in the stream has completed and its memory writes are visible.
+__device__ __forceinline__ void pdl_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // byte offset of (key row j, 16-byte chunk c) inside one 128-byte-swizzled TMA box
 __device__ __forceinline__ uint32_t swz(int j, int c) {
     return (uint32_t) (j * 128 + ((c ^ (j & 7)) << 4));
@@ -168,7 +179,7 @@ __device__ __forceinline__ uint32_t swz(int j, int c) {
 //                  distributed shared memory behind a cluster barrier - no global partials,
 //                  fences or atomics; the workspace only carries the status word.
 template <int D, bool BF16, int NT, bool CLUSTER, int NS>
-__global__ void __launch_bounds__(MMA_THREADS, NS <= 3 ? 2 : 1)
+__global__ void __launch_bounds__(MMA_THREADS, 2)
     fa_decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                          const DecodeParams p) {
     using L          = MmaSmem<D, NT, NS>;
@@ -187,11 +198,12 @@ __global__ void __launch_bounds__(MMA_THREADS, NS <= 3 ? 2 : 1)
     const int warp = tid >> 5;
     const int lane = tid & 31;
 
+    // the stages this CTA streams: in cluster mode the unit's C-key chunks rank, rank + CS,
+    // rank + 2 CS, ... (interleaved, so the cluster sweeps the slab together and every CTA sees
+    // the same mix of memory); otherwise a contiguous range of the stream-K cut
     int64_t g0, g1;
     if (CLUSTER) {
-        const int64_t ubase = (int64_t) (blockIdx.x / p.cluster) * p.n_kv;
-        g0                  = min(ubase + (int64_t) (blockIdx.x % p.cluster) * p.keys_per_cta, ubase + p.n_kv);
-        g1                  = min(g0 + p.keys_per_cta, ubase + p.n_kv);  // may be empty: still joins the cluster
+        g0 = g1 = 0;
     } else {
         const int64_t total = p.n_units * (int64_t) p.n_kv;
         g0                  = (int64_t) blockIdx.x * p.keys_per_cta;
@@ -212,12 +224,15 @@ __global__ void __launch_bounds__(MMA_THREADS, NS <= 3 ? 2 : 1)
         fence_mbar_init();
     }
     __syncthreads();
+    pdl_wait();  // nothing global (inputs, dst, workspace) is touched before this point
     const uint64_t deadline = global_timer_ns() + p.timeout_ns;
 
     // ================================================================ producer warp
     if (warp == MMA_CONSUMERS) {
         if (lane == 0) {
-            StageIter it{ g0, g1, p.n_kv, MMA_C };
+            StageIter it = CLUSTER ? StageIter((int64_t) (blockIdx.x / p.cluster), (int) (blockIdx.x % p.cluster) * MMA_C,
+                                          p.cluster * MMA_C, p.n_kv, MMA_C)
+                                : StageIter(g0, g1, p.n_kv, MMA_C);
             int        s = 0;
             bool       ok = true;
             while (it.has()) {
@@ -246,12 +261,16 @@ __global__ void __launch_bounds__(MMA_THREADS, NS <= 3 ? 2 : 1)
                 }
                 s++;
             }
+            pdl_launch_dependents();
             // the last loads issued must land before this CTA's shared memory is released
             // (consumers normally wait for them too; this matters when a wait expired)
             const uint64_t drain = global_timer_ns() + p.timeout_ns;
             for (int t = max(0, s - NS); t < s; t++) {
                 mbar_wait_bounded(&full[t % NS], (uint32_t) ((t / NS) & 1), drain);
             }
+        }
+        else {
+            pdl_launch_dependents();
         }
         if (!CLUSTER) {
             return;
@@ -511,9 +530,10 @@ __global__ void __launch_bounds__(MMA_THREADS, NS <= 3 ? 2 : 1)
     if (CLUSTER) {  // the cluster's unit, even when this CTA's key slice is empty
         cur_unit = blockIdx.x / p.cluster;
         begin_unit(cur_unit);
-        seg_j0 = seg_j1 = (int) (g0 - cur_unit * (int64_t) p.n_kv);
     }
-    StageIter it{ g0, g1, p.n_kv, MMA_C };
+    StageIter it = CLUSTER ? StageIter((int64_t) (blockIdx.x / p.cluster), (int) (blockIdx.x % p.cluster) * MMA_C,
+                                          p.cluster * MMA_C, p.n_kv, MMA_C)
+                                : StageIter(g0, g1, p.n_kv, MMA_C);
     int        s = 0;
     while (it.has()) {
         int64_t unit;
@@ -684,6 +704,7 @@ __global__ void __launch_bounds__(MMA_THREADS, NS <= 3 ? 2 : 1)
         }
         s++;
     }
+    pdl_launch_dependents();
     if (cur_unit >= 0) {
         end_unit(cur_unit);
     }
@@ -794,19 +815,20 @@ bool encode_kv_map(CUtensorMap * tm, const void * data, bool bf16, int64_t D, in
 
 template <int D, bool BF16, int NT, bool CL>
 void * mma_kernel(int ns, int & smem) {
-    if (ns == 6) {
-        smem = MmaSmem<D, NT, 6>::TOTAL;
-        return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT, CL, 6>);
+    if (ns == 2) {
+        smem = MmaSmem<D, NT, 2>::TOTAL;
+        return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT, CL, 2>);
     }
     smem = MmaSmem<D, NT, 3>::TOTAL;
     return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT, CL, 3>);
 }
 
-// Ring depth: 3 stages (two CTAs per SM) or 6 (one CTA per SM); MM3FA_DECODE_NSTAGE overrides.
+// Ring depth: 3 stages of 64 keys per CTA (two CTAs, 192 KiB of K/V in flight per SM at
+// D=128) or 2; MM3FA_DECODE_NSTAGE=2 overrides.
 int mma_nstage() {
     static const int ns = [] {
         const char * e = std::getenv("MM3FA_DECODE_NSTAGE");
-        return (e && std::atoi(e) == 6) ? 6 : 3;
+        return (e && std::atoi(e) == 2) ? 2 : 3;
     }();
     return ns;
 }
@@ -943,11 +965,7 @@ cudaError_t launch_decode_mma(DecodeParams p, const DecodeGeometry & g, int D, i
     p.cluster         = cluster;
     unsigned grid     = (unsigned) g.n_ctas;
     if (cluster > 0) {
-        // one unit per cluster; each CTA a slice of whole stages
-        int64_t w      = (p.n_kv + cluster - 1) / cluster;
-        w              = (w + MMA_C - 1) / MMA_C * MMA_C;
-        p.keys_per_cta = w;
-        grid           = (unsigned) (g.n_units * cluster);
+        grid = (unsigned) (g.n_units * cluster);  // one unit per cluster, chunks interleaved over its CTAs
     }
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) {
@@ -960,19 +978,30 @@ cudaError_t launch_decode_mma(DecodeParams p, const DecodeGeometry & g, int D, i
         }
     }
     cudaLaunchConfig_t  cfg{};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     cfg.gridDim          = dim3(grid);
     cfg.blockDim         = dim3(MMA_THREADS);
     cfg.dynamicSmemBytes = (size_t) smem;
     cfg.stream           = stream;
+    cfg.attrs            = attr;
     cfg.numAttrs         = 0;
+    // programmatic dependent launch (opt-in, MM3FA_PDL=1): lets this launch overlap the
+    // previous kernel's tail; measured neutral on back-to-back decode layers, so off by default
+    static const bool pdl = [] {
+        const char * e = std::getenv("MM3FA_PDL");
+        return e && std::atoi(e) == 1;
+    }();
+    if (pdl) {
+        attr[cfg.numAttrs].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs++;
+    }
     if (cluster > 0) {
-        attr[0].id               = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = (unsigned) cluster;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs                = attr;
-        cfg.numAttrs             = 1;
+        attr[cfg.numAttrs].id               = cudaLaunchAttributeClusterDimension;
+        attr[cfg.numAttrs].val.clusterDim.x = (unsigned) cluster;
+        attr[cfg.numAttrs].val.clusterDim.y = 1;
+        attr[cfg.numAttrs].val.clusterDim.z = 1;
+        cfg.numAttrs++;
     }
     void * args[] = { &tmk, &tmv, &p };
     return cudaLaunchKernelExC(&cfg, fn, args);
