@@ -8,6 +8,7 @@ tree; it statically links the CUDA runtime and has no torch dependency.
 from __future__ import annotations
 
 import argparse
+import concurrent.futures
 import os
 import subprocess
 import sys
@@ -18,8 +19,8 @@ LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libmm3fa.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["mm3fa_abi.cu", "fa_decode.cu", "fa_decode_mma.cu", "mm3fa_noalloc.cu"]
-HEADERS = ["fa_common.cuh", "fa_decode.cuh"]
+SOURCES = ["mm3fa_abi.cu", "fa_decode.cu", "fa_decode_mma.cu", "fa_dense_sm100.cu", "mm3fa_noalloc.cu"]
+HEADERS = ["fa_common.cuh", "fa_decode.cuh", "fa_dense.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -48,11 +49,24 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     if not force and not ptxas_info and not _stale():
         return LIB
     os.makedirs(LIBDIR, exist_ok=True)
+    objdir = os.path.join(HERE, "_build")
+    os.makedirs(objdir, exist_ok=True)
+
+    def compile_one(src: str) -> str:
+        obj = os.path.join(objdir, os.path.splitext(src)[0] + ".o")
+        cmd = [nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-c", os.path.join(CSRC, src), "-o", obj]
+        if ptxas_info:
+            cmd += ["-Xptxas", "-v"]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        subprocess.run(cmd, check=True)
+        return obj
+
+    # translation units compile in parallel; the link is one nvcc -shared step
+    with concurrent.futures.ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
+        objs = list(ex.map(compile_one, SOURCES))
     tmp = LIB + ".tmp"
-    cmd = [nvcc(), *NVCC_FLAGS, "-shared", "-I", INCLUDE, "-o", tmp]
-    if ptxas_info:
-        cmd += ["-Xptxas", "-v"]
-    cmd += [os.path.join(CSRC, f) for f in SOURCES]
+    cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp, *objs]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)

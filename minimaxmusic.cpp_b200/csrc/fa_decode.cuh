@@ -3,6 +3,7 @@
 
 #include "fa_common.cuh"
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace mm3fa {
@@ -174,6 +175,13 @@ size_t decode_workspace_bytes(const DecodeGeometry & g, int D);
 
 cudaError_t launch_decode(DecodeParams p, const DecodeGeometry & g, int D, int kvt, bool bulk, void * workspace,
                           cudaStream_t stream);
+
+// TMA tensor map of a [D, n_kv, Hkv, S_k] F16/BF16 ggml view: boxes of 64 elements x box_rows
+// keys, 128-byte swizzle (fa_decode_mma.cu).  False when the driver entry point is missing or the
+// strides cannot be expressed.
+bool encode_kv_tensor_map(CUtensorMap * tm, const void * data, bool bf16, int64_t D, int64_t n_kv, int64_t hkv,
+                          int64_t sk, int64_t nb1, int64_t nb2, int64_t nb3, int box_rows);
+bool tensor_maps_available();
 
 // Tensor-core variant (fa_decode_mma.cu): F16/BF16 K/V, D 64 or 128, <= 16 rows per unit,
 // strides that a TMA tensor map can express.

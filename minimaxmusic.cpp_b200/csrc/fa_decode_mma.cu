@@ -771,8 +771,6 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
 
 // ------------------------------------------------------------------ host side
 
-namespace {
-
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag                     once;
@@ -788,9 +786,9 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// 4-D map of a [D, n_kv, Hkv, S_k] ggml view, box = 64 elements x 64 keys, 128-byte swizzle.
-bool encode_kv_map(CUtensorMap * tm, const void * data, bool bf16, int64_t D, int64_t n_kv, int64_t hkv,
-                   int64_t sk, int64_t nb1, int64_t nb2, int64_t nb3) {
+// 4-D map of a [D, n_kv, Hkv, S_k] ggml view, box = 64 elements x box_rows keys, 128-byte swizzle.
+bool encode_kv_tensor_map(CUtensorMap * tm, const void * data, bool bf16, int64_t D, int64_t n_kv, int64_t hkv,
+                          int64_t sk, int64_t nb1, int64_t nb2, int64_t nb3, int box_rows) {
     auto enc = tensor_map_encoder();
     if (!enc) {
         return false;
@@ -804,7 +802,7 @@ bool encode_kv_map(CUtensorMap * tm, const void * data, bool bf16, int64_t D, in
     }
     cuuint64_t dims[4]    = { (cuuint64_t) D, (cuuint64_t) n_kv, (cuuint64_t) hkv, (cuuint64_t) sk };
     cuuint64_t strides[3] = { (cuuint64_t) nb1, (cuuint64_t) nb2, (cuuint64_t) nb3 };
-    cuuint32_t box[4]     = { 64, (cuuint32_t) MMA_C, 1, 1 };
+    cuuint32_t box[4]     = { 64, (cuuint32_t) box_rows, 1, 1 };
     cuuint32_t estr[4]    = { 1, 1, 1, 1 };
     CUresult   r = enc(tm, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
                        const_cast<void *>(data), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -812,6 +810,12 @@ bool encode_kv_map(CUtensorMap * tm, const void * data, bool bf16, int64_t D, in
                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
+
+bool tensor_maps_available() {
+    return tensor_map_encoder() != nullptr;
+}
+
+namespace {
 
 template <int D, bool BF16, int NT, bool CL>
 void * mma_kernel(int ns, int & smem) {
@@ -946,8 +950,8 @@ cudaError_t launch_decode_mma(DecodeParams p, const DecodeGeometry & g, int D, i
         return cudaErrorInvalidValue;
     }
     alignas(64) CUtensorMap tmk, tmv;
-    if (!encode_kv_map(&tmk, p.k, bf16, D, p.n_kv, n_head_kv, n_seq_k, p.k_nb1, p.k_nb2, p.k_nb3) ||
-        !encode_kv_map(&tmv, p.v, bf16, D, p.n_kv, n_head_kv, n_seq_k, p.v_nb1, p.v_nb2, p.v_nb3)) {
+    if (!encode_kv_tensor_map(&tmk, p.k, bf16, D, p.n_kv, n_head_kv, n_seq_k, p.k_nb1, p.k_nb2, p.k_nb3, MMA_C) ||
+        !encode_kv_tensor_map(&tmv, p.v, bf16, D, p.n_kv, n_head_kv, n_seq_k, p.v_nb1, p.v_nb2, p.v_nb3, MMA_C)) {
         return cudaErrorInvalidValue;
     }
     char *       ws   = static_cast<char *>(workspace);

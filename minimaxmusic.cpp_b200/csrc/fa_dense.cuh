@@ -1,0 +1,48 @@
+// fa_dense.cuh - host interface of the tensor-core (tcgen05) flash-attention kernel for many
+// query rows (fa_dense_sm100.cu): LM prefill and DiT attention.
+#pragma once
+
+#include "fa_common.cuh"
+
+#include <cuda_runtime.h>
+
+namespace mm3fa {
+
+// Class of one 128 x 128 (query, key) block of a mask plane.
+enum : uint8_t { BLK_NONE = 0, BLK_MIXED = 1, BLK_SKIP = 2 };
+
+struct DenseParams {
+    const char * q;
+    const char * k;
+    const char * v;
+    const char * mask;  // F16, may be null
+    char *       dst;
+    int64_t      q_nb1, q_nb2, q_nb3;
+    int64_t      k_nb1, k_nb2, k_nb3;
+    int64_t      v_nb1, v_nb2, v_nb3;
+    int64_t      m_nb1, m_nb2, m_nb3;
+    int64_t      d_nb1, d_nb2, d_nb3;
+    int          q_type;
+    int          q_vec;     // Q rows start 16-byte aligned: 16-byte loads
+    int          dst_vec;   // dst rows start 16-byte aligned: 16-byte stores
+    int          mask_vec;  // mask rows start 16-byte aligned: 16-byte loads
+    int          n_q, n_kv;
+    int          ratio;     // n_head / n_head_kv
+    int          rk3;       // n_seq / n_seq_k
+    int          m_ne2, m_ne3;
+    float        scale, softcap, max_bias, m0, m1;
+    int          n_head_log2;
+    int          n_qt, n_kt;              // 128-row query tiles, 128-key tiles
+    const uint8_t * blocks;               // [plane][n_qt][n_kt] block classes, null without mask
+    uint32_t *   status;
+    uint64_t     timeout_ns;
+};
+
+// F16/BF16 K and V, D = DV = 64 or 128, TMA-expressible strides.
+bool        dense_eligible(int D, int kvt);
+// Workspace bytes: status word and the mask block classes.
+size_t      dense_workspace_bytes(int64_t n_q, int64_t n_kv, int64_t planes);
+cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64_t n_seq_k, int64_t n_head,
+                         int64_t n_seq, void * workspace, cudaStream_t stream);
+
+}  // namespace mm3fa

@@ -1,0 +1,741 @@
+// fa_dense_sm100.cu - flash attention for many query rows on the 5th-generation tensor cores
+// (tcgen05 + TMEM + TMA), sm_100a.
+//
+// Serves GGML_OP_FLASH_ATTN_EXT when every (sequence, query head) has many query rows: the causal
+// LM prefill of src/qwen3-lm.h:395-436 (Q [128, S, 32] F32 permuted view, K/V F16 views of the
+// cache, F16 causal mask [n_kv_pad, S]) and the bidirectional DiT attention of src/dit.h:201-222
+// (Q [64, S, 32, B], K/V F16 contiguous, no mask).
+//
+// One CTA per (128-query tile, query head, sequence); 192 threads in fixed roles:
+//   warp 0, lane 0   TMA producer: 128-key tiles of K and V (boxes of 64 elements x 128 keys,
+//                    128-byte swizzle, no multicast) into 2-deep rings, full/empty mbarriers.
+//   warp 1           allocates 512 TMEM columns; lane 0 issues every tcgen05.mma:
+//                      S[i%2] (TMEM, 128 x 128 f32)  = Q . K_i^T     A, B K-major in smem
+//                      O      (TMEM, 128 x D   f32) += P_i . V_i     A = P (smem, K-major),
+//                                                                    B = V (smem, MN-major)
+//                    in the order QK0, QK1, PV0, QK2, PV1, ... so the tensor core computes
+//                    S_{i+1} while the softmax works on S_i; completion is signalled with
+//                    tcgen05.commit on mbarriers.
+//   warps 2-5        softmax warpgroup: thread t owns query row t (TMEM lane t), so a row's
+//                    max and sum never leave the thread.  Per tile: tcgen05.ld S, scale /
+//                    softcap / mask (log2 units), online softmax with a lazily updated
+//                    maximum (O is rescaled only when the row maximum grows by more than 2^8;
+//                    otherwise the stale maximum is kept, which is exact), P rounded to K's type
+//                    into swizzled smem, then O rescaled in TMEM if needed.  At the end O / l is
+//                    written to dst.
+// Q is converted from F32 (any ggml strides) to K's type by the softmax warps while the first
+// tiles load - ggml's convention of rounding Q to K's vec-dot type.
+//
+// Masks: a pre-pass classifies every 128 x 128 (query, key) block of each mask plane as
+// all -inf (the tile is skipped - causal prefill skips about half the work), all zero (no mask
+// arithmetic) or mixed (mask added element by element).  Keys past n_kv are masked explicitly.
+//
+// Every wait is bounded by the global timer; on expiry the CTA records the status word, waits
+// (bounded) for its copies and tensor-core work in flight, frees its TMEM and returns.  Waits of
+// the softmax warps are made warp-uniform so the .sync.aligned TMEM accesses never diverge.
+#include "fa_dense.cuh"
+#include "fa_decode.cuh"
+
+#include <cuda.h>
+
+#include <algorithm>
+#include <cstdlib>
+
+namespace mm3fa {
+
+constexpr int DN_THREADS = 192;
+constexpr int DN_M       = 128;  // query rows per CTA (UMMA M)
+constexpr int DN_N       = 128;  // keys per tile (UMMA N of QK, K of PV)
+constexpr int DN_TMEM    = 512;  // allocated columns: S0 [0,128), S1 [128,256), O [256, 256+D)
+constexpr uint32_t DN_OCOL = 256;
+
+template <int D>
+struct DenseSmem {
+    static constexpr int HALVES   = D / 64;              // 128-byte column blocks of a D-wide row
+    static constexpr int QT       = HALVES * DN_M * 128;  // Q tile
+    static constexpr int KT       = HALVES * DN_N * 128;  // K or V tile
+    static constexpr int PT       = 2 * DN_M * 128;       // P tile: 128 keys = two 64-key blocks
+    static constexpr int OFF_Q    = 0;
+    static constexpr int OFF_K    = OFF_Q + QT;            // [2]
+    static constexpr int OFF_V    = OFF_K + 2 * KT;        // [2]
+    static constexpr int OFF_P    = OFF_V + 2 * KT;
+    static constexpr int OFF_BAR  = OFF_P + PT;            // 16 mbarriers
+    static constexpr int OFF_MISC = OFF_BAR + 16 * 8;      // tmem base, abort flag
+    static constexpr int TOTAL    = OFF_MISC + 32 + 1024;  // + alignment slack
+};
+
+// mbarrier slots
+enum : int {
+    B_KFULL   = 0,   // [2]
+    B_KEMPTY  = 2,   // [2]
+    B_VFULL   = 4,   // [2]
+    B_VEMPTY  = 6,   // [2]
+    B_SFULL   = 8,   // [2]
+    B_SFREE   = 10,  // [2]
+    B_PFULL   = 12,
+    B_ODONE   = 13,
+    B_QREADY  = 14,
+    B_MMADONE = 15,
+};
+
+// ------------------------------------------------------------------ PTX helpers
+
+__device__ __forceinline__ void dn_tma_load_4d(void * dst, const CUtensorMap * tm, int c0, int c1, int c2, int c3,
+                                               uint64_t * bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void dn_mbar_arrive(uint64_t * bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// warp-uniform bounded wait: true only if every lane saw the phase complete
+__device__ __forceinline__ bool dn_wait_warp(uint64_t * bar, uint32_t parity, uint64_t deadline) {
+    return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, deadline));
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t * dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D (TMEM) = A (smem desc) * B (smem desc) [+ D]; issued by one thread
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// arrive on `bar` once every tcgen05 operation this thread issued before has completed
+__device__ __forceinline__ void umma_commit(uint64_t * bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_addr(bar))
+                 : "memory");
+}
+
+// 32 consecutive 32-bit columns of this thread's TMEM lane (r[0..31] must stay in registers)
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t * r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t * r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_wait() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 2^x on the special-function unit (PTX ex2.approx, flushes denormal results to zero); 2^-inf = 0
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Shared-memory matrix descriptor of a 128-byte-swizzled operand (sm_100 format, version 1).
+// K-major: sbo = 1024 (8-row groups), lbo unused (16).  MN-major: lbo = stride between 64-element
+// column blocks, sbo = 1024 (8-row groups along K).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t) ((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t) ((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t) ((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t) 1 << 46;  // descriptor version of sm_100
+    d |= (uint64_t) 2 << 61;  // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor of kind::f16, F32 accumulator, M = 128, dense.
+__host__ __device__ constexpr uint32_t umma_idesc(bool bf16, int n, bool b_mn_major) {
+    return (1u << 4)                              // D format: F32
+           | ((bf16 ? 1u : 0u) << 7)              // A format: F16 / BF16
+           | ((bf16 ? 1u : 0u) << 10)             // B format
+           | ((b_mn_major ? 1u : 0u) << 16)       // B major (A is K-major: bit 15 = 0)
+           | ((uint32_t) (n >> 3) << 17)          // N / 8
+           | ((uint32_t) (DN_M >> 4) << 24);      // M / 16
+}
+
+// byte offset of (row, 16-byte chunk) in a 128-byte-swizzled tile of 128-byte rows
+__device__ __forceinline__ uint32_t sw128_off(int row, int chunk) {
+    return (uint32_t) (row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2_dn(float lo, float hi) {
+    if (BF16) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<uint32_t *>(&v);
+    }
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// 8 consecutive Q elements (F32/F16/BF16) of a row from element e0; vec: the row and e0 allow
+// 16-byte loads
+__device__ __forceinline__ void ld_q8(const char * row, int type, int e0, bool vec, float (&x)[8]) {
+    if (vec) {
+        if (type == KV_F32) {
+            const float4 a = *reinterpret_cast<const float4 *>(row + (int64_t) e0 * 4);
+            const float4 b = *reinterpret_cast<const float4 *>(row + (int64_t) e0 * 4 + 16);
+            x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+            return;
+        }
+        const uint4    u    = *reinterpret_cast<const uint4 *>(row + (int64_t) e0 * 2);
+        const uint32_t w[4] = { u.x, u.y, u.z, u.w };
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const float2 f = type == KV_F16 ? h2_to_f2(w[j]) : bf2_to_f2(w[j]);
+            x[2 * j]       = f.x;
+            x[2 * j + 1]   = f.y;
+        }
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        x[j] = ld_q_elem(row, type, e0 + j);
+    }
+}
+
+__device__ __forceinline__ int tile_class(const DenseParams & p, int plane, int qt, int kt) {
+    if (!p.blocks) {
+        return BLK_NONE;
+    }
+    return p.blocks[((int64_t) plane * p.n_qt + qt) * p.n_kt + kt];
+}
+
+// ------------------------------------------------------------------ kernel
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(DN_THREADS, 1)
+    fa_dense_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                    const DenseParams p) {
+    using L          = DenseSmem<D>;
+    constexpr int KS = D / 16;  // k-steps of QK
+    extern __shared__ __align__(16) char smem_raw[];
+    char * smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
+    uint64_t * bar       = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(smem + L::OFF_MISC);
+    int *      abort_f   = reinterpret_cast<int *>(smem + L::OFF_MISC + 4);
+
+    const int tid   = threadIdx.x;
+    const int warp  = tid >> 5;
+    const int lane  = tid & 31;
+    const int qt    = blockIdx.x;
+    const int h     = blockIdx.y;
+    const int sq    = blockIdx.z;
+    const int g     = h / p.ratio;
+    const int ks3   = sq / p.rk3;
+    const int q0    = qt * DN_M;
+    const int nrow  = min(DN_M, p.n_q - q0);
+    const int plane = (sq % p.m_ne3) * p.m_ne2 + (h % p.m_ne2);
+
+    if (tid == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
+        for (int i = 0; i < 16; i++) {
+            // the softmax warpgroup's 128 threads arrive on these; one thread on the others
+            const bool wg = i == B_SFREE || i == B_SFREE + 1 || i == B_PFULL || i == B_QREADY;
+            mbar_init(&bar[i], wg ? 128u : 1u);
+        }
+        *abort_f = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, DN_TMEM);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem     = *tmem_slot;
+    const uint64_t deadline = global_timer_ns() + p.timeout_ns;
+
+    // the kv tiles this query tile needs, in order (tiles whose mask block is all -inf are skipped)
+    auto next_tile = [&](int kt) {
+        while (kt < p.n_kt && tile_class(p, plane, qt, kt) == BLK_SKIP) {
+            kt++;
+        }
+        return kt;
+    };
+
+    if (warp == 0) {
+        // ======================================================= TMA producer
+        if (lane == 0) {
+            int  kiss[2] = { 0, 0 }, viss[2] = { 0, 0 };  // loads issued per stage
+            int  i       = 0;
+            bool ok      = true;
+            for (int kt = next_tile(0); kt < p.n_kt; kt = next_tile(kt + 1), i++) {
+                const int st = i & 1;
+                if (i >= 2 && !mbar_wait_bounded(&bar[B_KEMPTY + st], (uint32_t) (((i >> 1) - 1) & 1), deadline)) {
+                    ok = false;
+                    break;
+                }
+                char * dk = smem + L::OFF_K + st * L::KT;
+                mbar_arrive_expect_tx(&bar[B_KFULL + st], (uint32_t) L::KT);
+#pragma unroll
+                for (int hh = 0; hh < L::HALVES; hh++) {
+                    dn_tma_load_4d(dk + hh * DN_N * 128, &tmk, hh * 64, kt * DN_N, g, ks3, &bar[B_KFULL + st]);
+                }
+                kiss[st]++;
+                if (i >= 2 && !mbar_wait_bounded(&bar[B_VEMPTY + st], (uint32_t) (((i >> 1) - 1) & 1), deadline)) {
+                    ok = false;
+                    break;
+                }
+                char * dv = smem + L::OFF_V + st * L::KT;
+                mbar_arrive_expect_tx(&bar[B_VFULL + st], (uint32_t) L::KT);
+#pragma unroll
+                for (int hh = 0; hh < L::HALVES; hh++) {
+                    dn_tma_load_4d(dv + hh * DN_N * 128, &tmv, hh * 64, kt * DN_N, g, ks3, &bar[B_VFULL + st]);
+                }
+                viss[st]++;
+            }
+            if (!ok) {
+                atomicExch(abort_f, 1);
+            }
+            // a load into a stage is issued only after the previous one landed and was consumed, so
+            // the last load of each stage is the only one that can still be in flight
+            const uint64_t drain = global_timer_ns() + p.timeout_ns;
+            for (int st = 0; st < 2; st++) {
+                if (kiss[st] > 0) {
+                    mbar_wait_bounded(&bar[B_KFULL + st], (uint32_t) ((kiss[st] - 1) & 1), drain);
+                }
+                if (viss[st] > 0) {
+                    mbar_wait_bounded(&bar[B_VFULL + st], (uint32_t) ((viss[st] - 1) & 1), drain);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ======================================================= MMA issuer
+        if (lane == 0) {
+            const uint32_t id_qk = umma_idesc(BF16, DN_N, false);
+            const uint32_t id_pv = umma_idesc(BF16, D, true);
+            const uint32_t sq_a  = smem_addr(smem + L::OFF_Q);
+            const uint32_t sp_a  = smem_addr(smem + L::OFF_P);
+            auto issue_qk = [&](int i) -> bool {
+                const int st = i & 1;
+                if (!mbar_wait_bounded(&bar[B_KFULL + st], (uint32_t) ((i >> 1) & 1), deadline)) {
+                    return false;
+                }
+                if (i >= 2 && !mbar_wait_bounded(&bar[B_SFREE + st], (uint32_t) (((i >> 1) - 1) & 1), deadline)) {
+                    return false;
+                }
+                tc_fence_after();
+                const uint32_t sk_a = smem_addr(smem + L::OFF_K + st * L::KT);
+#pragma unroll
+                for (int ks = 0; ks < KS; ks++) {
+                    const uint32_t offq = (uint32_t) ((ks >> 2) * DN_M * 128 + (ks & 3) * 32);
+                    const uint32_t offk = (uint32_t) ((ks >> 2) * DN_N * 128 + (ks & 3) * 32);
+                    umma_f16(tmem + (uint32_t) (st * DN_N), sw128_desc(sq_a + offq, 16, 1024),
+                             sw128_desc(sk_a + offk, 16, 1024), id_qk, ks > 0 ? 1u : 0u);
+                }
+                umma_commit(&bar[B_SFULL + st]);
+                umma_commit(&bar[B_KEMPTY + st]);
+                return true;
+            };
+            auto issue_pv = [&](int i) -> bool {
+                const int st = i & 1;
+                if (!mbar_wait_bounded(&bar[B_PFULL], (uint32_t) (i & 1), deadline)) {
+                    return false;
+                }
+                if (!mbar_wait_bounded(&bar[B_VFULL + st], (uint32_t) ((i >> 1) & 1), deadline)) {
+                    return false;
+                }
+                tc_fence_after();
+                const uint32_t sv_a = smem_addr(smem + L::OFF_V + st * L::KT);
+#pragma unroll
+                for (int kk = 0; kk < DN_N / 16; kk++) {
+                    const uint32_t offp = (uint32_t) ((kk >> 2) * DN_M * 128 + (kk & 3) * 32);
+                    umma_f16(tmem + DN_OCOL, sw128_desc(sp_a + offp, 16, 1024),
+                             sw128_desc(sv_a + (uint32_t) (kk * 16 * 128), (uint32_t) (DN_N * 128), 1024), id_pv,
+                             (i > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(&bar[B_ODONE]);
+                umma_commit(&bar[B_VEMPTY + st]);
+                return true;
+            };
+            int n_tiles = 0;
+            for (int kt = next_tile(0); kt < p.n_kt; kt = next_tile(kt + 1)) {
+                n_tiles++;
+            }
+            bool ok = mbar_wait_bounded(&bar[B_QREADY], 0, deadline);
+            tc_fence_after();
+            if (ok && n_tiles > 0) {
+                ok = issue_qk(0);
+                for (int i = 0; ok && i < n_tiles; i++) {
+                    if (i + 1 < n_tiles) {
+                        ok = issue_qk(i + 1);
+                    }
+                    if (ok) {
+                        ok = issue_pv(i);
+                    }
+                }
+            }
+            if (!ok) {
+                atomicExch(abort_f, 1);
+            }
+            // every MMA issued must have completed before TMEM and shared memory are released
+            umma_commit(&bar[B_MMADONE]);
+            mbar_wait_bounded(&bar[B_MMADONE], 0, global_timer_ns() + p.timeout_ns);
+        }
+    } else {
+        // ======================================================= softmax warpgroup (warps 2-5)
+        const int      quad  = warp & 3;          // TMEM lane quadrant this warp may access
+        const int      r     = quad * 32 + lane;  // query row of this thread (= TMEM lane)
+        const uint32_t tlane = (uint32_t) (quad * 32) << 16;
+        const bool     valid = r < nrow;
+        const int      qi    = q0 + (valid ? r : 0);
+        const float    slope = alibi_slope(h, p.max_bias, p.n_head_log2, p.m0, p.m1);
+
+        // ---- stage Q row r into the swizzled K-major tile, rounded to K's type
+        {
+            const char * qrow = p.q + (int64_t) qi * p.q_nb1 + (int64_t) h * p.q_nb2 + (int64_t) sq * p.q_nb3;
+            char *       qs   = smem + L::OFF_Q;
+#pragma unroll 4
+            for (int c = 0; c < D / 8; c++) {
+                float x[8];
+                if (valid) {
+                    ld_q8(qrow, p.q_type, c * 8, p.q_vec != 0, x);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        x[e] = 0.0f;
+                    }
+                }
+                uint4 v;
+                v.x = pack2_dn<BF16>(x[0], x[1]);
+                v.y = pack2_dn<BF16>(x[2], x[3]);
+                v.z = pack2_dn<BF16>(x[4], x[5]);
+                v.w = pack2_dn<BF16>(x[6], x[7]);
+                *reinterpret_cast<uint4 *>(qs + (c >> 3) * (DN_M * 128) + sw128_off(r, c & 7)) = v;
+            }
+            fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
+            dn_mbar_arrive(&bar[B_QREADY]);
+        }
+
+        const char * mrow = p.mask ? p.mask + (int64_t) qi * p.m_nb1 + (int64_t) (h % p.m_ne2) * p.m_nb2 +
+                                         (int64_t) (sq % p.m_ne3) * p.m_nb3
+                                   : nullptr;
+        const float  sc   = p.softcap != 0.0f ? p.scale / p.softcap : p.scale;
+        const float  ml2  = slope * LOG2E;  // mask -> log2 units
+        float        m    = -INFINITY;      // running maximum (log2 units; may be stale by < 8)
+        float        l    = 0.0f;
+        bool         ok   = true;
+        int          i    = 0;
+        for (int kt = next_tile(0); kt < p.n_kt; kt = next_tile(kt + 1), i++) {
+            const int sb = i & 1;
+            if (!dn_wait_warp(&bar[B_SFULL + sb], (uint32_t) ((i >> 1) & 1), deadline)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t sr[DN_N];
+#pragma unroll
+            for (int c = 0; c < DN_N / 32; c++) {
+                tmem_ld32(tmem + tlane + (uint32_t) (sb * DN_N + c * 32), &sr[c * 32]);
+            }
+            tmem_ld_wait();
+            tc_fence_before();
+            dn_mbar_arrive(&bar[B_SFREE + sb]);  // the S buffer may now take QK_{i+2}
+
+            // scores in log2 units: softcap, scale, mask, keys past n_kv
+            const int nk = p.n_kv - kt * DN_N;  // keys of this tile that exist (may exceed 128)
+            float     s[DN_N];
+#pragma unroll
+            for (int k = 0; k < DN_N; k++) {
+                const float x = __uint_as_float(sr[k]);
+                s[k] = p.softcap != 0.0f ? p.softcap * tanhf(x * sc) * LOG2E : x * (sc * LOG2E);
+            }
+            if (valid && tile_class(p, plane, qt, kt) == BLK_MIXED) {
+                const __half * mp = reinterpret_cast<const __half *>(mrow) + (int64_t) kt * DN_N;
+#pragma unroll
+                for (int c = 0; c < DN_N / 8; c++) {
+                    float mv[8];
+                    if (p.mask_vec && c * 8 + 8 <= nk) {
+                        const uint4    u    = *reinterpret_cast<const uint4 *>(mp + c * 8);
+                        const uint32_t w[4] = { u.x, u.y, u.z, u.w };
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const float2 f = h2_to_f2(w[j]);
+                            mv[2 * j]      = f.x;
+                            mv[2 * j + 1]  = f.y;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            mv[j] = c * 8 + j < nk ? __half2float(mp[c * 8 + j]) : 0.0f;
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        s[c * 8 + j] += ml2 * mv[j];
+                    }
+                }
+            }
+            float mt = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < DN_N; k++) {
+                if (k >= nk) {
+                    s[k] = -INFINITY;
+                }
+                mt = fmaxf(mt, s[k]);
+            }
+            // lazy maximum: rescale only when the row maximum grows by more than 8 (a factor 2^8)
+            float alpha = 1.0f;
+            if (mt > m + 8.0f) {
+                alpha = (m == -INFINITY) ? 0.0f : ex2(m - mt);
+                m     = mt;
+            }
+            float ls = 0.0f;
+            if (m != -INFINITY) {
+#pragma unroll
+                for (int k = 0; k < DN_N; k++) {
+                    s[k] = ex2(s[k] - m);
+                    ls += s[k];
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < DN_N; k++) {
+                    s[k] = 0.0f;
+                }
+            }
+            l = l * alpha + ls;
+
+            // PV_{i-1} must be complete: it reads the P buffer and accumulates into O
+            if (i > 0) {
+                if (!dn_wait_warp(&bar[B_ODONE], (uint32_t) ((i - 1) & 1), deadline)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+                    for (int c = 0; c < D / 32; c++) {
+                        uint32_t o[32];
+                        tmem_ld32(tmem + tlane + DN_OCOL + (uint32_t) (c * 32), o);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int e = 0; e < 32; e++) {
+                            o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                        }
+                        tmem_st32(tmem + tlane + DN_OCOL + (uint32_t) (c * 32), o);
+                    }
+                    tmem_st_wait();
+                }
+            }
+            // P row -> swizzled K-major tile (keys 0-63 in block 0, 64-127 in block 1)
+            char * ps = smem + L::OFF_P;
+#pragma unroll
+            for (int c = 0; c < DN_N / 8; c++) {
+                uint4 v;
+                v.x = pack2_dn<BF16>(s[c * 8 + 0], s[c * 8 + 1]);
+                v.y = pack2_dn<BF16>(s[c * 8 + 2], s[c * 8 + 3]);
+                v.z = pack2_dn<BF16>(s[c * 8 + 4], s[c * 8 + 5]);
+                v.w = pack2_dn<BF16>(s[c * 8 + 6], s[c * 8 + 7]);
+                *reinterpret_cast<uint4 *>(ps + (c >> 3) * (DN_M * 128) + sw128_off(r, c & 7)) = v;
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            dn_mbar_arrive(&bar[B_PFULL]);
+        }
+        if (!ok) {
+            atomicExch(abort_f, 1);
+        }
+
+        // ---- epilogue: O / l -> dst row (rows without any key, or after an abort, are zero)
+        const int n_tiles = i;
+        bool      have_o  = ok && n_tiles > 0;
+        if (have_o) {
+            have_o = dn_wait_warp(&bar[B_ODONE], (uint32_t) ((n_tiles - 1) & 1), deadline);
+            if (!have_o) {
+                atomicExch(abort_f, 1);
+            }
+            tc_fence_after();
+        }
+        const float inv = (have_o && l > 0.0f) ? 1.0f / l : 0.0f;
+        float *     out =
+            reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 + (int64_t) qi * p.d_nb2 + (int64_t) sq * p.d_nb3);
+#pragma unroll
+        for (int c = 0; c < D / 32; c++) {
+            uint32_t o[32];
+            if (have_o) {
+                tmem_ld32(tmem + tlane + DN_OCOL + (uint32_t) (c * 32), o);
+                tmem_ld_wait();
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; e++) {
+                    o[e] = 0u;
+                }
+            }
+            if (valid) {
+                if (p.dst_vec) {
+#pragma unroll
+                    for (int e = 0; e < 32; e += 4) {
+                        *reinterpret_cast<float4 *>(out + c * 32 + e) =
+                            make_float4(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv,
+                                        __uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+                    }
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        out[c * 32 + e] = __uint_as_float(o[e]) * inv;
+                    }
+                }
+            }
+        }
+    }
+
+    // ---- teardown: all TMEM traffic is complete before the columns are released
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, DN_TMEM);
+    }
+    if (tid == 0 && *abort_f) {
+        atomicOr(&p.status[0], ST_TIMEOUT);
+        atomicExch(&p.status[1], (uint32_t) (blockIdx.x | (blockIdx.y << 16)));
+    }
+}
+
+// ------------------------------------------------------------------ mask block classes
+
+// One CTA per (kv tile, query tile, mask plane): SKIP if every entry is -inf, NONE if every
+// entry is 0, MIXED otherwise.  Only rows < n_q and columns < n_kv are examined.
+__global__ void mask_block_class_kernel(const char * mask, int64_t nb1, int64_t nb2, int64_t nb3, int m_ne2,
+                                        int n_q, int n_kv, int n_qt, int n_kt, uint8_t * blocks) {
+    const int kt = blockIdx.x, qt = blockIdx.y, plane = blockIdx.z;
+    const int i2 = plane % m_ne2, i3 = plane / m_ne2;
+    const int r0 = qt * DN_M, c0 = kt * DN_N;
+    const int nr = min(DN_M, n_q - r0), nc = min(DN_N, n_kv - c0);
+    int       finite = 0, nonzero = 0;
+    for (int idx = threadIdx.x; idx < nr * nc; idx += blockDim.x) {
+        const int   rr = idx / nc, c = idx % nc;
+        const float v  = __half2float(*reinterpret_cast<const __half *>(
+            mask + (int64_t) (r0 + rr) * nb1 + (int64_t) i2 * nb2 + (int64_t) i3 * nb3 + (int64_t) (c0 + c) * 2));
+        finite |= v != -INFINITY;
+        nonzero |= v != 0.0f;
+    }
+    finite  = __syncthreads_or(finite);
+    nonzero = __syncthreads_or(nonzero);
+    if (threadIdx.x == 0) {
+        blocks[((int64_t) plane * n_qt + qt) * n_kt + kt] =
+            (uint8_t) (!finite ? BLK_SKIP : (!nonzero ? BLK_NONE : BLK_MIXED));
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+namespace {
+
+template <int D, bool BF16>
+void * dense_kernel_ptr(int & smem) {
+    smem = DenseSmem<D>::TOTAL;
+    return reinterpret_cast<void *>(&fa_dense_kernel<D, BF16>);
+}
+
+void * select_dense_kernel(int D, bool bf16, int & smem) {
+    if (D == 128) {
+        return bf16 ? dense_kernel_ptr<128, true>(smem) : dense_kernel_ptr<128, false>(smem);
+    }
+    if (D == 64) {
+        return bf16 ? dense_kernel_ptr<64, true>(smem) : dense_kernel_ptr<64, false>(smem);
+    }
+    return nullptr;
+}
+
+}  // namespace
+
+bool dense_eligible(int D, int kvt) {
+    return (kvt == KV_F16 || kvt == KV_BF16) && (D == 64 || D == 128) && tensor_maps_available();
+}
+
+size_t dense_workspace_bytes(int64_t n_q, int64_t n_kv, int64_t planes) {
+    const int64_t n_qt = (n_q + DN_M - 1) / DN_M, n_kt = (n_kv + DN_N - 1) / DN_N;
+    return WS_STATUS_BYTES + (size_t) ((planes * n_qt * n_kt + 255) / 256 * 256);
+}
+
+cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64_t n_seq_k, int64_t n_head,
+                         int64_t n_seq, void * workspace, cudaStream_t stream) {
+    const bool bf16 = kvt == KV_BF16;
+    int        smem = 0;
+    void *     fn   = select_dense_kernel(D, bf16, smem);
+    if (!fn) {
+        return cudaErrorInvalidValue;
+    }
+    alignas(64) CUtensorMap tmk, tmv;
+    if (!encode_kv_tensor_map(&tmk, p.k, bf16, D, p.n_kv, n_head_kv, n_seq_k, p.k_nb1, p.k_nb2, p.k_nb3, DN_N) ||
+        !encode_kv_tensor_map(&tmv, p.v, bf16, D, p.n_kv, n_head_kv, n_seq_k, p.v_nb1, p.v_nb2, p.v_nb3, DN_N)) {
+        return cudaErrorInvalidValue;
+    }
+    char * ws = static_cast<char *>(workspace);
+    p.status  = reinterpret_cast<uint32_t *>(ws);
+    p.n_qt    = (int) ((p.n_q + DN_M - 1) / DN_M);
+    p.n_kt    = (int) ((p.n_kv + DN_N - 1) / DN_N);
+    p.blocks  = nullptr;
+    if (p.mask) {
+        uint8_t * blocks = reinterpret_cast<uint8_t *>(ws + WS_STATUS_BYTES);
+        const int planes = p.m_ne2 * p.m_ne3;
+        mask_block_class_kernel<<<dim3((unsigned) p.n_kt, (unsigned) p.n_qt, (unsigned) planes), 256, 0, stream>>>(
+            p.mask, p.m_nb1, p.m_nb2, p.m_nb3, p.m_ne2, p.n_q, p.n_kv, p.n_qt, p.n_kt, blocks);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            return e;
+        }
+        p.blocks = blocks;
+    }
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+        return e;
+    }
+    void * args[] = { &tmk, &tmv, &p };
+    return cudaLaunchKernel(fn, dim3((unsigned) p.n_qt, (unsigned) n_head, (unsigned) n_seq), dim3(DN_THREADS), args,
+                            (size_t) smem, stream);
+}
+
+}  // namespace mm3fa

@@ -7,6 +7,7 @@
 #include "../../include/mm3fa.h"
 #include "fa_common.cuh"
 #include "fa_decode.cuh"
+#include "fa_dense.cuh"
 
 #include <cuda_runtime.h>
 
@@ -115,6 +116,21 @@ int decode_preference() {
     }
     return 0;
 }
+
+// MM3FA_DENSE=0|1|auto (default auto): 0 never runs the tensor-core prefill kernel, 1 runs it
+// whenever the operands allow, auto from DENSE_MIN_ROWS query rows on.
+int dense_preference() {
+    const char * e = std::getenv("MM3FA_DENSE");
+    if (e && std::strcmp(e, "0") == 0) {
+        return 0;
+    }
+    if (e && std::strcmp(e, "1") == 0) {
+        return 1;
+    }
+    return 2;
+}
+
+constexpr int64_t DENSE_MIN_ROWS = 64;
 
 uint64_t wait_timeout_ns() {
     static uint64_t ns = [] {
@@ -283,6 +299,75 @@ DecodeGeometry geometry_for(const OpShape & s, Variant var) {
                            di.sms, cps);
 }
 
+// The tensor-core prefill kernel can take these operands.
+bool dense_applicable(const OpShape & s, const mm3fa_tensor * mask) {
+    if (!s.tma || !dense_eligible((int) s.D, s.kvt) || s.n_seq > 65535) {
+        return false;
+    }
+    return !mask || mask->ne[2] * mask->ne[3] <= 65535;
+}
+
+bool use_dense(const OpShape & s, const mm3fa_tensor * mask) {
+    const int pref = dense_preference();
+    if (pref == 0 || !dense_applicable(s, mask)) {
+        return false;
+    }
+    return pref == 1 || s.n_q >= DENSE_MIN_ROWS;
+}
+
+bool rows_vec16(const mm3fa_tensor * t) {
+    return aligned(t->data, 16) && t->nb[1] % 16 == 0 && t->nb[2] % 16 == 0 && t->nb[3] % 16 == 0;
+}
+
+int run_dense(const OpShape & s, const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+              const mm3fa_tensor * mask, float scale, float max_bias, float softcap, mm3fa_tensor * dst,
+              void * workspace, size_t workspace_bytes, uint64_t timeout_ns, cudaStream_t cs) {
+    const int64_t planes = mask ? mask->ne[2] * mask->ne[3] : 1;
+    if (!workspace || workspace_bytes < dense_workspace_bytes(s.n_q, s.n_kv, planes)) {
+        return MM3FA_ERR_WORKSPACE;
+    }
+    DenseParams p{};
+    p.q        = static_cast<const char *>(q->data);
+    p.k        = static_cast<const char *>(k->data);
+    p.v        = static_cast<const char *>(v->data);
+    p.mask     = mask ? static_cast<const char *>(mask->data) : nullptr;
+    p.dst      = static_cast<char *>(dst->data);
+    p.q_nb1    = (int64_t) q->nb[1];
+    p.q_nb2    = (int64_t) q->nb[2];
+    p.q_nb3    = (int64_t) q->nb[3];
+    p.k_nb1    = (int64_t) k->nb[1];
+    p.k_nb2    = (int64_t) k->nb[2];
+    p.k_nb3    = (int64_t) k->nb[3];
+    p.v_nb1    = (int64_t) v->nb[1];
+    p.v_nb2    = (int64_t) v->nb[2];
+    p.v_nb3    = (int64_t) v->nb[3];
+    p.m_nb1    = mask ? (int64_t) mask->nb[1] : 0;
+    p.m_nb2    = mask ? (int64_t) mask->nb[2] : 0;
+    p.m_nb3    = mask ? (int64_t) mask->nb[3] : 0;
+    p.m_ne2    = mask ? (int) mask->ne[2] : 1;
+    p.m_ne3    = mask ? (int) mask->ne[3] : 1;
+    p.d_nb1    = (int64_t) dst->nb[1];
+    p.d_nb2    = (int64_t) dst->nb[2];
+    p.d_nb3    = (int64_t) dst->nb[3];
+    p.q_type   = q->type;
+    p.q_vec    = rows_vec16(q);
+    p.dst_vec  = rows_vec16(dst);
+    p.mask_vec = mask ? rows_vec16(mask) : 0;
+    p.n_q      = (int) s.n_q;
+    p.n_kv     = (int) s.n_kv;
+    p.ratio    = s.ratio;
+    p.rk3      = s.rk3;
+    p.scale    = scale;
+    p.softcap  = softcap;
+    p.max_bias = max_bias;
+    const int n_head_log2 = 1 << (int) std::floor(std::log2((double) s.n_head));
+    p.n_head_log2 = n_head_log2;
+    p.m0          = std::pow(2.0f, -max_bias / (float) n_head_log2);
+    p.m1          = std::pow(2.0f, -max_bias / 2.0f / (float) n_head_log2);
+    p.timeout_ns  = timeout_ns;
+    return record_cuda(launch_dense(p, (int) s.D, s.kvt, s.n_head_kv, s.n_seq_k, s.n_head, s.n_seq, workspace, cs));
+}
+
 __global__ void zero_rows_kernel(char * dst, int64_t dv, int64_t n1, int64_t n2, int64_t n3, int64_t nb1,
                                  int64_t nb2, int64_t nb3) {
     const int64_t total = dv * n1 * n2 * n3;
@@ -392,6 +477,10 @@ size_t mm3fa_workspace_size(const mm3fa_tensor * q, const mm3fa_tensor * k, cons
         }
         need = std::max(need, decode_workspace_bytes(geometry_for(s, var), (int) s.DV));
     }
+    if (dense_applicable(s, mask)) {
+        const int64_t planes = mask ? mask->ne[2] * mask->ne[3] : 1;
+        need                 = std::max(need, dense_workspace_bytes(s.n_q, s.n_kv, planes));
+    }
     return need;
 }
 
@@ -418,6 +507,10 @@ int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const m
         zero_rows_kernel<<<148, 256, 0, cs>>>(static_cast<char *>(dst->data), s.DV, s.n_head, s.n_q, s.n_seq,
                                               (int64_t) dst->nb[1], (int64_t) dst->nb[2], (int64_t) dst->nb[3]);
         return record_cuda(cudaGetLastError());
+    }
+    if (use_dense(s, mask)) {
+        return run_dense(s, q, k, v, mask, scale, max_bias, logit_softcap, dst, workspace, workspace_bytes,
+                         wait_timeout_ns(), cs);
     }
     const Variant        var = variant_for(s);
     const DecodeGeometry g   = geometry_for(s, var);
