@@ -6,28 +6,33 @@
 // cache, F16 causal mask [n_kv_pad, S]) and the bidirectional DiT attention of src/dit.h:201-222
 // (Q [64, S, 32, B], K/V F16 contiguous, no mask).
 //
-// One CTA per (128-query tile, query head, sequence); 192 threads in fixed roles:
-//   warp 0, lane 0   TMA producer: 128-key tiles of K and V (boxes of 64 elements x 128 keys,
-//                    128-byte swizzle, no multicast) into 2-deep rings, full/empty mbarriers.
-//   warp 1           allocates 512 TMEM columns; lane 0 issues every tcgen05.mma:
-//                      S[i%2] (TMEM, 128 x 128 f32)  = Q . K_i^T     A, B K-major in smem
-//                      O      (TMEM, 128 x D   f32) += P_i . V_i     A = P (smem, K-major),
-//                                                                    B = V (smem, MN-major)
-//                    in the order QK0, QK1, PV0, QK2, PV1, ... so the tensor core computes
-//                    S_{i+1} while the softmax works on S_i; completion is signalled with
-//                    tcgen05.commit on mbarriers.
-//   warps 2-5        softmax warpgroup: thread t owns query row t (TMEM lane t), so a row's
-//                    max and sum never leave the thread.  Per tile: tcgen05.ld S, scale /
-//                    softcap / mask (log2 units), online softmax with a lazily updated
-//                    maximum (O is rescaled only when the row maximum grows by more than 2^8;
-//                    otherwise the stale maximum is kept, which is exact), P rounded to K's type
-//                    into swizzled smem, then O rescaled in TMEM if needed.  At the end O / l is
-//                    written to dst.
-// Q is converted from F32 (any ggml strides) to K's type by the softmax warps while the first
+// One CTA per (256 query rows = two 128-row Q tiles, query head, sequence); both Q tiles share
+// every K/V tile.  384 threads in three warpgroups with fixed roles:
+//   warpgroup 0   warp 0 lane 0: TMA producer - 128-key tiles of K and V (boxes of 64 elements x
+//                 128 keys, 128-byte swizzle, no multicast) into NS-deep rings.
+//                 warp 1: allocates all 512 TMEM columns; lane 0 issues every tcgen05.mma:
+//                   S_t (TMEM cols [128t, 128t+128), f32) = Q_t . K_j^T   A, B K-major in smem
+//                   O_t (TMEM cols [256+Dt, ...), f32)  += P_t . V_j     A = P_t in TMEM (16-bit,
+//                                                                        aliasing S_t), B = V
+//                                                                        MN-major in smem
+//                 in the order QK0(j), PV1(j-1), QK1(j), PV0(j): while softmax warpgroup 0 works on
+//                 S_0(j) the tensor core runs PV1(j-1) and QK1(j), and the other way round.
+//                 tcgen05 operations of one thread execute in issue order, so QK_t(j+1) may
+//                 overwrite S_t / P_t right after PV_t(j) was issued.
+//   warpgroups 1, 2  softmax of Q tile 0 / 1: thread r owns query row r of its tile (TMEM lane r),
+//                 so a row's maximum and sum never leave the thread.  Per K/V tile: tcgen05.ld
+//                 S, scale / softcap / mask (log2 units), online softmax with a lazily updated
+//                 maximum (O is rescaled in TMEM only when the row maximum grows by more than 2^8;
+//                 otherwise the stale maximum is kept, which is exact), P rounded to K's type and
+//                 stored into TMEM with tcgen05.st.  S_t(j) being complete implies PV_t(j-1) is
+//                 complete (issue order), so the rescale needs no extra wait.  At the end O / l
+//                 is written to dst.
+// Registers are rebalanced with setmaxnreg: the softmax warpgroups hold a 128-score row.
+// Q is converted from F32 (any ggml strides) to K's type by the softmax threads while the first
 // tiles load - ggml's convention of rounding Q to K's vec-dot type.
 //
-// Masks: a pre-pass classifies every 128 x 128 (query, key) block of each mask plane as
-// all -inf (the tile is skipped - causal prefill skips about half the work), all zero (no mask
+// Masks: a pre-pass classifies every 256 x 128 (query, key) block of each mask plane as all -inf
+// (the K/V tile is skipped - causal prefill skips about half the work), all zero (no mask
 // arithmetic) or mixed (mask added element by element).  Keys past n_kv are masked explicitly.
 //
 // Every wait is bounded by the global timer; on expiry the CTA records the status word, waits
@@ -40,42 +45,48 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <mutex>
 
 namespace mm3fa {
 
-constexpr int DN_THREADS = 192;
-constexpr int DN_M       = 128;  // query rows per CTA (UMMA M)
-constexpr int DN_N       = 128;  // keys per tile (UMMA N of QK, K of PV)
-constexpr int DN_TMEM    = 512;  // allocated columns: S0 [0,128), S1 [128,256), O [256, 256+D)
-constexpr uint32_t DN_OCOL = 256;
+constexpr int DN_THREADS = 384;  // 3 warpgroups
+constexpr int DN_M       = 128;  // query rows per Q tile (UMMA M)
+constexpr int DN_QT      = 2;    // Q tiles per CTA
+constexpr int DN_ROWS    = DN_M * DN_QT;
+constexpr int DN_N       = 128;  // keys per K/V tile (UMMA N of QK, K of PV)
+constexpr int DN_TMEM    = 512;  // S0 [0,128), S1 [128,256), O0 [256,256+D), O1 [256+D, 256+2D)
+constexpr int DN_REGS_LAUNCH  = 168;  // 65536 / 384, rounded down to a multiple of 8
+constexpr int DN_REGS_SOFTMAX = 224;  // 2 x 128 x 224 + 128 x 56 = 384 x 168
+constexpr int DN_REGS_OTHER   = 56;
+static_assert(2 * 128 * DN_REGS_SOFTMAX + 128 * DN_REGS_OTHER <= DN_THREADS * DN_REGS_LAUNCH,
+              "register split exceeds the launch allocation");
 
 template <int D>
 struct DenseSmem {
-    static constexpr int HALVES   = D / 64;              // 128-byte column blocks of a D-wide row
-    static constexpr int QT       = HALVES * DN_M * 128;  // Q tile
-    static constexpr int KT       = HALVES * DN_N * 128;  // K or V tile
-    static constexpr int PT       = 2 * DN_M * 128;       // P tile: 128 keys = two 64-key blocks
-    static constexpr int OFF_Q    = 0;
-    static constexpr int OFF_K    = OFF_Q + QT;            // [2]
-    static constexpr int OFF_V    = OFF_K + 2 * KT;        // [2]
-    static constexpr int OFF_P    = OFF_V + 2 * KT;
-    static constexpr int OFF_BAR  = OFF_P + PT;            // 16 mbarriers
-    static constexpr int OFF_MISC = OFF_BAR + 16 * 8;      // tmem base, abort flag
-    static constexpr int TOTAL    = OFF_MISC + 32 + 1024;  // + alignment slack
+    static constexpr int HALVES   = D / 64;               // 128-byte column blocks of a D-wide row
+    static constexpr int NS       = D == 128 ? 2 : 4;     // K and V ring depth
+    static constexpr int QT       = HALVES * DN_M * 128;  // one Q tile
+    static constexpr int KT       = HALVES * DN_N * 128;  // one K or V tile
+    static constexpr int OFF_Q    = 0;                    // [DN_QT]
+    static constexpr int OFF_K    = OFF_Q + DN_QT * QT;   // [NS]
+    static constexpr int OFF_V    = OFF_K + NS * KT;      // [NS]
+    static constexpr int OFF_BAR  = OFF_V + NS * KT;      // 32 mbarriers
+    static constexpr int OFF_MISC = OFF_BAR + 32 * 8;     // tmem base, abort flag
+    static constexpr int TOTAL    = OFF_MISC + 32 + 1024; // + alignment slack
 };
 
-// mbarrier slots
+// mbarrier slots (NS <= 4)
 enum : int {
-    B_KFULL   = 0,   // [2]
-    B_KEMPTY  = 2,   // [2]
-    B_VFULL   = 4,   // [2]
-    B_VEMPTY  = 6,   // [2]
-    B_SFULL   = 8,   // [2]
-    B_SFREE   = 10,  // [2]
-    B_PFULL   = 12,
-    B_ODONE   = 13,
-    B_QREADY  = 14,
-    B_MMADONE = 15,
+    B_KFULL   = 0,   // [NS]
+    B_KEMPTY  = 4,   // [NS]
+    B_VFULL   = 8,   // [NS]
+    B_VEMPTY  = 12,  // [NS]
+    B_SFULL   = 16,  // [2] S_t complete (tcgen05.commit)
+    B_PREADY  = 18,  // [2] P_t in TMEM, O_t rescaled (128 softmax threads)
+    B_ODONE   = 20,  // [2] last PV_t complete
+    B_QREADY  = 22,  // [2] Q_t staged in smem (128 softmax threads)
+    B_MMADONE = 24,
+    B_COUNT   = 25,
 };
 
 // ------------------------------------------------------------------ PTX helpers
@@ -249,6 +260,27 @@ __device__ __forceinline__ int tile_class(const DenseParams & p, int plane, int 
     return p.blocks[((int64_t) plane * p.n_qt + qt) * p.n_kt + kt];
 }
 
+// D (TMEM) = A (TMEM, 16-bit, row m = lane m) * B (smem desc) [+ D]; issued by one thread
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ------------------------------------------------------------------ kernel
 
 template <int D, bool BF16>
@@ -256,6 +288,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
     fa_dense_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                     const DenseParams p) {
     using L          = DenseSmem<D>;
+    constexpr int NS = L::NS;
     constexpr int KS = D / 16;  // k-steps of QK
     extern __shared__ __align__(16) char smem_raw[];
     char * smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
@@ -266,22 +299,21 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
     const int tid   = threadIdx.x;
     const int warp  = tid >> 5;
     const int lane  = tid & 31;
-    const int qt    = blockIdx.x;
+    const int wg    = warp >> 2;
+    const int cq    = blockIdx.x;  // 256-row query block
     const int h     = blockIdx.y;
     const int sq    = blockIdx.z;
     const int g     = h / p.ratio;
     const int ks3   = sq / p.rk3;
-    const int q0    = qt * DN_M;
-    const int nrow  = min(DN_M, p.n_q - q0);
     const int plane = (sq % p.m_ne3) * p.m_ne2 + (h % p.m_ne2);
 
     if (tid == 0) {
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
-        for (int i = 0; i < 16; i++) {
-            // the softmax warpgroup's 128 threads arrive on these; one thread on the others
-            const bool wg = i == B_SFREE || i == B_SFREE + 1 || i == B_PFULL || i == B_QREADY;
-            mbar_init(&bar[i], wg ? 128u : 1u);
+        for (int i = 0; i < B_COUNT; i++) {
+            // the softmax warpgroups' 128 threads arrive on these; one thread (or a commit) on the others
+            const bool grp = (i >= B_PREADY && i < B_PREADY + 2) || (i >= B_QREADY && i < B_QREADY + 2);
+            mbar_init(&bar[i], grp ? 128u : 1u);
         }
         *abort_f = 0;
         fence_mbar_init();
@@ -296,23 +328,25 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
     const uint32_t tmem     = *tmem_slot;
     const uint64_t deadline = global_timer_ns() + p.timeout_ns;
 
-    // the kv tiles this query tile needs, in order (tiles whose mask block is all -inf are skipped)
+    // the K/V tiles this query block needs, in order (blocks whose mask is all -inf are skipped)
     auto next_tile = [&](int kt) {
-        while (kt < p.n_kt && tile_class(p, plane, qt, kt) == BLK_SKIP) {
+        while (kt < p.n_kt && tile_class(p, plane, cq, kt) == BLK_SKIP) {
             kt++;
         }
         return kt;
     };
 
-    if (warp == 0) {
-        // ======================================================= TMA producer
-        if (lane == 0) {
-            int  kiss[2] = { 0, 0 }, viss[2] = { 0, 0 };  // loads issued per stage
-            int  i       = 0;
-            bool ok      = true;
+    if (wg == 0) {
+        regs_dec<DN_REGS_OTHER>();
+        if (warp == 0 && lane == 0) {
+            // ======================================================= TMA producer
+            int  nk_ld = 0, nv_ld = 0;  // K and V tile loads issued (stage = load index % NS)
+            int  i     = 0;
+            bool ok    = true;
             for (int kt = next_tile(0); kt < p.n_kt; kt = next_tile(kt + 1), i++) {
-                const int st = i & 1;
-                if (i >= 2 && !mbar_wait_bounded(&bar[B_KEMPTY + st], (uint32_t) (((i >> 1) - 1) & 1), deadline)) {
+                const int      st  = i % NS;
+                const uint32_t par = (uint32_t) ((i / NS - 1) & 1);
+                if (i >= NS && !mbar_wait_bounded(&bar[B_KEMPTY + st], par, deadline)) {
                     ok = false;
                     break;
                 }
@@ -322,8 +356,8 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                 for (int hh = 0; hh < L::HALVES; hh++) {
                     dn_tma_load_4d(dk + hh * DN_N * 128, &tmk, hh * 64, kt * DN_N, g, ks3, &bar[B_KFULL + st]);
                 }
-                kiss[st]++;
-                if (i >= 2 && !mbar_wait_bounded(&bar[B_VEMPTY + st], (uint32_t) (((i >> 1) - 1) & 1), deadline)) {
+                nk_ld++;
+                if (i >= NS && !mbar_wait_bounded(&bar[B_VEMPTY + st], par, deadline)) {
                     ok = false;
                     break;
                 }
@@ -333,7 +367,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                 for (int hh = 0; hh < L::HALVES; hh++) {
                     dn_tma_load_4d(dv + hh * DN_N * 128, &tmv, hh * 64, kt * DN_N, g, ks3, &bar[B_VFULL + st]);
                 }
-                viss[st]++;
+                nv_ld++;
             }
             if (!ok) {
                 atomicExch(abort_f, 1);
@@ -341,79 +375,98 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             // a load into a stage is issued only after the previous one landed and was consumed, so
             // the last load of each stage is the only one that can still be in flight
             const uint64_t drain = global_timer_ns() + p.timeout_ns;
-            for (int st = 0; st < 2; st++) {
-                if (kiss[st] > 0) {
-                    mbar_wait_bounded(&bar[B_KFULL + st], (uint32_t) ((kiss[st] - 1) & 1), drain);
+#pragma unroll
+            for (int st = 0; st < NS; st++) {
+                const int kc = (nk_ld - st + NS - 1) / NS, vc = (nv_ld - st + NS - 1) / NS;  // loads into st
+                if (kc > 0) {
+                    mbar_wait_bounded(&bar[B_KFULL + st], (uint32_t) ((kc - 1) & 1), drain);
                 }
-                if (viss[st] > 0) {
-                    mbar_wait_bounded(&bar[B_VFULL + st], (uint32_t) ((viss[st] - 1) & 1), drain);
+                if (vc > 0) {
+                    mbar_wait_bounded(&bar[B_VFULL + st], (uint32_t) ((vc - 1) & 1), drain);
                 }
             }
-        }
-    } else if (warp == 1) {
-        // ======================================================= MMA issuer
-        if (lane == 0) {
+        } else if (warp == 1 && lane == 0) {
+            // ======================================================= MMA issuer
             const uint32_t id_qk = umma_idesc(BF16, DN_N, false);
             const uint32_t id_pv = umma_idesc(BF16, D, true);
-            const uint32_t sq_a  = smem_addr(smem + L::OFF_Q);
-            const uint32_t sp_a  = smem_addr(smem + L::OFF_P);
-            auto issue_qk = [&](int i) -> bool {
-                const int st = i & 1;
-                if (!mbar_wait_bounded(&bar[B_KFULL + st], (uint32_t) ((i >> 1) & 1), deadline)) {
-                    return false;
-                }
-                if (i >= 2 && !mbar_wait_bounded(&bar[B_SFREE + st], (uint32_t) (((i >> 1) - 1) & 1), deadline)) {
-                    return false;
-                }
-                tc_fence_after();
-                const uint32_t sk_a = smem_addr(smem + L::OFF_K + st * L::KT);
+            const uint32_t q_a   = smem_addr(smem + L::OFF_Q);
+            auto qk = [&](int t, int i) {  // S_t = Q_t . K_i^T
+                const uint32_t sk = smem_addr(smem + L::OFF_K + (i % NS) * L::KT);
+                const uint32_t sq_a = q_a + (uint32_t) (t * L::QT);
 #pragma unroll
                 for (int ks = 0; ks < KS; ks++) {
-                    const uint32_t offq = (uint32_t) ((ks >> 2) * DN_M * 128 + (ks & 3) * 32);
-                    const uint32_t offk = (uint32_t) ((ks >> 2) * DN_N * 128 + (ks & 3) * 32);
-                    umma_f16(tmem + (uint32_t) (st * DN_N), sw128_desc(sq_a + offq, 16, 1024),
-                             sw128_desc(sk_a + offk, 16, 1024), id_qk, ks > 0 ? 1u : 0u);
+                    const uint32_t off = (uint32_t) ((ks >> 2) * DN_M * 128 + (ks & 3) * 32);
+                    umma_f16(tmem + (uint32_t) (t * DN_N), sw128_desc(sq_a + off, 16, 1024),
+                             sw128_desc(sk + off, 16, 1024), id_qk, ks > 0 ? 1u : 0u);
                 }
-                umma_commit(&bar[B_SFULL + st]);
-                umma_commit(&bar[B_KEMPTY + st]);
-                return true;
             };
-            auto issue_pv = [&](int i) -> bool {
-                const int st = i & 1;
-                if (!mbar_wait_bounded(&bar[B_PFULL], (uint32_t) (i & 1), deadline)) {
-                    return false;
-                }
-                if (!mbar_wait_bounded(&bar[B_VFULL + st], (uint32_t) ((i >> 1) & 1), deadline)) {
-                    return false;
-                }
-                tc_fence_after();
-                const uint32_t sv_a = smem_addr(smem + L::OFF_V + st * L::KT);
+            auto pv = [&](int t, int i) {  // O_t += P_t . V_i
+                const uint32_t sv = smem_addr(smem + L::OFF_V + (i % NS) * L::KT);
 #pragma unroll
                 for (int kk = 0; kk < DN_N / 16; kk++) {
-                    const uint32_t offp = (uint32_t) ((kk >> 2) * DN_M * 128 + (kk & 3) * 32);
-                    umma_f16(tmem + DN_OCOL, sw128_desc(sp_a + offp, 16, 1024),
-                             sw128_desc(sv_a + (uint32_t) (kk * 16 * 128), (uint32_t) (DN_N * 128), 1024), id_pv,
-                             (i > 0 || kk > 0) ? 1u : 0u);
+                    umma_f16_ts(tmem + 256u + (uint32_t) (t * D), tmem + (uint32_t) (t * DN_N + kk * 8),
+                                sw128_desc(sv + (uint32_t) (kk * 16 * 128), (uint32_t) (DN_N * 128), 1024), id_pv,
+                                (i > 0 || kk > 0) ? 1u : 0u);
                 }
-                umma_commit(&bar[B_ODONE]);
-                umma_commit(&bar[B_VEMPTY + st]);
-                return true;
             };
-            int n_tiles = 0;
+            auto wait = [&](int b, int i) { return mbar_wait_bounded(&bar[b], (uint32_t) (i & 1), deadline); };
+            int n = 0;
             for (int kt = next_tile(0); kt < p.n_kt; kt = next_tile(kt + 1)) {
-                n_tiles++;
+                n++;
             }
-            bool ok = mbar_wait_bounded(&bar[B_QREADY], 0, deadline);
+            bool ok = wait(B_QREADY, 0) && wait(B_QREADY + 1, 0);
             tc_fence_after();
-            if (ok && n_tiles > 0) {
-                ok = issue_qk(0);
-                for (int i = 0; ok && i < n_tiles; i++) {
-                    if (i + 1 < n_tiles) {
-                        ok = issue_qk(i + 1);
+            if (ok && n > 0) {
+                // prologue: S0(0), S1(0), O0 += P0(0) V0
+                ok = wait(B_KFULL + 0, 0);
+                if (ok) {
+                    tc_fence_after();
+                    qk(0, 0);
+                    umma_commit(&bar[B_SFULL + 0]);
+                    qk(1, 0);
+                    umma_commit(&bar[B_SFULL + 1]);
+                    umma_commit(&bar[B_KEMPTY + 0]);
+                    ok = wait(B_VFULL + 0, 0) && wait(B_PREADY + 0, 0);
+                }
+                if (ok) {
+                    tc_fence_after();
+                    pv(0, 0);
+                }
+                for (int i = 1; ok && i < n; i++) {
+                    const int st = i % NS;
+                    ok           = wait(B_KFULL + st, i / NS);
+                    if (!ok) {
+                        break;
                     }
-                    if (ok) {
-                        ok = issue_pv(i);
+                    tc_fence_after();
+                    qk(0, i);  // S0/P0 are free: PV0(i-1) was issued before
+                    umma_commit(&bar[B_SFULL + 0]);
+                    ok = wait(B_PREADY + 1, i - 1);
+                    if (!ok) {
+                        break;
                     }
+                    tc_fence_after();
+                    pv(1, i - 1);
+                    umma_commit(&bar[B_VEMPTY + (i - 1) % NS]);
+                    qk(1, i);
+                    umma_commit(&bar[B_SFULL + 1]);
+                    umma_commit(&bar[B_KEMPTY + st]);
+                    ok = wait(B_VFULL + st, i / NS) && wait(B_PREADY + 0, i);
+                    if (!ok) {
+                        break;
+                    }
+                    tc_fence_after();
+                    pv(0, i);
+                }
+                if (ok) {
+                    umma_commit(&bar[B_ODONE + 0]);
+                    ok = wait(B_PREADY + 1, n - 1);
+                }
+                if (ok) {
+                    tc_fence_after();
+                    pv(1, n - 1);
+                    umma_commit(&bar[B_VEMPTY + (n - 1) % NS]);
+                    umma_commit(&bar[B_ODONE + 1]);
                 }
             }
             if (!ok) {
@@ -424,18 +477,23 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             mbar_wait_bounded(&bar[B_MMADONE], 0, global_timer_ns() + p.timeout_ns);
         }
     } else {
-        // ======================================================= softmax warpgroup (warps 2-5)
+        regs_inc<DN_REGS_SOFTMAX>();
+        // ======================================================= softmax warpgroups 1, 2
+        const int      t     = wg - 1;            // Q tile
         const int      quad  = warp & 3;          // TMEM lane quadrant this warp may access
-        const int      r     = quad * 32 + lane;  // query row of this thread (= TMEM lane)
-        const uint32_t tlane = (uint32_t) (quad * 32) << 16;
-        const bool     valid = r < nrow;
-        const int      qi    = q0 + (valid ? r : 0);
+        const int      r     = quad * 32 + lane;  // row in the tile (= TMEM lane)
+        const uint32_t tl    = (uint32_t) (quad * 32) << 16;
+        const uint32_t s_col = tmem + tl + (uint32_t) (t * DN_N);
+        const uint32_t o_col = tmem + tl + 256u + (uint32_t) (t * D);
+        const int      row   = cq * DN_ROWS + t * DN_M + r;
+        const bool     valid = row < p.n_q;
+        const int      qi    = valid ? row : 0;
         const float    slope = alibi_slope(h, p.max_bias, p.n_head_log2, p.m0, p.m1);
 
-        // ---- stage Q row r into the swizzled K-major tile, rounded to K's type
+        // ---- stage Q row r into the swizzled K-major tile t, rounded to K's type
         {
             const char * qrow = p.q + (int64_t) qi * p.q_nb1 + (int64_t) h * p.q_nb2 + (int64_t) sq * p.q_nb3;
-            char *       qs   = smem + L::OFF_Q;
+            char *       qs   = smem + L::OFF_Q + t * L::QT;
 #pragma unroll 4
             for (int c = 0; c < D / 8; c++) {
                 float x[8];
@@ -455,75 +513,101 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                 *reinterpret_cast<uint4 *>(qs + (c >> 3) * (DN_M * 128) + sw128_off(r, c & 7)) = v;
             }
             fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
-            dn_mbar_arrive(&bar[B_QREADY]);
+            dn_mbar_arrive(&bar[B_QREADY + t]);
         }
 
-        const char * mrow = p.mask ? p.mask + (int64_t) qi * p.m_nb1 + (int64_t) (h % p.m_ne2) * p.m_nb2 +
-                                         (int64_t) (sq % p.m_ne3) * p.m_nb3
-                                   : nullptr;
-        const float  sc   = p.softcap != 0.0f ? p.scale / p.softcap : p.scale;
-        const float  ml2  = slope * LOG2E;  // mask -> log2 units
-        float        m    = -INFINITY;      // running maximum (log2 units; may be stale by < 8)
-        float        l    = 0.0f;
-        bool         ok   = true;
-        int          i    = 0;
+        const __half * mrow = p.mask ? reinterpret_cast<const __half *>(
+                                           p.mask + (int64_t) qi * p.m_nb1 + (int64_t) (h % p.m_ne2) * p.m_nb2 +
+                                           (int64_t) (sq % p.m_ne3) * p.m_nb3)
+                                     : nullptr;
+        const float sc   = p.softcap != 0.0f ? p.scale / p.softcap : p.scale;
+        const float sl2  = sc * LOG2E;      // raw score -> log2 units (no softcap)
+        const float ml2  = slope * LOG2E;   // mask -> log2 units
+        const bool  fast = p.softcap == 0.0f && sl2 > 0.0f;
+        float       m    = -INFINITY;       // running maximum (log2 units; may be stale by < 8)
+        float       l    = 0.0f;
+        bool        ok   = true;
+        int         i    = 0;
         for (int kt = next_tile(0); kt < p.n_kt; kt = next_tile(kt + 1), i++) {
-            const int sb = i & 1;
-            if (!dn_wait_warp(&bar[B_SFULL + sb], (uint32_t) ((i >> 1) & 1), deadline)) {
+            if (!dn_wait_warp(&bar[B_SFULL + t], (uint32_t) (i & 1), deadline)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             uint32_t sr[DN_N];
-#pragma unroll
-            for (int c = 0; c < DN_N / 32; c++) {
-                tmem_ld32(tmem + tlane + (uint32_t) (sb * DN_N + c * 32), &sr[c * 32]);
-            }
+            tmem_ld32(s_col + 0, &sr[0]);
+            tmem_ld32(s_col + 32, &sr[32]);
+            tmem_ld32(s_col + 64, &sr[64]);
+            tmem_ld32(s_col + 96, &sr[96]);
             tmem_ld_wait();
-            tc_fence_before();
-            dn_mbar_arrive(&bar[B_SFREE + sb]);  // the S buffer may now take QK_{i+2}
-
-            // scores in log2 units: softcap, scale, mask, keys past n_kv
-            const int nk = p.n_kv - kt * DN_N;  // keys of this tile that exist (may exceed 128)
-            float     s[DN_N];
+            float s[DN_N];
 #pragma unroll
             for (int k = 0; k < DN_N; k++) {
-                const float x = __uint_as_float(sr[k]);
-                s[k] = p.softcap != 0.0f ? p.softcap * tanhf(x * sc) * LOG2E : x * (sc * LOG2E);
+                s[k] = __uint_as_float(sr[k]);
             }
-            if (valid && tile_class(p, plane, qt, kt) == BLK_MIXED) {
-                const __half * mp = reinterpret_cast<const __half *>(mrow) + (int64_t) kt * DN_N;
+
+            const int  nk    = p.n_kv - kt * DN_N;  // keys of this tile that exist (may exceed 128)
+            const bool mixed = tile_class(p, plane, cq, kt) == BLK_MIXED;
+            float      mt;
+            if (fast && !mixed && nk >= DN_N) {
+                // common case: the maximum of the raw scores, scaled once
+                float a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
 #pragma unroll
-                for (int c = 0; c < DN_N / 8; c++) {
-                    float mv[8];
-                    if (p.mask_vec && c * 8 + 8 <= nk) {
-                        const uint4    u    = *reinterpret_cast<const uint4 *>(mp + c * 8);
-                        const uint32_t w[4] = { u.x, u.y, u.z, u.w };
+                for (int k = 4; k < DN_N; k += 4) {
+                    a0 = fmaxf(a0, s[k]);
+                    a1 = fmaxf(a1, s[k + 1]);
+                    a2 = fmaxf(a2, s[k + 2]);
+                    a3 = fmaxf(a3, s[k + 3]);
+                }
+                mt = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3)) * sl2;
+            } else {
+                // general case: scores in log2 units in place (softcap, mask, keys past n_kv)
+                if (p.softcap != 0.0f) {
+                    const float cl2 = p.softcap * LOG2E;
 #pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            const float2 f = h2_to_f2(w[j]);
-                            mv[2 * j]      = f.x;
-                            mv[2 * j + 1]  = f.y;
+                    for (int k = 0; k < DN_N; k++) {
+                        s[k] = cl2 * tanhf(s[k] * sc);
+                    }
+                } else {
+#pragma unroll
+                    for (int k = 0; k < DN_N; k++) {
+                        s[k] *= sl2;
+                    }
+                }
+                if (mixed && valid) {
+                    const __half * mp = mrow + (int64_t) kt * DN_N;
+#pragma unroll
+                    for (int c = 0; c < DN_N / 8; c++) {
+                        float mv[8];
+                        if (p.mask_vec && c * 8 + 8 <= nk) {
+                            const uint4    u    = *reinterpret_cast<const uint4 *>(mp + c * 8);
+                            const uint32_t w[4] = { u.x, u.y, u.z, u.w };
+#pragma unroll
+                            for (int j = 0; j < 4; j++) {
+                                const float2 f = h2_to_f2(w[j]);
+                                mv[2 * j]      = f.x;
+                                mv[2 * j + 1]  = f.y;
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 8; j++) {
+                                mv[j] = c * 8 + j < nk ? __half2float(mp[c * 8 + j]) : 0.0f;
+                            }
                         }
-                    } else {
 #pragma unroll
                         for (int j = 0; j < 8; j++) {
-                            mv[j] = c * 8 + j < nk ? __half2float(mp[c * 8 + j]) : 0.0f;
+                            s[c * 8 + j] += ml2 * mv[j];
                         }
                     }
+                }
+                mt = -INFINITY;
 #pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        s[c * 8 + j] += ml2 * mv[j];
+                for (int k = 0; k < DN_N; k++) {
+                    if (k >= nk) {
+                        s[k] = -INFINITY;
                     }
+                    mt = fmaxf(mt, s[k]);
                 }
-            }
-            float mt = -INFINITY;
-#pragma unroll
-            for (int k = 0; k < DN_N; k++) {
-                if (k >= nk) {
-                    s[k] = -INFINITY;
-                }
-                mt = fmaxf(mt, s[k]);
             }
             // lazy maximum: rescale only when the row maximum grows by more than 8 (a factor 2^8)
             float alpha = 1.0f;
@@ -531,67 +615,74 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                 alpha = (m == -INFINITY) ? 0.0f : ex2(m - mt);
                 m     = mt;
             }
-            float ls = 0.0f;
-            if (m != -INFINITY) {
+            float    l0 = 0.0f, l1 = 0.0f, l2 = 0.0f, l3 = 0.0f;
+            uint32_t pk[DN_N / 2];
+            if (m == -INFINITY) {
 #pragma unroll
-                for (int k = 0; k < DN_N; k++) {
-                    s[k] = ex2(s[k] - m);
-                    ls += s[k];
+                for (int k = 0; k < DN_N / 2; k++) {
+                    pk[k] = 0u;
+                }
+            } else if (fast && !mixed && nk >= DN_N) {
+                const float nm = -m;
+#pragma unroll
+                for (int k = 0; k < DN_N; k += 4) {
+                    const float p0 = ex2(fmaf(s[k], sl2, nm));
+                    const float p1 = ex2(fmaf(s[k + 1], sl2, nm));
+                    const float p2 = ex2(fmaf(s[k + 2], sl2, nm));
+                    const float p3 = ex2(fmaf(s[k + 3], sl2, nm));
+                    l0 += p0;
+                    l1 += p1;
+                    l2 += p2;
+                    l3 += p3;
+                    pk[k / 2]     = pack2_dn<BF16>(p0, p1);
+                    pk[k / 2 + 1] = pack2_dn<BF16>(p2, p3);
                 }
             } else {
 #pragma unroll
-                for (int k = 0; k < DN_N; k++) {
-                    s[k] = 0.0f;
+                for (int k = 0; k < DN_N; k += 4) {
+                    const float p0 = ex2(s[k] - m);
+                    const float p1 = ex2(s[k + 1] - m);
+                    const float p2 = ex2(s[k + 2] - m);
+                    const float p3 = ex2(s[k + 3] - m);
+                    l0 += p0;
+                    l1 += p1;
+                    l2 += p2;
+                    l3 += p3;
+                    pk[k / 2]     = pack2_dn<BF16>(p0, p1);
+                    pk[k / 2 + 1] = pack2_dn<BF16>(p2, p3);
                 }
             }
-            l = l * alpha + ls;
+            l = l * alpha + ((l0 + l1) + (l2 + l3));
 
-            // PV_{i-1} must be complete: it reads the P buffer and accumulates into O
-            if (i > 0) {
-                if (!dn_wait_warp(&bar[B_ODONE], (uint32_t) ((i - 1) & 1), deadline)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+            // O_t rescale: PV_t(i-1) is complete because QK_t(i) was issued after it
+            if (i > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll
-                    for (int c = 0; c < D / 32; c++) {
-                        uint32_t o[32];
-                        tmem_ld32(tmem + tlane + DN_OCOL + (uint32_t) (c * 32), o);
-                        tmem_ld_wait();
+                for (int c = 0; c < D / 32; c++) {
+                    uint32_t o[32];
+                    tmem_ld32(o_col + (uint32_t) (c * 32), o);
+                    tmem_ld_wait();
 #pragma unroll
-                        for (int e = 0; e < 32; e++) {
-                            o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                        }
-                        tmem_st32(tmem + tlane + DN_OCOL + (uint32_t) (c * 32), o);
+                    for (int e = 0; e < 32; e++) {
+                        o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
                     }
-                    tmem_st_wait();
+                    tmem_st32(o_col + (uint32_t) (c * 32), o);
                 }
             }
-            // P row -> swizzled K-major tile (keys 0-63 in block 0, 64-127 in block 1)
-            char * ps = smem + L::OFF_P;
-#pragma unroll
-            for (int c = 0; c < DN_N / 8; c++) {
-                uint4 v;
-                v.x = pack2_dn<BF16>(s[c * 8 + 0], s[c * 8 + 1]);
-                v.y = pack2_dn<BF16>(s[c * 8 + 2], s[c * 8 + 3]);
-                v.z = pack2_dn<BF16>(s[c * 8 + 4], s[c * 8 + 5]);
-                v.w = pack2_dn<BF16>(s[c * 8 + 6], s[c * 8 + 7]);
-                *reinterpret_cast<uint4 *>(ps + (c >> 3) * (DN_M * 128) + sw128_off(r, c & 7)) = v;
-            }
-            fence_proxy_async_smem();
+            // P (16-bit, 2 per column) into the first 64 columns of S_t
+            tmem_st32(s_col + 0, &pk[0]);
+            tmem_st32(s_col + 32, &pk[32]);
+            tmem_st_wait();
             tc_fence_before();
-            dn_mbar_arrive(&bar[B_PFULL]);
+            dn_mbar_arrive(&bar[B_PREADY + t]);
         }
         if (!ok) {
             atomicExch(abort_f, 1);
         }
 
         // ---- epilogue: O / l -> dst row (rows without any key, or after an abort, are zero)
-        const int n_tiles = i;
-        bool      have_o  = ok && n_tiles > 0;
+        bool have_o = ok && i > 0;
         if (have_o) {
-            have_o = dn_wait_warp(&bar[B_ODONE], (uint32_t) ((n_tiles - 1) & 1), deadline);
+            have_o = dn_wait_warp(&bar[B_ODONE + t], 0, deadline);
             if (!have_o) {
                 atomicExch(abort_f, 1);
             }
@@ -604,7 +695,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
         for (int c = 0; c < D / 32; c++) {
             uint32_t o[32];
             if (have_o) {
-                tmem_ld32(tmem + tlane + DN_OCOL + (uint32_t) (c * 32), o);
+                tmem_ld32(o_col + (uint32_t) (c * 32), o);
                 tmem_ld_wait();
             } else {
 #pragma unroll
@@ -645,14 +736,14 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
 
 // ------------------------------------------------------------------ mask block classes
 
-// One CTA per (kv tile, query tile, mask plane): SKIP if every entry is -inf, NONE if every
-// entry is 0, MIXED otherwise.  Only rows < n_q and columns < n_kv are examined.
+// One CTA per (kv tile, 256-row query block, mask plane): SKIP if every entry is -inf, NONE if
+// every entry is 0, MIXED otherwise.  Only rows < n_q and columns < n_kv are examined.
 __global__ void mask_block_class_kernel(const char * mask, int64_t nb1, int64_t nb2, int64_t nb3, int m_ne2,
                                         int n_q, int n_kv, int n_qt, int n_kt, uint8_t * blocks) {
     const int kt = blockIdx.x, qt = blockIdx.y, plane = blockIdx.z;
     const int i2 = plane % m_ne2, i3 = plane / m_ne2;
-    const int r0 = qt * DN_M, c0 = kt * DN_N;
-    const int nr = min(DN_M, n_q - r0), nc = min(DN_N, n_kv - c0);
+    const int r0 = qt * DN_ROWS, c0 = kt * DN_N;
+    const int nr = min(DN_ROWS, n_q - r0), nc = min(DN_N, n_kv - c0);
     int       finite = 0, nonzero = 0;
     for (int idx = threadIdx.x; idx < nr * nc; idx += blockDim.x) {
         const int   rr = idx / nc, c = idx % nc;
@@ -689,6 +780,18 @@ void * select_dense_kernel(int D, bool bf16, int & smem) {
     return nullptr;
 }
 
+// The register split of the warpgroups assumes the kernel launches with DN_REGS_LAUNCH registers
+// per thread; a build that allocates fewer would make setmaxnreg.inc wait forever, so it is
+// refused here instead of launched.
+cudaError_t check_launch_registers(const void * fn) {
+    cudaFuncAttributes a{};
+    cudaError_t        e = cudaFuncGetAttributes(&a, fn);
+    if (e != cudaSuccess) {
+        return e;
+    }
+    return a.numRegs == DN_REGS_LAUNCH ? cudaSuccess : cudaErrorInvalidConfiguration;
+}
+
 }  // namespace
 
 bool dense_eligible(int D, int kvt) {
@@ -696,7 +799,7 @@ bool dense_eligible(int D, int kvt) {
 }
 
 size_t dense_workspace_bytes(int64_t n_q, int64_t n_kv, int64_t planes) {
-    const int64_t n_qt = (n_q + DN_M - 1) / DN_M, n_kt = (n_kv + DN_N - 1) / DN_N;
+    const int64_t n_qt = (n_q + DN_ROWS - 1) / DN_ROWS, n_kt = (n_kv + DN_N - 1) / DN_N;
     return WS_STATUS_BYTES + (size_t) ((planes * n_qt * n_kt + 255) / 256 * 256);
 }
 
@@ -708,6 +811,10 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
     if (!fn) {
         return cudaErrorInvalidValue;
     }
+    cudaError_t e = check_launch_registers(fn);
+    if (e != cudaSuccess) {
+        return e;
+    }
     alignas(64) CUtensorMap tmk, tmv;
     if (!encode_kv_tensor_map(&tmk, p.k, bf16, D, p.n_kv, n_head_kv, n_seq_k, p.k_nb1, p.k_nb2, p.k_nb3, DN_N) ||
         !encode_kv_tensor_map(&tmv, p.v, bf16, D, p.n_kv, n_head_kv, n_seq_k, p.v_nb1, p.v_nb2, p.v_nb3, DN_N)) {
@@ -715,7 +822,7 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
     }
     char * ws = static_cast<char *>(workspace);
     p.status  = reinterpret_cast<uint32_t *>(ws);
-    p.n_qt    = (int) ((p.n_q + DN_M - 1) / DN_M);
+    p.n_qt    = (int) ((p.n_q + DN_ROWS - 1) / DN_ROWS);
     p.n_kt    = (int) ((p.n_kv + DN_N - 1) / DN_N);
     p.blocks  = nullptr;
     if (p.mask) {
@@ -723,13 +830,13 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
         const int planes = p.m_ne2 * p.m_ne3;
         mask_block_class_kernel<<<dim3((unsigned) p.n_kt, (unsigned) p.n_qt, (unsigned) planes), 256, 0, stream>>>(
             p.mask, p.m_nb1, p.m_nb2, p.m_nb3, p.m_ne2, p.n_q, p.n_kv, p.n_qt, p.n_kt, blocks);
-        cudaError_t e = cudaGetLastError();
+        e = cudaGetLastError();
         if (e != cudaSuccess) {
             return e;
         }
         p.blocks = blocks;
     }
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) {
         return e;
     }
