@@ -56,8 +56,9 @@ constexpr int DN_ROWS    = DN_M * DN_QT;
 constexpr int DN_N       = 128;  // keys per K/V tile (UMMA N of QK, K of PV)
 constexpr int DN_TMEM    = 512;  // S0 [0,128), S1 [128,256), O0 [256,256+D), O1 [256+D, 256+2D)
 constexpr int DN_REGS_LAUNCH  = 168;  // 65536 / 384, rounded down to a multiple of 8
-constexpr int DN_REGS_SOFTMAX = 224;  // 2 x 128 x 224 + 128 x 56 = 384 x 168
-constexpr int DN_REGS_OTHER   = 56;
+constexpr int DN_REGS_SOFTMAX = 216;  // 2 x 128 x 216 + 128 x 72 = 384 x 168
+constexpr int DN_REGS_OTHER   = 72;
+constexpr int DN_EMU          = 3;    // of every 8 exp2 pairs, those computed by polynomial
 static_assert(2 * 128 * DN_REGS_SOFTMAX + 128 * DN_REGS_OTHER <= DN_THREADS * DN_REGS_LAUNCH,
               "register split exceeds the launch allocation");
 
@@ -131,22 +132,29 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
-// D (TMEM) = A (smem desc) * B (smem desc) [+ D]; issued by one thread
+// The tcgen05.mma / tcgen05.commit wrappers below are executed by a whole converged warp: the
+// operands are computed by every lane (so they stay in the uniform datapath) and elect.sync picks
+// the one lane that issues the instruction.
+
+// D (TMEM) = A (smem desc) * B (smem desc) [+ D]
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                          uint32_t accumulate) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
+        "{\n\t.reg .pred e, p;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
 // arrive on `bar` once every tcgen05 operation this thread issued before has completed
 __device__ __forceinline__ void umma_commit(uint64_t * bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_addr(bar))
-                 : "memory");
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_addr(bar))
+        : "memory");
 }
 
 // 32 consecutive 32-bit columns of this thread's TMEM lane (r[0..31] must stay in registers)
@@ -260,13 +268,14 @@ __device__ __forceinline__ int tile_class(const DenseParams & p, int plane, int 
     return p.blocks[((int64_t) plane * p.n_qt + qt) * p.n_kt + kt];
 }
 
-// D (TMEM) = A (TMEM, 16-bit, row m = lane m) * B (smem desc) [+ D]; issued by one thread
+// D (TMEM) = A (TMEM, 16-bit, row m = lane m) * B (smem desc) [+ D]; whole warp, one lane issues
 __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
                                             uint32_t accumulate) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
+        "{\n\t.reg .pred e, p;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
@@ -279,6 +288,61 @@ __device__ __forceinline__ void regs_inc() {
 template <int N>
 __device__ __forceinline__ void regs_dec() {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// max of three (PTX max.f32 with three sources, sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// Packed pairs of f32 (PTX .f32x2 arithmetic, sm_100): lo in the low 32 bits.
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+
+__device__ __forceinline__ void f2unpack(uint64_t v, float & lo, float & hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// 2^x for a pair, on the FMA pipe: x = n + f with n = round(x) (added to the exponent field) and
+// f in [-1/2, 1/2]; 2^f by a degree-3 polynomial fitted here for minimum relative error on that
+// interval (max 7.5e-5, below half an f16 ulp).  x is clamped to >= -126 so n never underflows the
+// exponent; 2^-126 instead of 0 for x = -inf is far below what a 16-bit P can hold.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
+    constexpr float C0 = 0.99992806f, C1 = 0.69326097f, C2 = 0.24261114f, C3 = 0.05517167f;
+    constexpr float MAGIC = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer
+    float xl, xh;
+    f2unpack(x2, xl, xh);
+    x2                = f2pack(fmaxf(xl, -126.0f), fmaxf(xh, -126.0f));
+    const uint64_t r2 = fadd2(x2, f2pack(MAGIC, MAGIC));
+    const uint64_t n2 = fadd2(r2, f2pack(-MAGIC, -MAGIC));
+    const uint64_t f2 = ffma2(n2, f2pack(-1.0f, -1.0f), x2);
+    uint64_t       p2 = ffma2(f2pack(C3, C3), f2, f2pack(C2, C2));
+    p2                = ffma2(p2, f2, f2pack(C1, C1));
+    p2                = ffma2(p2, f2, f2pack(C0, C0));
+    float rl, rh, pl, ph;
+    f2unpack(r2, rl, rh);
+    f2unpack(p2, pl, ph);
+    // the low bits of r hold n; shifted by 23 they land in the exponent field (the magic's own bits
+    // shift out)
+    return f2pack(__int_as_float(__float_as_int(pl) + (__float_as_int(rl) << 23)),
+                  __int_as_float(__float_as_int(ph) + (__float_as_int(rh) << 23)));
 }
 
 // ------------------------------------------------------------------ kernel
@@ -385,8 +449,8 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                     mbar_wait_bounded(&bar[B_VFULL + st], (uint32_t) ((vc - 1) & 1), drain);
                 }
             }
-        } else if (warp == 1 && lane == 0) {
-            // ======================================================= MMA issuer
+        } else if (warp == 1) {
+            // ======================================================= MMA issuer (whole warp, elected lane)
             const uint32_t id_qk = umma_idesc(BF16, DN_N, false);
             const uint32_t id_pv = umma_idesc(BF16, D, true);
             const uint32_t q_a   = smem_addr(smem + L::OFF_Q);
@@ -409,7 +473,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                                 (i > 0 || kk > 0) ? 1u : 0u);
                 }
             };
-            auto wait = [&](int b, int i) { return mbar_wait_bounded(&bar[b], (uint32_t) (i & 1), deadline); };
+            auto wait = [&](int b, int i) { return dn_wait_warp(&bar[b], (uint32_t) (i & 1), deadline); };
             int n = 0;
             for (int kt = next_tile(0); kt < p.n_kt; kt = next_tile(kt + 1)) {
                 n++;
@@ -474,7 +538,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             }
             // every MMA issued must have completed before TMEM and shared memory are released
             umma_commit(&bar[B_MMADONE]);
-            mbar_wait_bounded(&bar[B_MMADONE], 0, global_timer_ns() + p.timeout_ns);
+            dn_wait_warp(&bar[B_MMADONE], 0, global_timer_ns() + p.timeout_ns);
         }
     } else {
         regs_inc<DN_REGS_SOFTMAX>();
@@ -494,23 +558,41 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
         {
             const char * qrow = p.q + (int64_t) qi * p.q_nb1 + (int64_t) h * p.q_nb2 + (int64_t) sq * p.q_nb3;
             char *       qs   = smem + L::OFF_Q + t * L::QT;
-#pragma unroll 4
-            for (int c = 0; c < D / 8; c++) {
-                float x[8];
-                if (valid) {
-                    ld_q8(qrow, p.q_type, c * 8, p.q_vec != 0, x);
-                } else {
+            if (p.q_type == KV_F32 && p.q_vec) {
+                // the whole row in flight at once: D/4 16-byte loads, then convert and store
+                float4 x[D / 4];
 #pragma unroll
-                    for (int e = 0; e < 8; e++) {
-                        x[e] = 0.0f;
-                    }
+                for (int c = 0; c < D / 4; c++) {
+                    x[c] = valid ? reinterpret_cast<const float4 *>(qrow)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-                uint4 v;
-                v.x = pack2_dn<BF16>(x[0], x[1]);
-                v.y = pack2_dn<BF16>(x[2], x[3]);
-                v.z = pack2_dn<BF16>(x[4], x[5]);
-                v.w = pack2_dn<BF16>(x[6], x[7]);
-                *reinterpret_cast<uint4 *>(qs + (c >> 3) * (DN_M * 128) + sw128_off(r, c & 7)) = v;
+#pragma unroll
+                for (int c = 0; c < D / 8; c++) {
+                    uint4 v;
+                    v.x = pack2_dn<BF16>(x[2 * c].x, x[2 * c].y);
+                    v.y = pack2_dn<BF16>(x[2 * c].z, x[2 * c].w);
+                    v.z = pack2_dn<BF16>(x[2 * c + 1].x, x[2 * c + 1].y);
+                    v.w = pack2_dn<BF16>(x[2 * c + 1].z, x[2 * c + 1].w);
+                    *reinterpret_cast<uint4 *>(qs + (c >> 3) * (DN_M * 128) + sw128_off(r, c & 7)) = v;
+                }
+            } else {
+#pragma unroll 4
+                for (int c = 0; c < D / 8; c++) {
+                    float x[8];
+                    if (valid) {
+                        ld_q8(qrow, p.q_type, c * 8, p.q_vec != 0, x);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; e++) {
+                            x[e] = 0.0f;
+                        }
+                    }
+                    uint4 v;
+                    v.x = pack2_dn<BF16>(x[0], x[1]);
+                    v.y = pack2_dn<BF16>(x[2], x[3]);
+                    v.z = pack2_dn<BF16>(x[4], x[5]);
+                    v.w = pack2_dn<BF16>(x[6], x[7]);
+                    *reinterpret_cast<uint4 *>(qs + (c >> 3) * (DN_M * 128) + sw128_off(r, c & 7)) = v;
+                }
             }
             fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
             dn_mbar_arrive(&bar[B_QREADY + t]);
@@ -520,20 +602,68 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                                            p.mask + (int64_t) qi * p.m_nb1 + (int64_t) (h % p.m_ne2) * p.m_nb2 +
                                            (int64_t) (sq % p.m_ne3) * p.m_nb3)
                                      : nullptr;
-        const float sc   = p.softcap != 0.0f ? p.scale / p.softcap : p.scale;
-        const float sl2  = sc * LOG2E;      // raw score -> log2 units (no softcap)
-        const float ml2  = slope * LOG2E;   // mask -> log2 units
-        const bool  fast = p.softcap == 0.0f && sl2 > 0.0f;
-        float       m    = -INFINITY;       // running maximum (log2 units; may be stale by < 8)
-        float       l    = 0.0f;
-        bool        ok   = true;
-        int         i    = 0;
+        const float sc    = p.softcap != 0.0f ? p.scale / p.softcap : p.scale;
+        const float sl2   = sc * LOG2E;     // raw score -> log2 units (no softcap)
+        const float ml2   = slope * LOG2E;  // mask -> log2 units
+        const bool  plain = p.softcap == 0.0f && sl2 > 0.0f;
+        float       m     = -INFINITY;      // running maximum (log2 units; may be stale by < 8)
+        float       l     = 0.0f;
+        bool        ok    = true;
+        int         i     = 0;
         for (int kt = next_tile(0); kt < p.n_kt; kt = next_tile(kt + 1), i++) {
             if (!dn_wait_warp(&bar[B_SFULL + t], (uint32_t) (i & 1), deadline)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
+            const int  nk   = p.n_kv - kt * DN_N;  // keys of this tile that exist (may exceed 128)
+            const bool fast = plain && nk >= DN_N && tile_class(p, plane, cq, kt) != BLK_MIXED;
+            if (!fast) {
+                // general tile: rewrite S in TMEM in log2 units - softcap, mask, keys past n_kv -
+                // 32 columns at a time, so the row pass below treats every tile alike
+                const bool     mixed = valid && tile_class(p, plane, cq, kt) == BLK_MIXED;
+                const __half * mp    = mixed ? mrow + (int64_t) kt * DN_N : nullptr;
+#pragma unroll 1
+                for (int c = 0; c < DN_N / 32; c++) {
+                    uint32_t v[32];
+                    tmem_ld32(s_col + (uint32_t) (c * 32), v);
+                    tmem_ld_wait();
+                    float mv[32];
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        mv[e] = 0.0f;
+                    }
+                    if (mixed) {
+                        if (p.mask_vec && c * 32 + 32 <= nk) {
+#pragma unroll
+                            for (int q4 = 0; q4 < 4; q4++) {
+                                const uint4    u    = *reinterpret_cast<const uint4 *>(mp + c * 32 + q4 * 8);
+                                const uint32_t w[4] = { u.x, u.y, u.z, u.w };
+#pragma unroll
+                                for (int j = 0; j < 4; j++) {
+                                    const float2 f      = h2_to_f2(w[j]);
+                                    mv[q4 * 8 + 2 * j]     = f.x;
+                                    mv[q4 * 8 + 2 * j + 1] = f.y;
+                                }
+                            }
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 32; e++) {
+                                mv[e] = c * 32 + e < nk ? __half2float(mp[c * 32 + e]) : 0.0f;
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        const float x = __uint_as_float(v[e]);
+                        float       y = p.softcap != 0.0f ? p.softcap * LOG2E * tanhf(x * sc) : x * sl2;
+                        y             = fmaf(ml2, mv[e], y);
+                        v[e]          = __float_as_uint(c * 32 + e < nk ? y : -INFINITY);
+                    }
+                    tmem_st32(s_col + (uint32_t) (c * 32), v);
+                }
+                tmem_st_wait();
+            }
             uint32_t sr[DN_N];
             tmem_ld32(s_col + 0, &sr[0]);
             tmem_ld32(s_col + 32, &sr[32]);
@@ -545,118 +675,67 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             for (int k = 0; k < DN_N; k++) {
                 s[k] = __uint_as_float(sr[k]);
             }
-
-            const int  nk    = p.n_kv - kt * DN_N;  // keys of this tile that exist (may exceed 128)
-            const bool mixed = tile_class(p, plane, cq, kt) == BLK_MIXED;
-            float      mt;
-            if (fast && !mixed && nk >= DN_N) {
-                // common case: the maximum of the raw scores, scaled once
-                float a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
+            // scores are raw (fast tiles, times sl2 > 0 gives log2 units) or already in log2 units
+            const float mult = fast ? sl2 : 1.0f;
+            float       a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
 #pragma unroll
-                for (int k = 4; k < DN_N; k += 4) {
-                    a0 = fmaxf(a0, s[k]);
-                    a1 = fmaxf(a1, s[k + 1]);
-                    a2 = fmaxf(a2, s[k + 2]);
-                    a3 = fmaxf(a3, s[k + 3]);
-                }
-                mt = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3)) * sl2;
-            } else {
-                // general case: scores in log2 units in place (softcap, mask, keys past n_kv)
-                if (p.softcap != 0.0f) {
-                    const float cl2 = p.softcap * LOG2E;
-#pragma unroll
-                    for (int k = 0; k < DN_N; k++) {
-                        s[k] = cl2 * tanhf(s[k] * sc);
-                    }
-                } else {
-#pragma unroll
-                    for (int k = 0; k < DN_N; k++) {
-                        s[k] *= sl2;
-                    }
-                }
-                if (mixed && valid) {
-                    const __half * mp = mrow + (int64_t) kt * DN_N;
-#pragma unroll
-                    for (int c = 0; c < DN_N / 8; c++) {
-                        float mv[8];
-                        if (p.mask_vec && c * 8 + 8 <= nk) {
-                            const uint4    u    = *reinterpret_cast<const uint4 *>(mp + c * 8);
-                            const uint32_t w[4] = { u.x, u.y, u.z, u.w };
-#pragma unroll
-                            for (int j = 0; j < 4; j++) {
-                                const float2 f = h2_to_f2(w[j]);
-                                mv[2 * j]      = f.x;
-                                mv[2 * j + 1]  = f.y;
-                            }
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 8; j++) {
-                                mv[j] = c * 8 + j < nk ? __half2float(mp[c * 8 + j]) : 0.0f;
-                            }
-                        }
-#pragma unroll
-                        for (int j = 0; j < 8; j++) {
-                            s[c * 8 + j] += ml2 * mv[j];
-                        }
-                    }
-                }
-                mt = -INFINITY;
-#pragma unroll
-                for (int k = 0; k < DN_N; k++) {
-                    if (k >= nk) {
-                        s[k] = -INFINITY;
-                    }
-                    mt = fmaxf(mt, s[k]);
-                }
+            for (int k = 4; k < DN_N - 4; k += 8) {
+                a0 = fmax3(a0, s[k], s[k + 1]);
+                a1 = fmax3(a1, s[k + 2], s[k + 3]);
+                a2 = fmax3(a2, s[k + 4], s[k + 5]);
+                a3 = fmax3(a3, s[k + 6], s[k + 7]);
             }
+            a0 = fmax3(a0, s[DN_N - 4], s[DN_N - 3]);
+            a1 = fmax3(a1, s[DN_N - 2], s[DN_N - 1]);
+            const float mt = fmax3(a0, a1, fmaxf(a2, a3)) * mult;
             // lazy maximum: rescale only when the row maximum grows by more than 8 (a factor 2^8)
             float alpha = 1.0f;
             if (mt > m + 8.0f) {
                 alpha = (m == -INFINITY) ? 0.0f : ex2(m - mt);
                 m     = mt;
             }
-            float    l0 = 0.0f, l1 = 0.0f, l2 = 0.0f, l3 = 0.0f;
             uint32_t pk[DN_N / 2];
+            float    lsum = 0.0f;
             if (m == -INFINITY) {
 #pragma unroll
                 for (int k = 0; k < DN_N / 2; k++) {
                     pk[k] = 0u;
                 }
-            } else if (fast && !mixed && nk >= DN_N) {
-                const float nm = -m;
-#pragma unroll
-                for (int k = 0; k < DN_N; k += 4) {
-                    const float p0 = ex2(fmaf(s[k], sl2, nm));
-                    const float p1 = ex2(fmaf(s[k + 1], sl2, nm));
-                    const float p2 = ex2(fmaf(s[k + 2], sl2, nm));
-                    const float p3 = ex2(fmaf(s[k + 3], sl2, nm));
-                    l0 += p0;
-                    l1 += p1;
-                    l2 += p2;
-                    l3 += p3;
-                    pk[k / 2]     = pack2_dn<BF16>(p0, p1);
-                    pk[k / 2 + 1] = pack2_dn<BF16>(p2, p3);
-                }
             } else {
+                // p = 2^(s * mult - m): pairs in packed f32x2 arithmetic; DN_EMU of every 8 pairs
+                // take the FMA-pipe polynomial, the others the special-function unit
+                const uint64_t mul2 = f2pack(mult, mult), nm2 = f2pack(-m, -m);
+                uint64_t       acc[4] = { 0ull, 0ull, 0ull, 0ull };
 #pragma unroll
-                for (int k = 0; k < DN_N; k += 4) {
-                    const float p0 = ex2(s[k] - m);
-                    const float p1 = ex2(s[k + 1] - m);
-                    const float p2 = ex2(s[k + 2] - m);
-                    const float p3 = ex2(s[k + 3] - m);
-                    l0 += p0;
-                    l1 += p1;
-                    l2 += p2;
-                    l3 += p3;
-                    pk[k / 2]     = pack2_dn<BF16>(p0, p1);
-                    pk[k / 2 + 1] = pack2_dn<BF16>(p2, p3);
+                for (int j = 0; j < DN_N / 2; j++) {
+                    const uint64_t x2 = ffma2(f2pack(s[2 * j], s[2 * j + 1]), mul2, nm2);
+                    uint64_t       p2;
+                    if ((j & 7) < DN_EMU) {
+                        p2 = exp2_poly2(x2);
+                    } else {
+                        float xl, xh;
+                        f2unpack(x2, xl, xh);
+                        p2 = f2pack(ex2(xl), ex2(xh));
+                    }
+                    acc[j & 3] = fadd2(acc[j & 3], p2);
+                    float pl, ph;
+                    f2unpack(p2, pl, ph);
+                    pk[j] = pack2_dn<BF16>(pl, ph);
                 }
+                float s0, s1, s2, s3, s4, s5, s6, s7;
+                f2unpack(fadd2(acc[0], acc[1]), s0, s1);
+                f2unpack(fadd2(acc[2], acc[3]), s2, s3);
+                (void) s4, (void) s5, (void) s6, (void) s7;
+                lsum = (s0 + s1) + (s2 + s3);
             }
-            l = l * alpha + ((l0 + l1) + (l2 + l3));
+            l = l * alpha + lsum;
 
+            // P (16-bit, 2 per column) into the first 64 columns of S_t
+            tmem_st32(s_col + 0, &pk[0]);
+            tmem_st32(s_col + 32, &pk[32]);
             // O_t rescale: PV_t(i-1) is complete because QK_t(i) was issued after it
             if (i > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-#pragma unroll
+#pragma unroll 1
                 for (int c = 0; c < D / 32; c++) {
                     uint32_t o[32];
                     tmem_ld32(o_col + (uint32_t) (c * 32), o);
@@ -668,9 +747,6 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                     tmem_st32(o_col + (uint32_t) (c * 32), o);
                 }
             }
-            // P (16-bit, 2 per column) into the first 64 columns of S_t
-            tmem_st32(s_col + 0, &pk[0]);
-            tmem_st32(s_col + 32, &pk[32]);
             tmem_st_wait();
             tc_fence_before();
             dn_mbar_arrive(&bar[B_PREADY + t]);
