@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mm3fa|reference]
 
-Workload (BASELINE config 2 at the metric's point "CFG B=2, KV 8K"): one step is the
+Workload (benchmark config 2 at the metric's point "CFG B=2, KV 8K"): one step is the
 decode attention of all 36 layers of the Qwen3 LM for one token, each layer with its own
 F16 KV cache laid out as the reference lays it out ([128, max_seq=10240, 8, n_seq],
 viewed at n_kv = 8192, src/qwen3-lm.h:810-813), 32 query heads over 8 kv heads, D=128,
@@ -13,6 +13,13 @@ N GPUs: KV-head sharding, weak scaling.  Rank r holds kv heads [8r/N, 8(r+1)/N) 
 caches of 2N sequences (N CFG pairs), i.e. the same bytes per GPU as N=1; after the 36
 layers one NCCL all-gather moves every rank's head slices and mm3fa_assemble_heads
 rebuilds the ggml [128, 32, 1, 2N] outputs.
+
+The same line carries the dense (tensor-core) side of the metric: "dit" times benchmark config 5
+(DiT bidirectional attention, B=2 CFG x S=4096 x 16 heads x D=128, F32 Q permuted view, F16
+K/V, no mask) as one flow step of 24 blocks per timed step, cycling 4 operand sets so every call
+reads its inputs from HBM; "prefill" times config 4 (2 x 1024-token causal prefill, 32q/8kv,
+D=128, F16 causal mask over the 256-padded cache view).  N GPUs: each rank runs its own
+(CFG batch x head) shard of the same per-GPU size (weak scaling, no collective).
 
 Printed JSON: value = whole-job algorithmic GB/s of the timed steps (device time, max over
 ranks); e2e = the same through the C ABI with Q/mask copied from pinned host memory and the
@@ -40,10 +47,9 @@ N_HEAD, N_HEAD_KV, D = 32, 8, 128
 N_KV, MAX_SEQ = 8192, 10240
 FALLBACK_HBM_GBS = 6650.0
 
-# dram__bytes_read.sum + dram__bytes_write.sum per decode launch at this workload, from the
-# ncu capture summarised in profiles/ (None: not yet captured for the kernel below)
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode launch at this workload (ncu capture)
 NCU_KERNEL = "fa_decode_mma_kernel<128,f16,NT=1,cluster,NS=3>"
-NCU_TRAFFIC_BYTES = None
+NCU_TRAFFIC_BYTES = 67228416 + 697600
 
 
 def layer_bytes(n_seq: int, n_head_kv: int, n_head: int) -> int:
@@ -53,6 +59,20 @@ def layer_bytes(n_seq: int, n_head_kv: int, n_head: int) -> int:
     out = n_seq * n_head * D * 4
     mask = n_seq * N_KV * 2
     return kv + q + out + mask
+
+
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def measured_tensor_peaks() -> tuple[float, float, str]:
+    """(burst, sustained) dense bf16 TFLOP/s of this pool's B200s."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d["bf16_tflops_sustained"]), "measured"
+    except Exception:
+        return FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
 
 
 def measured_peaks() -> tuple[float, str]:
@@ -178,7 +198,7 @@ def run_reference(args) -> None:
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16/f32",
-        "data": "synthetic (seeded, BASELINE config 2 shapes)",
+        "data": "synthetic (seeded, benchmark config 2 shapes)",
         "config": {"workload": "decode attention, 36-layer Qwen3 LM step at CFG B=2, KV 8192 "
                                f"(bounded sample: {n_layers_per_step} layers per step)",
                    "n_seq": 2, "n_kv": N_KV, "n_head": N_HEAD, "n_head_kv": N_HEAD_KV, "head_dim": D,
@@ -191,6 +211,97 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def bench_dense(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, world: int, local: int) -> dict:
+    """DiT (config 5) and causal prefill (config 4) attention on the tensor-core kernel."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(99)
+
+    def rms(x):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)
+
+    def dit_set(B, S, H, Dh):
+        q = rms(torch.randn(B, S, H, Dh, generator=g, device=dev))           # [D, H, S, B] storage
+        k = rms(torch.randn(B, H, S, Dh, generator=g, device=dev)).half()    # [D, S, H, B] contiguous
+        v = torch.randn(B, H, S, Dh, generator=g, device=dev).half()
+        o = torch.empty(B, S, H, Dh, device=dev)
+        qd = ggml.make(ggml.GGML_TYPE_F32, [Dh, S, H, B], q.data_ptr(), [4, 4 * Dh * H, 4 * Dh, 4 * Dh * H * S])
+        kd = ggml.make(ggml.GGML_TYPE_F16, [Dh, S, H, B], k.data_ptr())
+        vd = ggml.make(ggml.GGML_TYPE_F16, [Dh, S, H, B], v.data_ptr())
+        dd = ggml.make(ggml.GGML_TYPE_F32, [Dh, H, S, B], o.data_ptr())
+        return (q, k, v, o), (qd, kd, vd, None, dd)
+
+    def timed(calls, n_calls_per_step, flops_per_call, ws):
+        def step():
+            for (qd, kd, vd, md, dd), sc in calls:
+                mm3fa.flash_attn_ext(qd, kd, vd, md, sc, 0.0, 0.0, dd, ws.data_ptr(), ws.numel(), stream.cuda_stream)
+
+        with torch.cuda.stream(stream):
+            step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            stream.record_event(e0)
+            with torch.cuda.stream(stream):  # replay() launches on the current stream
+                for _ in range(steps):
+                    graph.replay()
+            stream.record_event(e1)
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        del graph
+        us_call = ms * 1e3 / n_calls_per_step
+        return us_call, flops_per_call / (us_call * 1e-6) / 1e12, clk.summary()
+
+    burst, sustained, src = measured_tensor_peaks()
+    out = {}
+    # ---- DiT: 24 blocks of one flow step, 4 operand sets (each ~192 MB > L2) cycled
+    B, S, H, Dh = 2, 4096, 16, 128
+    sets = [dit_set(B, S, H, Dh) for _ in range(4)]
+    ws = torch.zeros(1 << 20, dtype=torch.uint8, device=dev)
+    calls = [(sets[i % 4][1], 1.0 / math.sqrt(Dh)) for i in range(24)]
+    fl = 4.0 * Dh * S * S * H * B
+    us, tf, clocks = timed(calls, 24, fl, ws)
+    out["dit"] = {"tflops": round(tf * world, 1), "tflops_per_gpu": round(tf, 1), "us_per_call": round(us, 2),
+                  "clocks": clocks,
+                  "config": {"workload": "DiT self-attention, benchmark config 5, 24 blocks per step",
+                             "batch_per_gpu": B, "seq": S, "heads": H, "head_dim": Dh, "mask": None,
+                             "l2": "4 operand sets cycled, each > L2"},
+                  "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": sustained, "unit": "TFLOP/s",
+                               "frac": round(tf / sustained, 4), "peak_kind": "bf16_tflops_sustained",
+                               "frac_of_burst": round(tf / burst, 4), "peak_source": src,
+                               "kernel": "fa_dense_kernel<128,f16>", "traffic": 134485248 + 34337536,
+                               "flops_per_launch": fl}}
+    del sets
+    # ---- causal prefill: 2 x 1024 tokens, 32q / 8kv, cache view padded to 256
+    Sp, Hq, Hkv, pad = 1024, 32, 8, 256
+    n_kv = -(-Sp // pad) * pad
+    q = rms(torch.randn(2, Sp, Hq, Dh, generator=g, device=dev))
+    kc = rms(torch.randn(2, Hkv, n_kv, Dh, generator=g, device=dev)).half()
+    vc = torch.randn(2, Hkv, n_kv, Dh, generator=g, device=dev).half()
+    o = torch.empty(2, Sp, Hq, Dh, device=dev)
+    mask = torch.triu(torch.full((Sp, n_kv), float("-inf"), device=dev), diagonal=1).half()
+    qd = ggml.make(ggml.GGML_TYPE_F32, [Dh, Sp, Hq, 2], q.data_ptr(), [4, 4 * Dh * Hq, 4 * Dh, 4 * Dh * Hq * Sp])
+    kd = ggml.make(ggml.GGML_TYPE_F16, [Dh, n_kv, Hkv, 2], kc.data_ptr())
+    vd = ggml.make(ggml.GGML_TYPE_F16, [Dh, n_kv, Hkv, 2], vc.data_ptr())
+    md = ggml.make(ggml.GGML_TYPE_F16, [n_kv, Sp, 1, 1], mask.data_ptr())
+    dd = ggml.make(ggml.GGML_TYPE_F32, [Dh, Hq, Sp, 2], o.data_ptr())
+    need = mm3fa.workspace_size(qd, kd, vd, md, dd)
+    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
+    flp = 4.0 * Dh * (Sp * (Sp + 1) / 2) * Hq * 2
+    us, tf, clocks = timed([((qd, kd, vd, md, dd), 1.0 / math.sqrt(Dh))], 1, flp, ws)
+    out["prefill"] = {"tflops": round(tf * world, 1), "tflops_per_gpu": round(tf, 1), "us_per_call": round(us, 2),
+                      "frac_of_sustained": round(tf / sustained, 4), "clocks": clocks,
+                      "config": {"workload": "causal LM prefill, benchmark config 4", "n_seq": 2, "tokens": Sp,
+                                 "n_head": Hq, "n_head_kv": Hkv, "head_dim": Dh, "n_kv_view": n_kv}}
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -199,6 +310,7 @@ def main() -> None:
     ap.add_argument("--impl", default="mm3fa", choices=["mm3fa", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-dense", action="store_true", help="skip the DiT / prefill (tensor-core) lines")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers per step (36 = the LM; fewer only for small ncu captures)")
     args = ap.parse_args()
@@ -361,6 +473,10 @@ def main() -> None:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = job_bytes * args.steps / (float(te.item()) * 1e-3) / 1e9
 
+    dense = None if args.no_dense else bench_dense(torch, mm3fa, ggml, dev, stream, args.steps, args.warmup, world, local)
+    if dense is not None and world > 1:
+        dist.barrier()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_seconds)
@@ -370,7 +486,7 @@ def main() -> None:
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16 (K/V) / f32 (Q, accum, out)",
-            "data": "synthetic (seeded, BASELINE config 2 shapes; inputs larger than L2, no flush)",
+            "data": "synthetic (seeded, benchmark config 2 shapes; inputs larger than L2, no flush)",
             "config": {"workload": "decode attention, 36-layer Qwen3 LM step at CFG B=2 per GPU, KV 8192 "
                                    "(F16 cache views [128, 8192, 8, B] of [128, 10240, 8, B])",
                        "global_batch": n_seq, "n_kv": N_KV, "n_layers": n_layers, "n_head": N_HEAD,
@@ -387,6 +503,8 @@ def main() -> None:
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
         }
+        if dense is not None:
+            line.update(dense)
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)

@@ -125,7 +125,7 @@ def kv_cache(rng, n_seq: int, n_head_kv: int, n_kv: int, D: int, std: float, max
 
 
 def q8_0_random_blocks(rng, lead: tuple, D: int) -> np.ndarray:
-    """Q8_0 rows with int8 ~U[-127,127] and fp16 scales ~U[0.001,0.02]."""
+    """Q8_0 rows with int8 ~U[-127,127] and fp16 scales ~U[0.001,0.02] (benchmark config 3)."""
     nblk = D // ggml.QK8_0
     out = np.empty(lead + (nblk, ggml.Q8_0_BLOCK_BYTES), dtype=np.uint8)
     d = rng.uniform(0.001, 0.02, size=lead + (nblk,)).astype(np.float16)
@@ -138,7 +138,7 @@ def q8_0_random_blocks(rng, lead: tuple, D: int) -> np.ndarray:
 def decode_case(n_seq: int = 2, n_kv: int = 2048, n_head: int = 32, n_head_kv: int = 8, D: int = 128,
                 n_q: int = 1, kv_std: float = 0.5, seed: int = 1, max_seq: int | None = None,
                 kv_type: int = ggml.GGML_TYPE_F16, kv_len: list | None = None, name: str = "decode") -> Case:
-    """LM batched CFG decode (2, 3): 1..8 query rows per KV set.
+    """LM batched CFG decode (benchmark configs 1, 2, 3): 1..8 query rows per KV set.
 
     kv_len, when given, is the per-sequence visible length; the mask is 0 below it and
     -inf from it on (src/qwen3-lm.h:909-920).  Default: every position visible.
@@ -160,7 +160,7 @@ def decode_case(n_seq: int = 2, n_kv: int = 2048, n_head: int = 32, n_head_kv: i
 
 def prefill_case(n_seq: int = 2, S: int = 1024, n_head: int = 32, n_head_kv: int = 8, D: int = 128,
                  seed: int = 4, kv_pos: int = 0, pad: int = 256, theta: float = 1e6) -> Case:
-    """Causal LM prefill: RMS-normed (w=1), NeoX-RoPE'd Q/K.
+    """Causal LM prefill (benchmark config 4): RMS-normed (w=1), NeoX-RoPE'd Q/K.
 
     Q is the permuted F32 view [D, S, H, n_seq] of the [D, H, S, n_seq] projection; the
     causal mask [n_kv_pad, S] lets row i see columns <= kv_pos + i (src/qwen3-lm.h:604-617).
@@ -193,7 +193,7 @@ def prefill_case(n_seq: int = 2, S: int = 1024, n_head: int = 32, n_head_kv: int
 
 
 def dit_case(B: int = 2, S: int = 4096, H: int = 16, D: int = 128, seed: int = 5, name: str = "dit") -> Case:
-    """Bidirectional DiT attention (real model: S=690, H=32, D=64).
+    """Bidirectional DiT attention (benchmark config 5; real model: S=690, H=32, D=64).
 
     Q is the permuted F32 view [D, S, H, B] of the [D, H, S, B] projection; K/V are F16
     contiguous [D, S, H, B] (the ggml_cast nodes at src/dit.h:219-220); no mask.

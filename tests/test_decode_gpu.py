@@ -51,7 +51,7 @@ def check(c, dev, exact_abs=2e-3, exact_cos=0.99999):
 
 
 def test_config1_decode(kernel, cuda_device):
-    """CFG B=2, 32q/8kv, D=128, KV 2048, F16 cache view (max_seq 2560)."""
+    """benchmark config 1: CFG B=2, 32q/8kv, D=128, KV 2048, F16 cache view (max_seq 2560)."""
     check(workloads.decode_case(n_seq=2, n_kv=2048, max_seq=2560, seed=1), cuda_device)
 
 

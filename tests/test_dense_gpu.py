@@ -100,7 +100,7 @@ def test_dit_real_model(dense, cuda_device):
 
 
 def test_dit_config5_rows(dense, cuda_device):
-    """BASELINE config 5 (S=4096, H=16, D=128, B=2), checked on sampled query rows."""
+    """benchmark config 5 (S=4096, H=16, D=128, B=2), checked on sampled query rows."""
     check_rows(workloads.dit_case(B=2, S=4096, H=16, D=128, seed=331), cuda_device, n_rows=40)
 
 
