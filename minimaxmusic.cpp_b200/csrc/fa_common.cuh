@@ -147,6 +147,7 @@ struct DecodeParams {
     int64_t      keys_per_cta;   // W
     int          max_slots;      // partial slots per unit
     int          cluster;        // CTAs per thread-block cluster (tensor-core cluster mode)
+    int          dst_vec;        // dst rows start 16-byte aligned: 16-byte stores
     // workspace
     uint32_t *   status;
     uint32_t *   counters;

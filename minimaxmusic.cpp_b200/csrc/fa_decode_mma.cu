@@ -144,6 +144,21 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void * local, uint32_t rank
     return r;
 }
 
+__device__ __forceinline__ float2 ld_dsmem2(uint32_t addr) {
+    float2 v;
+    asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ float4 ld_dsmem4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+
 __device__ __forceinline__ float ld_dsmem(uint32_t addr) {
     float v;
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
@@ -382,6 +397,65 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
     };
 
     auto end_unit = [&](int64_t unit) {
+        if constexpr (CLUSTER) {
+            // one unit per CTA, so the ring is free: each warp parks its raw O fragments there,
+            // then all consumer threads combine the 4 warps per (row, 4 dims) in one pass
+            float * o4 = reinterpret_cast<float *>(smem);  // [warp][8 NT rows][D]
+            named_barrier_consumers();  // every warp is done reading the ring
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    float l = l_run[nt][e];
+                    l += __shfl_xor_sync(0xffffffffu, l, 4);
+                    l += __shfl_xor_sync(0xffffffffu, l, 8);
+                    l += __shfl_xor_sync(0xffffffffu, l, 16);
+                    if (g4 == 0) {
+                        const int r                        = nt * 8 + 2 * q4 + e;
+                        redML[(warp * 8 * NT + r) * 2 + 0] = m_run[nt][e];
+                        redML[(warp * 8 * NT + r) * 2 + 1] = l;
+                    }
+                }
+#pragma unroll
+                for (int m = 0; m < KS; m++) {
+                    const int r  = nt * 8 + 2 * q4;
+                    const int d  = m * 16 + g4;
+                    float *   ow = o4 + (size_t) warp * 8 * NT * D;
+                    ow[r * D + d]           = acc[m][nt][0];
+                    ow[(r + 1) * D + d]     = acc[m][nt][1];
+                    ow[r * D + d + 8]       = acc[m][nt][2];
+                    ow[(r + 1) * D + d + 8] = acc[m][nt][3];
+                }
+            }
+            named_barrier_consumers();
+            for (int it4 = tid; it4 < nrow * (D / 4); it4 += 32 * MMA_CONSUMERS) {
+                const int r = it4 / (D / 4), d = (it4 % (D / 4)) * 4;
+                float     mw[MMA_CONSUMERS], M = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < MMA_CONSUMERS; w++) {
+                    mw[w] = redML[(w * 8 * NT + r) * 2];
+                    M     = fmaxf(M, mw[w]);
+                }
+                float4 O  = make_float4(0.f, 0.f, 0.f, 0.f);
+                float  Ls = 0.0f;
+#pragma unroll
+                for (int w = 0; w < MMA_CONSUMERS; w++) {
+                    const float  wt = mw[w] == -INFINITY ? 0.0f : exp2f(mw[w] - M);
+                    const float4 v  = *reinterpret_cast<const float4 *>(o4 + ((size_t) w * 8 * NT + r) * D + d);
+                    O.x += wt * v.x;
+                    O.y += wt * v.y;
+                    O.z += wt * v.z;
+                    O.w += wt * v.w;
+                    Ls += wt * redML[(w * 8 * NT + r) * 2 + 1];
+                }
+                *reinterpret_cast<float4 *>(&redO[r * D + d]) = O;
+                if (d == 0) {
+                    cml[r * 2]     = M;
+                    cml[r * 2 + 1] = Ls;
+                }
+            }
+            return;  // the cluster barrier that follows orders these writes before the peers read
+        } else {
         // each warp's (m, l) per row to shared memory, l summed over the 8 key lanes
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
@@ -436,25 +510,6 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                 }
             }
             named_barrier_consumers();
-        }
-        if (CLUSTER) {
-            // this CTA's (m, l) per row; the cluster epilogue merges the CTAs over DSMEM
-            if (tid < nrow) {
-                float M = -INFINITY;
-#pragma unroll
-                for (int w = 0; w < MMA_CONSUMERS; w++) {
-                    M = fmaxf(M, redML[(w * 8 * NT + tid) * 2]);
-                }
-                float Ls = 0.0f;
-#pragma unroll
-                for (int w = 0; w < MMA_CONSUMERS; w++) {
-                    const float mw = redML[(w * 8 * NT + tid) * 2];
-                    Ls += (mw == -INFINITY ? 0.0f : exp2f(mw - M)) * redML[(w * 8 * NT + tid) * 2 + 1];
-                }
-                cml[tid * 2]     = M;
-                cml[tid * 2 + 1] = Ls;
-            }
-            return;
         }
         // flag[0] can be raised by the producer at any time: decide once, for all warps alike
         if (!consumers_any(flag[0] != 0)) {
@@ -525,6 +580,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
             }
         }
         named_barrier_consumers();  // shared reduction buffers are free again
+        }
     };
 
     if (CLUSTER) {  // the cluster's unit, even when this CTA's key slice is empty
@@ -723,42 +779,53 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
         const int     nr   = min(p.rows_per_unit, p.rows_per_pair - rgrp * MMA_RMAX);
         const int     CS   = p.cluster;
         const int     rank = (int) cluster_ctarank();
-        // rank c takes the (row, dim) items c, c + CS, c + 2*CS, ... (any cluster size)
-        for (int idx = rank + tid * CS; idx < nr * D; idx += MMA_THREADS * CS) {
-            const int r = idx / D, d = idx % D;
-            // all remote loads of the item issued together (one DSMEM latency, not 3*CS)
-            float mv[16], lv[16], ov[16];
+        // rank c takes the (row, 4 dims) items c, c + CS, c + 2*CS, ... (any cluster size); all
+        // remote loads of an item are issued together (one DSMEM latency)
+        for (int idx = rank + tid * CS; idx < nr * (D / 4); idx += MMA_THREADS * CS) {
+            const int r = idx / (D / 4), d = (idx % (D / 4)) * 4;
+            float2    ml[16];
+            float4    ov[16];
 #pragma unroll
             for (int c = 0; c < 16; c++) {
-                mv[c] = -INFINITY;
-                lv[c] = 0.0f;
-                ov[c] = 0.0f;
+                ml[c] = make_float2(-INFINITY, 0.0f);
+                ov[c] = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (c < CS) {
-                    mv[c] = ld_dsmem(dsmem_addr(&cml[r * 2], (uint32_t) c));
-                    lv[c] = ld_dsmem(dsmem_addr(&cml[r * 2 + 1], (uint32_t) c));
-                    ov[c] = ld_dsmem(dsmem_addr(&redO[r * D + d], (uint32_t) c));
+                    ml[c] = ld_dsmem2(dsmem_addr(&cml[r * 2], (uint32_t) c));
+                    ov[c] = ld_dsmem4(dsmem_addr(&redO[r * D + d], (uint32_t) c));
                 }
             }
             float M = -INFINITY;
 #pragma unroll
             for (int c = 0; c < 16; c++) {
-                M = fmaxf(M, mv[c]);
+                M = fmaxf(M, ml[c].x);
             }
-            float O = 0.0f, Ls = 0.0f;
+            float4 O  = make_float4(0.f, 0.f, 0.f, 0.f);
+            float  Ls = 0.0f;
             if (M != -INFINITY) {
 #pragma unroll
                 for (int c = 0; c < 16; c++) {
-                    const float w = mv[c] == -INFINITY ? 0.0f : exp2f(mv[c] - M);
-                    O += w * ov[c];
-                    Ls += w * lv[c];
+                    const float w = ml[c].x == -INFINITY ? 0.0f : exp2f(ml[c].x - M);
+                    O.x += w * ov[c].x;
+                    O.y += w * ov[c].y;
+                    O.z += w * ov[c].z;
+                    O.w += w * ov[c].w;
+                    Ls += w * ml[c].y;
                 }
             }
-            const int rf  = rgrp * MMA_RMAX + r;
-            const int h   = g * p.ratio + rf / p.n_q;
-            const int i   = rf % p.n_q;
-            float *   out = reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 + (int64_t) i * p.d_nb2 +
-                                                    (int64_t) sq * p.d_nb3);
-            out[d]        = Ls > 0.0f ? O / Ls : 0.0f;
+            const float inv = Ls > 0.0f ? 1.0f / Ls : 0.0f;
+            const int   rf  = rgrp * MMA_RMAX + r;
+            const int   h   = g * p.ratio + rf / p.n_q;
+            const int   i   = rf % p.n_q;
+            float *     out = reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 + (int64_t) i * p.d_nb2 +
+                                                    (int64_t) sq * p.d_nb3) + d;
+            if (p.dst_vec) {
+                *reinterpret_cast<float4 *>(out) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+            } else {
+                out[0] = O.x * inv;
+                out[1] = O.y * inv;
+                out[2] = O.z * inv;
+                out[3] = O.w * inv;
+            }
         }
         __syncwarp();
         cluster_sync_all();  // peers may still be reading this CTA's shared memory

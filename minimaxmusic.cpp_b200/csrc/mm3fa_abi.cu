@@ -557,6 +557,7 @@ int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const m
     p.m0        = std::pow(2.0f, -max_bias / (float) n_head_log2);
     p.m1        = std::pow(2.0f, -max_bias / 2.0f / (float) n_head_log2);
     p.timeout_ns = wait_timeout_ns();
+    p.dst_vec    = rows_vec16(dst);
     if (var >= V_MMA_8) {
         const int slots   = device_info().sms * ctas_per_sm_cached((int) s.D, s.kvt, var);
         const int pref    = decode_mma_mode_preference();
