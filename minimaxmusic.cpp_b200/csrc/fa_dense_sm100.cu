@@ -182,8 +182,17 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t * r) {
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld_wait() {
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+// tcgen05.wait::ld that also names the 32 registers a tcgen05.ld wrote: the compiler cannot move
+// any use of them above the wait (the load writes them asynchronously)
+__device__ __forceinline__ void tmem_ld_wait_tie(uint32_t * r) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
 }
 
 __device__ __forceinline__ void tmem_st_wait() {
@@ -364,9 +373,11 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
     const int warp  = tid >> 5;
     const int lane  = tid & 31;
     const int wg    = warp >> 2;
-    const int cq    = blockIdx.x;  // 256-row query block
-    const int h     = blockIdx.y;
-    const int sq    = blockIdx.z;
+    // query blocks are the slowest grid dimension and run last-first: under a causal mask the last
+    // blocks see the most keys, so the longest CTAs start in the first wave
+    const int h     = blockIdx.x;
+    const int sq    = blockIdx.y;
+    const int cq    = (int) (gridDim.z - 1 - blockIdx.z);  // 256-row query block
     const int g     = h / p.ratio;
     const int ks3   = sq / p.rk3;
     const int plane = (sq % p.m_ne3) * p.m_ne2 + (h % p.m_ne2);
@@ -611,23 +622,31 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
         bool        ok    = true;
         int         i     = 0;
         for (int kt = next_tile(0); kt < p.n_kt; kt = next_tile(kt + 1), i++) {
+            const int  nk    = p.n_kv - kt * DN_N;  // keys of this tile that exist (may exceed DN_N)
+            const int  cls   = tile_class(p, plane, cq, kt);
+            const bool fast  = plain && nk >= DN_N && cls != BLK_MIXED;
+            const bool mixed = valid && cls == BLK_MIXED;
+            // this row's mask values of the tile: pulled into L1 before S is ready, so the loads of
+            // the pass below hit
+            const __half * mp = mixed ? mrow + (int64_t) kt * DN_N : nullptr;
+            if (mixed) {
+#pragma unroll
+                for (int c = 0; c < DN_N * 2; c += 128) {
+                    asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const char *>(mp) + c));
+                }
+            }
             if (!dn_wait_warp(&bar[B_SFULL + t], (uint32_t) (i & 1), deadline)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const int  nk   = p.n_kv - kt * DN_N;  // keys of this tile that exist (may exceed 128)
-            const bool fast = plain && nk >= DN_N && tile_class(p, plane, cq, kt) != BLK_MIXED;
             if (!fast) {
                 // general tile: rewrite S in TMEM in log2 units - softcap, mask, keys past n_kv -
                 // 32 columns at a time, so the row pass below treats every tile alike
-                const bool     mixed = valid && tile_class(p, plane, cq, kt) == BLK_MIXED;
-                const __half * mp    = mixed ? mrow + (int64_t) kt * DN_N : nullptr;
 #pragma unroll 1
                 for (int c = 0; c < DN_N / 32; c++) {
                     uint32_t v[32];
                     tmem_ld32(s_col + (uint32_t) (c * 32), v);
-                    tmem_ld_wait();
                     float mv[32];
 #pragma unroll
                     for (int e = 0; e < 32; e++) {
@@ -653,6 +672,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                             }
                         }
                     }
+                    tmem_ld_wait_tie(v);
 #pragma unroll
                     for (int e = 0; e < 32; e++) {
                         const float x = __uint_as_float(v[e]);
@@ -664,51 +684,22 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                 }
                 tmem_st_wait();
             }
-            uint32_t sr[DN_N];
-            tmem_ld32(s_col + 0, &sr[0]);
-            tmem_ld32(s_col + 32, &sr[32]);
-            tmem_ld32(s_col + 64, &sr[64]);
-            tmem_ld32(s_col + 96, &sr[96]);
-            tmem_ld_wait();
-            float s[DN_N];
-#pragma unroll
-            for (int k = 0; k < DN_N; k++) {
-                s[k] = __uint_as_float(sr[k]);
-            }
             // scores are raw (fast tiles, times sl2 > 0 gives log2 units) or already in log2 units
-            const float mult = fast ? sl2 : 1.0f;
-            float       a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
-#pragma unroll
-            for (int k = 4; k < DN_N - 4; k += 8) {
-                a0 = fmax3(a0, s[k], s[k + 1]);
-                a1 = fmax3(a1, s[k + 2], s[k + 3]);
-                a2 = fmax3(a2, s[k + 4], s[k + 5]);
-                a3 = fmax3(a3, s[k + 6], s[k + 7]);
-            }
-            a0 = fmax3(a0, s[DN_N - 4], s[DN_N - 3]);
-            a1 = fmax3(a1, s[DN_N - 2], s[DN_N - 1]);
-            const float mt = fmax3(a0, a1, fmaxf(a2, a3)) * mult;
-            // lazy maximum: rescale only when the row maximum grows by more than 8 (a factor 2^8)
-            float alpha = 1.0f;
-            if (mt > m + 8.0f) {
-                alpha = (m == -INFINITY) ? 0.0f : ex2(m - mt);
-                m     = mt;
-            }
-            uint32_t pk[DN_N / 2];
-            float    lsum = 0.0f;
-            if (m == -INFINITY) {
-#pragma unroll
-                for (int k = 0; k < DN_N / 2; k++) {
-                    pk[k] = 0u;
-                }
-            } else {
-                // p = 2^(s * mult - m): pairs in packed f32x2 arithmetic; DN_EMU of every 8 pairs
-                // take the FMA-pipe polynomial, the others the special-function unit
-                const uint64_t mul2 = f2pack(mult, mult), nm2 = f2pack(-m, -m);
-                uint64_t       acc[4] = { 0ull, 0ull, 0ull, 0ull };
+            const float    mult = fast ? sl2 : 1.0f;
+            const uint64_t mul2 = f2pack(mult, mult);
+            uint32_t       sr[DN_N];
+            uint32_t       pk[DN_N / 2];
+            uint64_t       acc[4];
+            // p = 2^(s * mult - m) for pairs [j0, j1): packed f32x2 arithmetic; DN_EMU of every 8 pairs
+            // take the FMA-pipe polynomial, the others the special-function unit
+            auto exp_pairs = [&](int j0, int j1) {
+                const uint64_t nm2 = f2pack(-m, -m);
 #pragma unroll
                 for (int j = 0; j < DN_N / 2; j++) {
-                    const uint64_t x2 = ffma2(f2pack(s[2 * j], s[2 * j + 1]), mul2, nm2);
+                    if (j < j0 || j >= j1) {
+                        continue;
+                    }
+                    const uint64_t x2 = ffma2(f2pack(__uint_as_float(sr[2 * j]), __uint_as_float(sr[2 * j + 1])), mul2, nm2);
                     uint64_t       p2;
                     if ((j & 7) < DN_EMU) {
                         p2 = exp2_poly2(x2);
@@ -722,11 +713,75 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                     f2unpack(p2, pl, ph);
                     pk[j] = pack2_dn<BF16>(pl, ph);
                 }
-                float s0, s1, s2, s3, s4, s5, s6, s7;
+            };
+            auto acc_sum = [&]() {
+                float s0, s1, s2, s3;
                 f2unpack(fadd2(acc[0], acc[1]), s0, s1);
                 f2unpack(fadd2(acc[2], acc[3]), s2, s3);
-                (void) s4, (void) s5, (void) s6, (void) s7;
-                lsum = (s0 + s1) + (s2 + s3);
+                return (s0 + s1) + (s2 + s3);
+            };
+            auto load_all = [&]() {
+#pragma unroll
+                for (int c = 0; c < DN_N / 32; c++) {
+                    tmem_ld32(s_col + (uint32_t) (c * 32), &sr[c * 32]);
+                }
+#pragma unroll
+                for (int c = 0; c < DN_N / 32; c++) {
+                    tmem_ld_wait_tie(&sr[c * 32]);
+                }
+            };
+            float alpha = 1.0f, lsum = 0.0f;
+            // The row maximum is needed while it is unknown (first tile of a row) or when the stale
+            // maximum would let a p overflow 16 bits.  A tile sum <= 2^15 bounds every p below the
+            // f16 limit, so the exp pass runs first with the stale maximum and the exact maximum is
+            // computed (and the pass redone) only when some row's sum exceeds that.
+            bool full = __any_sync(0xffffffffu, m == -INFINITY);
+            if (!full) {
+                // first half of the row in registers, second half loading while the first is used
+                tmem_ld32(s_col + 0, &sr[0]);
+                tmem_ld32(s_col + 32, &sr[32]);
+                tmem_ld_wait_tie(&sr[0]);
+                tmem_ld_wait_tie(&sr[32]);
+                tmem_ld32(s_col + 64, &sr[64]);
+                tmem_ld32(s_col + 96, &sr[96]);
+                acc[0] = acc[1] = acc[2] = acc[3] = 0ull;
+                exp_pairs(0, DN_N / 4);
+                tmem_ld_wait_tie(&sr[64]);
+                tmem_ld_wait_tie(&sr[96]);
+                exp_pairs(DN_N / 4, DN_N / 2);
+                lsum = acc_sum();
+                full = __any_sync(0xffffffffu, !(lsum <= 32768.0f));  // NaN included
+            }
+            if (full) {
+                load_all();
+                float a0 = __uint_as_float(sr[0]), a1 = __uint_as_float(sr[1]), a2 = __uint_as_float(sr[2]),
+                      a3 = __uint_as_float(sr[3]);
+#pragma unroll
+                for (int k = 4; k < DN_N - 4; k += 8) {
+                    a0 = fmax3(a0, __uint_as_float(sr[k]), __uint_as_float(sr[k + 1]));
+                    a1 = fmax3(a1, __uint_as_float(sr[k + 2]), __uint_as_float(sr[k + 3]));
+                    a2 = fmax3(a2, __uint_as_float(sr[k + 4]), __uint_as_float(sr[k + 5]));
+                    a3 = fmax3(a3, __uint_as_float(sr[k + 6]), __uint_as_float(sr[k + 7]));
+                }
+                a0 = fmax3(a0, __uint_as_float(sr[DN_N - 4]), __uint_as_float(sr[DN_N - 3]));
+                a1 = fmax3(a1, __uint_as_float(sr[DN_N - 2]), __uint_as_float(sr[DN_N - 1]));
+                const float mt = fmax3(a0, a1, fmaxf(a2, a3)) * mult;
+                // lazy maximum: rescale only when the row maximum grows by more than 8 (a factor 2^8)
+                if (mt > m + 8.0f) {
+                    alpha = (m == -INFINITY) ? 0.0f : ex2(m - mt);
+                    m     = mt;
+                }
+                if (m == -INFINITY) {
+#pragma unroll
+                    for (int k = 0; k < DN_N / 2; k++) {
+                        pk[k] = 0u;
+                    }
+                    lsum = 0.0f;
+                } else {
+                    acc[0] = acc[1] = acc[2] = acc[3] = 0ull;
+                    exp_pairs(0, DN_N / 2);
+                    lsum = acc_sum();
+                }
             }
             l = l * alpha + lsum;
 
@@ -739,7 +794,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                 for (int c = 0; c < D / 32; c++) {
                     uint32_t o[32];
                     tmem_ld32(o_col + (uint32_t) (c * 32), o);
-                    tmem_ld_wait();
+                    tmem_ld_wait_tie(o);
 #pragma unroll
                     for (int e = 0; e < 32; e++) {
                         o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
@@ -772,7 +827,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             uint32_t o[32];
             if (have_o) {
                 tmem_ld32(o_col + (uint32_t) (c * 32), o);
-                tmem_ld_wait();
+                tmem_ld_wait_tie(o);
             } else {
 #pragma unroll
                 for (int e = 0; e < 32; e++) {
@@ -813,20 +868,39 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
 // ------------------------------------------------------------------ mask block classes
 
 // One CTA per (kv tile, 256-row query block, mask plane): SKIP if every entry is -inf, NONE if
-// every entry is 0, MIXED otherwise.  Only rows < n_q and columns < n_kv are examined.
-__global__ void mask_block_class_kernel(const char * mask, int64_t nb1, int64_t nb2, int64_t nb3, int m_ne2,
-                                        int n_q, int n_kv, int n_qt, int n_kt, uint8_t * blocks) {
-    const int kt = blockIdx.x, qt = blockIdx.y, plane = blockIdx.z;
-    const int i2 = plane % m_ne2, i3 = plane / m_ne2;
-    const int r0 = qt * DN_ROWS, c0 = kt * DN_N;
-    const int nr = min(DN_ROWS, n_q - r0), nc = min(DN_N, n_kv - c0);
-    int       finite = 0, nonzero = 0;
-    for (int idx = threadIdx.x; idx < nr * nc; idx += blockDim.x) {
-        const int   rr = idx / nc, c = idx % nc;
-        const float v  = __half2float(*reinterpret_cast<const __half *>(
-            mask + (int64_t) (r0 + rr) * nb1 + (int64_t) i2 * nb2 + (int64_t) i3 * nb3 + (int64_t) (c0 + c) * 2));
-        finite |= v != -INFINITY;
-        nonzero |= v != 0.0f;
+// every entry is 0, MIXED otherwise.  Only rows < n_q and columns < n_kv are examined.  With
+// 16-byte aligned rows a row of a full tile is 16 lanes x 8 halves; the bits are tested directly
+// (-inf = 0xFC00; zero = +-0).
+constexpr int MASK_CLASS_THREADS = 512;
+
+__global__ void __launch_bounds__(MASK_CLASS_THREADS)
+    mask_block_class_kernel(const char * mask, int64_t nb1, int64_t nb2, int64_t nb3, int m_ne2, int n_q, int n_kv,
+                            int n_qt, int n_kt, int vec, uint8_t * blocks) {
+    const int    kt = blockIdx.x, qt = blockIdx.y, plane = blockIdx.z;
+    const int    i2 = plane % m_ne2, i3 = plane / m_ne2;
+    const int    r0 = qt * DN_ROWS, c0 = kt * DN_N;
+    const int    nr = min(DN_ROWS, n_q - r0), nc = min(DN_N, n_kv - c0);
+    const char * base = mask + (int64_t) r0 * nb1 + (int64_t) i2 * nb2 + (int64_t) i3 * nb3 + (int64_t) c0 * 2;
+    int          finite = 0, nonzero = 0;
+    if (vec && nc == DN_N) {
+        constexpr int LPR = DN_N / 8;  // lanes per row
+        for (int rr = threadIdx.x / LPR; rr < nr; rr += MASK_CLASS_THREADS / LPR) {
+            const uint4    u    = *reinterpret_cast<const uint4 *>(base + (int64_t) rr * nb1 + (threadIdx.x % LPR) * 16);
+            const uint32_t w[4] = { u.x, u.y, u.z, u.w };
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const uint32_t lo = w[j] & 0xFFFFu, hi = w[j] >> 16;
+                finite |= (lo != 0xFC00u) | (hi != 0xFC00u);
+                nonzero |= ((lo & 0x7FFFu) != 0u) | ((hi & 0x7FFFu) != 0u);
+            }
+        }
+    } else {
+        for (int idx = threadIdx.x; idx < nr * nc; idx += MASK_CLASS_THREADS) {
+            const int   rr = idx / nc, c = idx % nc;
+            const float v  = __half2float(*reinterpret_cast<const __half *>(base + (int64_t) rr * nb1 + (int64_t) c * 2));
+            finite |= v != -INFINITY;
+            nonzero |= v != 0.0f;
+        }
     }
     finite  = __syncthreads_or(finite);
     nonzero = __syncthreads_or(nonzero);
@@ -904,8 +978,9 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
     if (p.mask) {
         uint8_t * blocks = reinterpret_cast<uint8_t *>(ws + WS_STATUS_BYTES);
         const int planes = p.m_ne2 * p.m_ne3;
-        mask_block_class_kernel<<<dim3((unsigned) p.n_kt, (unsigned) p.n_qt, (unsigned) planes), 256, 0, stream>>>(
-            p.mask, p.m_nb1, p.m_nb2, p.m_nb3, p.m_ne2, p.n_q, p.n_kv, p.n_qt, p.n_kt, blocks);
+        mask_block_class_kernel<<<dim3((unsigned) p.n_kt, (unsigned) p.n_qt, (unsigned) planes), MASK_CLASS_THREADS, 0,
+                                  stream>>>(p.mask, p.m_nb1, p.m_nb2, p.m_nb3, p.m_ne2, p.n_q, p.n_kv, p.n_qt, p.n_kt,
+                                            p.mask_vec, blocks);
         e = cudaGetLastError();
         if (e != cudaSuccess) {
             return e;
@@ -917,7 +992,7 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
         return e;
     }
     void * args[] = { &tmk, &tmv, &p };
-    return cudaLaunchKernel(fn, dim3((unsigned) p.n_qt, (unsigned) n_head, (unsigned) n_seq), dim3(DN_THREADS), args,
+    return cudaLaunchKernel(fn, dim3((unsigned) n_head, (unsigned) n_seq, (unsigned) p.n_qt), dim3(DN_THREADS), args,
                             (size_t) smem, stream);
 }
 

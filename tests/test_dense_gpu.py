@@ -108,9 +108,12 @@ def test_dit_config5_rows(dense, cuda_device):
 
 @pytest.mark.parametrize("D", [64, 128])
 def test_bf16_kv(dense, cuda_device, D):
-    check(to_bf16(workloads.dit_case(B=1, S=200, H=4, D=D, seed=340 + D)), cuda_device)
+    """BF16 K/V: the tensor-core PV needs P in K/V's type, so P carries bf16 rounding (8-bit
+    mantissa) that ggml's CPU path (P in F32) does not; against the ggml convention the north-star
+    bound holds, against exact math the bound is that of the 8-bit Q8_0 case."""
+    check(to_bf16(workloads.dit_case(B=1, S=200, H=4, D=D, seed=340 + D)), cuda_device, 5e-3, 0.9999)
     check(to_bf16(workloads.prefill_case(n_seq=1, S=150, n_head=4, n_head_kv=2, D=D, kv_pos=30, seed=342 + D)),
-          cuda_device)
+          cuda_device, 5e-3, 0.9999)
 
 
 @pytest.mark.parametrize("ratio", [1, 4, 8])
