@@ -4,6 +4,7 @@
 #include "fa_common.cuh"
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 namespace mm3fa {
@@ -182,6 +183,8 @@ cudaError_t launch_decode(DecodeParams p, const DecodeGeometry & g, int D, int k
 bool encode_kv_tensor_map(CUtensorMap * tm, const void * data, bool bf16, int64_t D, int64_t n_kv, int64_t hkv,
                           int64_t sk, int64_t nb1, int64_t nb2, int64_t nb3, int box_rows);
 bool tensor_maps_available();
+// cuTensorMapEncodeTiled from the driver (nullptr when unavailable)
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 // Tensor-core variant (fa_decode_mma.cu): F16/BF16 K/V, D 64 or 128, <= 16 rows per unit,
 // strides that a TMA tensor map can express.

@@ -26,6 +26,7 @@ struct DenseParams {
     int          q_vec;     // Q rows start 16-byte aligned: 16-byte loads
     int          dst_vec;   // dst rows start 16-byte aligned: 16-byte stores
     int          mask_vec;  // mask rows start 16-byte aligned: 16-byte loads
+    int          tma_store; // the result is written by TMA (tensor map argument valid)
     int          n_q, n_kv;
     int          ratio;     // n_head / n_head_kv
     int          rk3;       // n_seq / n_seq_k

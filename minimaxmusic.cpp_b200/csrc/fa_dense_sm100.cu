@@ -101,6 +101,19 @@ __device__ __forceinline__ void dn_tma_load_4d(void * dst, const CUtensorMap * t
         : "memory");
 }
 
+// 4-D tiled TMA store shared -> global (bulk group); rows outside the tensor are not written
+__device__ __forceinline__ void dn_tma_store_4d(const CUtensorMap * tm, const void * src, int c0, int c1, int c2,
+                                                int c3) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+                     reinterpret_cast<uint64_t>(tm)),
+                 "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(src))
+                 : "memory");
+}
+
+__device__ __forceinline__ void dn_named_barrier(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 __device__ __forceinline__ void dn_mbar_arrive(uint64_t * bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
@@ -359,7 +372,7 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
 template <int D, bool BF16>
 __global__ void __launch_bounds__(DN_THREADS, 1)
     fa_dense_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                    const DenseParams p) {
+                    const __grid_constant__ CUtensorMap tmo, const DenseParams p) {
     using L          = DenseSmem<D>;
     constexpr int NS = L::NS;
     constexpr int KS = D / 16;  // k-steps of QK
@@ -570,20 +583,32 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             const char * qrow = p.q + (int64_t) qi * p.q_nb1 + (int64_t) h * p.q_nb2 + (int64_t) sq * p.q_nb3;
             char *       qs   = smem + L::OFF_Q + t * L::QT;
             if (p.q_type == KV_F32 && p.q_vec) {
-                // the whole row in flight at once: D/4 16-byte loads, then convert and store
-                float4 x[D / 4];
+                // coalesced: the lanes of a warp load whole rows (LPR lanes x 16 bytes per row) of this
+                // warp's 32 rows, all loads in flight, then each lane writes its 4 rounded values
+                // (8 bytes) into the row's swizzled 16-byte chunk
+                constexpr int LPR = D / 4;       // lanes per row
+                constexpr int RPI = 32 / LPR;    // rows per load instruction
+                constexpr int NLD = 32 / RPI;    // loads per lane
+                float4 x[NLD];
 #pragma unroll
-                for (int c = 0; c < D / 4; c++) {
-                    x[c] = valid ? reinterpret_cast<const float4 *>(qrow)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int it = 0; it < NLD; it++) {
+                    const int rr  = quad * 32 + it * RPI + lane / LPR;  // row in the tile
+                    const int row = cq * DN_ROWS + t * DN_M + rr;
+                    x[it]         = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (row < p.n_q) {
+                        x[it] = reinterpret_cast<const float4 *>(p.q + (int64_t) row * p.q_nb1 + (int64_t) h * p.q_nb2 +
+                                                                 (int64_t) sq * p.q_nb3)[lane % LPR];
+                    }
                 }
+                const int e  = (lane % LPR) * 4;  // first element of this lane
+                const int hb = e / 64, ch = (e % 64) / 8, sub = (e % 8) * 2;
 #pragma unroll
-                for (int c = 0; c < D / 8; c++) {
-                    uint4 v;
-                    v.x = pack2_dn<BF16>(x[2 * c].x, x[2 * c].y);
-                    v.y = pack2_dn<BF16>(x[2 * c].z, x[2 * c].w);
-                    v.z = pack2_dn<BF16>(x[2 * c + 1].x, x[2 * c + 1].y);
-                    v.w = pack2_dn<BF16>(x[2 * c + 1].z, x[2 * c + 1].w);
-                    *reinterpret_cast<uint4 *>(qs + (c >> 3) * (DN_M * 128) + sw128_off(r, c & 7)) = v;
+                for (int it = 0; it < NLD; it++) {
+                    const int rr = quad * 32 + it * RPI + lane / LPR;
+                    uint2     v;
+                    v.x = pack2_dn<BF16>(x[it].x, x[it].y);
+                    v.y = pack2_dn<BF16>(x[it].z, x[it].w);
+                    *reinterpret_cast<uint2 *>(qs + hb * (DN_M * 128) + sw128_off(rr, ch) + sub) = v;
                 }
             } else {
 #pragma unroll 4
@@ -673,11 +698,22 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                         }
                     }
                     tmem_ld_wait_tie(v);
+                    // the softcap branch stays outside the element loops (tanhf must not be if-converted)
+                    if (p.softcap != 0.0f) {
+                        const float cl2 = p.softcap * LOG2E;
+#pragma unroll
+                        for (int e = 0; e < 32; e++) {
+                            v[e] = __float_as_uint(cl2 * tanhf(__uint_as_float(v[e]) * sc));
+                        }
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 32; e++) {
+                            v[e] = __float_as_uint(__uint_as_float(v[e]) * sl2);
+                        }
+                    }
 #pragma unroll
                     for (int e = 0; e < 32; e++) {
-                        const float x = __uint_as_float(v[e]);
-                        float       y = p.softcap != 0.0f ? p.softcap * LOG2E * tanhf(x * sc) : x * sl2;
-                        y             = fmaf(ml2, mv[e], y);
+                        const float y = fmaf(ml2, mv[e], __uint_as_float(v[e]));
                         v[e]          = __float_as_uint(c * 32 + e < nk ? y : -INFINITY);
                     }
                     tmem_st32(s_col + (uint32_t) (c * 32), v);
@@ -820,7 +856,47 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             tc_fence_after();
         }
         const float inv = (have_o && l > 0.0f) ? 1.0f / l : 0.0f;
-        float *     out =
+        if (p.tma_store) {
+            // every MMA is done once MMADONE completes, so the K/V ring is free: each thread writes its
+            // scaled O row into 128-byte-swizzled [128 rows][32 floats] tiles there, and one thread
+            // of the warpgroup stores them with TMA (rows past n_q are clipped by the tensor map)
+            if (!dn_wait_warp(&bar[B_MMADONE], 0, deadline)) {
+                atomicExch(abort_f, 1);
+            }
+            char * stage = smem + L::OFF_K + t * (D / 32) * (DN_M * 128);
+#pragma unroll
+            for (int c = 0; c < D / 32; c++) {
+                uint32_t o[32];
+                if (have_o) {
+                    tmem_ld32(o_col + (uint32_t) (c * 32), o);
+                    tmem_ld_wait_tie(o);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        o[e] = 0u;
+                    }
+                }
+                char * tile = stage + c * (DN_M * 128);
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    *reinterpret_cast<float4 *>(tile + sw128_off(r, j)) =
+                        make_float4(__uint_as_float(o[4 * j]) * inv, __uint_as_float(o[4 * j + 1]) * inv,
+                                    __uint_as_float(o[4 * j + 2]) * inv, __uint_as_float(o[4 * j + 3]) * inv);
+                }
+            }
+            fence_proxy_async_smem();
+            dn_named_barrier(1 + t, 128);
+            if (quad == 0 && lane == 0) {
+                const int q0t = cq * DN_ROWS + t * DN_M;
+#pragma unroll
+                for (int c = 0; c < D / 32; c++) {
+                    dn_tma_store_4d(&tmo, stage + c * (DN_M * 128), c * 32, h, q0t, sq);
+                }
+                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+            }
+        } else {
+        float * out =
             reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 + (int64_t) qi * p.d_nb2 + (int64_t) sq * p.d_nb3);
 #pragma unroll
         for (int c = 0; c < D / 32; c++) {
@@ -849,6 +925,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                     }
                 }
             }
+        }
         }
     }
 
@@ -970,6 +1047,24 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
         !encode_kv_tensor_map(&tmv, p.v, bf16, D, p.n_kv, n_head_kv, n_seq_k, p.v_nb1, p.v_nb2, p.v_nb3, DN_N)) {
         return cudaErrorInvalidValue;
     }
+    // result tensor map for the TMA-store epilogue: [D, n_head, n_q, n_seq] F32 (ggml's layout),
+    // boxes of 32 floats x 128 rows, 128-byte swizzle; element stores are the fallback
+    alignas(64) CUtensorMap tmo;
+    p.tma_store = 0;
+    if (p.dst_vec && p.d_nb1 % 16 == 0 && p.d_nb2 % 16 == 0 && p.d_nb3 % 16 == 0) {
+        auto enc = tensor_map_encoder();
+        if (enc) {
+            const int64_t nb2 = p.n_q > 1 ? p.d_nb2 : p.d_nb1 * n_head, nb1 = n_head > 1 ? p.d_nb1 : 4 * D;
+            const int64_t nb3 = n_seq > 1 ? p.d_nb3 : nb2 * p.n_q;
+            cuuint64_t dims[4]    = { (cuuint64_t) D, (cuuint64_t) n_head, (cuuint64_t) p.n_q, (cuuint64_t) n_seq };
+            cuuint64_t strides[3] = { (cuuint64_t) nb1, (cuuint64_t) nb2, (cuuint64_t) nb3 };
+            cuuint32_t box[4]     = { 32, 1, (cuuint32_t) DN_M, 1 };
+            cuuint32_t estr[4]    = { 1, 1, 1, 1 };
+            p.tma_store = enc(&tmo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.dst, dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        }
+    }
     char * ws = static_cast<char *>(workspace);
     p.status  = reinterpret_cast<uint32_t *>(ws);
     p.n_qt    = (int) ((p.n_q + DN_ROWS - 1) / DN_ROWS);
@@ -991,7 +1086,7 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
     if (e != cudaSuccess) {
         return e;
     }
-    void * args[] = { &tmk, &tmv, &p };
+    void * args[] = { &tmk, &tmv, &tmo, &p };
     return cudaLaunchKernel(fn, dim3((unsigned) n_head, (unsigned) n_seq, (unsigned) p.n_qt), dim3(DN_THREADS), args,
                             (size_t) smem, stream);
 }

@@ -188,3 +188,20 @@ def test_repeat_calls_bit_identical(dense, cuda_device):
     assert np.array_equal(a, b)
     st, raw = mm3fa.workspace_status(ws.buf.data_ptr(), torch.cuda.current_stream().cuda_stream)
     assert st == mm3fa.OK and raw == 0
+
+
+def test_padded_destination_rows(dense, cuda_device):
+    """A result view whose rows are not 16-byte aligned takes the element-store epilogue instead
+    of the TMA store; both write exactly ggml's [Dv, H, n_q, S] view."""
+    c = workloads.dit_case(B=1, S=200, H=2, D=64, seed=397)
+    dev = cuda_device
+    q = torch.from_numpy(np.ascontiguousarray(c.q.storage)).to(dev)
+    k = torch.from_numpy(np.ascontiguousarray(c.k.storage)).to(dev)
+    v = torch.from_numpy(np.ascontiguousarray(c.v.storage)).to(dev)
+    store = torch.full((1, 200, 2, 65), float("nan"), dtype=torch.float32, device=dev)  # one pad float per row
+    dst = ggml.make(F32, [64, 2, 200, 1], store.data_ptr(), [4, 4 * 65, 4 * 65 * 2, 4 * 65 * 2 * 200])
+    mm3fa.run(c.q.device_desc(q), c.k.device_desc(k), c.v.device_desc(v), None, dst, c.scale)
+    torch.cuda.synchronize(dev)
+    got = store[..., :64].cpu().numpy()
+    assert np.all(np.isnan(store[..., 64].cpu().numpy())), "padding was written"
+    assert_close(got, run_oracle(c, oracle.MODE_GGML), what="padded dst vs ggml-convention oracle")
