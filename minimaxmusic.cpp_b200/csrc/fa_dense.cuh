@@ -28,6 +28,8 @@ struct DenseParams {
     int          mask_vec;  // mask rows start 16-byte aligned: 16-byte loads
     int          tma_store; // the result is written by TMA (tensor map argument valid)
     int          n_q, n_kv;
+    int          n_head, n_seq;
+    int          n_regular;       // CTAs with a whole work item; the rest come in split pairs
     int          ratio;     // n_head / n_head_kv
     int          rk3;       // n_seq / n_seq_k
     int          m_ne2, m_ne3;

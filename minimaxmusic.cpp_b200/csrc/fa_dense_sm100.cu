@@ -110,6 +110,33 @@ __device__ __forceinline__ void dn_tma_store_4d(const CUtensorMap * tm, const vo
                  : "memory");
 }
 
+// distributed shared memory of the other CTA of a 2-CTA cluster
+__device__ __forceinline__ uint32_t dn_mapa(const void * local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(local)), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ float2 dn_ld_dsmem2(uint32_t addr) {
+    float2 v;
+    asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ float4 dn_ld_dsmem4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+
+// all threads of both CTAs of the cluster; orders shared-memory writes before the peer's reads
+__device__ __forceinline__ void dn_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void dn_named_barrier(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
@@ -386,11 +413,21 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
     const int warp  = tid >> 5;
     const int lane  = tid & 31;
     const int wg    = warp >> 2;
-    // query blocks are the slowest grid dimension and run last-first: under a causal mask the last
-    // blocks see the most keys, so the longest CTAs start in the first wave
-    const int h     = blockIdx.x;
-    const int sq    = blockIdx.y;
-    const int cq    = (int) (gridDim.z - 1 - blockIdx.z);  // 256-row query block
+    // Work item = (256-row query block, head, sequence), query blocks last-first: under a causal
+    // mask the last blocks see the most keys, so the longest CTAs start in the first wave.  CTAs
+    // from n_regular on come in 2-CTA clusters that share one item, each taking half of its K/V
+    // tiles (the last, partial wave of a launch, or all items of a small launch), and merge their
+    // (O, m, l) through distributed shared memory.
+    int item = (int) blockIdx.x, half = -1;
+    if (item >= p.n_regular) {
+        const int rel = item - p.n_regular;
+        item          = p.n_regular + rel / 2;
+        half          = rel % 2;  // the CTA's rank in its cluster
+    }
+    const int hs    = p.n_head * p.n_seq;
+    const int cq    = p.n_qt - 1 - item / hs;  // 256-row query block
+    const int h     = (item % hs) % p.n_head;
+    const int sq    = (item % hs) / p.n_head;
     const int g     = h / p.ratio;
     const int ks3   = sq / p.rk3;
     const int plane = (sq % p.m_ne3) * p.m_ne2 + (h % p.m_ne2);
@@ -423,6 +460,17 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
         }
         return kt;
     };
+    // this CTA's share of them: positions [pos_lo, pos_lo + n_mine) of the list
+    int n_all = 0;
+    for (int kt = next_tile(0); kt < p.n_kt; kt = next_tile(kt + 1)) {
+        n_all++;
+    }
+    const int pos_lo = half == 1 ? (n_all + 1) / 2 : 0;
+    const int n_mine = half == 0 ? (n_all + 1) / 2 : n_all - pos_lo;
+    int       kt_lo  = next_tile(0);
+    for (int k = 0; k < pos_lo; k++) {
+        kt_lo = next_tile(kt_lo + 1);
+    }
 
     if (wg == 0) {
         regs_dec<DN_REGS_OTHER>();
@@ -431,7 +479,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             int  nk_ld = 0, nv_ld = 0;  // K and V tile loads issued (stage = load index % NS)
             int  i     = 0;
             bool ok    = true;
-            for (int kt = next_tile(0); kt < p.n_kt; kt = next_tile(kt + 1), i++) {
+            for (int kt = kt_lo; i < n_mine; kt = next_tile(kt + 1), i++) {
                 const int      st  = i % NS;
                 const uint32_t par = (uint32_t) ((i / NS - 1) & 1);
                 if (i >= NS && !mbar_wait_bounded(&bar[B_KEMPTY + st], par, deadline)) {
@@ -498,10 +546,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                 }
             };
             auto wait = [&](int b, int i) { return dn_wait_warp(&bar[b], (uint32_t) (i & 1), deadline); };
-            int n = 0;
-            for (int kt = next_tile(0); kt < p.n_kt; kt = next_tile(kt + 1)) {
-                n++;
-            }
+            const int n = n_mine;
             bool ok = wait(B_QREADY, 0) && wait(B_QREADY + 1, 0);
             tc_fence_after();
             if (ok && n > 0) {
@@ -563,6 +608,10 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             // every MMA issued must have completed before TMEM and shared memory are released
             umma_commit(&bar[B_MMADONE]);
             dn_wait_warp(&bar[B_MMADONE], 0, global_timer_ns() + p.timeout_ns);
+        }
+        if (half >= 0) {  // the two cluster barriers of the split epilogue
+            dn_cluster_sync();
+            dn_cluster_sync();
         }
     } else {
         regs_inc<DN_REGS_SOFTMAX>();
@@ -646,7 +695,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
         float       l     = 0.0f;
         bool        ok    = true;
         int         i     = 0;
-        for (int kt = next_tile(0); kt < p.n_kt; kt = next_tile(kt + 1), i++) {
+        for (int kt = kt_lo; i < n_mine; kt = next_tile(kt + 1), i++) {
             const int  nk    = p.n_kv - kt * DN_N;  // keys of this tile that exist (may exceed DN_N)
             const int  cls   = tile_class(p, plane, cq, kt);
             const bool fast  = plain && nk >= DN_N && cls != BLK_MIXED;
@@ -856,7 +905,102 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             tc_fence_after();
         }
         const float inv = (have_o && l > 0.0f) ? 1.0f / l : 0.0f;
-        if (p.tma_store) {
+        if (half >= 0) {
+            // split item: rank 1 publishes its raw O rows and (m, l) in its (now free) ring and Q
+            // space; rank 0 combines them with its own and stores the result
+            if (!dn_wait_warp(&bar[B_MMADONE], 0, deadline)) {
+                atomicExch(abort_f, 1);
+            }
+            float2 * mls   = reinterpret_cast<float2 *>(smem + L::OFF_Q);  // [tile][row] (m, l)
+            char *   stage = smem + L::OFF_K + t * (D / 32) * (DN_M * 128);
+            if (half == 1) {
+#pragma unroll
+                for (int c = 0; c < D / 32; c++) {
+                    uint32_t o[32];
+                    if (have_o) {
+                        tmem_ld32(o_col + (uint32_t) (c * 32), o);
+                        tmem_ld_wait_tie(o);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 32; e++) {
+                            o[e] = 0u;
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        *reinterpret_cast<uint4 *>(stage + c * (DN_M * 128) + sw128_off(r, j)) =
+                            make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+                    }
+                }
+                mls[t * DN_M + r] = have_o ? make_float2(m, l) : make_float2(-INFINITY, 0.0f);
+            }
+            dn_cluster_sync();
+            if (half == 0) {
+                const float2 mb = dn_ld_dsmem2(dn_mapa(&mls[t * DN_M + r], 1));
+                const float  ma = have_o ? m : -INFINITY, la = have_o ? l : 0.0f;
+                const float  M  = fmaxf(ma, mb.x);
+                const float  wa = ma == -INFINITY ? 0.0f : ex2(ma - M);
+                const float  wb = mb.x == -INFINITY ? 0.0f : ex2(mb.x - M);
+                const float  Ls = wa * la + wb * mb.y;
+                const float  iv = Ls > 0.0f ? 1.0f / Ls : 0.0f;
+                const float  ca = wa * iv, cb = wb * iv;
+#pragma unroll
+                for (int c = 0; c < D / 32; c++) {
+                    uint32_t o[32];
+                    if (have_o) {
+                        tmem_ld32(o_col + (uint32_t) (c * 32), o);
+                        tmem_ld_wait_tie(o);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 32; e++) {
+                            o[e] = 0u;
+                        }
+                    }
+                    char * tile = stage + c * (DN_M * 128);
+                    float4 ob[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        ob[j] = dn_ld_dsmem4(dn_mapa(tile + sw128_off(r, j), 1));
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        *reinterpret_cast<float4 *>(tile + sw128_off(r, j)) =
+                            make_float4(ca * __uint_as_float(o[4 * j]) + cb * ob[j].x,
+                                        ca * __uint_as_float(o[4 * j + 1]) + cb * ob[j].y,
+                                        ca * __uint_as_float(o[4 * j + 2]) + cb * ob[j].z,
+                                        ca * __uint_as_float(o[4 * j + 3]) + cb * ob[j].w);
+                    }
+                }
+                if (p.tma_store) {
+                    fence_proxy_async_smem();
+                    dn_named_barrier(1 + t, 128);
+                    if (quad == 0 && lane == 0) {
+                        const int q0t = cq * DN_ROWS + t * DN_M;
+#pragma unroll
+                        for (int c = 0; c < D / 32; c++) {
+                            dn_tma_store_4d(&tmo, stage + c * (DN_M * 128), c * 32, h, q0t, sq);
+                        }
+                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+                    }
+                } else if (valid) {
+                    float * out = reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 + (int64_t) qi * p.d_nb2 +
+                                                            (int64_t) sq * p.d_nb3);
+#pragma unroll
+                    for (int c = 0; c < D / 32; c++) {
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            const float4 v = *reinterpret_cast<const float4 *>(stage + c * (DN_M * 128) + sw128_off(r, j));
+                            out[c * 32 + 4 * j]     = v.x;
+                            out[c * 32 + 4 * j + 1] = v.y;
+                            out[c * 32 + 4 * j + 2] = v.z;
+                            out[c * 32 + 4 * j + 3] = v.w;
+                        }
+                    }
+                }
+            }
+            dn_cluster_sync();  // rank 1's shared memory stays alive until rank 0 has read it
+        } else if (p.tma_store) {
             // every MMA is done once MMADONE completes, so the K/V ring is free: each thread writes its
             // scaled O row into 128-byte-swizzled [128 rows][32 floats] tiles there, and one thread
             // of the warpgroup stores them with TMA (rows past n_q are clipped by the tensor map)
@@ -1086,9 +1230,50 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
     if (e != cudaSuccess) {
         return e;
     }
+    // work items and the split of the last wave: one CTA per SM at a time, so a final wave that
+    // would leave more than a quarter of the SMs idle is run as 2-CTA clusters that halve each
+    // item's K/V range (all items, when there are at most half as many items as SMs)
+    p.n_head          = (int) n_head;
+    p.n_seq           = (int) n_seq;
+    const int n_items = p.n_qt * p.n_head * p.n_seq;
+    int       sms     = 148;
+    int       dev     = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) {
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    int         n_split = 0;
+    const char * env    = std::getenv("MM3FA_DENSE_SPLIT");
+    // a half item has its own Q staging, epilogue and merge: only items of at least 16 K/V tiles
+    // gain from halving
+    if (!(env && env[0] == '0') && p.n_kt >= 16) {
+        if (2 * n_items <= sms) {
+            n_split = n_items;
+        } else {
+            const int tail = n_items % sms;
+            n_split        = (tail > 0 && 4 * tail < 3 * sms) ? tail : 0;
+        }
+        if (n_split > 0 && (n_items - n_split) % 2) {
+            n_split++;  // clusters tile the grid, so the whole items come in an even number
+        }
+    }
+    p.n_regular   = n_items - n_split;
     void * args[] = { &tmk, &tmv, &tmo, &p };
-    return cudaLaunchKernel(fn, dim3((unsigned) n_head, (unsigned) n_seq, (unsigned) p.n_qt), dim3(DN_THREADS), args,
-                            (size_t) smem, stream);
+    cudaLaunchConfig_t  cfg{};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim          = dim3((unsigned) (p.n_regular + 2 * n_split));
+    cfg.blockDim         = dim3(DN_THREADS);
+    cfg.dynamicSmemBytes = (size_t) smem;
+    cfg.stream           = stream;
+    cfg.numAttrs         = 0;
+    if (n_split > 0) {
+        attr[0].id               = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs                = attr;
+        cfg.numAttrs             = 1;
+    }
+    return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 }  // namespace mm3fa

@@ -21,10 +21,14 @@ pytestmark = pytest.mark.gpu
 F16, BF16, F32 = ggml.GGML_TYPE_F16, ggml.GGML_TYPE_BF16, ggml.GGML_TYPE_F32
 
 
-@pytest.fixture(params=["dense"])
+@pytest.fixture(params=["dense", "dense-nosplit"])
 def dense(request, monkeypatch):
-    """Forces the tensor-core prefill kernel wherever the operands allow it."""
+    """Forces the tensor-core prefill kernel wherever the operands allow it; small launches then
+    split every work item over a 2-CTA cluster (DSMEM merge), "dense-nosplit" runs each item in one
+    CTA (MM3FA_DENSE_SPLIT=0)."""
     monkeypatch.setenv("MM3FA_DENSE", "1")
+    if request.param == "dense-nosplit":
+        monkeypatch.setenv("MM3FA_DENSE_SPLIT", "0")
     return request.param
 
 
