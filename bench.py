@@ -275,7 +275,7 @@ def bench_dense(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, world:
                   "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": sustained, "unit": "TFLOP/s",
                                "frac": round(tf / sustained, 4), "peak_kind": "bf16_tflops_sustained",
                                "frac_of_burst": round(tf / burst, 4), "peak_source": src,
-                               "kernel": "fa_dense_kernel<128,f16>", "traffic": 134485248 + 34337536,
+                               "kernel": "fa_dense_kernel<128,f16>", "traffic": 134490000 + 37360000,
                                "flops_per_launch": fl}}
     del sets
     # ---- causal prefill: 2 x 1024 tokens, 32q / 8kv, cache view padded to 256

@@ -413,8 +413,9 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
     const int warp  = tid >> 5;
     const int lane  = tid & 31;
     const int wg    = warp >> 2;
-    // Work item = (256-row query block, head, sequence), query blocks last-first: under a causal
-    // mask the last blocks see the most keys, so the longest CTAs start in the first wave.  CTAs
+    // Work item = (256-row query block, head, sequence).  With a mask, query blocks run last-first:
+    // under a causal mask the last blocks see the most keys, so the longest CTAs start in the
+    // first wave.  CTAs
     // from n_regular on come in 2-CTA clusters that share one item, each taking half of its K/V
     // tiles (the last, partial wave of a launch, or all items of a small launch), and merge their
     // (O, m, l) through distributed shared memory.
@@ -424,10 +425,13 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
         item          = p.n_regular + rel / 2;
         half          = rel % 2;  // the CTA's rank in its cluster
     }
+    // without a mask every item has the same length: query blocks vary fastest, so the CTAs in
+    // flight share few (head, sequence) K/V slabs and those stay in L2
     const int hs    = p.n_head * p.n_seq;
-    const int cq    = p.n_qt - 1 - item / hs;  // 256-row query block
-    const int h     = (item % hs) % p.n_head;
-    const int sq    = (item % hs) / p.n_head;
+    const int cq    = p.mask ? p.n_qt - 1 - item / hs : item % p.n_qt;  // 256-row query block
+    const int hsi   = p.mask ? item % hs : item / p.n_qt;
+    const int h     = hsi % p.n_head;
+    const int sq    = hsi / p.n_head;
     const int g     = h / p.ratio;
     const int ks3   = sq / p.rk3;
     const int plane = (sq % p.m_ne3) * p.m_ne2 + (h % p.m_ne2);
