@@ -17,6 +17,18 @@
 //   O^T[D x 8r]           += V^T[D x 16] . P^T       (A via ldmatrix.trans)
 // Q is rounded to K's type (ggml's convention for F16/BF16 K); P is rounded to that type for
 // the PV product; accumulation, softmax and the running row sums are F32.
+//
+// Q8_0 K/V (Q8 = true; 34-byte blocks of an f16 scale d and 32 int8 values, rows of D/32
+// blocks packed back to back, so a row is not 16-byte aligned and no tensor map applies):
+//   * stages are 1-D bulk copies (cp.async.bulk, no multicast) of C whole rows, exact bytes;
+//   * Q is quantized to Q8_0 per unit exactly as ggml's reference quantizer (d = amax/127
+//     rounded to f16, q = round(x/d)), and S[key][row] = sum over blocks b of
+//     int32 dot(qk_b, qq_b) * (dk_b * dq_b) - the integer block dots come from
+//     mma.sync m16n8k32 s8 (one per block), exact like ggml's vec_dot_q8_0_q8_0;
+//   * V is dequantized exactly: int8 values become f16 integers (magic-number conversion:
+//     0x6400 | (v ^ 0x80) is the f16 value 1152 + v, minus 1152), and each key's block
+//     scale is folded into P (P * dv_b rounded to f16 once, like P itself on the F16 path),
+//     so O^T += V^T (P * dv)^T per 32-dim block with m16n8k16 f16 products and F32 sums.
 #include "fa_decode.cuh"
 
 #include <cuda.h>
@@ -24,6 +36,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -35,11 +48,12 @@ constexpr int MMA_THREADS   = 32 * (MMA_CONSUMERS + 1);  // + producer warp
 constexpr int MMA_C         = 16 * MMA_CONSUMERS;        // keys per stage (16 per consumer warp)
 constexpr int MMA_RMAX      = 32;                        // rows per unit in the partial layout
 
-template <int D, int NT, int NS>
+template <int D, int NT, int NS, bool Q8 = false>
 struct MmaSmem {
     static constexpr int HALVES     = D / 64;                 // 128-byte column blocks per row
     static constexpr int TILE       = MMA_C * 128;            // one TMA box: MMA_C keys x 128 B
-    static constexpr int MAT        = HALVES * TILE;          // K or V of one stage
+    static constexpr int RB         = D / QK8_0 * Q8_0_BLOCK; // bytes of one Q8_0 row
+    static constexpr int MAT        = Q8 ? MMA_C * RB : HALVES * TILE;  // K or V of one stage
     static constexpr int STAGE      = 2 * MAT;
     static constexpr int OFF_RED_O  = NS * STAGE;     // [row][D] merged O of the 4 warps
     static constexpr int OFF_RED_ML = OFF_RED_O + 8 * NT * D * 4;  // [warp][row][2] (m, l)
@@ -75,6 +89,41 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t & r0, uint32_t
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(addr));
+}
+
+// D = A.B + C on 16x32 int8 A (row) and 32x8 int8 B (col), int32 accumulators.
+__device__ __forceinline__ void mma_s8_16832(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// 4 bytes of shared memory at p, which lies MOD4 bytes past a 4-byte boundary (0 or 2).
+template <int MOD4>
+__device__ __forceinline__ uint32_t lds_word(const char * p) {
+    if constexpr (MOD4 == 0) {
+        return *reinterpret_cast<const uint32_t *>(p);
+    } else {
+        const uint32_t * w = reinterpret_cast<const uint32_t *>(p - 2);
+        return __funnelshift_r(w[0], w[1], 16);
+    }
+}
+
+__device__ __forceinline__ float lds_half(const char * p) {
+    return __half2float(*reinterpret_cast<const __half *>(p));
+}
+
+// Two int8 values of one V dim for two keys, from a byte-interleaved word (x0 y0 x1 y1, each
+// biased by 128 with ^0x80): SEL 0x4140 takes (x0, y0), 0x4342 takes (x1, y1).  Placing a
+// byte u under the exponent bits 0x64 gives the f16 value 1024 + u, so subtracting 1152
+// leaves u - 128, the signed value, exactly.
+template <uint32_t SEL>
+__device__ __forceinline__ uint32_t i8x2_to_h2(uint32_t il) {
+    uint32_t h = __byte_perm(il, 0x64646464u, SEL), r;
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64806480u));
+    return r;
 }
 
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
@@ -193,14 +242,18 @@ __device__ __forceinline__ uint32_t swz(int j, int c) {
 //                  slice [r*W, (r+1)*W) of the unit, and the CTAs merge their (m, l, O) over
 //                  distributed shared memory behind a cluster barrier - no global partials,
 //                  fences or atomics; the workspace only carries the status word.
-template <int D, bool BF16, int NT, bool CLUSTER, int NS>
+template <int D, bool BF16, int NT, bool CLUSTER, int NS, bool Q8>
 __global__ void __launch_bounds__(MMA_THREADS, 2)
     fa_decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                          const DecodeParams p) {
-    using L          = MmaSmem<D, NT, NS>;
-    constexpr int KS = D / 16;  // k-steps of QK, m-tiles of PV
+    using L            = MmaSmem<D, NT, NS, Q8>;
+    constexpr int KS   = D / 16;     // k-steps of QK, m-tiles of PV
+    constexpr int NBLK = D / QK8_0;  // Q8_0 blocks per row (Q8)
+    static_assert(!(Q8 && BF16), "Q8_0 V is multiplied in f16");
     extern __shared__ __align__(16) char smem_raw[];
-    char * smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
+    // 1024-byte aligned base, derived from smem_raw by pointer arithmetic (not through an
+    // integer) so that the compiler keeps plain accesses in the shared address space
+    char * smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
 
     float *    redO  = reinterpret_cast<float *>(smem + L::OFF_RED_O);
     float *    redML = reinterpret_cast<float *>(smem + L::OFF_RED_ML);
@@ -228,8 +281,10 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
         }
     }
     if (tid == 32 * MMA_CONSUMERS) {  // the producer thread: start the descriptor fetches first
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
+        if (!Q8) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
+        }
         for (int s = 0; s < NS; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], MMA_CONSUMERS);
@@ -268,11 +323,22 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                 const int ks3 = sq / p.rk3;
                 char *        dk  = smem + slot * L::STAGE;
                 char *        dv  = dk + L::MAT;
-                mbar_arrive_expect_tx(&full[slot], (uint32_t) L::STAGE);
+                if constexpr (Q8) {
+                    // n whole rows of K and of V; j0 * RB and n * RB are multiples of 16 (the
+                    // host only picks this kernel for packed rows and 16-byte aligned slabs)
+                    const uint32_t bytes = (uint32_t) (n * L::RB);
+                    const char *   sk = p.k + (int64_t) g * p.k_nb2 + (int64_t) ks3 * p.k_nb3 + (int64_t) j0 * L::RB;
+                    const char *   sv = p.v + (int64_t) g * p.v_nb2 + (int64_t) ks3 * p.v_nb3 + (int64_t) j0 * L::RB;
+                    mbar_arrive_expect_tx(&full[slot], 2 * bytes);
+                    bulk_copy_g2s(dk, sk, bytes, &full[slot]);
+                    bulk_copy_g2s(dv, sv, bytes, &full[slot]);
+                } else {
+                    mbar_arrive_expect_tx(&full[slot], (uint32_t) L::STAGE);
 #pragma unroll
-                for (int h = 0; h < L::HALVES; h++) {
-                    tma_load_4d(dk + h * L::TILE, &tmk, h * 64, j0, g, ks3, &full[slot]);
-                    tma_load_4d(dv + h * L::TILE, &tmv, h * 64, j0, g, ks3, &full[slot]);
+                    for (int h = 0; h < L::HALVES; h++) {
+                        tma_load_4d(dk + h * L::TILE, &tmk, h * 64, j0, g, ks3, &full[slot]);
+                        tma_load_4d(dv + h * L::TILE, &tmv, h * 64, j0, g, ks3, &full[slot]);
+                    }
                 }
                 s++;
             }
@@ -295,8 +361,16 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
     const int g4 = lane >> 2;  // fragment row group
     const int q4 = lane & 3;   // fragment column pair
 
-    uint32_t qb[NT][KS][2];   // Q^T B fragments
-    float    acc[KS][NT][4];  // O^T fragments: (dim = 16*m + g4 (+8), row = 8*nt + 2*q4 (+1))
+    uint32_t qb[NT][Q8 ? 1 : KS][2];   // Q^T B fragments
+    uint32_t q8b[NT][Q8 ? NBLK : 1][2];  // Q8: int8 Q^T B fragments per block (dims 4*q4.., 16+4*q4..)
+    float    dq[NT][Q8 ? NBLK : 1][2];   // Q8: Q block scales of rows 8*nt + 2*q4 (+1)
+    // O^T fragments: (dim = acc_dim(m, 0|1), row = 8*nt + 2*q4 (+1)); F16/BF16 tile m holds dims
+    // 16*m + g4 (+8), Q8_0 tile m holds dims 32*(m/2) + 4*g4 + 2*(m%2) (+1), so that one thread's
+    // V bytes of a block are 4 adjacent dims and every tile lies inside one 32-dim block
+    float    acc[KS][NT][4];
+    auto     acc_dim = [&](int m, int hi) -> int {
+        return Q8 ? 32 * (m >> 1) + 4 * g4 + 2 * (m & 1) + hi : 16 * m + g4 + 8 * hi;
+    };
     float    m_run[NT][2], l_run[NT][2];
     float    slope[NT][2];
     int64_t  moff[NT][2];
@@ -355,18 +429,59 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
             const int  hb = g * p.ratio + rf / p.n_q;
             const int  ib = rf % p.n_q;
             const char * qrow = p.q + (int64_t) ib * p.q_nb1 + (int64_t) hb * p.q_nb2 + (int64_t) sq * p.q_nb3;
+            if constexpr (Q8) {
+                // the quad's 4 lanes hold the 32 values of one block of row rb: Q8_0-quantize them
+                // as ggml's reference quantizer does (amax over the block, d = amax/127, stored
+                // as f16, q = round(x / d) with the f32 reciprocal of d)
 #pragma unroll
-            for (int ks = 0; ks < KS; ks++) {
-                float x[4] = { 0.f, 0.f, 0.f, 0.f };
-                if (vb) {
-                    const int d0 = ks * 16 + 2 * q4;
-                    x[0]         = ld_q_elem(qrow, p.q_type, d0);
-                    x[1]         = ld_q_elem(qrow, p.q_type, d0 + 1);
-                    x[2]         = ld_q_elem(qrow, p.q_type, d0 + 8);
-                    x[3]         = ld_q_elem(qrow, p.q_type, d0 + 9);
+                for (int b = 0; b < NBLK; b++) {
+                    float x[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int d0 = b * QK8_0 + (i >> 2) * 16 + 4 * q4 + (i & 3);
+                        x[i]         = vb ? ld_q_elem(qrow, p.q_type, d0) : 0.0f;
+                    }
+                    float amax = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        amax = fmaxf(amax, fabsf(x[i]));
+                    }
+                    amax           = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                    amax           = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+                    const float d  = amax / 127.0f;
+                    const float id = d != 0.0f ? 1.0f / d : 0.0f;
+                    uint32_t    w[2];
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        uint32_t v = 0;
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const int qv = (int) roundf(x[h * 4 + i] * id);
+                            v |= ((uint32_t) qv & 0xffu) << (8 * i);
+                        }
+                        w[h] = v;
+                    }
+                    q8b[nt][b][0] = w[0];
+                    q8b[nt][b][1] = w[1];
+                    // C-fragment rows 8*nt + 2*q4 + e live on the quads g4 = 2*q4 + e
+                    const float dh = round_to_f16(d);
+                    dq[nt][b][0]   = __shfl_sync(0xffffffffu, dh, (2 * q4) << 2);
+                    dq[nt][b][1]   = __shfl_sync(0xffffffffu, dh, (2 * q4 + 1) << 2);
                 }
-                qb[nt][ks][0] = pack2<BF16>(x[0], x[1]);
-                qb[nt][ks][1] = pack2<BF16>(x[2], x[3]);
+            } else {
+#pragma unroll
+                for (int ks = 0; ks < KS; ks++) {
+                    float x[4] = { 0.f, 0.f, 0.f, 0.f };
+                    if (vb) {
+                        const int d0 = ks * 16 + 2 * q4;
+                        x[0]         = ld_q_elem(qrow, p.q_type, d0);
+                        x[1]         = ld_q_elem(qrow, p.q_type, d0 + 1);
+                        x[2]         = ld_q_elem(qrow, p.q_type, d0 + 8);
+                        x[3]         = ld_q_elem(qrow, p.q_type, d0 + 9);
+                    }
+                    qb[nt][ks][0] = pack2<BF16>(x[0], x[1]);
+                    qb[nt][ks][1] = pack2<BF16>(x[2], x[3]);
+                }
             }
             // softmax state rows: 8*nt + 2*q4 + {0,1}
 #pragma unroll
@@ -419,12 +534,12 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
 #pragma unroll
                 for (int m = 0; m < KS; m++) {
                     const int r  = nt * 8 + 2 * q4;
-                    const int d  = m * 16 + g4;
+                    const int d  = acc_dim(m, 0), d1 = acc_dim(m, 1);
                     float *   ow = o4 + (size_t) warp * 8 * NT * D;
-                    ow[r * D + d]           = acc[m][nt][0];
-                    ow[(r + 1) * D + d]     = acc[m][nt][1];
-                    ow[r * D + d + 8]       = acc[m][nt][2];
-                    ow[(r + 1) * D + d + 8] = acc[m][nt][3];
+                    ow[r * D + d]        = acc[m][nt][0];
+                    ow[(r + 1) * D + d]  = acc[m][nt][1];
+                    ow[r * D + d1]       = acc[m][nt][2];
+                    ow[(r + 1) * D + d1] = acc[m][nt][3];
                 }
             }
             named_barrier_consumers();
@@ -495,11 +610,11 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
 #pragma unroll
                     for (int m = 0; m < KS; m++) {
                         const int r   = nt * 8 + 2 * q4;
-                        const int d   = m * 16 + g4;
+                        const int d   = acc_dim(m, 0), d1 = acc_dim(m, 1);
                         float *   o00 = &redO[r * D + d];
                         float *   o10 = &redO[(r + 1) * D + d];
-                        float *   o01 = &redO[r * D + d + 8];
-                        float *   o11 = &redO[(r + 1) * D + d + 8];
+                        float *   o01 = &redO[r * D + d1];
+                        float *   o11 = &redO[(r + 1) * D + d1];
                         const float v00 = scl[nt][0] * acc[m][nt][0], v10 = scl[nt][1] * acc[m][nt][1];
                         const float v01 = scl[nt][0] * acc[m][nt][2], v11 = scl[nt][1] * acc[m][nt][3];
                         *o00 = w == 0 ? v00 : *o00 + v00;
@@ -643,7 +758,40 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                     sc[nt][e] = 0.0f;
                 }
             }
-            {
+            if constexpr (Q8) {
+                // per block: int8 A fragments of key rows kb + g4 and kb + g4 + 8 (bytes
+                // 4*q4.. and 16 + 4*q4.. of the block's values; blocks at even indices start
+                // 2 bytes past a word boundary), the exact int32 dot, then the two f16 scales
+                const char * r0 = smem + slot * L::STAGE + (kb + g4) * L::RB;
+                const char * r1 = r0 + 8 * L::RB;
+#pragma unroll
+                for (int b = 0; b < NBLK; b++) {
+                    const int o = b * Q8_0_BLOCK + 2 + 4 * q4;
+                    uint32_t  a0, a1, a2, a3;
+                    if (b & 1) {
+                        a0 = lds_word<0>(r0 + o);
+                        a1 = lds_word<0>(r1 + o);
+                        a2 = lds_word<0>(r0 + o + 16);
+                        a3 = lds_word<0>(r1 + o + 16);
+                    } else {
+                        a0 = lds_word<2>(r0 + o);
+                        a1 = lds_word<2>(r1 + o);
+                        a2 = lds_word<2>(r0 + o + 16);
+                        a3 = lds_word<2>(r1 + o + 16);
+                    }
+                    const float dk0 = lds_half(r0 + b * Q8_0_BLOCK);
+                    const float dk1 = lds_half(r1 + b * Q8_0_BLOCK);
+#pragma unroll
+                    for (int nt = 0; nt < NT; nt++) {
+                        int c[4] = { 0, 0, 0, 0 };
+                        mma_s8_16832(c, a0, a1, a2, a3, q8b[nt][b][0], q8b[nt][b][1]);
+                        sc[nt][0] += (float) c[0] * (dk0 * dq[nt][b][0]);
+                        sc[nt][1] += (float) c[1] * (dk0 * dq[nt][b][1]);
+                        sc[nt][2] += (float) c[2] * (dk1 * dq[nt][b][0]);
+                        sc[nt][3] += (float) c[3] * (dk1 * dq[nt][b][1]);
+                    }
+                }
+            } else {
                 // all K fragments first (one shared-memory latency), then two independent
                 // accumulation chains over the even and odd k-steps
                 const int krow = kb + (lane & 7) + ((lane >> 3) & 1) * 8;  // A rows supplied by this lane
@@ -680,6 +828,18 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
             }
             // ---- online softmax (per warp), P^T -> P fragments
             uint32_t pb[NT][2];
+            uint32_t pb8[NT][Q8 ? NBLK : 1][2];  // Q8: P scaled by each key's V block scale
+            float    dv0[Q8 ? NBLK : 1], dv1[Q8 ? NBLK : 1];
+            if constexpr (Q8) {
+                // V scales of keys kb + g4 and kb + g4 + 8; zero past the stage's keys, where
+                // the ring holds stale bytes (P is zero there, and 0 * NaN must not occur)
+                const char * r0 = smem + slot * L::STAGE + L::MAT + (kb + g4) * L::RB;
+#pragma unroll
+                for (int b = 0; b < NBLK; b++) {
+                    dv0[b] = kb + g4 < n ? lds_half(r0 + b * Q8_0_BLOCK) : 0.0f;
+                    dv1[b] = kb + g4 + 8 < n ? lds_half(r0 + 8 * L::RB + b * Q8_0_BLOCK) : 0.0f;
+                }
+            }
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
                 float x[4];
@@ -720,11 +880,54 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                     acc[m][nt][2] *= al0;
                     acc[m][nt][3] *= al1;
                 }
-                pb[nt][0] = movmatrix_t(pack2<BF16>(p0, p1));  // keys 0-7 of the warp's 16
-                pb[nt][1] = movmatrix_t(pack2<BF16>(p2, p3));  // keys 8-15
+                if constexpr (Q8) {
+#pragma unroll
+                    for (int b = 0; b < NBLK; b++) {
+                        pb8[nt][b][0] = movmatrix_t(pack2<false>(p0 * dv0[b], p1 * dv0[b]));
+                        pb8[nt][b][1] = movmatrix_t(pack2<false>(p2 * dv1[b], p3 * dv1[b]));
+                    }
+                } else {
+                    pb[nt][0] = movmatrix_t(pack2<BF16>(p0, p1));  // keys 0-7 of the warp's 16
+                    pb[nt][1] = movmatrix_t(pack2<BF16>(p2, p3));  // keys 8-15
+                }
             }
             // ---- O^T += V^T P^T over this warp's 16 keys
-            {
+            if constexpr (Q8) {
+                // per block: 4 adjacent dims 32*b + 4*g4.. of the B-fragment keys kb + 2*q4 +
+                // {0, 1, 8, 9}, byte-interleaved per key pair and widened to f16 (exact)
+                const char * v0 = smem + slot * L::STAGE + L::MAT + (kb + 2 * q4) * L::RB;
+#pragma unroll
+                for (int b = 0; b < NBLK; b++) {
+                    const int o = b * Q8_0_BLOCK + 2 + 4 * g4;
+                    uint32_t  w0, w1, w8, w9;
+                    if (b & 1) {
+                        w0 = lds_word<0>(v0 + o);
+                        w1 = lds_word<0>(v0 + L::RB + o);
+                        w8 = lds_word<0>(v0 + 8 * L::RB + o);
+                        w9 = lds_word<0>(v0 + 9 * L::RB + o);
+                    } else {
+                        w0 = lds_word<2>(v0 + o);
+                        w1 = lds_word<2>(v0 + L::RB + o);
+                        w8 = lds_word<2>(v0 + 8 * L::RB + o);
+                        w9 = lds_word<2>(v0 + 9 * L::RB + o);
+                    }
+                    w0 ^= 0x80808080u;
+                    w1 ^= 0x80808080u;
+                    w8 ^= 0x80808080u;
+                    w9 ^= 0x80808080u;
+                    const uint32_t lo01 = __byte_perm(w0, w1, 0x5140), hi01 = __byte_perm(w0, w1, 0x7362);
+                    const uint32_t lo89 = __byte_perm(w8, w9, 0x5140), hi89 = __byte_perm(w8, w9, 0x7362);
+                    const uint32_t e0 = i8x2_to_h2<0x4140>(lo01), e1 = i8x2_to_h2<0x4342>(lo01);
+                    const uint32_t e2 = i8x2_to_h2<0x4140>(lo89), e3 = i8x2_to_h2<0x4342>(lo89);
+                    const uint32_t f0 = i8x2_to_h2<0x4140>(hi01), f1 = i8x2_to_h2<0x4342>(hi01);
+                    const uint32_t f2 = i8x2_to_h2<0x4140>(hi89), f3 = i8x2_to_h2<0x4342>(hi89);
+#pragma unroll
+                    for (int nt = 0; nt < NT; nt++) {
+                        mma16816<false>(acc[2 * b][nt], e0, e1, e2, e3, pb8[nt][b][0], pb8[nt][b][1]);
+                        mma16816<false>(acc[2 * b + 1][nt], f0, f1, f2, f3, pb8[nt][b][0], pb8[nt][b][1]);
+                    }
+                }
+            } else {
                 const int vkey = kb + (lane & 7) + ((lane >> 4) & 1) * 8;  // stored V row for ldmatrix.trans
                 uint32_t  vf[KS][4];
 #pragma unroll
@@ -884,40 +1087,54 @@ bool tensor_maps_available() {
 
 namespace {
 
-template <int D, bool BF16, int NT, bool CL>
+// Q8_0 ring depth: 6 stages of 64 keys (17 KiB each at D=128), about the bytes in flight of
+// the F16 kernel's 3 stages.
+constexpr int Q8_NSTAGE = 6;
+
+template <int D, bool BF16, int NT, bool CL, bool Q8>
 void * mma_kernel(int ns, int & smem) {
+    if constexpr (Q8) {
+        smem = MmaSmem<D, NT, Q8_NSTAGE, true>::TOTAL;
+        return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, false, NT, CL, Q8_NSTAGE, true>);
+    }
     if (ns == 2) {
         smem = MmaSmem<D, NT, 2>::TOTAL;
-        return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT, CL, 2>);
+        return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT, CL, 2, false>);
     }
     smem = MmaSmem<D, NT, 3>::TOTAL;
-    return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT, CL, 3>);
+    return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT, CL, 3, false>);
 }
 
-// Ring depth: 3 stages of 64 keys per CTA (two CTAs, 192 KiB of K/V in flight per SM at
-// D=128) or 2; MM3FA_DECODE_NSTAGE=2 overrides.
+// F16/BF16 ring depth: 2 stages of 64 keys per CTA (three CTAs, 192 KiB of K/V in flight per
+// SM at D=128; measured 3% faster than 3 stages with two CTAs per SM) or 3 with
+// MM3FA_DECODE_NSTAGE=3.
 int mma_nstage() {
     static const int ns = [] {
         const char * e = std::getenv("MM3FA_DECODE_NSTAGE");
-        return (e && std::atoi(e) == 2) ? 2 : 3;
+        return (e && std::atoi(e) == 3) ? 3 : 2;
     }();
     return ns;
 }
 
-void * select_mma_kernel(int D, bool bf16, int nt, bool cluster, int & smem) {
-    const int ns = mma_nstage();
-#define MM3FA_SELM(DD, BB, NN)                                                                          \
-    if (D == DD && bf16 == BB && nt == NN) {                                                            \
-        return cluster ? mma_kernel<DD, BB, NN, true>(ns, smem) : mma_kernel<DD, BB, NN, false>(ns, smem); \
+void * select_mma_kernel(int D, int kvt, int nt, bool cluster, int & smem) {
+    const int  ns   = mma_nstage();
+    const bool bf16 = kvt == KV_BF16, q8 = kvt == KV_Q8_0;
+#define MM3FA_SELM(DD, BB, QQ, NN)                                                                 \
+    if (D == DD && bf16 == BB && q8 == QQ && nt == NN) {                                           \
+        return cluster ? mma_kernel<DD, BB, NN, true, QQ>(ns, smem) : mma_kernel<DD, BB, NN, false, QQ>(ns, smem); \
     }
-    MM3FA_SELM(128, false, 1)
-    MM3FA_SELM(128, false, 2)
-    MM3FA_SELM(128, true, 1)
-    MM3FA_SELM(128, true, 2)
-    MM3FA_SELM(64, false, 1)
-    MM3FA_SELM(64, false, 2)
-    MM3FA_SELM(64, true, 1)
-    MM3FA_SELM(64, true, 2)
+    MM3FA_SELM(128, false, false, 1)
+    MM3FA_SELM(128, false, false, 2)
+    MM3FA_SELM(128, true, false, 1)
+    MM3FA_SELM(128, true, false, 2)
+    MM3FA_SELM(128, false, true, 1)
+    MM3FA_SELM(128, false, true, 2)
+    MM3FA_SELM(64, false, false, 1)
+    MM3FA_SELM(64, false, false, 2)
+    MM3FA_SELM(64, true, false, 1)
+    MM3FA_SELM(64, true, false, 2)
+    MM3FA_SELM(64, false, true, 1)
+    MM3FA_SELM(64, false, true, 2)
 #undef MM3FA_SELM
     return nullptr;
 }
@@ -952,13 +1169,16 @@ int max_active_clusters(void * fn, int cs, int smem) {
 }  // namespace
 
 bool decode_mma_eligible(int D, int kvt, int rows_per_pair) {
+    if (kvt == KV_Q8_0) {
+        return (D == 64 || D == 128) && rows_per_pair <= 16;
+    }
     return (kvt == KV_F16 || kvt == KV_BF16) && (D == 64 || D == 128) && rows_per_pair <= 16 &&
            tensor_map_encoder() != nullptr;
 }
 
 int decode_mma_ctas_per_sm(int D, int kvt, int rows_per_pair) {
     int    smem = 0;
-    void * fn   = select_mma_kernel(D, kvt == KV_BF16, rows_per_pair <= 8 ? 1 : 2, false, smem);
+    void * fn   = select_mma_kernel(D, kvt, rows_per_pair <= 8 ? 1 : 2, false, smem);
     if (!fn) {
         return 0;
     }
@@ -991,7 +1211,7 @@ int decode_mma_cluster_size(int D, int kvt, int rows_per_pair, int64_t n_units, 
         return it->second;
     }
     int    smem = 0;
-    void * fn   = select_mma_kernel(D, kvt == KV_BF16, nt, true, smem);
+    void * fn   = select_mma_kernel(D, kvt, nt, true, smem);
     if (!fn) {
         return 0;
     }
@@ -1012,13 +1232,25 @@ cudaError_t launch_decode_mma(DecodeParams p, const DecodeGeometry & g, int D, i
     const bool bf16 = kvt == KV_BF16;
     const int  nt   = p.rows_per_pair <= 8 ? 1 : 2;
     int        smem = 0;
-    void *     fn   = select_mma_kernel(D, bf16, nt, cluster > 0, smem);
+    void *     fn   = select_mma_kernel(D, kvt, nt, cluster > 0, smem);
     if (!fn) {
         return cudaErrorInvalidValue;
     }
     alignas(64) CUtensorMap tmk, tmv;
-    if (!encode_kv_tensor_map(&tmk, p.k, bf16, D, p.n_kv, n_head_kv, n_seq_k, p.k_nb1, p.k_nb2, p.k_nb3, MMA_C) ||
-        !encode_kv_tensor_map(&tmv, p.v, bf16, D, p.n_kv, n_head_kv, n_seq_k, p.v_nb1, p.v_nb2, p.v_nb3, MMA_C)) {
+    if (kvt == KV_Q8_0) {
+        // bulk copies of packed rows: every slab start and chunk must be 16-byte aligned
+        const int64_t rb = (int64_t) D / QK8_0 * Q8_0_BLOCK;
+        if (p.k_nb1 != rb || p.v_nb1 != rb || (rb * (p.n_kv % 16)) % 16 != 0 ||
+            (reinterpret_cast<uintptr_t>(p.k) | reinterpret_cast<uintptr_t>(p.v)) % 16 != 0 ||
+            (n_head_kv > 1 && (p.k_nb2 % 16 || p.v_nb2 % 16)) || (n_seq_k > 1 && (p.k_nb3 % 16 || p.v_nb3 % 16))) {
+            return cudaErrorInvalidValue;
+        }
+        std::memset(&tmk, 0, sizeof(tmk));  // unused by the Q8_0 instances
+        std::memset(&tmv, 0, sizeof(tmv));
+    } else if (!encode_kv_tensor_map(&tmk, p.k, bf16, D, p.n_kv, n_head_kv, n_seq_k, p.k_nb1, p.k_nb2, p.k_nb3,
+                                     MMA_C) ||
+               !encode_kv_tensor_map(&tmv, p.v, bf16, D, p.n_kv, n_head_kv, n_seq_k, p.v_nb1, p.v_nb2, p.v_nb3,
+                                     MMA_C)) {
         return cudaErrorInvalidValue;
     }
     char *       ws   = static_cast<char *>(workspace);

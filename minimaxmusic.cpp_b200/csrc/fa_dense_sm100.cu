@@ -404,7 +404,9 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
     constexpr int NS = L::NS;
     constexpr int KS = D / 16;  // k-steps of QK
     extern __shared__ __align__(16) char smem_raw[];
-    char * smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
+    // 1024-byte aligned base, derived from smem_raw by pointer arithmetic (not through an
+    // integer) so that the compiler keeps plain accesses in the shared address space
+    char * smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     uint64_t * bar       = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(smem + L::OFF_MISC);
     int *      abort_f   = reinterpret_cast<int *>(smem + L::OFF_MISC + 4);

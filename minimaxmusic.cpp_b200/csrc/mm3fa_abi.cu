@@ -285,7 +285,9 @@ int check_op(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor 
 Variant variant_for(const OpShape & s) {
     const int  pref = decode_preference();
     const int  rows = s.ratio * (int) s.n_q;
-    const bool mma  = pref != 1 && s.tma && decode_mma_eligible((int) s.D, s.kvt, rows);
+    // F16/BF16 stages are TMA tensor tiles; Q8_0 rows (not 16-byte multiples) are bulk copies
+    const bool tiles = s.kvt == MM3FA_TYPE_Q8_0 ? s.bulk : s.tma;
+    const bool mma   = pref != 1 && tiles && decode_mma_eligible((int) s.D, s.kvt, rows);
     if (mma) {
         return rows <= 8 ? V_MMA_8 : V_MMA_16;
     }

@@ -59,7 +59,7 @@ def test_headline_decode_kv8192(kernel, cuda_device):
     check(workloads.decode_case(n_seq=2, n_kv=8192, max_seq=10240, seed=2), cuda_device)
 
 
-def test_config3_q8_0_kv8192(cuda_device):
+def test_config3_q8_0_kv8192(kernel, cuda_device):
     c = workloads.decode_case(n_seq=2, n_kv=8192, kv_type=Q8, seed=3)
     check(c, cuda_device, exact_abs=5e-3, exact_cos=0.9999)
 
@@ -85,8 +85,22 @@ def test_odd_kv_lengths(kernel, cuda_device, n_kv):
 
 
 @pytest.mark.parametrize("n_kv", [2, 62, 258])
-def test_q8_0_small_and_odd(cuda_device, n_kv):
+def test_q8_0_small_and_odd(kernel, cuda_device, n_kv):
     check(workloads.decode_case(n_seq=2, n_kv=n_kv, kv_type=Q8, seed=200 + n_kv), cuda_device, 5e-3, 0.9999)
+
+
+@pytest.mark.parametrize("n_q", [2, 4])
+def test_q8_0_multirow_ragged(kernel, cuda_device, n_q):
+    """Q8_0 cache with 8 and 16 GQA rows per unit and a -inf padded tail per sequence."""
+    c = workloads.decode_case(n_seq=2, n_kv=1536, n_q=n_q, kv_len=[1000, 1536], kv_type=Q8, seed=300 + n_q)
+    check(c, cuda_device, 5e-3, 0.9999)
+
+
+def test_q8_0_softcap_alibi_kv_view(kernel, cuda_device):
+    """Q8_0 view into a longer cache (nb2 = max_seq rows), softcap and ALiBi on."""
+    c = workloads.decode_case(n_seq=2, n_kv=1280, max_seq=2048, n_head=8, n_head_kv=2, kv_type=Q8, seed=31)
+    c.softcap, c.max_bias = 30.0, 4.0
+    check(c, cuda_device, 5e-3, 0.9999)
 
 
 def test_q8_0_odd_length_takes_element_copy_path(cuda_device):
