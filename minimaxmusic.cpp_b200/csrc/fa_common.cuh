@@ -148,6 +148,7 @@ struct DecodeParams {
     int          max_slots;      // partial slots per unit
     int          cluster;        // CTAs per thread-block cluster (tensor-core cluster mode)
     int          dst_vec;        // dst rows start 16-byte aligned: 16-byte stores
+    int          mask_tma;       // mask rows staged by TMA with K/V (cluster mode)
     // workspace
     uint32_t *   status;
     uint32_t *   counters;

@@ -45,7 +45,7 @@ namespace mm3fa {
 
 constexpr int MMA_CONSUMERS = 4;                         // consumer warps
 constexpr int MMA_THREADS   = 32 * (MMA_CONSUMERS + 1);  // + producer warp
-constexpr int MMA_C         = 16 * MMA_CONSUMERS;        // keys per stage (16 per consumer warp)
+constexpr int MMA_C         = 16 * MMA_CONSUMERS;        // F16/BF16 keys per stage (16 per consumer warp)
 constexpr int MMA_RMAX      = 32;                        // rows per unit in the partial layout
 
 template <int D, int NT, int NS, bool Q8 = false>
@@ -53,13 +53,22 @@ struct MmaSmem {
     static constexpr int HALVES     = D / 64;                 // 128-byte column blocks per row
     static constexpr int TILE       = MMA_C * 128;            // one TMA box: MMA_C keys x 128 B
     static constexpr int RB         = D / QK8_0 * Q8_0_BLOCK; // bytes of one Q8_0 row
-    static constexpr int MAT        = Q8 ? MMA_C * RB : HALVES * TILE;  // K or V of one stage
-    static constexpr int STAGE      = 2 * MAT;
-    static constexpr int OFF_RED_O  = NS * STAGE;     // [row][D] merged O of the 4 warps
-    static constexpr int OFF_RED_ML = OFF_RED_O + 8 * NT * D * 4;  // [warp][row][2] (m, l)
-    static constexpr int OFF_CML    = OFF_RED_ML + MMA_CONSUMERS * 8 * NT * 2 * 4;  // [row][2] CTA (m, l)
-    static constexpr int OFF_BAR    = OFF_CML + 8 * NT * 2 * 4;
-    static constexpr int OFF_FLAG   = OFF_BAR + 2 * NS * 8;
+    // keys per stage: Q8_0 with 8 rows per unit takes 32 per warp (two 16-key sub-tiles)
+    static constexpr int CK         = (Q8 && NT == 1) ? 2 * MMA_C : MMA_C;
+    static constexpr int MAT        = Q8 ? CK * RB : HALVES * TILE;  // K or V of one stage
+    static constexpr int MASKB      = CK * 2;                 // the stage's mask row (TMA mask)
+    // K, V, mask row; F16/BF16 stages keep the 1024-byte alignment of the 128-byte swizzle
+    static constexpr int SALIGN     = Q8 ? 128 : 1024;
+    static constexpr int STAGE      = (2 * MAT + MASKB + SALIGN - 1) / SALIGN * SALIGN;
+    // [row][D] merged O of the 4 warps (stream-K); in cluster mode the receive buffer of this
+    // CTA's share of the cluster merge: [source rank][item] float4, items <= rows * D/4 / CS + 1
+    static constexpr int RED_O_B    = 8 * NT * D * 4 > (8 * NT * D / 4 + 16) * 16 ? 8 * NT * D * 4
+                                                                                 : (8 * NT * D / 4 + 16) * 16;
+    static constexpr int OFF_RED_O  = NS * STAGE;
+    static constexpr int OFF_RECV_ML = OFF_RED_O + RED_O_B;           // [source rank][row][2] (m, l)
+    static constexpr int OFF_RED_ML = OFF_RECV_ML + 16 * 8 * NT * 2 * 4;  // [warp][row][2] (m, l)
+    static constexpr int OFF_BAR    = OFF_RED_ML + MMA_CONSUMERS * 8 * NT * 2 * 4;
+    static constexpr int OFF_FLAG   = OFF_BAR + (2 * NS + 1) * 8;  // full[NS], empty[NS], pushed
     static constexpr int TOTAL      = OFF_FLAG + 16 + 1024;   // + alignment slack for the ring
 };
 
@@ -219,6 +228,53 @@ __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ void st_dsmem2(uint32_t addr, float2 v) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(v.x), "f"(v.y) : "memory");
+}
+
+// Split cluster barrier: every thread arrives once its CTA's mbarriers are initialised; a
+// thread that will touch another CTA's shared memory waits first.
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void st_dsmem4(uint32_t addr, float4 v) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+                 "f"(v.w)
+                 : "memory");
+}
+
+// Arrive on an mbarrier of another CTA of the cluster (addr from mapa), releasing at cluster
+// scope the writes this thread has made or observed (the CTA barrier before it).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+
+// Bounded wait on a local mbarrier phase whose arrivals come from other CTAs of the cluster.
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t * bar, uint32_t parity, uint64_t deadline_ns) {
+    uint32_t spins = 0;
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred q;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 q, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, q;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_addr(bar)), "r"(parity)
+            : "memory");
+        if (ok) {
+            return true;
+        }
+        if ((++spins & 255u) == 0 && global_timer_ns() > deadline_ns) {
+            return false;
+        }
+    }
+}
+
 // ---- programmatic dependent launch: the next kernel in the stream may launch (and run up to
 // its own griddepcontrol.wait) once every CTA here has signalled; wait() returns when the
 // previous kernel in the stream has completed and its memory writes are visible.
@@ -245,10 +301,13 @@ __device__ __forceinline__ uint32_t swz(int j, int c) {
 template <int D, bool BF16, int NT, bool CLUSTER, int NS, bool Q8>
 __global__ void __launch_bounds__(MMA_THREADS, 2)
     fa_decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                         const DecodeParams p) {
+                         const __grid_constant__ CUtensorMap tmm, const DecodeParams p) {
     using L            = MmaSmem<D, NT, NS, Q8>;
     constexpr int KS   = D / 16;     // k-steps of QK, m-tiles of PV
     constexpr int NBLK = D / QK8_0;  // Q8_0 blocks per row (Q8)
+    constexpr int SUB  = L::CK / MMA_C;  // 16-key sub-tiles per warp and stage
+    constexpr int KPW  = 16 * SUB;    // keys per warp and stage
+    constexpr int CK   = L::CK;       // keys per stage
     static_assert(!(Q8 && BF16), "Q8_0 V is multiplied in f16");
     extern __shared__ __align__(16) char smem_raw[];
     // 1024-byte aligned base, derived from smem_raw by pointer arithmetic (not through an
@@ -257,9 +316,9 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
 
     float *    redO  = reinterpret_cast<float *>(smem + L::OFF_RED_O);
     float *    redML = reinterpret_cast<float *>(smem + L::OFF_RED_ML);
-    float *    cml   = reinterpret_cast<float *>(smem + L::OFF_CML);
     uint64_t * full  = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
     uint64_t * empty = full + NS;
+    uint64_t * pushed = full + 2 * NS;  // cluster mode: this CTA's share of the partials has arrived
     int *      flag  = reinterpret_cast<int *>(smem + L::OFF_FLAG);  // [0] abort, [1] last-arriver
 
     const int tid  = threadIdx.x;
@@ -285,24 +344,31 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
         }
+        if (p.mask_tma) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmm)) : "memory");
+        }
         for (int s = 0; s < NS; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], MMA_CONSUMERS);
         }
+        mbar_init(pushed, CLUSTER ? (uint32_t) p.cluster : 1u);
         flag[0] = 0;
         flag[1] = 0;
         fence_mbar_init();
     }
     __syncthreads();
+    if (CLUSTER) {
+        cluster_arrive();  // waited for before the first remote store (cluster merge)
+    }
     pdl_wait();  // nothing global (inputs, dst, workspace) is touched before this point
     const uint64_t deadline = global_timer_ns() + p.timeout_ns;
 
     // ================================================================ producer warp
     if (warp == MMA_CONSUMERS) {
         if (lane == 0) {
-            StageIter it = CLUSTER ? StageIter((int64_t) (blockIdx.x / p.cluster), (int) (blockIdx.x % p.cluster) * MMA_C,
-                                          p.cluster * MMA_C, p.n_kv, MMA_C)
-                                : StageIter(g0, g1, p.n_kv, MMA_C);
+            StageIter it = CLUSTER ? StageIter((int64_t) (blockIdx.x / p.cluster), (int) (blockIdx.x % p.cluster) * CK,
+                                          p.cluster * CK, p.n_kv, CK)
+                                : StageIter(g0, g1, p.n_kv, CK);
             int        s = 0;
             bool       ok = true;
             while (it.has()) {
@@ -323,22 +389,29 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                 const int ks3 = sq / p.rk3;
                 char *        dk  = smem + slot * L::STAGE;
                 char *        dv  = dk + L::MAT;
+                // TMA mask (cluster mode, so j0 is a multiple of CK; one query row and a mask
+                // shared by all heads, so every row of the unit reads the same mask row): one box
+                // of CK keys, zero-filled past n_kv
+                const uint32_t mbytes = p.mask_tma ? (uint32_t) L::MASKB : 0u;
                 if constexpr (Q8) {
                     // n whole rows of K and of V; j0 * RB and n * RB are multiples of 16 (the
                     // host only picks this kernel for packed rows and 16-byte aligned slabs)
                     const uint32_t bytes = (uint32_t) (n * L::RB);
                     const char *   sk = p.k + (int64_t) g * p.k_nb2 + (int64_t) ks3 * p.k_nb3 + (int64_t) j0 * L::RB;
                     const char *   sv = p.v + (int64_t) g * p.v_nb2 + (int64_t) ks3 * p.v_nb3 + (int64_t) j0 * L::RB;
-                    mbar_arrive_expect_tx(&full[slot], 2 * bytes);
+                    mbar_arrive_expect_tx(&full[slot], 2 * bytes + mbytes);
                     bulk_copy_g2s(dk, sk, bytes, &full[slot]);
                     bulk_copy_g2s(dv, sv, bytes, &full[slot]);
                 } else {
-                    mbar_arrive_expect_tx(&full[slot], (uint32_t) L::STAGE);
+                    mbar_arrive_expect_tx(&full[slot], (uint32_t) (2 * L::MAT) + mbytes);
 #pragma unroll
                     for (int h = 0; h < L::HALVES; h++) {
                         tma_load_4d(dk + h * L::TILE, &tmk, h * 64, j0, g, ks3, &full[slot]);
                         tma_load_4d(dv + h * L::TILE, &tmv, h * 64, j0, g, ks3, &full[slot]);
                     }
+                }
+                if (p.mask_tma) {
+                    tma_load_4d(dk + 2 * L::MAT, &tmm, j0, 0, 0, sq % p.m_ne3, &full[slot]);
                 }
                 s++;
             }
@@ -382,29 +455,36 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
     int     u_rgrp = 0, u_g = 0, u_sq = 0;  // the current unit's row group, kv head, q sequence
     bool    aborted  = false;
 
-    float mk_cur[NT][2][2], mk_nxt[NT][2][2];  // mask values [nt][row 2*q4 + e][key g4 + 8*kh]
-    bool  mk_have = false;                      // mk_cur already holds the coming stage's values
+    // mask values [sub-tile][nt][row 2*q4 + e][key 16u + g4 + 8*kh]
+    float mk_cur[SUB][NT][2][2], mk_nxt[SUB][NT][2][2];
+    bool  mk_have = false;  // mk_cur already holds the coming stage's values
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-#pragma unroll
-        for (int e = 0; e < 2; e++) {
-            mk_cur[nt][e][0] = mk_cur[nt][e][1] = 0.0f;
-            mk_nxt[nt][e][0] = mk_nxt[nt][e][1] = 0.0f;
-        }
-    }
-    auto load_mask = [&](float (&mk)[NT][2][2], int j0_, int n_) {
-        const int kb_ = warp * 16;
+    for (int u = 0; u < SUB; u++) {
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
 #pragma unroll
             for (int e = 0; e < 2; e++) {
+                mk_cur[u][nt][e][0] = mk_cur[u][nt][e][1] = 0.0f;
+                mk_nxt[u][nt][e][0] = mk_nxt[u][nt][e][1] = 0.0f;
+            }
+        }
+    }
+    auto load_mask = [&](float (&mk)[SUB][NT][2][2], int j0_, int n_) {
+        const int kb_ = warp * KPW;
 #pragma unroll
-                for (int kh = 0; kh < 2; kh++) {
-                    const int j   = kb_ + g4 + 8 * kh;
-                    mk[nt][e][kh] = 0.0f;
-                    if (rvalid[nt][e] && j < n_) {
-                        mk[nt][e][kh] = __half2float(
-                            *reinterpret_cast<const __half *>(p.mask + moff[nt][e] + (int64_t) (j0_ + j) * 2));
+        for (int u = 0; u < SUB; u++) {
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+#pragma unroll
+                    for (int kh = 0; kh < 2; kh++) {
+                        const int j      = kb_ + 16 * u + g4 + 8 * kh;
+                        mk[u][nt][e][kh] = 0.0f;
+                        if (rvalid[nt][e] && j < n_) {
+                            mk[u][nt][e][kh] = __half2float(
+                                *reinterpret_cast<const __half *>(p.mask + moff[nt][e] + (int64_t) (j0_ + j) * 2));
+                        }
                     }
                 }
             }
@@ -543,7 +623,20 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                 }
             }
             named_barrier_consumers();
-            for (int it4 = tid; it4 < nrow * (D / 4); it4 += 32 * MMA_CONSUMERS) {
+            // Cluster merge by pushing (reduce-scatter over DSMEM): item (row, 4 dims) number it
+            // belongs to rank it % CS.  This CTA combines its 4 warps per item and stores the result
+            // into the owner's receive buffer, and its (m, l) per row into every rank's; then one
+            // thread per rank arrives on that rank's `pushed` barrier.  Each rank waits for the CS
+            // arrivals on its own barrier and merges its items from local memory, so no CTA ever
+            // reads another's memory and no cluster barrier follows.
+            const int      CS    = p.cluster;
+            const uint32_t rank  = cluster_ctarank();
+            const int      total = nrow * (D / 4);
+            const int      IPR   = (total + CS - 1) / CS;  // items per rank
+            float4 *       rcv_o  = reinterpret_cast<float4 *>(redO);  // [source][IPR]
+            float2 *       rcv_ml = reinterpret_cast<float2 *>(smem + L::OFF_RECV_ML);  // [source][8 NT]
+            cluster_wait();  // every CTA of the cluster has initialised its barriers
+            for (int it4 = tid; it4 < total; it4 += 32 * MMA_CONSUMERS) {
                 const int r = it4 / (D / 4), d = (it4 % (D / 4)) * 4;
                 float     mw[MMA_CONSUMERS], M = -INFINITY;
 #pragma unroll
@@ -563,13 +656,65 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                     O.w += wt * v.w;
                     Ls += wt * redML[(w * 8 * NT + r) * 2 + 1];
                 }
-                *reinterpret_cast<float4 *>(&redO[r * D + d]) = O;
+                const uint32_t owner = (uint32_t) (it4 % CS);
+                st_dsmem4(dsmem_addr(&rcv_o[(int) rank * IPR + it4 / CS], owner), O);
                 if (d == 0) {
-                    cml[r * 2]     = M;
-                    cml[r * 2 + 1] = Ls;
+                    for (int c = 0; c < CS; c++) {
+                        st_dsmem2(dsmem_addr(&rcv_ml[(int) rank * 8 * NT + r], (uint32_t) c), make_float2(M, Ls));
+                    }
                 }
             }
-            return;  // the cluster barrier that follows orders these writes before the peers read
+            asm volatile("fence.acq_rel.cluster;" ::: "memory");
+            named_barrier_consumers();
+            if (tid < CS) {
+                mbar_arrive_remote(dsmem_addr(pushed, (uint32_t) tid));
+            }
+            if (!mbar_wait_cluster_bounded(pushed, 0, global_timer_ns() + p.timeout_ns)) {
+                if (tid == 0) {
+                    atomicExch(&flag[0], 1);
+                }
+                return;
+            }
+            for (int li = tid; li < IPR; li += 32 * MMA_CONSUMERS) {
+                const int it4 = li * CS + (int) rank;
+                if (it4 >= total) {
+                    break;
+                }
+                const int r = it4 / (D / 4), d = (it4 % (D / 4)) * 4;
+                float     M = -INFINITY;
+                for (int c = 0; c < CS; c++) {
+                    M = fmaxf(M, rcv_ml[c * 8 * NT + r].x);
+                }
+                float4 O  = make_float4(0.f, 0.f, 0.f, 0.f);
+                float  Ls = 0.0f;
+                if (M != -INFINITY) {
+                    for (int c = 0; c < CS; c++) {
+                        const float2 ml = rcv_ml[c * 8 * NT + r];
+                        const float  w  = ml.x == -INFINITY ? 0.0f : exp2f(ml.x - M);
+                        const float4 v  = rcv_o[c * IPR + li];
+                        O.x += w * v.x;
+                        O.y += w * v.y;
+                        O.z += w * v.z;
+                        O.w += w * v.w;
+                        Ls += w * ml.y;
+                    }
+                }
+                const float inv = Ls > 0.0f ? 1.0f / Ls : 0.0f;
+                const int   rf  = u_rgrp * MMA_RMAX + r;
+                const int   h   = u_g * p.ratio + rf / p.n_q;
+                const int   i   = rf % p.n_q;
+                float *     out = reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 + (int64_t) i * p.d_nb2 +
+                                                        (int64_t) u_sq * p.d_nb3) + d;
+                if (p.dst_vec) {
+                    *reinterpret_cast<float4 *>(out) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+                } else {
+                    out[0] = O.x * inv;
+                    out[1] = O.y * inv;
+                    out[2] = O.z * inv;
+                    out[3] = O.w * inv;
+                }
+            }
+            return;
         } else {
         // each warp's (m, l) per row to shared memory, l summed over the 8 key lanes
 #pragma unroll
@@ -702,9 +847,9 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
         cur_unit = blockIdx.x / p.cluster;
         begin_unit(cur_unit);
     }
-    StageIter it = CLUSTER ? StageIter((int64_t) (blockIdx.x / p.cluster), (int) (blockIdx.x % p.cluster) * MMA_C,
-                                          p.cluster * MMA_C, p.n_kv, MMA_C)
-                                : StageIter(g0, g1, p.n_kv, MMA_C);
+    StageIter it = CLUSTER ? StageIter((int64_t) (blockIdx.x / p.cluster), (int) (blockIdx.x % p.cluster) * CK,
+                                          p.cluster * CK, p.n_kv, CK)
+                                : StageIter(g0, g1, p.n_kv, CK);
     int        s = 0;
     while (it.has()) {
         int64_t unit;
@@ -721,10 +866,10 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
         seg_j1 = j0 + n;
 
         const int slot = s % NS;
-        const int kb   = warp * 16;  // this warp's first key in the stage
+        const int kb   = warp * KPW;  // this warp's first key in the stage
         // mask values of this warp's keys: mk_cur for this stage (prefetched one stage ahead when
         // the next stage is in the same unit), mk_nxt requested now for the next stage
-        if (p.mask) {
+        if (p.mask && !p.mask_tma) {
             if (!mk_have) {
                 load_mask(mk_cur, j0, n);
             }
@@ -746,201 +891,290 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                 atomicExch(&flag[0], 1);
             }
         }
-        if (!aborted && kb < n) {
-            const uint32_t sk = smem_addr(smem + slot * L::STAGE);
-            const uint32_t sv = sk + L::MAT;
-            // ---- S^T = K Q^T for this warp's 16 keys
-            float sc[NT][4];
+        if (!aborted && kb < n && p.mask_tma) {  // this stage's mask rows, staged with K and V
+            const char * mrow = smem + slot * L::STAGE + 2 * L::MAT;
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
+            for (int u = 0; u < SUB; u++) {
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    sc[nt][e] = 0.0f;
+                for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+#pragma unroll
+                        for (int kh = 0; kh < 2; kh++) {
+                            const int j          = kb + 16 * u + g4 + 8 * kh;
+                            mk_cur[u][nt][e][kh] = rvalid[nt][e] ? lds_half(mrow + j * 2) : 0.0f;
+                        }
+                    }
                 }
             }
+        }
+        if (!aborted && kb < n) {
             if constexpr (Q8) {
-                // per block: int8 A fragments of key rows kb + g4 and kb + g4 + 8 (bytes
-                // 4*q4.. and 16 + 4*q4.. of the block's values; blocks at even indices start
-                // 2 bytes past a word boundary), the exact int32 dot, then the two f16 scales
-                const char * r0 = smem + slot * L::STAGE + (kb + g4) * L::RB;
-                const char * r1 = r0 + 8 * L::RB;
+                // This warp's KPW keys as SUB independent 16-key sub-tiles (their loads, int8 dots
+                // and conversions interleave), one online-softmax update for all of them.
+                const char * kst = smem + slot * L::STAGE;
+                const char * vst = kst + L::MAT;
+                // ---- S^T = K Q^T: per block, int8 A fragments of key rows kb + 16u + g4 (+8)
+                // (bytes 4*q4.. and 16 + 4*q4.. of the block's values; blocks at even indices
+                // start 2 bytes past a word boundary), the exact int32 dot, then both f16 scales
+                float sc[SUB][NT][4];
 #pragma unroll
                 for (int b = 0; b < NBLK; b++) {
-                    const int o = b * Q8_0_BLOCK + 2 + 4 * q4;
-                    uint32_t  a0, a1, a2, a3;
-                    if (b & 1) {
-                        a0 = lds_word<0>(r0 + o);
-                        a1 = lds_word<0>(r1 + o);
-                        a2 = lds_word<0>(r0 + o + 16);
-                        a3 = lds_word<0>(r1 + o + 16);
-                    } else {
-                        a0 = lds_word<2>(r0 + o);
-                        a1 = lds_word<2>(r1 + o);
-                        a2 = lds_word<2>(r0 + o + 16);
-                        a3 = lds_word<2>(r1 + o + 16);
-                    }
-                    const float dk0 = lds_half(r0 + b * Q8_0_BLOCK);
-                    const float dk1 = lds_half(r1 + b * Q8_0_BLOCK);
 #pragma unroll
-                    for (int nt = 0; nt < NT; nt++) {
-                        int c[4] = { 0, 0, 0, 0 };
-                        mma_s8_16832(c, a0, a1, a2, a3, q8b[nt][b][0], q8b[nt][b][1]);
-                        sc[nt][0] += (float) c[0] * (dk0 * dq[nt][b][0]);
-                        sc[nt][1] += (float) c[1] * (dk0 * dq[nt][b][1]);
-                        sc[nt][2] += (float) c[2] * (dk1 * dq[nt][b][0]);
-                        sc[nt][3] += (float) c[3] * (dk1 * dq[nt][b][1]);
+                    for (int u = 0; u < SUB; u++) {
+                        const char * r0 = kst + (kb + 16 * u + g4) * L::RB;
+                        const char * r1 = r0 + 8 * L::RB;
+                        const int    o  = b * Q8_0_BLOCK + 2 + 4 * q4;
+                        uint32_t     a0, a1, a2, a3;
+                        if (b & 1) {
+                            a0 = lds_word<0>(r0 + o);
+                            a1 = lds_word<0>(r1 + o);
+                            a2 = lds_word<0>(r0 + o + 16);
+                            a3 = lds_word<0>(r1 + o + 16);
+                        } else {
+                            a0 = lds_word<2>(r0 + o);
+                            a1 = lds_word<2>(r1 + o);
+                            a2 = lds_word<2>(r0 + o + 16);
+                            a3 = lds_word<2>(r1 + o + 16);
+                        }
+                        const float dk0 = lds_half(r0 + b * Q8_0_BLOCK);
+                        const float dk1 = lds_half(r1 + b * Q8_0_BLOCK);
+#pragma unroll
+                        for (int nt = 0; nt < NT; nt++) {
+                            int c[4] = { 0, 0, 0, 0 };
+                            mma_s8_16832(c, a0, a1, a2, a3, q8b[nt][b][0], q8b[nt][b][1]);
+                            const float f[4] = { dk0 * dq[nt][b][0], dk0 * dq[nt][b][1], dk1 * dq[nt][b][0],
+                                                 dk1 * dq[nt][b][1] };
+#pragma unroll
+                            for (int e = 0; e < 4; e++) {
+                                sc[u][nt][e] = b == 0 ? (float) c[e] * f[e] : sc[u][nt][e] + (float) c[e] * f[e];
+                            }
+                        }
+                    }
+                }
+                // V block scales of keys kb + 16u + g4 (+8); zero past the stage's keys, where the
+                // ring holds stale bytes (P is zero there, and 0 * NaN must not occur)
+                float dv[SUB][2][NBLK];
+#pragma unroll
+                for (int u = 0; u < SUB; u++) {
+#pragma unroll
+                    for (int kh = 0; kh < 2; kh++) {
+                        const int    j  = kb + 16 * u + g4 + 8 * kh;
+                        const char * vr = vst + j * L::RB;
+#pragma unroll
+                        for (int b = 0; b < NBLK; b++) {
+                            dv[u][kh][b] = j < n ? lds_half(vr + b * Q8_0_BLOCK) : 0.0f;
+                        }
+                    }
+                }
+                // ---- online softmax over the warp's keys; P scaled by each key's V block scale
+                uint32_t pb8[SUB][NT][NBLK][2];
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) {
+                    float x[SUB][4];
+#pragma unroll
+                    for (int u = 0; u < SUB; u++) {
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const int re = e & 1;   // row 2*q4 + re
+                            const int kh = e >> 1;  // key 16u + g4 + 8*kh
+                            const int j  = kb + 16 * u + g4 + 8 * kh;
+                            float     v  = sc[u][nt][e] * p.scale;
+                            if (p.softcap != 0.0f) {
+                                v = p.softcap * tanhf(v / p.softcap);
+                            }
+                            v += slope[nt][re] * mk_cur[u][nt][re][kh];
+                            x[u][e] = j < n ? v * LOG2E : -INFINITY;
+                        }
+                    }
+                    float mx0 = fmaxf(x[0][0], x[0][2]), mx1 = fmaxf(x[0][1], x[0][3]);
+#pragma unroll
+                    for (int u = 1; u < SUB; u++) {
+                        mx0 = fmaxf(mx0, fmaxf(x[u][0], x[u][2]));
+                        mx1 = fmaxf(mx1, fmaxf(x[u][1], x[u][3]));
+                    }
+#pragma unroll
+                    for (int o = 4; o < 32; o <<= 1) {
+                        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+                        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+                    }
+                    const float mn0 = fmaxf(m_run[nt][0], mx0);
+                    const float mn1 = fmaxf(m_run[nt][1], mx1);
+                    const float al0 = mn0 == -INFINITY ? 1.0f : exp2f(m_run[nt][0] - mn0);
+                    const float al1 = mn1 == -INFINITY ? 1.0f : exp2f(m_run[nt][1] - mn1);
+                    m_run[nt][0]    = mn0;
+                    m_run[nt][1]    = mn1;
+                    float ls0 = 0.0f, ls1 = 0.0f;
+#pragma unroll
+                    for (int u = 0; u < SUB; u++) {
+                        const float p0 = mn0 == -INFINITY ? 0.0f : exp2f(x[u][0] - mn0);
+                        const float p1 = mn1 == -INFINITY ? 0.0f : exp2f(x[u][1] - mn1);
+                        const float p2 = mn0 == -INFINITY ? 0.0f : exp2f(x[u][2] - mn0);
+                        const float p3 = mn1 == -INFINITY ? 0.0f : exp2f(x[u][3] - mn1);
+                        ls0 += p0 + p2;
+                        ls1 += p1 + p3;
+#pragma unroll
+                        for (int b = 0; b < NBLK; b++) {
+                            pb8[u][nt][b][0] = movmatrix_t(pack2<false>(p0 * dv[u][0][b], p1 * dv[u][0][b]));
+                            pb8[u][nt][b][1] = movmatrix_t(pack2<false>(p2 * dv[u][1][b], p3 * dv[u][1][b]));
+                        }
+                    }
+                    l_run[nt][0] = l_run[nt][0] * al0 + ls0;
+                    l_run[nt][1] = l_run[nt][1] * al1 + ls1;
+#pragma unroll
+                    for (int m = 0; m < KS; m++) {
+                        acc[m][nt][0] *= al0;
+                        acc[m][nt][1] *= al1;
+                        acc[m][nt][2] *= al0;
+                        acc[m][nt][3] *= al1;
+                    }
+                }
+                // ---- O^T += V^T (P dv)^T: per block, 4 adjacent dims 32*b + 4*g4.. of the
+                // B-fragment keys kb + 16u + 2*q4 + {0, 1, 8, 9}, byte-interleaved per key pair
+                // and widened to f16 (exact)
+#pragma unroll
+                for (int b = 0; b < NBLK; b++) {
+#pragma unroll
+                    for (int u = 0; u < SUB; u++) {
+                        const char * v0 = vst + (kb + 16 * u + 2 * q4) * L::RB;
+                        const int    o  = b * Q8_0_BLOCK + 2 + 4 * g4;
+                        uint32_t     w0, w1, w8, w9;
+                        if (b & 1) {
+                            w0 = lds_word<0>(v0 + o);
+                            w1 = lds_word<0>(v0 + L::RB + o);
+                            w8 = lds_word<0>(v0 + 8 * L::RB + o);
+                            w9 = lds_word<0>(v0 + 9 * L::RB + o);
+                        } else {
+                            w0 = lds_word<2>(v0 + o);
+                            w1 = lds_word<2>(v0 + L::RB + o);
+                            w8 = lds_word<2>(v0 + 8 * L::RB + o);
+                            w9 = lds_word<2>(v0 + 9 * L::RB + o);
+                        }
+                        w0 ^= 0x80808080u;
+                        w1 ^= 0x80808080u;
+                        w8 ^= 0x80808080u;
+                        w9 ^= 0x80808080u;
+                        const uint32_t lo01 = __byte_perm(w0, w1, 0x5140), hi01 = __byte_perm(w0, w1, 0x7362);
+                        const uint32_t lo89 = __byte_perm(w8, w9, 0x5140), hi89 = __byte_perm(w8, w9, 0x7362);
+                        const uint32_t e0 = i8x2_to_h2<0x4140>(lo01), e1 = i8x2_to_h2<0x4342>(lo01);
+                        const uint32_t e2 = i8x2_to_h2<0x4140>(lo89), e3 = i8x2_to_h2<0x4342>(lo89);
+                        const uint32_t f0 = i8x2_to_h2<0x4140>(hi01), f1 = i8x2_to_h2<0x4342>(hi01);
+                        const uint32_t f2 = i8x2_to_h2<0x4140>(hi89), f3 = i8x2_to_h2<0x4342>(hi89);
+#pragma unroll
+                        for (int nt = 0; nt < NT; nt++) {
+                            mma16816<false>(acc[2 * b][nt], e0, e1, e2, e3, pb8[u][nt][b][0], pb8[u][nt][b][1]);
+                            mma16816<false>(acc[2 * b + 1][nt], f0, f1, f2, f3, pb8[u][nt][b][0], pb8[u][nt][b][1]);
+                        }
                     }
                 }
             } else {
-                // all K fragments first (one shared-memory latency), then two independent
-                // accumulation chains over the even and odd k-steps
-                const int krow = kb + (lane & 7) + ((lane >> 3) & 1) * 8;  // A rows supplied by this lane
-                uint32_t  af[KS][4];
-#pragma unroll
-                for (int ks = 0; ks < KS; ks++) {
-                    const int dim0 = ks * 16 + (lane >> 4) * 8;
-                    ldsm_x4(sk + (dim0 >> 6) * L::TILE + swz(krow, (dim0 & 63) >> 3), af[ks][0], af[ks][1],
-                            af[ks][2], af[ks][3]);
-                }
-                float sc1[NT][4];
+                const uint32_t sk = smem_addr(smem + slot * L::STAGE);
+                const uint32_t sv = sk + L::MAT;
+                // ---- S^T = K Q^T for this warp's 16 keys
+                float sc[NT][4];
 #pragma unroll
                 for (int nt = 0; nt < NT; nt++) {
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
-                        sc1[nt][e] = 0.0f;
+                        sc[nt][e] = 0.0f;
                     }
                 }
+                {
+                    // all K fragments first (one shared-memory latency), then two independent
+                    // accumulation chains over the even and odd k-steps
+                    const int krow = kb + (lane & 7) + ((lane >> 3) & 1) * 8;  // A rows supplied by this lane
+                    uint32_t  af[KS][4];
 #pragma unroll
-                for (int ks = 0; ks < KS; ks++) {
+                    for (int ks = 0; ks < KS; ks++) {
+                        const int dim0 = ks * 16 + (lane >> 4) * 8;
+                        ldsm_x4(sk + (dim0 >> 6) * L::TILE + swz(krow, (dim0 & 63) >> 3), af[ks][0], af[ks][1],
+                                af[ks][2], af[ks][3]);
+                    }
+                    float sc1[NT][4];
 #pragma unroll
                     for (int nt = 0; nt < NT; nt++) {
-                        mma16816<BF16>((ks & 1) ? sc1[nt] : sc[nt], af[ks][0], af[ks][1], af[ks][2], af[ks][3],
-                                       qb[nt][ks][0], qb[nt][ks][1]);
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            sc1[nt][e] = 0.0f;
+                        }
+                    }
+#pragma unroll
+                    for (int ks = 0; ks < KS; ks++) {
+#pragma unroll
+                        for (int nt = 0; nt < NT; nt++) {
+                            mma16816<BF16>((ks & 1) ? sc1[nt] : sc[nt], af[ks][0], af[ks][1], af[ks][2], af[ks][3],
+                                           qb[nt][ks][0], qb[nt][ks][1]);
+                        }
+                    }
+#pragma unroll
+                    for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            sc[nt][e] += sc1[nt][e];
+                        }
                     }
                 }
+                // ---- online softmax (per warp), P^T -> P fragments
+                uint32_t pb[NT][2];
 #pragma unroll
                 for (int nt = 0; nt < NT; nt++) {
+                    float x[4];
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
-                        sc[nt][e] += sc1[nt][e];
+                        const int re = e & 1;       // row 2*q4 + re
+                        const int kh = e >> 1;      // key g4 + 8*kh
+                        const int j  = kb + g4 + 8 * kh;
+                        float     v  = sc[nt][e] * p.scale;
+                        if (p.softcap != 0.0f) {
+                            v = p.softcap * tanhf(v / p.softcap);
+                        }
+                        v += slope[nt][re] * mk_cur[0][nt][re][kh];
+                        x[e] = j < n ? v * LOG2E : -INFINITY;
                     }
-                }
-            }
-            // ---- online softmax (per warp), P^T -> P fragments
-            uint32_t pb[NT][2];
-            uint32_t pb8[NT][Q8 ? NBLK : 1][2];  // Q8: P scaled by each key's V block scale
-            float    dv0[Q8 ? NBLK : 1], dv1[Q8 ? NBLK : 1];
-            if constexpr (Q8) {
-                // V scales of keys kb + g4 and kb + g4 + 8; zero past the stage's keys, where
-                // the ring holds stale bytes (P is zero there, and 0 * NaN must not occur)
-                const char * r0 = smem + slot * L::STAGE + L::MAT + (kb + g4) * L::RB;
+                    float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
 #pragma unroll
-                for (int b = 0; b < NBLK; b++) {
-                    dv0[b] = kb + g4 < n ? lds_half(r0 + b * Q8_0_BLOCK) : 0.0f;
-                    dv1[b] = kb + g4 + 8 < n ? lds_half(r0 + 8 * L::RB + b * Q8_0_BLOCK) : 0.0f;
-                }
-            }
-#pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-                float x[4];
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int re = e & 1;       // row 2*q4 + re
-                    const int kh = e >> 1;      // key g4 + 8*kh
-                    const int j  = kb + g4 + 8 * kh;
-                    float     v  = sc[nt][e] * p.scale;
-                    if (p.softcap != 0.0f) {
-                        v = p.softcap * tanhf(v / p.softcap);
+                    for (int o = 4; o < 32; o <<= 1) {
+                        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+                        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
                     }
-                    v += slope[nt][re] * mk_cur[nt][re][kh];
-                    x[e] = j < n ? v * LOG2E : -INFINITY;
-                }
-                float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
+                    const float mn0 = fmaxf(m_run[nt][0], mx0);
+                    const float mn1 = fmaxf(m_run[nt][1], mx1);
+                    const float al0 = mn0 == -INFINITY ? 1.0f : exp2f(m_run[nt][0] - mn0);
+                    const float al1 = mn1 == -INFINITY ? 1.0f : exp2f(m_run[nt][1] - mn1);
+                    m_run[nt][0]    = mn0;
+                    m_run[nt][1]    = mn1;
+                    const float p0  = mn0 == -INFINITY ? 0.0f : exp2f(x[0] - mn0);
+                    const float p1  = mn1 == -INFINITY ? 0.0f : exp2f(x[1] - mn1);
+                    const float p2  = mn0 == -INFINITY ? 0.0f : exp2f(x[2] - mn0);
+                    const float p3  = mn1 == -INFINITY ? 0.0f : exp2f(x[3] - mn1);
+                    l_run[nt][0]    = l_run[nt][0] * al0 + p0 + p2;
+                    l_run[nt][1]    = l_run[nt][1] * al1 + p1 + p3;
 #pragma unroll
-                for (int o = 4; o < 32; o <<= 1) {
-                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-                }
-                const float mn0 = fmaxf(m_run[nt][0], mx0);
-                const float mn1 = fmaxf(m_run[nt][1], mx1);
-                const float al0 = mn0 == -INFINITY ? 1.0f : exp2f(m_run[nt][0] - mn0);
-                const float al1 = mn1 == -INFINITY ? 1.0f : exp2f(m_run[nt][1] - mn1);
-                m_run[nt][0]    = mn0;
-                m_run[nt][1]    = mn1;
-                const float p0  = mn0 == -INFINITY ? 0.0f : exp2f(x[0] - mn0);
-                const float p1  = mn1 == -INFINITY ? 0.0f : exp2f(x[1] - mn1);
-                const float p2  = mn0 == -INFINITY ? 0.0f : exp2f(x[2] - mn0);
-                const float p3  = mn1 == -INFINITY ? 0.0f : exp2f(x[3] - mn1);
-                l_run[nt][0]    = l_run[nt][0] * al0 + p0 + p2;
-                l_run[nt][1]    = l_run[nt][1] * al1 + p1 + p3;
-#pragma unroll
-                for (int m = 0; m < KS; m++) {
-                    acc[m][nt][0] *= al0;
-                    acc[m][nt][1] *= al1;
-                    acc[m][nt][2] *= al0;
-                    acc[m][nt][3] *= al1;
-                }
-                if constexpr (Q8) {
-#pragma unroll
-                    for (int b = 0; b < NBLK; b++) {
-                        pb8[nt][b][0] = movmatrix_t(pack2<false>(p0 * dv0[b], p1 * dv0[b]));
-                        pb8[nt][b][1] = movmatrix_t(pack2<false>(p2 * dv1[b], p3 * dv1[b]));
+                    for (int m = 0; m < KS; m++) {
+                        acc[m][nt][0] *= al0;
+                        acc[m][nt][1] *= al1;
+                        acc[m][nt][2] *= al0;
+                        acc[m][nt][3] *= al1;
                     }
-                } else {
                     pb[nt][0] = movmatrix_t(pack2<BF16>(p0, p1));  // keys 0-7 of the warp's 16
                     pb[nt][1] = movmatrix_t(pack2<BF16>(p2, p3));  // keys 8-15
                 }
-            }
-            // ---- O^T += V^T P^T over this warp's 16 keys
-            if constexpr (Q8) {
-                // per block: 4 adjacent dims 32*b + 4*g4.. of the B-fragment keys kb + 2*q4 +
-                // {0, 1, 8, 9}, byte-interleaved per key pair and widened to f16 (exact)
-                const char * v0 = smem + slot * L::STAGE + L::MAT + (kb + 2 * q4) * L::RB;
+                // ---- O^T += V^T P^T over this warp's 16 keys
+                {
+                    const int vkey = kb + (lane & 7) + ((lane >> 4) & 1) * 8;  // stored V row for ldmatrix.trans
+                    uint32_t  vf[KS][4];
 #pragma unroll
-                for (int b = 0; b < NBLK; b++) {
-                    const int o = b * Q8_0_BLOCK + 2 + 4 * g4;
-                    uint32_t  w0, w1, w8, w9;
-                    if (b & 1) {
-                        w0 = lds_word<0>(v0 + o);
-                        w1 = lds_word<0>(v0 + L::RB + o);
-                        w8 = lds_word<0>(v0 + 8 * L::RB + o);
-                        w9 = lds_word<0>(v0 + 9 * L::RB + o);
-                    } else {
-                        w0 = lds_word<2>(v0 + o);
-                        w1 = lds_word<2>(v0 + L::RB + o);
-                        w8 = lds_word<2>(v0 + 8 * L::RB + o);
-                        w9 = lds_word<2>(v0 + 9 * L::RB + o);
+                    for (int m = 0; m < KS; m++) {
+                        const int dim0 = m * 16 + ((lane >> 3) & 1) * 8;
+                        ldsm_x4_t(sv + (dim0 >> 6) * L::TILE + swz(vkey, (dim0 & 63) >> 3), vf[m][0], vf[m][1],
+                                  vf[m][2], vf[m][3]);
                     }
-                    w0 ^= 0x80808080u;
-                    w1 ^= 0x80808080u;
-                    w8 ^= 0x80808080u;
-                    w9 ^= 0x80808080u;
-                    const uint32_t lo01 = __byte_perm(w0, w1, 0x5140), hi01 = __byte_perm(w0, w1, 0x7362);
-                    const uint32_t lo89 = __byte_perm(w8, w9, 0x5140), hi89 = __byte_perm(w8, w9, 0x7362);
-                    const uint32_t e0 = i8x2_to_h2<0x4140>(lo01), e1 = i8x2_to_h2<0x4342>(lo01);
-                    const uint32_t e2 = i8x2_to_h2<0x4140>(lo89), e3 = i8x2_to_h2<0x4342>(lo89);
-                    const uint32_t f0 = i8x2_to_h2<0x4140>(hi01), f1 = i8x2_to_h2<0x4342>(hi01);
-                    const uint32_t f2 = i8x2_to_h2<0x4140>(hi89), f3 = i8x2_to_h2<0x4342>(hi89);
 #pragma unroll
-                    for (int nt = 0; nt < NT; nt++) {
-                        mma16816<false>(acc[2 * b][nt], e0, e1, e2, e3, pb8[nt][b][0], pb8[nt][b][1]);
-                        mma16816<false>(acc[2 * b + 1][nt], f0, f1, f2, f3, pb8[nt][b][0], pb8[nt][b][1]);
-                    }
-                }
-            } else {
-                const int vkey = kb + (lane & 7) + ((lane >> 4) & 1) * 8;  // stored V row for ldmatrix.trans
-                uint32_t  vf[KS][4];
+                    for (int m = 0; m < KS; m++) {
 #pragma unroll
-                for (int m = 0; m < KS; m++) {
-                    const int dim0 = m * 16 + ((lane >> 3) & 1) * 8;
-                    ldsm_x4_t(sv + (dim0 >> 6) * L::TILE + swz(vkey, (dim0 & 63) >> 3), vf[m][0], vf[m][1],
-                              vf[m][2], vf[m][3]);
-                }
-#pragma unroll
-                for (int m = 0; m < KS; m++) {
-#pragma unroll
-                    for (int nt = 0; nt < NT; nt++) {
-                        mma16816<BF16>(acc[m][nt], vf[m][0], vf[m][1], vf[m][2], vf[m][3], pb[nt][0], pb[nt][1]);
+                        for (int nt = 0; nt < NT; nt++) {
+                            mma16816<BF16>(acc[m][nt], vf[m][0], vf[m][1], vf[m][2], vf[m][3], pb[nt][0], pb[nt][1]);
+                        }
                     }
                 }
             }
@@ -949,14 +1183,17 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
         if (lane == 0) {
             mbar_arrive(&empty[slot]);  // this warp is done with the ring slot
         }
-        if (p.mask) {
+        if (p.mask && !p.mask_tma) {
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
+            for (int u = 0; u < SUB; u++) {
 #pragma unroll
-                for (int e = 0; e < 2; e++) {
+                for (int nt = 0; nt < NT; nt++) {
 #pragma unroll
-                    for (int kh = 0; kh < 2; kh++) {
-                        mk_cur[nt][e][kh] = mk_nxt[nt][e][kh];
+                    for (int e = 0; e < 2; e++) {
+#pragma unroll
+                        for (int kh = 0; kh < 2; kh++) {
+                            mk_cur[u][nt][e][kh] = mk_nxt[u][nt][e][kh];
+                        }
                     }
                 }
             }
@@ -969,70 +1206,6 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
     }
     }  // consumer warps
 
-    if (CLUSTER) {
-        // every CTA's (m, l) rows and merged O are in its shared memory: CTA rank c of the
-        // cluster merges dims [c*D/CS, (c+1)*D/CS) of every row from all CS CTAs over DSMEM
-        __syncwarp();
-        cluster_sync_all();
-        const int64_t unit = blockIdx.x / p.cluster;
-        const int     rgrp = (int) (unit % p.groups);
-        const int64_t sg   = unit / p.groups;
-        const int     g    = (int) (sg % p.n_head_kv);
-        const int     sq   = (int) (sg / p.n_head_kv);
-        const int     nr   = min(p.rows_per_unit, p.rows_per_pair - rgrp * MMA_RMAX);
-        const int     CS   = p.cluster;
-        const int     rank = (int) cluster_ctarank();
-        // rank c takes the (row, 4 dims) items c, c + CS, c + 2*CS, ... (any cluster size); all
-        // remote loads of an item are issued together (one DSMEM latency)
-        for (int idx = rank + tid * CS; idx < nr * (D / 4); idx += MMA_THREADS * CS) {
-            const int r = idx / (D / 4), d = (idx % (D / 4)) * 4;
-            float2    ml[16];
-            float4    ov[16];
-#pragma unroll
-            for (int c = 0; c < 16; c++) {
-                ml[c] = make_float2(-INFINITY, 0.0f);
-                ov[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (c < CS) {
-                    ml[c] = ld_dsmem2(dsmem_addr(&cml[r * 2], (uint32_t) c));
-                    ov[c] = ld_dsmem4(dsmem_addr(&redO[r * D + d], (uint32_t) c));
-                }
-            }
-            float M = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < 16; c++) {
-                M = fmaxf(M, ml[c].x);
-            }
-            float4 O  = make_float4(0.f, 0.f, 0.f, 0.f);
-            float  Ls = 0.0f;
-            if (M != -INFINITY) {
-#pragma unroll
-                for (int c = 0; c < 16; c++) {
-                    const float w = ml[c].x == -INFINITY ? 0.0f : exp2f(ml[c].x - M);
-                    O.x += w * ov[c].x;
-                    O.y += w * ov[c].y;
-                    O.z += w * ov[c].z;
-                    O.w += w * ov[c].w;
-                    Ls += w * ml[c].y;
-                }
-            }
-            const float inv = Ls > 0.0f ? 1.0f / Ls : 0.0f;
-            const int   rf  = rgrp * MMA_RMAX + r;
-            const int   h   = g * p.ratio + rf / p.n_q;
-            const int   i   = rf % p.n_q;
-            float *     out = reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 + (int64_t) i * p.d_nb2 +
-                                                    (int64_t) sq * p.d_nb3) + d;
-            if (p.dst_vec) {
-                *reinterpret_cast<float4 *>(out) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
-            } else {
-                out[0] = O.x * inv;
-                out[1] = O.y * inv;
-                out[2] = O.z * inv;
-                out[3] = O.w * inv;
-            }
-        }
-        __syncwarp();
-        cluster_sync_all();  // peers may still be reading this CTA's shared memory
-    }
     if (flag[0] && tid == 0) {
         atomicOr(&p.status[0], ST_TIMEOUT);
         atomicExch(&p.status[1], (uint32_t) blockIdx.x);
@@ -1087,9 +1260,44 @@ bool tensor_maps_available() {
 
 namespace {
 
-// Q8_0 ring depth: 6 stages of 64 keys (17 KiB each at D=128), about the bytes in flight of
-// the F16 kernel's 3 stages.
-constexpr int Q8_NSTAGE = 6;
+// 4-D map of an F16 mask [n_kv, n_q, m_ne2, m_ne3] (rows n_q and up are never read), box = ck
+// keys of one row, no swizzle, keys past n_kv read as zero.  False unless the base and the row
+// strides are 16-byte multiples.  The kernel uses it for one query row and a mask shared by
+// all heads, where all rows of a unit read the same mask row.
+bool encode_mask_tensor_map(CUtensorMap * tm, const DecodeParams & p, int ck) {
+    auto enc = tensor_map_encoder();
+    if (!enc || !p.mask || reinterpret_cast<uintptr_t>(p.mask) % 16 != 0) {
+        return false;
+    }
+    int64_t nb1 = p.m_nb1, nb2 = p.m_nb2, nb3 = p.m_nb3;
+    if (p.n_q == 1) {
+        nb1 = ((int64_t) p.n_kv * 2 + 15) / 16 * 16;  // never stepped
+    }
+    if (p.m_ne2 == 1) {
+        nb2 = nb1 * p.n_q;
+    }
+    if (p.m_ne3 == 1) {
+        nb3 = nb2 * p.m_ne2;
+    }
+    if (nb1 % 16 || nb2 % 16 || nb3 % 16) {
+        return false;
+    }
+    cuuint64_t dims[4]    = { (cuuint64_t) p.n_kv, (cuuint64_t) p.n_q, (cuuint64_t) p.m_ne2, (cuuint64_t) p.m_ne3 };
+    cuuint64_t strides[3] = { (cuuint64_t) nb1, (cuuint64_t) nb2, (cuuint64_t) nb3 };
+    cuuint32_t box[4]     = { (cuuint32_t) ck, 1, 1, 1 };
+    cuuint32_t estr[4]    = { 1, 1, 1, 1 };
+    CUresult   r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<char *>(p.mask), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+namespace {
+
+// Q8_0 ring depth: 3 stages of 128 keys (34 KiB each at D=128; 64 keys with 16 rows per unit).
+constexpr int Q8_NSTAGE = 3;
 
 template <int D, bool BF16, int NT, bool CL, bool Q8>
 void * mma_kernel(int ns, int & smem) {
@@ -1191,31 +1399,40 @@ int decode_mma_ctas_per_sm(int D, int kvt, int rows_per_pair) {
     return nb;
 }
 
-// Cluster size for `n_units` units on a device with `slots` resident CTAs: the largest size
-// <= 16 with n_units * cs <= slots whose clusters all fit at once; 0 selects the stream-K split
-// (too few units to fill the GPU with clusters).  Cached per (device, kernel, units).
-int decode_mma_cluster_size(int D, int kvt, int rows_per_pair, int64_t n_units, int slots) {
-    if (n_units * 16 < slots / 2 || n_units <= 0) {
-        return 0;
-    }
-    int cs = (int) std::min<int64_t>(16, std::max<int64_t>(1, slots / n_units));
+// Cluster size for `n_units` units on a device with n_sms SMs: the largest size <= 16 with
+// n_units * cs <= the cluster kernel's resident CTAs whose clusters all fit at once; 0 selects
+// the stream-K split (too few units to fill the GPU with clusters).  The cluster instance's
+// own occupancy counts (it needs fewer registers than the stream-K one).  Cached per
+// (device, kernel, units).
+int decode_mma_cluster_size(int D, int kvt, int rows_per_pair, int64_t n_units, int n_sms) {
     const int nt  = rows_per_pair <= 8 ? 1 : 2;
     int       dev = 0;
     cudaGetDevice(&dev);
     static std::mutex                                   mu;
     static std::map<std::tuple<int, int, int, int, int, int64_t>, int> cache;
     std::lock_guard<std::mutex>                         lock(mu);
-    const auto key = std::make_tuple(dev, D, kvt, nt, slots, n_units);
+    const auto key = std::make_tuple(dev, D, kvt, nt, n_sms, n_units);
     auto       it  = cache.find(key);
     if (it != cache.end()) {
         return it->second;
     }
     int    smem = 0;
     void * fn   = select_mma_kernel(D, kvt, nt, true, smem);
-    if (!fn) {
+    if (!fn || n_units <= 0) {
         return 0;
     }
     cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, MMA_THREADS, smem) != cudaSuccess || per_sm < 1) {
+        cudaGetLastError();
+        per_sm = 1;
+    }
+    const int slots = n_sms * per_sm;
+    if (n_units * 16 < slots / 2) {
+        cache[key] = 0;
+        return 0;
+    }
+    int cs = (int) std::min<int64_t>(16, std::max<int64_t>(1, slots / n_units));
     while (cs > 1) {
         const int n = max_active_clusters(fn, cs, smem);
         if ((int64_t) n >= std::min<int64_t>(n_units, (int64_t) slots / cs)) {
@@ -1236,7 +1453,19 @@ cudaError_t launch_decode_mma(DecodeParams p, const DecodeGeometry & g, int D, i
     if (!fn) {
         return cudaErrorInvalidValue;
     }
-    alignas(64) CUtensorMap tmk, tmv;
+    alignas(64) CUtensorMap tmk, tmv, tmm;
+    std::memset(&tmm, 0, sizeof(tmm));
+    // cluster mode stages its mask rows by TMA (stage starts are multiples of the chunk size)
+    const int ck = (kvt == KV_Q8_0 && nt == 1) ? 2 * MMA_C : MMA_C;
+    static const int mask_tma_env = [] {
+        const char * e = std::getenv("MM3FA_DECODE_MASK_TMA");
+        return e ? std::atoi(e) : 1;
+    }();
+    p.mask_tma = (mask_tma_env && cluster > 0 && p.mask && p.n_q == 1 && p.m_ne2 == 1 &&
+                  encode_mask_tensor_map(&tmm, p, ck))
+                     ? 1
+                     : 0;
+
     if (kvt == KV_Q8_0) {
         // bulk copies of packed rows: every slab start and chunk must be 16-byte aligned
         const int64_t rb = (int64_t) D / QK8_0 * Q8_0_BLOCK;
@@ -1306,7 +1535,7 @@ cudaError_t launch_decode_mma(DecodeParams p, const DecodeGeometry & g, int D, i
         attr[cfg.numAttrs].val.clusterDim.z = 1;
         cfg.numAttrs++;
     }
-    void * args[] = { &tmk, &tmv, &p };
+    void * args[] = { &tmk, &tmv, &tmm, &p };
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 

@@ -561,10 +561,10 @@ int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const m
     p.timeout_ns = wait_timeout_ns();
     p.dst_vec    = rows_vec16(dst);
     if (var >= V_MMA_8) {
-        const int slots   = device_info().sms * ctas_per_sm_cached((int) s.D, s.kvt, var);
         const int pref    = decode_mma_mode_preference();
         const int cluster = pref == 1 ? 0
-                                      : decode_mma_cluster_size((int) s.D, s.kvt, p.rows_per_pair, g.n_units, slots);
+                                      : decode_mma_cluster_size((int) s.D, s.kvt, p.rows_per_pair, g.n_units,
+                                                                device_info().sms);
         return record_cuda(
             launch_decode_mma(p, g, (int) s.D, s.kvt, s.n_head_kv, s.n_seq_k, cluster, workspace, cs));
     }
