@@ -48,7 +48,7 @@ N_KV, MAX_SEQ = 8192, 10240
 FALLBACK_HBM_GBS = 6650.0
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode launch at this workload (ncu capture)
-NCU_KERNEL = "fa_decode_mma_kernel<128,f16,NT=1,cluster,NS=3>"
+NCU_KERNEL = "fa_decode_mma_kernel<128,f16,NT=1,cluster,NS=2>"
 NCU_TRAFFIC_BYTES = 67225344 + 506112
 
 
@@ -302,6 +302,78 @@ def bench_dense(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, world:
     return out
 
 
+def bench_q8(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, world: int, n_layers: int) -> dict:
+    """Q8_0 KV-cache decode (benchmark config 3: config 1 at KV 8192 with Q8_0 K/V, int8 ~U[-127,127],
+    fp16 scales ~U[0.001,0.02]), as a 36-layer step of independent caches in one CUDA graph; each
+    rank holds its kv-head shard of its own CFG pair, like the F16 line."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    n_seq, hkv, hq = 2, N_HEAD_KV // world, N_HEAD // world
+    nblk = D // 32
+    rb = nblk * 34
+
+    def q8_cache():
+        t = torch.randint(-127, 128, (n_seq, hkv, N_KV, nblk, 34), generator=g, device=dev,
+                          dtype=torch.int32).to(torch.int8).view(torch.uint8)
+        sc = (torch.rand(n_seq, hkv, N_KV, nblk, generator=g, device=dev) * 0.019 + 0.001).half()
+        t[..., :2] = sc.view(torch.uint8).view(n_seq, hkv, N_KV, nblk, 2)
+        return t.contiguous()
+
+    keep, descs = [], []
+    mask = torch.zeros(n_seq, 1, 1, N_KV, dtype=torch.float16, device=dev)
+    nb = [34, rb, rb * N_KV, rb * N_KV * hkv]
+    for _ in range(n_layers):
+        kc, vc = q8_cache(), q8_cache()
+        q = torch.randn(n_seq, hq, 1, D, generator=g, device=dev)
+        o = torch.empty(n_seq, 1, hq, D, device=dev)
+        keep += [kc, vc, q, o]
+        descs.append((ggml.make(ggml.GGML_TYPE_F32, [D, 1, hq, n_seq], q.data_ptr()),
+                      ggml.make(ggml.GGML_TYPE_Q8_0, [D, N_KV, hkv, n_seq], kc.data_ptr(), nb),
+                      ggml.make(ggml.GGML_TYPE_Q8_0, [D, N_KV, hkv, n_seq], vc.data_ptr(), nb),
+                      ggml.make(ggml.GGML_TYPE_F16, [N_KV, 1, 1, n_seq], mask.data_ptr()),
+                      ggml.make(ggml.GGML_TYPE_F32, [D, hq, 1, n_seq], o.data_ptr())))
+    need = mm3fa.workspace_size(*descs[0][:4], descs[0][4])
+    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
+    scale = 1.0 / math.sqrt(D)
+
+    def step():
+        for (qd, kd, vd, md, dd) in descs:
+            mm3fa.flash_attn_ext(qd, kd, vd, md, scale, 0.0, 0.0, dd, ws.data_ptr(), ws.numel(), stream.cuda_stream)
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream.record_event(e0)
+    with torch.cuda.stream(stream):
+        for _ in range(steps):
+            graph.replay()
+    stream.record_event(e1)
+    torch.cuda.synchronize()
+    del graph
+    us_layer = e0.elapsed_time(e1) * 1e3 / steps / n_layers
+    kv = 2 * n_seq * hkv * N_KV * rb
+    algo = kv + n_seq * hq * D * 8 + n_seq * N_KV * 2
+    peak, src = measured_peaks()
+    gbs = algo / (us_layer * 1e-6) / 1e9
+    return {"q8_decode": {"us_per_layer": round(us_layer, 3), "GBps": round(gbs, 1), "GBps_job": round(gbs * world, 1),
+                          "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                                       "frac": round(gbs / peak, 4), "peak_source": src,
+                                       "kernel": "fa_decode_mma_kernel<128,q8_0,NT=1,cluster>",
+                                       "bytes_per_layer": algo},
+                          "config": {"workload": "Q8_0 KV-cache decode, benchmark config 3 (B=2 CFG, KV 8192), "
+                                                 f"{n_layers} independent layers per CUDA graph",
+                                     "n_seq": n_seq, "n_kv": N_KV, "n_head": hq, "n_head_kv": hkv,
+                                     "head_dim": D, "l2": "inputs > L2"}}}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -311,6 +383,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-dense", action="store_true", help="skip the DiT / prefill (tensor-core) lines")
+    ap.add_argument("--no-q8", action="store_true", help="skip the Q8_0 KV-cache decode line (config 3)")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers per step (36 = the LM; fewer only for small ncu captures)")
     args = ap.parse_args()
@@ -476,6 +549,9 @@ def main() -> None:
     dense = None if args.no_dense else bench_dense(torch, mm3fa, ggml, dev, stream, args.steps, args.warmup, world, local)
     if dense is not None and world > 1:
         dist.barrier()
+    q8 = None if args.no_q8 else bench_q8(torch, mm3fa, ggml, dev, stream, args.steps, args.warmup, world, n_layers)
+    if q8 is not None and world > 1:
+        dist.barrier()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -505,6 +581,8 @@ def main() -> None:
         }
         if dense is not None:
             line.update(dense)
+        if q8 is not None:
+            line.update(q8)
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
