@@ -10,6 +10,8 @@ namespace mm3fa {
 
 // Class of one 128 x 128 (query, key) block of a mask plane.
 enum : uint8_t { BLK_NONE = 0, BLK_MIXED = 1, BLK_SKIP = 2 };
+// Flag bits of a block as the mask pre-pass records them: some entry is not -inf / not zero.
+enum : uint32_t { BLKF_FINITE = 1u, BLKF_NONZERO = 2u };
 
 struct DenseParams {
     const char * q;
@@ -36,14 +38,18 @@ struct DenseParams {
     float        scale, softcap, max_bias, m0, m1;
     int          n_head_log2;
     int          n_qt, n_kt;              // 128-row query tiles, 128-key tiles
-    const uint8_t * blocks;               // [plane][n_qt][n_kt] block classes, null without mask
+    const uint32_t * blocks;              // [plane][n_qt][n_kt] block flags (BLKF_*), null without mask
+    // [plane][row][3]: max(n_kv - first -inf column), max(last zero column + 1), any other value;
+    // a row is a step row (zeros, then -inf from column lim = n_kv - [0] on) when [2] == 0 and
+    // [0] + [1] <= n_kv.  Null without mask.
+    const int *  rowinfo;
     uint32_t *   status;
     uint64_t     timeout_ns;
 };
 
 // F16/BF16 K and V, D = DV = 64 or 128, TMA-expressible strides.
 bool        dense_eligible(int D, int kvt);
-// Workspace bytes: status word and the mask block classes.
+// Workspace bytes: status word, the mask block classes and the per-row mask summaries.
 size_t      dense_workspace_bytes(int64_t n_q, int64_t n_kv, int64_t planes);
 cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64_t n_seq_k, int64_t n_head,
                          int64_t n_seq, void * workspace, cudaStream_t stream);

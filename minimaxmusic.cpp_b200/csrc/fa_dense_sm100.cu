@@ -314,7 +314,8 @@ __device__ __forceinline__ int tile_class(const DenseParams & p, int plane, int 
     if (!p.blocks) {
         return BLK_NONE;
     }
-    return p.blocks[((int64_t) plane * p.n_qt + qt) * p.n_kt + kt];
+    const uint32_t f = p.blocks[((int64_t) plane * p.n_qt + qt) * p.n_kt + kt];
+    return !(f & BLKF_FINITE) ? BLK_SKIP : (!(f & BLKF_NONZERO) ? BLK_NONE : BLK_MIXED);
 }
 
 // D (TMEM) = A (TMEM, 16-bit, row m = lane m) * B (smem desc) [+ D]; whole warp, one lane issues
@@ -632,6 +633,15 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
         const bool     valid = row < p.n_q;
         const int      qi    = valid ? row : 0;
         const float    slope = alibi_slope(h, p.max_bias, p.n_head_log2, p.m0, p.m1);
+        // step rows (the mask is 0 before column lim and -inf from it on, as in causal masks):
+        // their mixed tiles take the fast path with a column bound instead of mask values
+        int lim = p.n_kv, ri0 = 0, ri1 = 0, ri2 = 0;
+        if (p.rowinfo && valid) {
+            const int * ri = p.rowinfo + ((int64_t) plane * p.n_q + qi) * 3;
+            ri0            = ri[0];
+            ri1            = ri[1];
+            ri2            = ri[2];
+        }
 
         // ---- stage Q row r into the swizzled K-major tile t, rounded to K's type
         {
@@ -697,6 +707,9 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
         const float sl2   = sc * LOG2E;     // raw score -> log2 units (no softcap)
         const float ml2   = slope * LOG2E;  // mask -> log2 units
         const bool  plain = p.softcap == 0.0f && sl2 > 0.0f;
+        const bool  is_step   = ri2 == 0 && ri0 + ri1 <= p.n_kv;
+        const bool  step_warp = p.rowinfo != nullptr && __all_sync(0xffffffffu, is_step);
+        lim                   = p.n_kv - ri0;
         float       m     = -INFINITY;      // running maximum (log2 units; may be stale by < 8)
         float       l     = 0.0f;
         bool        ok    = true;
@@ -704,8 +717,11 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
         for (int kt = kt_lo; i < n_mine; kt = next_tile(kt + 1), i++) {
             const int  nk    = p.n_kv - kt * DN_N;  // keys of this tile that exist (may exceed DN_N)
             const int  cls   = tile_class(p, plane, cq, kt);
-            const bool fast  = plain && nk >= DN_N && cls != BLK_MIXED;
-            const bool mixed = valid && cls == BLK_MIXED;
+            // warp-uniform: every row of the warp is a step row, so the tile needs only a bound
+            const bool use_lim = plain && step_warp && (cls == BLK_MIXED || nk < DN_N);
+            const bool fast    = use_lim || (plain && nk >= DN_N && cls != BLK_MIXED);
+            const bool mixed   = valid && cls == BLK_MIXED && !use_lim;
+            const int  lt      = lim - kt * DN_N;  // columns of this tile the row sees (step rows)
             // this row's mask values of the tile: pulled into L1 before S is ready, so the loads of
             // the pass below hit
             const __half * mp = mixed ? mrow + (int64_t) kt * DN_N : nullptr;
@@ -811,6 +827,17 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                 f2unpack(fadd2(acc[2], acc[3]), s2, s3);
                 return (s0 + s1) + (s2 + s3);
             };
+            // step rows: columns from lt on are -inf (raw score bits, before the scale)
+            auto apply_lim = [&](int j0, int j1) {
+                if (use_lim) {
+#pragma unroll
+                    for (int j = 0; j < DN_N; j++) {
+                        if (j >= j0 && j < j1) {
+                            sr[j] = j < lt ? sr[j] : 0xFF800000u;
+                        }
+                    }
+                }
+            };
             auto load_all = [&]() {
 #pragma unroll
                 for (int c = 0; c < DN_N / 32; c++) {
@@ -835,16 +862,19 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                 tmem_ld_wait_tie(&sr[32]);
                 tmem_ld32(s_col + 64, &sr[64]);
                 tmem_ld32(s_col + 96, &sr[96]);
+                apply_lim(0, DN_N / 2);
                 acc[0] = acc[1] = acc[2] = acc[3] = 0ull;
                 exp_pairs(0, DN_N / 4);
                 tmem_ld_wait_tie(&sr[64]);
                 tmem_ld_wait_tie(&sr[96]);
+                apply_lim(DN_N / 2, DN_N);
                 exp_pairs(DN_N / 4, DN_N / 2);
                 lsum = acc_sum();
                 full = __any_sync(0xffffffffu, !(lsum <= 32768.0f));  // NaN included
             }
             if (full) {
                 load_all();
+                apply_lim(0, DN_N);
                 float a0 = __uint_as_float(sr[0]), a1 = __uint_as_float(sr[1]), a2 = __uint_as_float(sr[2]),
                       a3 = __uint_as_float(sr[3]);
 #pragma unroll
@@ -987,7 +1017,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                             dn_tma_store_4d(&tmo, stage + c * (DN_M * 128), c * 32, h, q0t, sq);
                         }
                         asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+                        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
                     }
                 } else if (valid) {
                     float * out = reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 + (int64_t) qi * p.d_nb2 +
@@ -1043,7 +1073,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                     dn_tma_store_4d(&tmo, stage + c * (DN_M * 128), c * 32, h, q0t, sq);
                 }
                 asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+                asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
             }
         } else {
         float * out =
@@ -1094,46 +1124,92 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
 
 // ------------------------------------------------------------------ mask block classes
 
-// One CTA per (kv tile, 256-row query block, mask plane): SKIP if every entry is -inf, NONE if
-// every entry is 0, MIXED otherwise.  Only rows < n_q and columns < n_kv are examined.  With
-// 16-byte aligned rows a row of a full tile is 16 lanes x 8 halves; the bits are tested directly
-// (-inf = 0xFC00; zero = +-0).
+// One CTA per (kv tile, 32 query rows, mask plane), 512 threads = 16 lanes per row: the flags of
+// the 256 x 128 block the rows belong to (BLKF_FINITE: some entry is not -inf, BLKF_NONZERO: some
+// entry is not zero; OR-ed into the block's word, zeroed before the launch) and, per row, the
+// summary that identifies step rows (zeros, then -inf).  Only rows < n_q and columns < n_kv are
+// examined.  With 16-byte aligned rows a lane tests 8 halves directly (-inf = 0xFC00, zero = +-0).
 constexpr int MASK_CLASS_THREADS = 512;
+constexpr int MASK_ROWS          = MASK_CLASS_THREADS / (DN_N / 8);  // 32
 
 __global__ void __launch_bounds__(MASK_CLASS_THREADS)
     mask_block_class_kernel(const char * mask, int64_t nb1, int64_t nb2, int64_t nb3, int m_ne2, int n_q, int n_kv,
-                            int n_qt, int n_kt, int vec, uint8_t * blocks) {
-    const int    kt = blockIdx.x, qt = blockIdx.y, plane = blockIdx.z;
+                            int n_qt, int n_kt, int vec, uint32_t * bflags, int * rowinfo) {
+    const int    kt = blockIdx.x, plane = blockIdx.z;
     const int    i2 = plane % m_ne2, i3 = plane / m_ne2;
-    const int    r0 = qt * DN_ROWS, c0 = kt * DN_N;
-    const int    nr = min(DN_ROWS, n_q - r0), nc = min(DN_N, n_kv - c0);
+    const int    r0 = blockIdx.y * MASK_ROWS, c0 = kt * DN_N;
+    const int    nr = min(MASK_ROWS, n_q - r0), nc = min(DN_N, n_kv - c0);
     const char * base = mask + (int64_t) r0 * nb1 + (int64_t) i2 * nb2 + (int64_t) i3 * nb3 + (int64_t) c0 * 2;
     int          finite = 0, nonzero = 0;
+    // per row of this tile: first -inf column, last zero column, any value that is neither; folded
+    // into the row's summary (zeroed before the launch) with one set of atomics per row and tile
+    auto summarize = [&](int rr, int ninf_first, int zero_last, int other) {
+        int * ri = rowinfo + ((int64_t) plane * n_q + r0 + rr) * 3;
+        if (ninf_first < DN_N) {
+            atomicMax(&ri[0], n_kv - (c0 + ninf_first));
+        }
+        if (zero_last >= 0) {
+            atomicMax(&ri[1], c0 + zero_last + 1);
+        }
+        if (other) {
+            atomicOr(&ri[2], 1);
+        }
+    };
     if (vec && nc == DN_N) {
-        constexpr int LPR = DN_N / 8;  // lanes per row
-        for (int rr = threadIdx.x / LPR; rr < nr; rr += MASK_CLASS_THREADS / LPR) {
-            const uint4    u    = *reinterpret_cast<const uint4 *>(base + (int64_t) rr * nb1 + (threadIdx.x % LPR) * 16);
+        constexpr int LPR = DN_N / 8;  // lanes per row: 16, half a warp
+        const int     rr  = threadIdx.x / LPR, l = threadIdx.x % LPR;
+        if (rr < nr) {  // uniform over the 16 lanes of the row
+            const uint4    u    = *reinterpret_cast<const uint4 *>(base + (int64_t) rr * nb1 + l * 16);
             const uint32_t w[4] = { u.x, u.y, u.z, u.w };
+            int            nf = DN_N, zl = -1, ot = 0;
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 const uint32_t lo = w[j] & 0xFFFFu, hi = w[j] >> 16;
                 finite |= (lo != 0xFC00u) | (hi != 0xFC00u);
                 nonzero |= ((lo & 0x7FFFu) != 0u) | ((hi & 0x7FFFu) != 0u);
+                const int c = l * 8 + 2 * j;
+                if (lo == 0xFC00u) { nf = min(nf, c); }
+                if (hi == 0xFC00u) { nf = min(nf, c + 1); }
+                if ((lo & 0x7FFFu) == 0u) { zl = c; }
+                if ((hi & 0x7FFFu) == 0u) { zl = c + 1; }
+                ot |= (lo != 0xFC00u && (lo & 0x7FFFu) != 0u) | (hi != 0xFC00u && (hi & 0x7FFFu) != 0u);
+            }
+            // the 16 lanes of a row are one half of the warp; the other half may have no row
+            const unsigned hm = (threadIdx.x & 16u) ? 0xFFFF0000u : 0x0000FFFFu;
+#pragma unroll
+            for (int o = 1; o < LPR; o <<= 1) {
+                nf = min(nf, __shfl_xor_sync(hm, nf, o));
+                zl = max(zl, __shfl_xor_sync(hm, zl, o));
+                ot |= __shfl_xor_sync(hm, ot, o);
+            }
+            if (l == 0) {
+                summarize(rr, nf, zl, ot);
             }
         }
-    } else {
-        for (int idx = threadIdx.x; idx < nr * nc; idx += MASK_CLASS_THREADS) {
-            const int   rr = idx / nc, c = idx % nc;
-            const float v  = __half2float(*reinterpret_cast<const __half *>(base + (int64_t) rr * nb1 + (int64_t) c * 2));
+    } else if ((int) threadIdx.x < nr) {  // partial tile or unaligned rows: one thread per row
+        const int rr = threadIdx.x;
+        int       nf = DN_N, zl = -1, ot = 0;
+        for (int c = 0; c < nc; c++) {
+            const float v = __half2float(*reinterpret_cast<const __half *>(base + (int64_t) rr * nb1 + (int64_t) c * 2));
             finite |= v != -INFINITY;
             nonzero |= v != 0.0f;
+            if (v == -INFINITY) {
+                nf = min(nf, c);
+            } else if (v == 0.0f) {
+                zl = c;
+            } else {
+                ot = 1;
+            }
         }
+        summarize(rr, nf, zl, ot);
     }
     finite  = __syncthreads_or(finite);
     nonzero = __syncthreads_or(nonzero);
     if (threadIdx.x == 0) {
-        blocks[((int64_t) plane * n_qt + qt) * n_kt + kt] =
-            (uint8_t) (!finite ? BLK_SKIP : (!nonzero ? BLK_NONE : BLK_MIXED));
+        const uint32_t f = (finite ? BLKF_FINITE : 0u) | (nonzero ? BLKF_NONZERO : 0u);
+        if (f) {
+            atomicOr(&bflags[((int64_t) plane * n_qt + r0 / DN_ROWS) * n_kt + kt], f);
+        }
     }
 }
 
@@ -1177,7 +1253,8 @@ bool dense_eligible(int D, int kvt) {
 
 size_t dense_workspace_bytes(int64_t n_q, int64_t n_kv, int64_t planes) {
     const int64_t n_qt = (n_q + DN_ROWS - 1) / DN_ROWS, n_kt = (n_kv + DN_N - 1) / DN_N;
-    return WS_STATUS_BYTES + (size_t) ((planes * n_qt * n_kt + 255) / 256 * 256);
+    return WS_STATUS_BYTES + (size_t) ((planes * n_qt * n_kt * 4 + 255) / 256 * 256) +
+           (size_t) ((planes * n_q * 12 + 255) / 256 * 256);
 }
 
 cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64_t n_seq_k, int64_t n_head,
@@ -1220,17 +1297,26 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
     p.n_qt    = (int) ((p.n_q + DN_ROWS - 1) / DN_ROWS);
     p.n_kt    = (int) ((p.n_kv + DN_N - 1) / DN_N);
     p.blocks  = nullptr;
+    p.rowinfo = nullptr;
     if (p.mask) {
-        uint8_t * blocks = reinterpret_cast<uint8_t *>(ws + WS_STATUS_BYTES);
-        const int planes = p.m_ne2 * p.m_ne3;
-        mask_block_class_kernel<<<dim3((unsigned) p.n_kt, (unsigned) p.n_qt, (unsigned) planes), MASK_CLASS_THREADS, 0,
+        uint32_t *   blocks = reinterpret_cast<uint32_t *>(ws + WS_STATUS_BYTES);
+        const int    planes = p.m_ne2 * p.m_ne3;
+        const size_t nblk   = (size_t) (((int64_t) planes * p.n_qt * p.n_kt * 4 + 255) / 256 * 256);
+        int *        rinfo  = reinterpret_cast<int *>(ws + WS_STATUS_BYTES + nblk);
+        e = cudaMemsetAsync(blocks, 0, nblk + (size_t) planes * p.n_q * 12, stream);  // flags and row summaries
+        if (e != cudaSuccess) {
+            return e;
+        }
+        const unsigned rgroups = (unsigned) ((p.n_q + MASK_ROWS - 1) / MASK_ROWS);
+        mask_block_class_kernel<<<dim3((unsigned) p.n_kt, rgroups, (unsigned) planes), MASK_CLASS_THREADS, 0,
                                   stream>>>(p.mask, p.m_nb1, p.m_nb2, p.m_nb3, p.m_ne2, p.n_q, p.n_kv, p.n_qt, p.n_kt,
-                                            p.mask_vec, blocks);
+                                            p.mask_vec, blocks, rinfo);
         e = cudaGetLastError();
         if (e != cudaSuccess) {
             return e;
         }
-        p.blocks = blocks;
+        p.blocks  = blocks;
+        p.rowinfo = rinfo;
     }
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) {

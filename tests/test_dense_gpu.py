@@ -132,6 +132,16 @@ def test_softcap_and_alibi(dense, cuda_device):
     check(c, cuda_device)
 
 
+def test_causal_mask_with_some_biased_rows(dense, cuda_device):
+    """Step rows (zeros, then -inf) take a column bound on their mixed tiles; a warp with any other
+    row (here: finite biases in a few rows) takes the general masked pass for the same tile."""
+    c = workloads.prefill_case(n_seq=2, S=300, n_head=8, n_head_kv=2, kv_pos=37, seed=365)
+    m = c.mask.storage  # [S, n_kv_pad] f16, shared by heads and sequences
+    m[40, :20] = 0.5
+    m[290, 5] = -1.25
+    check(c, cuda_device)
+
+
 def test_random_mask_per_head(dense, cuda_device):
     """A non-causal mask with a plane per (head, sequence): random -inf holes, finite biases,
     whole -inf blocks (skipped) and whole zero blocks (no mask arithmetic)."""
