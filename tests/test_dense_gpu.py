@@ -75,6 +75,12 @@ def test_prefill_causal(dense, cuda_device, S, kv_pos):
     check(workloads.prefill_case(n_seq=2, S=S, n_head=8, n_head_kv=2, kv_pos=kv_pos, seed=300 + S), cuda_device)
 
 
+def test_prefill_config4_rows(dense, cuda_device):
+    """benchmark config 4 at full size (2 x 1024 tokens, 32q/8kv, D=128, causal): 256 work items,
+    more than one wave, checked on sampled query rows."""
+    check_rows(workloads.prefill_case(n_seq=2, S=1024, n_head=32, n_head_kv=8, seed=312), cuda_device, n_rows=40)
+
+
 def test_prefill_qwen3_heads(dense, cuda_device):
     """Qwen3-8B geometry (32 q heads over 8 kv heads, D=128), one 512-token prompt chunk."""
     check_rows(workloads.prefill_case(n_seq=1, S=512, n_head=32, n_head_kv=8, seed=310), cuda_device)
