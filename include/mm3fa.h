@@ -170,6 +170,32 @@ MM3FA_API const char * mm3fa_last_cuda_error(void);
 MM3FA_API int mm3fa_version(void);
 
 /*
+ * Fused decode prologue of one LM layer: the nodes the reference builds between the QKV
+ * projection and the attention call, for N sets (CFG sequences) of one decode step:
+ *   q_out        = rope_neox(rms_norm(q_in) * q_norm, pos[s])
+ *   k_cache[s]   row rows[s] = rope_neox(rms_norm(k_in) * k_norm, pos[s])
+ *   v_cache[s]   row rows[s] = v_in
+ * rms_norm over dim 0 with eps; NeoX RoPE over all D dims with base rope_theta (freq_scale 1,
+ * no YaRN); the cache rows are converted like ggml_set_rows (F32 -> F16/BF16 round to
+ * nearest even, or Q8_0 blocks).  The attention call that follows reads q_out as
+ * [D, 1, n_head, N] and the caches as its K/V views.
+ *   q_in     F32 [D, n_head, N], k_in/v_in F32 [D, n_head_kv, N]   (nb[0] = 4)
+ *   q_norm, k_norm   device F32 [D];  eps  the model's rms_norm_eps
+ *   pos      device int32 [N]: RoPE position of set s
+ *   rows     device int64 [N]: destination row of set s (rows outside [0, ne[1]) are not written)
+ *   k_cache, v_cache [D, max_seq, n_head_kv, N] views of the cache slices of the N sets,
+ *            F16, BF16 or Q8_0 (both the same type)
+ *   q_out    F32 [D, n_head, N]
+ * D = 64, 128 or 256.
+ * Replaces: ggml_rms_norm, ggml_mul, ggml_rope_ext, ggml_cont and ggml_set_rows at
+ *           src/qwen3-lm.h:764-800 (computed by the backend at src/static-graph.h:54-57).
+ */
+MM3FA_API int mm3fa_decode_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
+                                    const float * q_norm, const float * k_norm, float eps, const int32_t * pos,
+                                    float rope_theta, const int64_t * rows, mm3fa_tensor * k_cache,
+                                    mm3fa_tensor * v_cache, mm3fa_tensor * q_out, void * stream);
+
+/*
  * Multi-GPU output assembly.  With the kv heads partitioned over G ranks, rank r computes
  * dst_r [Dv, n_head/G, n_q, n_seq] for query heads [r*n_head/G, (r+1)*n_head/G).  After an
  * all-gather (NCCL, by the caller) the blocks sit rank-major as gathered[G][n_seq][n_q]

@@ -19,8 +19,8 @@ LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libmm3fa.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["mm3fa_abi.cu", "fa_decode.cu", "fa_decode_mma.cu", "fa_dense_sm100.cu", "mm3fa_noalloc.cu"]
-HEADERS = ["fa_common.cuh", "fa_decode.cuh", "fa_dense.cuh"]
+SOURCES = ["mm3fa_abi.cu", "fa_decode.cu", "fa_decode_mma.cu", "fa_dense_sm100.cu", "fa_prologue.cu", "mm3fa_noalloc.cu"]
+HEADERS = ["fa_common.cuh", "fa_decode.cuh", "fa_dense.cuh", "fa_prologue.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -1,0 +1,163 @@
+// fa_prologue.cu - fused decode prologue of one LM layer (sm_100a).
+//
+// The graph nodes the reference builds between the QKV projection and the attention call
+// (src/qwen3-lm.h:764-800), one warp per head vector:
+//   q -> ggml_rms_norm(eps) -> ggml_mul(q_norm) -> ggml_rope_ext(NEOX, all D dims) -> q_out
+//   k -> ggml_rms_norm(eps) -> ggml_mul(k_norm) -> ggml_rope_ext(NEOX)     -> ggml_set_rows(k cache)
+//   v                                                                       -> ggml_set_rows(v cache)
+// Lane l holds elements [l*E, l*E + E) of a D = 32*E vector; the NeoX pair (i, i + D/2) of lanes
+// l < 16 sits in lane l + 16 at the same offset, so the rotation is one shuffle.  Arithmetic
+// follows ggml's CPU kernels: the row's mean square, then scale = 1/sqrt(mean + eps), x*scale
+// and then times the weight (two roundings), the angle of pair i as the position times
+// theta_scale^i built by repeated multiplication (theta_scale = theta^(-2/D)), cos/sin of it;
+// the cache rows are rounded to F16/BF16 (nearest even) or quantized to Q8_0 blocks (amax/127
+// scale stored as f16, values round(x / d)).
+#include "fa_prologue.cuh"
+
+namespace mm3fa {
+
+
+constexpr int PRO_WARPS = 4;
+
+template <int E>
+__device__ __forceinline__ void store_cache_row(char * row, int kvt, const float (&y)[E], int lane) {
+    if (kvt == KV_Q8_0) {
+        // a 32-value block spans 32/E lanes
+        constexpr int LPB  = QK8_0 / E;
+        float         amax = 0.0f;
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            amax = fmaxf(amax, fabsf(y[e]));
+        }
+#pragma unroll
+        for (int o = 1; o < LPB; o <<= 1) {
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        }
+        const float d    = amax / 127.0f;
+        const float id   = d != 0.0f ? 1.0f / d : 0.0f;
+        const int   blk  = lane / LPB;
+        char *      bp   = row + blk * Q8_0_BLOCK;
+        const int   off  = (lane % LPB) * E;
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            bp[2 + off + e] = (char) (int8_t) roundf(y[e] * id);
+        }
+        if (lane % LPB == 0) {
+            *reinterpret_cast<__half *>(bp) = __float2half_rn(d);
+        }
+        return;
+    }
+    if (kvt == KV_BF16) {
+        __nv_bfloat16 * r = reinterpret_cast<__nv_bfloat16 *>(row) + lane * E;
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            r[e] = __float2bfloat16_rn(y[e]);
+        }
+        return;
+    }
+    __half * r = reinterpret_cast<__half *>(row) + lane * E;
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+        r[e] = __float2half_rn(y[e]);
+    }
+}
+
+template <int E>
+__global__ void __launch_bounds__(32 * PRO_WARPS) decode_prologue_kernel(const PrologueParams p) {
+    constexpr int D    = 32 * E;
+    const int     lane = threadIdx.x & 31;
+    const int     w    = (int) blockIdx.x * PRO_WARPS + (int) (threadIdx.x >> 5);
+    const int     per  = p.n_head + 2 * p.n_head_kv;  // vectors per set: q heads, k heads, v heads
+    if (w >= per * p.n_set) {
+        return;
+    }
+    const int s = w / per, j = w % per;
+    const int kind = j < p.n_head ? 0 : (j < p.n_head + p.n_head_kv ? 1 : 2);  // 0 q, 1 k, 2 v
+    const int hh   = kind == 0 ? j : (kind == 1 ? j - p.n_head : j - p.n_head - p.n_head_kv);
+    const char * src = kind == 0 ? p.q_in + (int64_t) hh * p.qi_nb1 + (int64_t) s * p.qi_nb2
+                     : kind == 1 ? p.k_in + (int64_t) hh * p.ki_nb1 + (int64_t) s * p.ki_nb2
+                                 : p.v_in + (int64_t) hh * p.vi_nb1 + (int64_t) s * p.vi_nb2;
+    float x[E];
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+        x[e] = reinterpret_cast<const float *>(src)[lane * E + e];
+    }
+    const int64_t r_dst = p.rows[s];
+    if (kind == 2) {  // v: conversion only
+        if (r_dst >= 0 && r_dst < p.v_rows) {
+            char * row = p.v_cache + r_dst * p.vc_nb1 + (int64_t) hh * p.vc_nb2 + (int64_t) s * p.vc_nb3;
+            store_cache_row<E>(row, p.kvt, x, lane);
+        }
+        return;
+    }
+    // ---- RMSNorm over the D values, then the weight
+    float ss = 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+        ss = fmaf(x[e], x[e], ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    }
+    const float   scale = 1.0f / sqrtf(ss / (float) D + p.eps);
+    const float * wn    = kind == 0 ? p.q_norm : p.k_norm;
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+        x[e] = (x[e] * scale) * wn[lane * E + e];
+    }
+    // ---- NeoX RoPE: pair i = lane*E + e (lanes 0-15) with i + D/2 (lane + 16, same e)
+    float y[E];
+    {
+        const int lo = lane & 15;  // pair index base of this lane: lo*E
+        // theta of pair i: position * theta_scale^i, the scale applied i times in turn
+        float th = (float) p.pos[s];
+        for (int k = 0; k < lo * E; k++) {
+            th *= p.theta_scale;
+        }
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            const float c  = cosf(th), sn = sinf(th);
+            const float xo = __shfl_xor_sync(0xffffffffu, x[e], 16);  // the pair's other value
+            // lanes 0-15 hold x0 (first half), lanes 16-31 hold x1 (second half)
+            y[e] = lane < 16 ? x[e] * c - xo * sn : xo * sn + x[e] * c;
+            th *= p.theta_scale;
+        }
+    }
+    if (kind == 0) {
+        float * dst = reinterpret_cast<float *>(p.q_out + (int64_t) hh * p.qo_nb1 + (int64_t) s * p.qo_nb2);
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            dst[lane * E + e] = y[e];
+        }
+        return;
+    }
+    if (r_dst >= 0 && r_dst < p.k_rows) {
+        char * row = p.k_cache + r_dst * p.kc_nb1 + (int64_t) hh * p.kc_nb2 + (int64_t) s * p.kc_nb3;
+        store_cache_row<E>(row, p.kvt, y, lane);
+    }
+}
+
+cudaError_t launch_decode_prologue(const PrologueParams & p, int D, cudaStream_t stream) {
+    const int64_t warps  = (int64_t) p.n_set * (p.n_head + 2 * p.n_head_kv);
+    const int64_t blocks = (warps + PRO_WARPS - 1) / PRO_WARPS;
+    if (blocks <= 0) {
+        return cudaSuccess;
+    }
+    switch (D) {
+        case 64:
+            decode_prologue_kernel<2><<<(unsigned) blocks, 32 * PRO_WARPS, 0, stream>>>(p);
+            break;
+        case 128:
+            decode_prologue_kernel<4><<<(unsigned) blocks, 32 * PRO_WARPS, 0, stream>>>(p);
+            break;
+        case 256:
+            decode_prologue_kernel<8><<<(unsigned) blocks, 32 * PRO_WARPS, 0, stream>>>(p);
+            break;
+        default:
+            return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace mm3fa

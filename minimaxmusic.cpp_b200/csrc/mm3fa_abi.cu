@@ -8,6 +8,7 @@
 #include "fa_common.cuh"
 #include "fa_decode.cuh"
 #include "fa_dense.cuh"
+#include "fa_prologue.cuh"
 
 #include <cuda_runtime.h>
 
@@ -569,6 +570,100 @@ int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const m
             launch_decode_mma(p, g, (int) s.D, s.kvt, s.n_head_kv, s.n_seq_k, cluster, workspace, cs));
     }
     return record_cuda(launch_decode(p, g, (int) s.D, s.kvt, s.bulk, workspace, cs));
+}
+
+int mm3fa_decode_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
+                          const float * q_norm, const float * k_norm, float eps, const int32_t * pos, float rope_theta,
+                          const int64_t * rows, mm3fa_tensor * k_cache, mm3fa_tensor * v_cache, mm3fa_tensor * q_out,
+                          void * stream) {
+    if (!q_in || !k_in || !v_in || !k_cache || !v_cache || !q_out || !q_norm || !k_norm || !pos || !rows) {
+        return MM3FA_ERR_NULL;
+    }
+    for (const mm3fa_tensor * t : { q_in, k_in, v_in, (const mm3fa_tensor *) k_cache, (const mm3fa_tensor *) v_cache,
+                                    (const mm3fa_tensor *) q_out }) {
+        if (!t->data) {
+            return MM3FA_ERR_NULL;
+        }
+    }
+    if (q_in->type != MM3FA_TYPE_F32 || k_in->type != MM3FA_TYPE_F32 || v_in->type != MM3FA_TYPE_F32 ||
+        q_out->type != MM3FA_TYPE_F32) {
+        return MM3FA_ERR_TYPE;
+    }
+    const int kvt = k_cache->type;
+    if ((kvt != MM3FA_TYPE_F16 && kvt != MM3FA_TYPE_BF16 && kvt != MM3FA_TYPE_Q8_0) || v_cache->type != kvt) {
+        return MM3FA_ERR_TYPE;
+    }
+    const int64_t D = q_in->ne[0], H = q_in->ne[1], N = q_in->ne[2], Hkv = k_in->ne[1];
+    if (D != 64 && D != 128 && D != 256) {
+        return MM3FA_ERR_UNSUPPORTED;
+    }
+    if (H <= 0 || Hkv <= 0 || N <= 0 || q_in->ne[3] != 1 || k_in->ne[0] != D || k_in->ne[2] != N ||
+        v_in->ne[0] != D || v_in->ne[1] != Hkv || v_in->ne[2] != N || q_out->ne[0] != D || q_out->ne[1] != H ||
+        q_out->ne[2] != N) {
+        return MM3FA_ERR_SHAPE;
+    }
+    for (const mm3fa_tensor * c : { (const mm3fa_tensor *) k_cache, (const mm3fa_tensor *) v_cache }) {
+        if (c->ne[0] != D || c->ne[1] < 1 || c->ne[2] != Hkv || c->ne[3] != N) {
+            return MM3FA_ERR_SHAPE;
+        }
+    }
+    if (H > 65535 || Hkv > 65535 || N > 65535 || H % Hkv != 0) {
+        return MM3FA_ERR_UNSUPPORTED;
+    }
+    // rows packed, strides multiples of the element (block) size, F32 data 4-byte aligned
+    const int64_t ce = type_unit_bytes(kvt);
+    for (const mm3fa_tensor * t : { q_in, k_in, v_in, (const mm3fa_tensor *) q_out }) {
+        if (t->nb[0] != 4 || t->nb[1] % 4 || t->nb[2] % 4 || (int64_t) t->nb[1] < 4 * D ||
+            !aligned(t->data, 4)) {
+            return MM3FA_ERR_STRIDE;
+        }
+    }
+    for (const mm3fa_tensor * c : { (const mm3fa_tensor *) k_cache, (const mm3fa_tensor *) v_cache }) {
+        if ((int64_t) c->nb[0] != ce || (int64_t) c->nb[1] < row_bytes(kvt, D) || c->nb[1] % 2 || c->nb[2] % 2 ||
+            c->nb[3] % 2 || !aligned(c->data, 2)) {
+            return MM3FA_ERR_STRIDE;
+        }
+    }
+    if (!(eps >= 0.0f) || !std::isfinite(rope_theta) || !(rope_theta > 0.0f)) {
+        return MM3FA_ERR_SHAPE;
+    }
+    if (device_info().major != 10) {
+        return MM3FA_ERR_DEVICE;
+    }
+    PrologueParams p{};
+    p.q_in        = static_cast<const char *>(q_in->data);
+    p.k_in        = static_cast<const char *>(k_in->data);
+    p.v_in        = static_cast<const char *>(v_in->data);
+    p.q_norm      = q_norm;
+    p.k_norm      = k_norm;
+    p.pos         = pos;
+    p.rows        = rows;
+    p.q_out       = static_cast<char *>(q_out->data);
+    p.k_cache     = static_cast<char *>(k_cache->data);
+    p.v_cache     = static_cast<char *>(v_cache->data);
+    p.qi_nb1      = (int64_t) q_in->nb[1];
+    p.qi_nb2      = (int64_t) q_in->nb[2];
+    p.ki_nb1      = (int64_t) k_in->nb[1];
+    p.ki_nb2      = (int64_t) k_in->nb[2];
+    p.vi_nb1      = (int64_t) v_in->nb[1];
+    p.vi_nb2      = (int64_t) v_in->nb[2];
+    p.qo_nb1      = (int64_t) q_out->nb[1];
+    p.qo_nb2      = (int64_t) q_out->nb[2];
+    p.kc_nb1      = (int64_t) k_cache->nb[1];
+    p.kc_nb2      = (int64_t) k_cache->nb[2];
+    p.kc_nb3      = (int64_t) k_cache->nb[3];
+    p.vc_nb1      = (int64_t) v_cache->nb[1];
+    p.vc_nb2      = (int64_t) v_cache->nb[2];
+    p.vc_nb3      = (int64_t) v_cache->nb[3];
+    p.kvt         = kvt;
+    p.n_head      = (int) H;
+    p.n_head_kv   = (int) Hkv;
+    p.n_set       = (int) N;
+    p.k_rows      = k_cache->ne[1];
+    p.v_rows      = v_cache->ne[1];
+    p.eps         = eps;
+    p.theta_scale = std::pow(rope_theta, -2.0f / (float) D);
+    return record_cuda(launch_decode_prologue(p, (int) D, static_cast<cudaStream_t>(stream)));
 }
 
 int mm3fa_assemble_heads(const float * gathered, float * dst, int64_t dv, int64_t n_head, int64_t n_q, int64_t n_seq,

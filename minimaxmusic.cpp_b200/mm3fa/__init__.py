@@ -76,6 +76,10 @@ def lib():
         L.mm3fa_flash_attn_ext_noalloc.argtypes = [P, P, P, P, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                                    ctypes.c_int, P, ctypes.c_void_p]
         L.mm3fa_flash_attn_ext_noalloc.restype = ctypes.c_int
+        L.mm3fa_decode_prologue.argtypes = [P, P, P, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float,
+                                            ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p, P, P, P,
+                                            ctypes.c_void_p]
+        L.mm3fa_decode_prologue.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -134,6 +138,19 @@ def flash_attn_ext_noalloc(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None,
                                             prec, _ref(dst), ctypes.c_void_p(stream or None))
     if st != OK:
         raise MM3FAError(st, "mm3fa_flash_attn_ext_noalloc")
+
+
+def decode_prologue(q_in: Tensor, k_in: Tensor, v_in: Tensor, q_norm_ptr: int, k_norm_ptr: int, eps: float,
+                    pos_ptr: int, rope_theta: float, rows_ptr: int, k_cache: Tensor, v_cache: Tensor, q_out: Tensor,
+                    stream: int = 0) -> None:
+    """Fused decode prologue (RMSNorm + NeoX RoPE of q and k, append of the new k/v rows into the caches);
+    pointers are device addresses (q_norm/k_norm F32 [D], pos int32 [N], rows int64 [N])."""
+    st = lib().mm3fa_decode_prologue(_ref(q_in), _ref(k_in), _ref(v_in), ctypes.c_void_p(q_norm_ptr),
+                                     ctypes.c_void_p(k_norm_ptr), eps, ctypes.c_void_p(pos_ptr), rope_theta,
+                                     ctypes.c_void_p(rows_ptr), _ref(k_cache), _ref(v_cache), _ref(q_out),
+                                     ctypes.c_void_p(stream or None))
+    if st != OK:
+        raise MM3FAError(st, "mm3fa_decode_prologue")
 
 
 def assemble_heads(gathered_ptr: int, dst_ptr: int, dv: int, n_head: int, n_q: int, n_seq: int, n_ranks: int,

@@ -92,6 +92,56 @@ def q8_0_dequantize(b: np.ndarray) -> np.ndarray:
     return out
 
 
+# ---------------------------------------------------------------- decode prologue
+# The nodes src/qwen3-lm.h:764-800 builds before the attention call, restated from ggml's CPU
+# kernels (ggml is an absent submodule of the reference; these follow ggml's published
+# ggml-cpu ops: rms_norm_f32, mul, rope_f32 in NEOX mode with its rope cache, set_rows):
+#   * rms_norm: sum of squares accumulated in double, mean = sum / D rounded to float,
+#     scale = 1 / sqrtf(mean + eps), y = x * scale (float); ggml_mul then y * w (float).
+#   * rope NEOX (freq_scale 1, ext_factor 0, attn_factor 1, all D dims): theta_scale =
+#     powf(theta, -2/D); the cache walks pairs i = 0 .. D/2-1 with angle t (starting at the
+#     position) and t *= theta_scale after each pair; out[i] = x[i] cos t - x[i + D/2] sin t,
+#     out[i + D/2] = x[i] sin t + x[i + D/2] cos t.
+#   * set_rows: F32 -> F16 / BF16 (round to nearest even) or Q8_0 (the block quantizer above).
+
+def rms_norm_mul(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """ggml_rms_norm over the last axis, then ggml_mul by w (float32 results)."""
+    x = np.asarray(x, dtype=np.float32)
+    mean = ((x.astype(np.float64) ** 2).sum(-1, keepdims=True) / x.shape[-1]).astype(np.float32)
+    scale = (np.float32(1.0) / np.sqrt(mean + np.float32(eps))).astype(np.float32)
+    return ((x * scale).astype(np.float32) * np.asarray(w, dtype=np.float32)).astype(np.float32)
+
+
+def rope_neox(x: np.ndarray, pos: np.ndarray, theta: float) -> np.ndarray:
+    """ggml_rope_ext in NEOX mode over all D dims; x [N, H, D], pos [N] (int)."""
+    x = np.asarray(x, dtype=np.float32)
+    n, _, d = x.shape
+    half = d // 2
+    ts = np.float32(np.power(np.float32(theta), np.float32(-2.0) / np.float32(d)))
+    out = np.empty_like(x)
+    for s in range(n):
+        t = np.float32(pos[s])
+        cs = np.empty(half, dtype=np.float32)
+        sn = np.empty(half, dtype=np.float32)
+        for i in range(half):
+            cs[i] = np.cos(t)
+            sn[i] = np.sin(t)
+            t = np.float32(t * ts)
+        x0, x1 = x[s, :, :half], x[s, :, half:]
+        out[s, :, :half] = (x0 * cs - x1 * sn).astype(np.float32)
+        out[s, :, half:] = (x0 * sn + x1 * cs).astype(np.float32)
+    return out
+
+
+def decode_prologue(q_in: np.ndarray, k_in: np.ndarray, v_in: np.ndarray, q_norm: np.ndarray, k_norm: np.ndarray,
+                    eps: float, pos: np.ndarray, theta: float) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """(q_out, k_new, v_new) in F32: q_in [N, H, D], k_in/v_in [N, Hkv, D]; the caller converts
+    k_new / v_new to the cache type (f32_to_f16_bits, q8_0_quantize) as set_rows does."""
+    q = rope_neox(rms_norm_mul(q_in, q_norm, eps), pos, theta)
+    k = rope_neox(rms_norm_mul(k_in, k_norm, eps), pos, theta)
+    return q, k, np.asarray(v_in, dtype=np.float32)
+
+
 def alibi_slope(h: int, n_head: int, max_bias: float) -> float:
     return float(lib().orc_alibi_slope(h, n_head, max_bias))
 

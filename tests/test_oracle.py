@@ -189,3 +189,23 @@ def test_oracle_reproduces_golden(path):
     assert np.array_equal(oracle.flash_attn_ext(*args, mode=oracle.MODE_GGML, threads=1), z["out_ggml"])
     if "out_torch" in z:
         np.testing.assert_allclose(z["out_exact"], z["out_torch"], atol=1e-6, rtol=0)
+
+
+def test_prologue_restatement_against_float64():
+    """The decode-prologue restatement (rms_norm * w, NEOX rope) against float64 formulas; at small
+    positions the float32 angle walk is exact to a few ulps."""
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((2, 3, 128)).astype(np.float32) * 2
+    w = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    y = oracle.rms_norm_mul(x, w, 1e-6)
+    ref = x / np.sqrt((x.astype(np.float64) ** 2).mean(-1, keepdims=True) + 1e-6) * w
+    assert np.abs(y - ref).max() <= 2e-6
+    pos = np.array([0, 37])
+    r = oracle.rope_neox(y, pos, 1e6)
+    ts = 1e6 ** (-2 / 128)
+    th = pos[:, None] * ts ** np.arange(64)
+    c, s = np.cos(th)[:, None], np.sin(th)[:, None]
+    ref2 = np.concatenate([y[..., :64] * c - y[..., 64:] * s, y[..., :64] * s + y[..., 64:] * c], -1)
+    assert np.abs(r - ref2).max() <= 2e-5
+    # position 0 is the identity
+    assert np.array_equal(r[0], y[0])
