@@ -374,6 +374,90 @@ def bench_q8(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, world: in
                                      "head_dim": D, "l2": "inputs > L2"}}}
 
 
+def bench_decode_step(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, world: int, n_layers: int) -> dict:
+    """Decode step with the fused prologue (the nodes of src/qwen3-lm.h:764-820 from the QKV projection
+    output on): per layer mm3fa_decode_prologue (RMSNorm + NeoX RoPE of q/k, k/v rows appended to the
+    F16 caches at row 8191) then the attention over the 8192-row views, 36 layers in one CUDA graph;
+    also the prologue alone.  Shapes of the headline (per rank: its kv-head shard of a CFG pair)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(55)
+    n_seq, hkv, hq = 2, N_HEAD_KV // world, N_HEAD // world
+    row = N_KV - 1
+    keep, layers = [], []
+    mask = torch.zeros(n_seq, 1, 1, N_KV, dtype=torch.float16, device=dev)
+    qn = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).float()
+    kn = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).float()
+    pos = torch.full((n_seq,), row, dtype=torch.int32, device=dev)
+    rows = torch.full((n_seq,), row, dtype=torch.int64, device=dev)
+    rb = 2 * D
+    cnb = [2, rb, rb * MAX_SEQ, rb * MAX_SEQ * hkv]
+    F32, F16 = ggml.GGML_TYPE_F32, ggml.GGML_TYPE_F16
+    for _ in range(n_layers):
+        kc = (torch.randn(n_seq, hkv, MAX_SEQ, D, generator=g, device=dev) * 0.5).half()
+        vc = (torch.randn(n_seq, hkv, MAX_SEQ, D, generator=g, device=dev) * 0.5).half()
+        q_in = torch.randn(n_seq, hq, D, generator=g, device=dev)
+        k_in = torch.randn(n_seq, hkv, D, generator=g, device=dev)
+        v_in = torch.randn(n_seq, hkv, D, generator=g, device=dev)
+        q = torch.empty(n_seq, hq, D, device=dev)
+        o = torch.empty(n_seq, 1, hq, D, device=dev)
+        keep += [kc, vc, q_in, k_in, v_in, q, o]
+        layers.append(dict(
+            q_in=ggml.make(F32, [D, hq, n_seq, 1], q_in.data_ptr()), k_in=ggml.make(F32, [D, hkv, n_seq, 1], k_in.data_ptr()),
+            v_in=ggml.make(F32, [D, hkv, n_seq, 1], v_in.data_ptr()),
+            kc=ggml.make(F16, [D, MAX_SEQ, hkv, n_seq], kc.data_ptr(), cnb),
+            vc=ggml.make(F16, [D, MAX_SEQ, hkv, n_seq], vc.data_ptr(), list(cnb)),
+            q_out=ggml.make(F32, [D, hq, n_seq, 1], q.data_ptr()), q4=ggml.make(F32, [D, 1, hq, n_seq], q.data_ptr()),
+            k=ggml.make(F16, [D, N_KV, hkv, n_seq], kc.data_ptr(), cnb),
+            v=ggml.make(F16, [D, N_KV, hkv, n_seq], vc.data_ptr(), list(cnb)),
+            m=ggml.make(F16, [N_KV, 1, 1, n_seq], mask.data_ptr()), o=ggml.make(F32, [D, hq, 1, n_seq], o.data_ptr())))
+    l0 = layers[0]
+    need = mm3fa.workspace_size(l0["q4"], l0["k"], l0["v"], l0["m"], l0["o"])
+    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
+    scale = 1.0 / math.sqrt(D)
+
+    def prologue(L):
+        mm3fa.decode_prologue(L["q_in"], L["k_in"], L["v_in"], qn.data_ptr(), kn.data_ptr(), 1e-6, pos.data_ptr(),
+                              1e6, rows.data_ptr(), L["kc"], L["vc"], L["q_out"], stream.cuda_stream)
+
+    def attention(L):
+        mm3fa.flash_attn_ext(L["q4"], L["k"], L["v"], L["m"], scale, 0.0, 0.0, L["o"], ws.data_ptr(), ws.numel(),
+                             stream.cuda_stream)
+
+    def timed(fn):
+        with torch.cuda.stream(stream):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            fn()
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        stream.record_event(e0)
+        with torch.cuda.stream(stream):
+            for _ in range(steps):
+                graph.replay()
+        stream.record_event(e1)
+        torch.cuda.synchronize()
+        del graph
+        return e0.elapsed_time(e1) * 1e3 / steps / n_layers
+
+    def step():
+        for L in layers:
+            prologue(L)
+            attention(L)
+
+    us_step = timed(step)
+    us_pro = timed(lambda: [prologue(L) for L in layers])
+    return {"decode_step": {"us_per_layer": round(us_step, 3), "prologue_us_per_layer": round(us_pro, 3),
+                            "config": {"workload": "decode step from the QKV projection output: fused prologue "
+                                                   "(QK-RMSNorm, NeoX RoPE theta 1e6, k/v append at row 8191) + "
+                                                   f"attention over KV 8192, {n_layers} layers per CUDA graph",
+                                       "n_seq": n_seq, "n_head": hq, "n_head_kv": hkv, "head_dim": D}}}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -384,6 +468,7 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-dense", action="store_true", help="skip the DiT / prefill (tensor-core) lines")
     ap.add_argument("--no-q8", action="store_true", help="skip the Q8_0 KV-cache decode line (config 3)")
+    ap.add_argument("--no-step", action="store_true", help="skip the decode-step line (fused prologue + attention)")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers per step (36 = the LM; fewer only for small ncu captures)")
     args = ap.parse_args()
@@ -552,6 +637,10 @@ def main() -> None:
     q8 = None if args.no_q8 else bench_q8(torch, mm3fa, ggml, dev, stream, args.steps, args.warmup, world, n_layers)
     if q8 is not None and world > 1:
         dist.barrier()
+    dstep = None if args.no_step else bench_decode_step(torch, mm3fa, ggml, dev, stream, args.steps, args.warmup, world,
+                                                        n_layers)
+    if dstep is not None and world > 1:
+        dist.barrier()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -583,6 +672,8 @@ def main() -> None:
             line.update(dense)
         if q8 is not None:
             line.update(q8)
+        if dstep is not None:
+            line.update(dstep)
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
