@@ -108,6 +108,21 @@ MM3FA_API int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * 
                          mm3fa_tensor * dst, void * workspace, size_t workspace_bytes, void * stream);
 
 /*
+ * mm3fa_flash_attn_ext with the key range of each query sequence given on the device:
+ * q sequence s sees keys [0, kv_len[s]) (clamped to [0, n_kv]); keys past it count as -inf, on
+ * top of `mask` (which may be NULL).  kv_len: device int32 [n_seq].  Equal to passing the mask
+ * the reference builds on the host every decode step (0 below kv_pos + 1, -inf from it on,
+ * src/qwen3-lm.h:909-920), without building or copying it; with the cluster split (the CFG
+ * decode shapes) the keys past kv_len are not read at all.  Uses the decode kernels for any
+ * number of query rows; same workspace as mm3fa_flash_attn_ext.
+ * Replaces: the host mask loop and its upload at src/qwen3-lm.h:909-920, and the attention node.
+ */
+MM3FA_API int mm3fa_flash_attn_ext_kvlen(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                                         const mm3fa_tensor * mask, const int32_t * kv_len, float scale,
+                                         float max_bias, float logit_softcap, int prec, mm3fa_tensor * dst,
+                                         void * workspace, size_t workspace_bytes, void * stream);
+
+/*
  * mm3fa_flash_attn_ext for callers that cannot allocate device memory: the same computation,
  * but the split-KV scratch comes from a buffer of MM3FA_NOALLOC_SCRATCH_BYTES built into the
  * library (one per GPU that loads it, held until the process exits) instead of a workspace

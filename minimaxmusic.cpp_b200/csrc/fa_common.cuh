@@ -107,6 +107,11 @@ __device__ __forceinline__ float2 bf2_to_f2(uint32_t u) {
     return __bfloat1622float2(h);
 }
 
+// Keys of q sequence s that are visible: kv_len[s] clamped to [0, n_kv], or n_kv without kv_len.
+__device__ __forceinline__ int seq_kv_len(const int * kv_len, int s, int n_kv) {
+    return kv_len ? min(max(kv_len[s], 0), n_kv) : n_kv;
+}
+
 // ALiBi slope of query head h; 1 when max_bias == 0.
 __device__ __forceinline__ float alibi_slope(int h, float max_bias, int n_head_log2, float m0, float m1) {
     if (max_bias <= 0.0f) {
@@ -149,6 +154,7 @@ struct DecodeParams {
     int          cluster;        // CTAs per thread-block cluster (tensor-core cluster mode)
     int          dst_vec;        // dst rows start 16-byte aligned: 16-byte stores
     int          mask_tma;       // mask rows staged by TMA with K/V (cluster mode)
+    const int *  kv_len;         // device [n_seq]: q sequence s sees keys [0, kv_len[s]) (null: all)
     // workspace
     uint32_t *   status;
     uint32_t *   counters;

@@ -179,6 +179,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) fa_decode_kernel(const DecodeP
     int       seg_j1    = 0;
     int       stage_idx = 0;
     bool      aborted   = false;
+    int       u_kvl     = p.n_kv;  // keys of the current unit's sequence that are visible
 
     // ---- unit begin: stage Q (rounded to K's convention), row metadata, reset state
     auto begin_unit = [&](int64_t unit) {
@@ -187,6 +188,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) fa_decode_kernel(const DecodeP
         const int     g    = (int) (sg % p.n_head_kv);
         const int     s    = (int) (sg / p.n_head_kv);
         nrow               = min(RU, p.rows_per_pair - rgrp * DEC_RMAX);
+        u_kvl              = seq_kv_len(p.kv_len, s, p.n_kv);
         for (int idx = tid; idx < nrow * D; idx += DEC_THREADS) {
             const int r  = idx / D;
             const int e  = idx % D;
@@ -471,7 +473,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) fa_decode_kernel(const DecodeP
 #pragma unroll
             for (int t = 0; t < C / 32; t++) {
                 const int j = lane + 32 * t;
-                sv_[t]      = j < n ? sS[r * C + j] : -INFINITY;
+                sv_[t]      = (j < n && j0 + j < u_kvl) ? sS[r * C + j] : -INFINITY;
                 mx          = fmaxf(mx, sv_[t]);
             }
 #pragma unroll

@@ -291,6 +291,12 @@ __device__ __forceinline__ uint32_t swz(int j, int c) {
     return (uint32_t) (j * 128 + ((c ^ (j & 7)) << 4));
 }
 
+// Visible keys of a unit (its q sequence's kv_len, or n_kv).
+__device__ __forceinline__ int unit_kv_len(const DecodeParams & p, int64_t unit) {
+    const int sq = (int) ((unit / p.groups) / p.n_head_kv);
+    return seq_kv_len(p.kv_len, sq, p.n_kv);
+}
+
 // ------------------------------------------------------------------ kernel
 
 // CLUSTER = false: the stream-K split of fa_decode.cu (partials merged through the workspace).
@@ -366,8 +372,9 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
     // ================================================================ producer warp
     if (warp == MMA_CONSUMERS) {
         if (lane == 0) {
+            // cluster mode streams only the unit's visible keys (kv_len); stream-K masks them instead
             StageIter it = CLUSTER ? StageIter((int64_t) (blockIdx.x / p.cluster), (int) (blockIdx.x % p.cluster) * CK,
-                                          p.cluster * CK, p.n_kv, CK)
+                                          p.cluster * CK, unit_kv_len(p, blockIdx.x / p.cluster), CK)
                                 : StageIter(g0, g1, p.n_kv, CK);
             int        s = 0;
             bool       ok = true;
@@ -394,9 +401,13 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                 // of CK keys, zero-filled past n_kv
                 const uint32_t mbytes = p.mask_tma ? (uint32_t) L::MASKB : 0u;
                 if constexpr (Q8) {
-                    // n whole rows of K and of V; j0 * RB and n * RB are multiples of 16 (the
-                    // host only picks this kernel for packed rows and 16-byte aligned slabs)
-                    const uint32_t bytes = (uint32_t) (n * L::RB);
+                    // whole rows of K and of V; j0 * RB is a multiple of 16, and the row count is
+                    // rounded up to KA rows (n * RB a multiple of 16, as bulk copies need) - a
+                    // kv_len can end a chunk anywhere, but the view's n_kv is a multiple of KA
+                    // (checked on the host), so the rounded rows stay inside it
+                    constexpr int  KA    = (L::RB % 16 == 0) ? 1 : ((L::RB % 8 == 0) ? 2 : ((L::RB % 4 == 0) ? 4 : 8));
+                    const int      nc    = min((n + KA - 1) / KA * KA, p.n_kv - j0);
+                    const uint32_t bytes = (uint32_t) (nc * L::RB);
                     const char *   sk = p.k + (int64_t) g * p.k_nb2 + (int64_t) ks3 * p.k_nb3 + (int64_t) j0 * L::RB;
                     const char *   sv = p.v + (int64_t) g * p.v_nb2 + (int64_t) ks3 * p.v_nb3 + (int64_t) j0 * L::RB;
                     mbar_arrive_expect_tx(&full[slot], 2 * bytes + mbytes);
@@ -453,6 +464,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
     int     nrow     = 0;
     int     seg_j0 = 0, seg_j1 = 0;
     int     u_rgrp = 0, u_g = 0, u_sq = 0;  // the current unit's row group, kv head, q sequence
+    int     u_kvl  = p.n_kv;                // the current unit's visible keys
     bool    aborted  = false;
 
     // mask values [sub-tile][nt][row 2*q4 + e][key 16u + g4 + 8*kh]
@@ -499,6 +511,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
         u_rgrp             = rgrp;
         u_g                = g;
         u_sq               = sq;
+        u_kvl              = seq_kv_len(p.kv_len, sq, p.n_kv);
         nrow               = min(p.rows_per_unit, p.rows_per_pair - rgrp * MMA_RMAX);
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
@@ -848,7 +861,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
         begin_unit(cur_unit);
     }
     StageIter it = CLUSTER ? StageIter((int64_t) (blockIdx.x / p.cluster), (int) (blockIdx.x % p.cluster) * CK,
-                                          p.cluster * CK, p.n_kv, CK)
+                                          p.cluster * CK, unit_kv_len(p, blockIdx.x / p.cluster), CK)
                                 : StageIter(g0, g1, p.n_kv, CK);
     int        s = 0;
     while (it.has()) {
@@ -984,7 +997,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                                 v = p.softcap * tanhf(v / p.softcap);
                             }
                             v += slope[nt][re] * mk_cur[u][nt][re][kh];
-                            x[u][e] = j < n ? v * LOG2E : -INFINITY;
+                            x[u][e] = (j < n && j0 + j < u_kvl) ? v * LOG2E : -INFINITY;
                         }
                     }
                     float mx0 = fmaxf(x[0][0], x[0][2]), mx1 = fmaxf(x[0][1], x[0][3]);
@@ -1129,7 +1142,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                             v = p.softcap * tanhf(v / p.softcap);
                         }
                         v += slope[nt][re] * mk_cur[0][nt][re][kh];
-                        x[e] = j < n ? v * LOG2E : -INFINITY;
+                        x[e] = (j < n && j0 + j < u_kvl) ? v * LOG2E : -INFINITY;
                     }
                     float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
 #pragma unroll

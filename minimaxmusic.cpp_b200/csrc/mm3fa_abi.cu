@@ -487,9 +487,16 @@ size_t mm3fa_workspace_size(const mm3fa_tensor * q, const mm3fa_tensor * k, cons
     return need;
 }
 
-int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
-                         const mm3fa_tensor * mask, float scale, float max_bias, float logit_softcap, int prec,
-                         mm3fa_tensor * dst, void * workspace, size_t workspace_bytes, void * stream) {
+}  // extern "C"
+
+namespace {
+
+// The operator with an optional device array of per-sequence key counts (kv_len[s]: q sequence
+// s sees keys [0, kv_len[s]) only, in addition to the mask).  With kv_len the decode kernels run
+// whatever the row count: they skip (cluster split) or mask (stream-K split) the keys past it.
+int flash_attn_impl(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v, const mm3fa_tensor * mask,
+                    const int32_t * kv_len, float scale, float max_bias, float logit_softcap, int prec,
+                    mm3fa_tensor * dst, void * workspace, size_t workspace_bytes, void * stream) {
     if (prec != MM3FA_PREC_DEFAULT && prec != MM3FA_PREC_F32) {
         return MM3FA_ERR_UNSUPPORTED;
     }
@@ -511,7 +518,7 @@ int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const m
                                               (int64_t) dst->nb[1], (int64_t) dst->nb[2], (int64_t) dst->nb[3]);
         return record_cuda(cudaGetLastError());
     }
-    if (use_dense(s, mask)) {
+    if (!kv_len && use_dense(s, mask)) {
         return run_dense(s, q, k, v, mask, scale, max_bias, logit_softcap, dst, workspace, workspace_bytes,
                          wait_timeout_ns(), cs);
     }
@@ -561,6 +568,7 @@ int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const m
     p.m1        = std::pow(2.0f, -max_bias / 2.0f / (float) n_head_log2);
     p.timeout_ns = wait_timeout_ns();
     p.dst_vec    = rows_vec16(dst);
+    p.kv_len     = kv_len;
     if (var >= V_MMA_8) {
         const int pref    = decode_mma_mode_preference();
         const int cluster = pref == 1 ? 0
@@ -570,6 +578,28 @@ int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const m
             launch_decode_mma(p, g, (int) s.D, s.kvt, s.n_head_kv, s.n_seq_k, cluster, workspace, cs));
     }
     return record_cuda(launch_decode(p, g, (int) s.D, s.kvt, s.bulk, workspace, cs));
+}
+
+}  // namespace
+
+extern "C" {
+
+int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                         const mm3fa_tensor * mask, float scale, float max_bias, float logit_softcap, int prec,
+                         mm3fa_tensor * dst, void * workspace, size_t workspace_bytes, void * stream) {
+    return flash_attn_impl(q, k, v, mask, nullptr, scale, max_bias, logit_softcap, prec, dst, workspace,
+                           workspace_bytes, stream);
+}
+
+int mm3fa_flash_attn_ext_kvlen(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                               const mm3fa_tensor * mask, const int32_t * kv_len, float scale, float max_bias,
+                               float logit_softcap, int prec, mm3fa_tensor * dst, void * workspace,
+                               size_t workspace_bytes, void * stream) {
+    if (!kv_len) {
+        return MM3FA_ERR_NULL;
+    }
+    return flash_attn_impl(q, k, v, mask, kv_len, scale, max_bias, logit_softcap, prec, dst, workspace,
+                           workspace_bytes, stream);
 }
 
 int mm3fa_decode_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,

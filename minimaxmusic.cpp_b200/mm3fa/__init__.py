@@ -80,6 +80,10 @@ def lib():
                                             ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p, P, P, P,
                                             ctypes.c_void_p]
         L.mm3fa_decode_prologue.restype = ctypes.c_int
+        L.mm3fa_flash_attn_ext_kvlen.argtypes = [P, P, P, P, ctypes.c_void_p, ctypes.c_float, ctypes.c_float,
+                                                 ctypes.c_float, ctypes.c_int, P, ctypes.c_void_p, ctypes.c_size_t,
+                                                 ctypes.c_void_p]
+        L.mm3fa_flash_attn_ext_kvlen.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -138,6 +142,17 @@ def flash_attn_ext_noalloc(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None,
                                             prec, _ref(dst), ctypes.c_void_p(stream or None))
     if st != OK:
         raise MM3FAError(st, "mm3fa_flash_attn_ext_noalloc")
+
+
+def flash_attn_ext_kvlen(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None, kv_len_ptr: int, scale: float,
+                         max_bias: float, logit_softcap: float, dst: Tensor, workspace: int, workspace_bytes: int,
+                         stream: int = 0, prec: int = GGML_PREC_F32) -> None:
+    """flash_attn_ext where q sequence s sees keys [0, kv_len[s]) (kv_len: device int32 [n_seq])."""
+    st = lib().mm3fa_flash_attn_ext_kvlen(_ref(q), _ref(k), _ref(v), _ref(mask), ctypes.c_void_p(kv_len_ptr), scale,
+                                          max_bias, logit_softcap, prec, _ref(dst), ctypes.c_void_p(workspace or None),
+                                          workspace_bytes, ctypes.c_void_p(stream or None))
+    if st != OK:
+        raise MM3FAError(st, "mm3fa_flash_attn_ext_kvlen")
 
 
 def decode_prologue(q_in: Tensor, k_in: Tensor, v_in: Tensor, q_norm_ptr: int, k_norm_ptr: int, eps: float,

@@ -222,3 +222,62 @@ def test_assemble_heads_matches_numpy(cuda_device):
     mm3fa.assemble_heads(g.data_ptr(), out.data_ptr(), Dv, H, n_q, n_seq, G, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     assert np.array_equal(out.cpu().numpy(), assemble_heads_np(g.cpu().numpy(), G))
+
+
+# ---------------------------------------------------------------- device kv_len (no host mask)
+
+def run_gpu_kvlen(c, dev, kv_len, with_mask=False):
+    """mm3fa_flash_attn_ext_kvlen on case c: keys past kv_len[s] are invisible to q sequence s."""
+    from gpu_util import to_device
+    tensors = {n: to_device(getattr(c, n), dev) for n in ("q", "k", "v", "mask") if getattr(c, n) is not None}
+    descs = {n: getattr(c, n).device_desc(t) for n, t in tensors.items()}
+    out = torch.full(c.dst_shape(), float("nan"), dtype=torch.float32, device=dev)
+    dst = mm3fa.dst_desc(descs["q"], descs["v"], out.data_ptr())
+    kl = torch.tensor(kv_len, dtype=torch.int32, device=dev)
+    md = descs.get("mask") if with_mask else None
+    need = mm3fa.workspace_size(descs["q"], descs["k"], descs["v"], md, dst)
+    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
+    mm3fa.flash_attn_ext_kvlen(descs["q"], descs["k"], descs["v"], md, kl.data_ptr(), c.scale, c.max_bias, c.softcap,
+                               dst, ws.data_ptr(), ws.numel(), torch.cuda.current_stream(dev).cuda_stream)
+    torch.cuda.synchronize(dev)
+    return out.cpu().numpy()
+
+
+def length_mask_case(c, kv_len):
+    """The same case with the reference's host-built length mask (src/qwen3-lm.h:909-920)."""
+    n_kv, n_q, n_seq = c.k.ne[1], c.q.ne[1], c.q.ne[3]
+    m = np.zeros((n_seq, 1, n_q, n_kv), dtype=np.float16)
+    for s in range(n_seq):
+        m[s, 0, :, max(0, min(kv_len[s], n_kv)):] = -np.inf
+    c.mask = workloads.Operand(m, F16, [n_kv, n_q, 1, n_seq], ggml.contiguous_nb(F16, [n_kv, n_q, 1, n_seq]))
+    return c
+
+
+@pytest.mark.parametrize("kvt", [F16, BF16, Q8])
+def test_kv_len_equals_length_mask(kernel, cuda_device, kvt):
+    """CFG decode over a padded view: the device kv_len gives the result of the reference's mask."""
+    kv_len = [1537, 2044]
+    c = workloads.decode_case(n_seq=2, n_kv=2048, max_seq=2560, kv_type=kvt if kvt != BF16 else F16, seed=61)
+    if kvt == BF16:
+        for name in ("k", "v"):
+            op = getattr(c, name)
+            bf = torch.from_numpy(op.storage.astype(np.float32)).to(torch.bfloat16).view(torch.int16).numpy()
+            setattr(c, name, workloads.Operand(bf.view(np.uint16), BF16, op.ne, op.nb))
+    got = run_gpu_kvlen(c, cuda_device, kv_len)
+    ref = run_oracle(length_mask_case(c, kv_len), oracle.MODE_GGML)
+    assert_close(got, ref, what="kv_len vs length mask")
+
+
+def test_kv_len_with_mask_multirow_and_edges(kernel, cuda_device):
+    """kv_len combined with a mask, several query rows per sequence, a zero length (zeros) and a
+    length past n_kv (clamped)."""
+    kv_len = [0, 700, 5000, 333]
+    c = workloads.decode_case(n_seq=4, n_kv=1024, n_q=2, kv_len=[1024, 1024, 900, 1024], seed=62)
+    got = run_gpu_kvlen(c, cuda_device, kv_len, with_mask=True)
+    m = c.mask.storage.copy()
+    for s in range(4):
+        m[s, :, :, max(0, min(kv_len[s], 1024)):] = -np.inf
+    c.mask = workloads.Operand(m, F16, c.mask.ne, c.mask.nb)
+    ref = run_oracle(c, oracle.MODE_GGML)
+    assert_close(got, ref, what="kv_len + mask vs oracle")
+    assert np.all(got[0] == 0)
