@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) fa_decode_kernel(const DecodeP
     constexpr int NBLK    = D / QK8_0;
     constexpr bool IS_Q8  = KVT == KV_Q8_0;
     constexpr int LPB     = QK8_0 / EPL;    // lanes per Q8_0 block (2 for D=128, 4 for D=64)
-    static_assert(D == 64 || D == 128, "head dim");
+    static_assert(D == 64 || D == 128 || D == 256, "head dim");
     static_assert(C % 32 == 0, "stage keys");
 
     extern __shared__ __align__(128) char smem[];
@@ -584,8 +584,9 @@ struct DecodeConfig {
 
 template <int D, int KVT, bool BULK>
 static void * decode_kernel_ptr(int & smem, int & C) {
-    constexpr int CC     = (D == 64 && KVT != KV_Q8_0) ? 128 : 64;
-    constexpr int NSTAGE = 4;
+    // D = 256 (the depth decoder's heads): 32-key stages, 2 deep, to stay within shared memory
+    constexpr int CC     = D == 256 ? 32 : ((D == 64 && KVT != KV_Q8_0) ? 128 : 64);
+    constexpr int NSTAGE = D == 256 ? 2 : 4;
     smem                 = DecodeSmem<D, KVT, CC, NSTAGE>::TOTAL;
     C                    = CC;
     return reinterpret_cast<void *>(&fa_decode_kernel<D, KVT, CC, NSTAGE, BULK>);
@@ -602,6 +603,9 @@ static void * select_decode_kernel(int D, int kvt, bool bulk, int & smem, int & 
     MM3FA_SEL(64, KV_F16)
     MM3FA_SEL(64, KV_BF16)
     MM3FA_SEL(64, KV_Q8_0)
+    MM3FA_SEL(256, KV_F16)
+    MM3FA_SEL(256, KV_BF16)
+    MM3FA_SEL(256, KV_Q8_0)
 #undef MM3FA_SEL
     return nullptr;
 }

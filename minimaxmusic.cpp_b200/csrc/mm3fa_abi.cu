@@ -238,7 +238,8 @@ int check_op(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor 
         }
     }
     // what the kernels here implement
-    if (s.DV != s.D || (s.D != 64 && s.D != 128)) {
+    // D = 256 (the depth decoder's heads) runs on the CUDA-core decode kernel
+    if (s.DV != s.D || (s.D != 64 && s.D != 128 && s.D != 256)) {
         return MM3FA_ERR_UNSUPPORTED;
     }
     // index math in the kernels uses 32-bit unit numbers and key counts

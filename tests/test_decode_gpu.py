@@ -281,3 +281,41 @@ def test_kv_len_with_mask_multirow_and_edges(kernel, cuda_device):
     ref = run_oracle(c, oracle.MODE_GGML)
     assert_close(got, ref, what="kv_len + mask vs oracle")
     assert np.all(got[0] == 0)
+
+
+# ---------------------------------------------------------------- D = 256 (depth decoder heads)
+
+def depth_decoder_case(S: int, B: int, seed: int, kvt=F16):
+    """The depth decoder's causal self-attention (src/depth-decoder.h:196-221: 16 heads of 256, no
+    RoPE, S <= 8 steps, B = 2N sequences) as a flash_attn_ext call: Q F32 [256, S, 16, B], K/V cast to
+    the cache type [256, S, 16, B], causal mask [S, S]."""
+    D, H = 256, 16
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((B, S, H, D), dtype=np.float32)
+    qop = workloads.Operand(q, ggml.GGML_TYPE_F32, [D, S, H, B], [4, 4 * D * H, 4 * D, 4 * D * H * S])
+    kf = rng.standard_normal((B, H, S, D), dtype=np.float32) * 0.5
+    vf = rng.standard_normal((B, H, S, D), dtype=np.float32) * 0.5
+    ops = []
+    for x in (kf, vf):
+        if kvt == Q8:
+            st = oracle.q8_0_quantize(x)
+        else:
+            st = oracle.f32_to_f16_bits(x).view(np.float16)
+        ops.append(workloads.Operand(st, kvt, [D, S, H, B], ggml.contiguous_nb(kvt, [D, S, H, B])))
+    m = np.triu(np.full((S, S), -np.inf, dtype=np.float32), k=1).astype(np.float16)
+    mop = workloads.Operand(m, F16, [S, S, 1, 1], ggml.contiguous_nb(F16, [S, S, 1, 1]))
+    return workloads.Case("depth", qop, ops[0], ops[1], mop, 1.0 / np.sqrt(D))
+
+
+@pytest.mark.parametrize("S,B", [(1, 2), (5, 4), (8, 2)])
+def test_depth_decoder_d256(cuda_device, S, B):
+    check(depth_decoder_case(S, B, seed=70 + S), cuda_device)
+
+
+def test_depth_decoder_d256_q8_0(cuda_device):
+    check(depth_decoder_case(8, 2, seed=79, kvt=Q8), cuda_device, 5e-3, 0.9999)
+
+
+def test_decode_d256_long_kv(cuda_device):
+    """D = 256 over several 32-key stages and the stream-K split (GQA 4, F16 cache view)."""
+    check(workloads.decode_case(n_seq=2, n_kv=700, D=256, n_head=8, n_head_kv=2, seed=80), cuda_device)
