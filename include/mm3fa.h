@@ -211,6 +211,25 @@ MM3FA_API int mm3fa_decode_prologue(const mm3fa_tensor * q_in, const mm3fa_tenso
                                     mm3fa_tensor * v_cache, mm3fa_tensor * q_out, void * stream);
 
 /*
+ * DiT attention prologue: the nodes between the QKV projection and the attention call of a
+ * DiT block, as one kernel (src/dit.h:201-220):
+ *   q_out = rope_neox(q_in, pos, rot_dims)          (F32, same [D, n_head, S, B] layout)
+ *   k_out = cast(rope_neox(k_in, pos, rot_dims))    ([D, S, n_head, B], F16 or BF16)
+ *   v_out = cast(v_in)                              ([D, S, n_head, B], same type as k_out)
+ * NeoX RoPE over the first rot_dims dims of each head (base rope_theta, freq_scale 1, no YaRN;
+ * dims from rot_dims on unchanged), casts round to nearest even.  The attention then takes q_out
+ * permuted to [D, S, n_head, B] (a view) and k_out / v_out.
+ *   q_in, k_in, v_in  F32 [D, n_head, S, B]  (nb[0] = 4)
+ *   pos      device int32 [S]: the position of each token
+ *   rot_dims even, 0 < rot_dims <= D, a multiple of D/16
+ * D = 64 or 128.
+ * Replaces: ggml_rope_ext (x2), ggml_permute and ggml_cast (x2) at src/dit.h:206-220.
+ */
+MM3FA_API int mm3fa_dit_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
+                                 const int32_t * pos, int rot_dims, float rope_theta, mm3fa_tensor * q_out,
+                                 mm3fa_tensor * k_out, mm3fa_tensor * v_out, void * stream);
+
+/*
  * Multi-GPU output assembly.  With the kv heads partitioned over G ranks, rank r computes
  * dst_r [Dv, n_head/G, n_q, n_seq] for query heads [r*n_head/G, (r+1)*n_head/G).  After an
  * all-gather (NCCL, by the caller) the blocks sit rank-major as gathered[G][n_seq][n_q]

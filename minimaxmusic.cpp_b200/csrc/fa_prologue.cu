@@ -138,6 +138,83 @@ __global__ void __launch_bounds__(32 * PRO_WARPS) decode_prologue_kernel(const P
     }
 }
 
+// ---- DiT attention prologue (src/dit.h:201-220): per (batch, token, head) the q and k vectors
+// get ggml_rope_ext NEOX over their first `rot` dims (pair i with i + rot/2, angle pos[token] *
+// theta_scale^i walked like ggml's rope cache, dims from rot on copied), q stays F32, k and v are
+// cast (round to nearest even) into the [D, S, H, B] layout the attention reads.
+template <int E>
+__global__ void __launch_bounds__(32 * PRO_WARPS) dit_prologue_kernel(const DitPrologueParams p) {
+    const int     lane = threadIdx.x & 31;
+    const int64_t w    = (int64_t) blockIdx.x * PRO_WARPS + (threadIdx.x >> 5);
+    const int64_t nv   = (int64_t) p.n_head * p.n_tok * p.n_batch;
+    if (w >= 3 * nv) {
+        return;
+    }
+    const int     kind = (int) (w / nv);  // 0 q, 1 k, 2 v
+    const int64_t u    = w % nv;
+    const int     hh   = (int) (u % p.n_head);
+    const int     t    = (int) ((u / p.n_head) % p.n_tok);
+    const int     b    = (int) (u / ((int64_t) p.n_head * p.n_tok));
+    const int64_t * si = kind == 0 ? p.sq_in : (kind == 1 ? p.sk_in : p.sv_in);
+    const int64_t * so = kind == 0 ? p.sq_out : (kind == 1 ? p.sk_out : p.sv_out);
+    const char *  src  = (kind == 0 ? p.q_in : (kind == 1 ? p.k_in : p.v_in)) + hh * si[0] + t * si[1] + b * si[2];
+    char *        dst  = (kind == 0 ? p.q_out : (kind == 1 ? p.k_out : p.v_out)) + hh * so[0] + t * so[1] + b * so[2];
+    float         x[E];
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+        x[e] = reinterpret_cast<const float *>(src)[lane * E + e];
+    }
+    if (kind < 2) {
+        // lanes [0, hl) hold the first halves of the rotated pairs, lanes [hl, 2 hl) the second
+        const int hl      = p.rot / (2 * E);
+        const int partner = lane < hl ? lane + hl : (lane < 2 * hl ? lane - hl : lane);
+        const int pi0     = (lane < hl ? lane : lane - hl) * E;  // first pair index of this lane
+        float     th      = (float) p.pos[t];
+        for (int k = 0; k < pi0 && lane < 2 * hl; k++) {
+            th *= p.theta_scale;
+        }
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            const float xo = __shfl_sync(0xffffffffu, x[e], partner);
+            if (lane < 2 * hl) {
+                const float c = cosf(th), sn = sinf(th);
+                x[e]          = lane < hl ? x[e] * c - xo * sn : xo * sn + x[e] * c;
+                th *= p.theta_scale;
+            }
+        }
+    }
+    if (kind == 0) {
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            reinterpret_cast<float *>(dst)[lane * E + e] = x[e];
+        }
+        return;
+    }
+    store_cache_row<E>(dst, p.kvt, x, lane);
+}
+
+cudaError_t launch_dit_prologue(const DitPrologueParams & p, int D, cudaStream_t stream) {
+    const int64_t warps  = 3 * (int64_t) p.n_head * p.n_tok * p.n_batch;
+    const int64_t blocks = (warps + PRO_WARPS - 1) / PRO_WARPS;
+    if (blocks <= 0) {
+        return cudaSuccess;
+    }
+    if (blocks > 0x7fffffff) {
+        return cudaErrorInvalidValue;
+    }
+    switch (D) {
+        case 64:
+            dit_prologue_kernel<2><<<(unsigned) blocks, 32 * PRO_WARPS, 0, stream>>>(p);
+            break;
+        case 128:
+            dit_prologue_kernel<4><<<(unsigned) blocks, 32 * PRO_WARPS, 0, stream>>>(p);
+            break;
+        default:
+            return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
 cudaError_t launch_decode_prologue(const PrologueParams & p, int D, cudaStream_t stream) {
     const int64_t warps  = (int64_t) p.n_set * (p.n_head + 2 * p.n_head_kv);
     const int64_t blocks = (warps + PRO_WARPS - 1) / PRO_WARPS;

@@ -30,4 +30,23 @@ struct PrologueParams {
 // D = 64, 128 or 256; one warp per q, k and v head vector of every set.
 cudaError_t launch_decode_prologue(const PrologueParams & p, int D, cudaStream_t stream);
 
+// DiT attention prologue: partial NeoX RoPE of q and k over the first rot dims, q to F32, k and
+// v to F16/BF16, every tensor addressed by (head, token, batch) strides.
+struct DitPrologueParams {
+    const char *    q_in;
+    const char *    k_in;
+    const char *    v_in;
+    const int32_t * pos;  // [S]
+    char *          q_out;
+    char *          k_out;
+    char *          v_out;
+    int64_t         sq_in[3], sk_in[3], sv_in[3];     // byte strides of (head, token, batch)
+    int64_t         sq_out[3], sk_out[3], sv_out[3];
+    int             kvt;  // F16 or BF16
+    int             n_head, n_tok, n_batch, rot;
+    float           theta_scale;
+};
+
+cudaError_t launch_dit_prologue(const DitPrologueParams & p, int D, cudaStream_t stream);
+
 }  // namespace mm3fa

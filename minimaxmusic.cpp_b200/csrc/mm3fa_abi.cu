@@ -697,6 +697,97 @@ int mm3fa_decode_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, 
     return record_cuda(launch_decode_prologue(p, (int) D, static_cast<cudaStream_t>(stream)));
 }
 
+int mm3fa_dit_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
+                       const int32_t * pos, int rot_dims, float rope_theta, mm3fa_tensor * q_out, mm3fa_tensor * k_out,
+                       mm3fa_tensor * v_out, void * stream) {
+    if (!q_in || !k_in || !v_in || !q_out || !k_out || !v_out || !pos) {
+        return MM3FA_ERR_NULL;
+    }
+    for (const mm3fa_tensor * t : { q_in, k_in, v_in, (const mm3fa_tensor *) q_out, (const mm3fa_tensor *) k_out,
+                                    (const mm3fa_tensor *) v_out }) {
+        if (!t->data) {
+            return MM3FA_ERR_NULL;
+        }
+    }
+    if (q_in->type != MM3FA_TYPE_F32 || k_in->type != MM3FA_TYPE_F32 || v_in->type != MM3FA_TYPE_F32 ||
+        q_out->type != MM3FA_TYPE_F32) {
+        return MM3FA_ERR_TYPE;
+    }
+    const int ot = k_out->type;
+    if ((ot != MM3FA_TYPE_F16 && ot != MM3FA_TYPE_BF16) || v_out->type != ot) {
+        return MM3FA_ERR_TYPE;
+    }
+    const int64_t D = q_in->ne[0], H = q_in->ne[1], S = q_in->ne[2], B = q_in->ne[3];
+    if (D != 64 && D != 128) {
+        return MM3FA_ERR_UNSUPPORTED;
+    }
+    for (const mm3fa_tensor * t : { k_in, v_in, (const mm3fa_tensor *) q_out }) {
+        if (t->ne[0] != D || t->ne[1] != H || t->ne[2] != S || t->ne[3] != B) {
+            return MM3FA_ERR_SHAPE;
+        }
+    }
+    for (const mm3fa_tensor * t : { (const mm3fa_tensor *) k_out, (const mm3fa_tensor *) v_out }) {
+        if (t->ne[0] != D || t->ne[1] != S || t->ne[2] != H || t->ne[3] != B) {
+            return MM3FA_ERR_SHAPE;
+        }
+    }
+    const int E = (int) D / 32;
+    if (rot_dims <= 0 || rot_dims > D || rot_dims % (2 * E) != 0) {
+        return MM3FA_ERR_SHAPE;
+    }
+    if (!std::isfinite(rope_theta) || !(rope_theta > 0.0f) || H <= 0 || S <= 0 || B <= 0) {
+        return MM3FA_ERR_SHAPE;
+    }
+    for (const mm3fa_tensor * t : { q_in, k_in, v_in, (const mm3fa_tensor *) q_out }) {
+        if (t->nb[0] != 4 || t->nb[1] % 4 || t->nb[2] % 4 || t->nb[3] % 4 || !aligned(t->data, 4)) {
+            return MM3FA_ERR_STRIDE;
+        }
+    }
+    for (const mm3fa_tensor * t : { (const mm3fa_tensor *) k_out, (const mm3fa_tensor *) v_out }) {
+        if (t->nb[0] != 2 || t->nb[1] % 2 || t->nb[2] % 2 || t->nb[3] % 2 || !aligned(t->data, 2)) {
+            return MM3FA_ERR_STRIDE;
+        }
+    }
+    if (device_info().major != 10) {
+        return MM3FA_ERR_DEVICE;
+    }
+    DitPrologueParams p{};
+    p.q_in  = static_cast<const char *>(q_in->data);
+    p.k_in  = static_cast<const char *>(k_in->data);
+    p.v_in  = static_cast<const char *>(v_in->data);
+    p.pos   = pos;
+    p.q_out = static_cast<char *>(q_out->data);
+    p.k_out = static_cast<char *>(k_out->data);
+    p.v_out = static_cast<char *>(v_out->data);
+    // (head, token, batch) strides: inputs and q_out are [D, H, S, B], k_out / v_out [D, S, H, B]
+    auto hsb = [](const mm3fa_tensor * t, int64_t (&o)[3]) {
+        o[0] = (int64_t) t->nb[1];
+        o[1] = (int64_t) t->nb[2];
+        o[2] = (int64_t) t->nb[3];
+    };
+    auto shb = [](const mm3fa_tensor * t, int64_t (&o)[3]) {
+        o[0] = (int64_t) t->nb[2];
+        o[1] = (int64_t) t->nb[1];
+        o[2] = (int64_t) t->nb[3];
+    };
+    hsb(q_in, p.sq_in);
+    hsb(k_in, p.sk_in);
+    hsb(v_in, p.sv_in);
+    hsb(q_out, p.sq_out);
+    shb(k_out, p.sk_out);
+    shb(v_out, p.sv_out);
+    p.kvt         = ot;
+    p.n_head      = (int) H;
+    p.n_tok       = (int) S;
+    p.n_batch     = (int) B;
+    p.rot         = rot_dims;
+    p.theta_scale = std::pow(rope_theta, -2.0f / (float) rot_dims);
+    if (H > 65535 || S > 0x7fffffff / 4 || B > 65535) {
+        return MM3FA_ERR_UNSUPPORTED;
+    }
+    return record_cuda(launch_dit_prologue(p, (int) D, static_cast<cudaStream_t>(stream)));
+}
+
 int mm3fa_assemble_heads(const float * gathered, float * dst, int64_t dv, int64_t n_head, int64_t n_q, int64_t n_seq,
                          int n_ranks, void * stream) {
     if (!gathered || !dst) {

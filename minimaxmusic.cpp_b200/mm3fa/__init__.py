@@ -84,6 +84,9 @@ def lib():
                                                  ctypes.c_float, ctypes.c_int, P, ctypes.c_void_p, ctypes.c_size_t,
                                                  ctypes.c_void_p]
         L.mm3fa_flash_attn_ext_kvlen.restype = ctypes.c_int
+        L.mm3fa_dit_prologue.argtypes = [P, P, P, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, P, P, P,
+                                         ctypes.c_void_p]
+        L.mm3fa_dit_prologue.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -153,6 +156,15 @@ def flash_attn_ext_kvlen(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None, k
                                           workspace_bytes, ctypes.c_void_p(stream or None))
     if st != OK:
         raise MM3FAError(st, "mm3fa_flash_attn_ext_kvlen")
+
+
+def dit_prologue(q_in: Tensor, k_in: Tensor, v_in: Tensor, pos_ptr: int, rot_dims: int, rope_theta: float,
+                 q_out: Tensor, k_out: Tensor, v_out: Tensor, stream: int = 0) -> None:
+    """DiT attention prologue: partial NeoX RoPE of q/k and the F16/BF16 cast of k/v ([D, S, H, B])."""
+    st = lib().mm3fa_dit_prologue(_ref(q_in), _ref(k_in), _ref(v_in), ctypes.c_void_p(pos_ptr), rot_dims,
+                                  rope_theta, _ref(q_out), _ref(k_out), _ref(v_out), ctypes.c_void_p(stream or None))
+    if st != OK:
+        raise MM3FAError(st, "mm3fa_dit_prologue")
 
 
 def decode_prologue(q_in: Tensor, k_in: Tensor, v_in: Tensor, q_norm_ptr: int, k_norm_ptr: int, eps: float,

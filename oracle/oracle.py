@@ -112,13 +112,15 @@ def rms_norm_mul(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
     return ((x * scale).astype(np.float32) * np.asarray(w, dtype=np.float32)).astype(np.float32)
 
 
-def rope_neox(x: np.ndarray, pos: np.ndarray, theta: float) -> np.ndarray:
-    """ggml_rope_ext in NEOX mode over all D dims; x [N, H, D], pos [N] (int)."""
+def rope_neox(x: np.ndarray, pos: np.ndarray, theta: float, n_dims: int | None = None) -> np.ndarray:
+    """ggml_rope_ext in NEOX mode over the first n_dims dims (all by default; the rest are copied);
+    x [N, H, D], pos [N] (int)."""
     x = np.asarray(x, dtype=np.float32)
     n, _, d = x.shape
-    half = d // 2
-    ts = np.float32(np.power(np.float32(theta), np.float32(-2.0) / np.float32(d)))
-    out = np.empty_like(x)
+    nd = n_dims or d
+    half = nd // 2
+    ts = np.float32(np.power(np.float32(theta), np.float32(-2.0) / np.float32(nd)))
+    out = x.copy()
     for s in range(n):
         t = np.float32(pos[s])
         cs = np.empty(half, dtype=np.float32)
@@ -127,9 +129,9 @@ def rope_neox(x: np.ndarray, pos: np.ndarray, theta: float) -> np.ndarray:
             cs[i] = np.cos(t)
             sn[i] = np.sin(t)
             t = np.float32(t * ts)
-        x0, x1 = x[s, :, :half], x[s, :, half:]
+        x0, x1 = x[s, :, :half], x[s, :, half:nd]
         out[s, :, :half] = (x0 * cs - x1 * sn).astype(np.float32)
-        out[s, :, half:] = (x0 * sn + x1 * cs).astype(np.float32)
+        out[s, :, half:nd] = (x0 * sn + x1 * cs).astype(np.float32)
     return out
 
 

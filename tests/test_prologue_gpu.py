@@ -159,3 +159,84 @@ def test_prologue_then_attention(cuda_device, kvt):
     got = attend(r["q"], r["kc"], r["vc"], True)
     ref = attend(r["q_ref"], r["kc_ref"], r["vc_ref"], False)
     assert_close(got.reshape(ref.shape), ref, what="prologue + attention vs oracle")
+
+
+# ---------------------------------------------------------------- DiT attention prologue
+
+@pytest.mark.parametrize("out_t", [F16, BF16])
+def test_dit_prologue_real_dit_shapes(cuda_device, out_t):
+    """The real DiT block (src/dit.h:201-222): 32 heads of 64, S = 690, partial NeoX RoPE over the
+    first 32 dims (theta 1e4), k/v cast to F16 (or BF16), then flash_attn_ext over the permuted views."""
+    dev = cuda_device
+    B, S, H, D, rot, theta = 2, 690, 32, 64, 32, 1e4
+    rng = np.random.default_rng(21 + out_t)
+    q_in = rng.standard_normal((B, S, H, D)).astype(np.float32)   # ggml [D, H, S, B]
+    k_in = rng.standard_normal((B, S, H, D)).astype(np.float32)
+    v_in = rng.standard_normal((B, S, H, D)).astype(np.float32)
+    pos = np.arange(S, dtype=np.int32)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    dq, dk, dv, dpos = t(q_in), t(k_in), t(v_in), t(pos)
+    dqo = torch.full((B, S, H, D), float("nan"), dtype=torch.float32, device=dev)
+    ko_dtype = torch.float16 if out_t == F16 else torch.bfloat16
+    dko = torch.zeros((B, H, S, D), dtype=ko_dtype, device=dev)  # ggml [D, S, H, B]
+    dvo = torch.zeros((B, H, S, D), dtype=ko_dtype, device=dev)
+    mk = lambda ty, ne, tt: ggml.make(ty, ne, tt.data_ptr())
+    mm3fa.dit_prologue(mk(F32, [D, H, S, B], dq), mk(F32, [D, H, S, B], dk), mk(F32, [D, H, S, B], dv),
+                       dpos.data_ptr(), rot, theta, mk(F32, [D, H, S, B], dqo), mk(out_t, [D, S, H, B], dko),
+                       mk(out_t, [D, S, H, B], dvo), torch.cuda.current_stream(dev).cuda_stream)
+    torch.cuda.synchronize(dev)
+    pos_bs = np.tile(pos, B)
+    q_ref = oracle.rope_neox(q_in.reshape(B * S, H, D), pos_bs, theta, rot).reshape(B, S, H, D)
+    k_ref = oracle.rope_neox(k_in.reshape(B * S, H, D), pos_bs, theta, rot).reshape(B, S, H, D)
+    err = float(np.abs(dqo.cpu().numpy() - q_ref).max())
+    assert err <= 1e-4, f"q_out max-abs {err:.3e}"
+    # the dims past rot are copied unchanged
+    assert np.array_equal(dqo.cpu().numpy()[..., rot:], q_in[..., rot:])
+    k_bits = to_cache_bytes(k_ref.transpose(0, 2, 1, 3), out_t)
+    v_bits = to_cache_bytes(v_in.transpose(0, 2, 1, 3), out_t)
+    got_k = dko.cpu().view(torch.int16).numpy().view(np.uint16)
+    got_v = dvo.cpu().view(torch.int16).numpy().view(np.uint16)
+    check_rows_close(got_k, k_bits, out_t, "k_out")
+    assert np.array_equal(got_v, v_bits), "v_out is a plain cast"
+    # attention over the prologue's outputs vs the oracle over the oracle's
+    qv = [4, 4 * D * H, 4 * D, 4 * D * H * S]   # q permuted to [D, S, H, B]
+    kvnb = ggml.contiguous_nb(out_t, [D, S, H, B])
+    out = torch.full((B, S, H, D), float("nan"), dtype=torch.float32, device=dev)
+    qd = ggml.make(F32, [D, S, H, B], dqo.data_ptr(), qv)
+    kd = ggml.make(out_t, [D, S, H, B], dko.data_ptr(), kvnb)
+    vd = ggml.make(out_t, [D, S, H, B], dvo.data_ptr(), list(kvnb))
+    dd = mm3fa.dst_desc(qd, vd, out.data_ptr())
+    mm3fa.run(qd, kd, vd, None, dd, 1.0 / np.sqrt(D), 0.0, 0.0, mm3fa.Workspace(dev))
+    torch.cuda.synchronize(dev)
+    qh = np.ascontiguousarray(q_ref)
+    kh, vh = np.ascontiguousarray(k_bits), np.ascontiguousarray(v_bits)
+    ref = oracle.flash_attn_ext(ggml.make(F32, [D, S, H, B], qh.ctypes.data, qv),
+                                ggml.make(out_t, [D, S, H, B], kh.ctypes.data, kvnb),
+                                ggml.make(out_t, [D, S, H, B], vh.ctypes.data, list(kvnb)), None,
+                                1.0 / np.sqrt(D), 0.0, 0.0, oracle.MODE_GGML)
+    assert_close(out.cpu().numpy(), ref, what="DiT prologue + attention vs oracle")
+
+
+def test_dit_prologue_full_rotation_d128(cuda_device):
+    """rot_dims = D at D = 128 (every dim rotated), F16 outputs."""
+    dev = cuda_device
+    B, S, H, D = 1, 100, 4, 128
+    rng = np.random.default_rng(33)
+    x = [rng.standard_normal((B, S, H, D)).astype(np.float32) for _ in range(3)]
+    pos = (np.arange(S, dtype=np.int32) * 7)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    dx = [t(a) for a in x]
+    dpos = t(pos)
+    dqo = torch.empty((B, S, H, D), dtype=torch.float32, device=dev)
+    dko = torch.empty((B, H, S, D), dtype=torch.float16, device=dev)
+    dvo = torch.empty((B, H, S, D), dtype=torch.float16, device=dev)
+    mk = lambda ty, ne, tt: ggml.make(ty, ne, tt.data_ptr())
+    mm3fa.dit_prologue(mk(F32, [D, H, S, B], dx[0]), mk(F32, [D, H, S, B], dx[1]), mk(F32, [D, H, S, B], dx[2]),
+                       dpos.data_ptr(), D, 1e4, mk(F32, [D, H, S, B], dqo), mk(F16, [D, S, H, B], dko),
+                       mk(F16, [D, S, H, B], dvo), torch.cuda.current_stream(dev).cuda_stream)
+    torch.cuda.synchronize(dev)
+    q_ref = oracle.rope_neox(x[0].reshape(B * S, H, D), np.tile(pos, B), 1e4).reshape(B, S, H, D)
+    assert float(np.abs(dqo.cpu().numpy() - q_ref).max()) <= 1e-4
+    k_ref = oracle.rope_neox(x[1].reshape(B * S, H, D), np.tile(pos, B), 1e4).reshape(B, S, H, D)
+    check_rows_close(dko.cpu().view(torch.int16).numpy().view(np.uint16),
+                     to_cache_bytes(k_ref.transpose(0, 2, 1, 3), F16), F16, "k_out")
