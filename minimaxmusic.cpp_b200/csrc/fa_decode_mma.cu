@@ -1,16 +1,22 @@
 // fa_decode_mma.cu - split-KV decode attention on tensor cores, TMA tensor staging (sm_100a).
 //
-// Same operator, work split and partial-merge protocol as fa_decode.cu (units of <= 32 GQA
-// rows sharing one K/V slab, a stream-K cut of all unit keys over one wave of CTAs, a last-
-// arriver merge of partials in fixed order), for F16/BF16 K/V with <= 16 rows per unit
-// (the CFG decode of src/qwen3-lm.h:784-824: 4 query heads per kv head, 1 query row).
+// Same operator and units as fa_decode.cu (<= 32 GQA rows sharing one K/V slab), for F16/BF16/
+// Q8_0 K/V with <= 16 rows per unit (the CFG decode of src/qwen3-lm.h:784-824: 4 query heads per
+// kv head, 1 query row).  Two work splits:
+//   cluster mode (the default when the units fill the GPU): one thread-block cluster of CS <= 16
+//     CTAs per unit, the CTAs taking interleaved chunks of the unit's keys, the partials merged by
+//     pushing them over distributed shared memory to the rank that owns each (row, 4 dims) item;
+//   stream-K: a cut of all unit keys over one wave of CTAs, partials merged through the
+//     workspace by the last-arriving CTA in fixed order.
 //
 // Pipeline per CTA (160 threads, two CTAs per SM at D=128):
-//   warp 4 (producer)  - one thread issues 2-D tiled TMA loads (cp.async.bulk.tensor, 128-byte
-//                        swizzle, no multicast) of C=64 keys x D of K and V per stage into an
-//                        NSTAGE ring; full/empty mbarriers, no block-wide barrier in the loop.
-//   warps 0-3          - each owns 16 keys of every stage and keeps its own online-softmax
-//                        state; the four warp partials are merged once per unit.
+//   warp 4 (producer)  - one thread issues the loads of each stage into an NS-deep ring: 4-D
+//                        tiled TMA boxes (cp.async.bulk.tensor, 128-byte swizzle, no multicast)
+//                        of 64 keys x D of K and V, plus (cluster mode, one shared mask row)
+//                        the stage's mask row; full/empty mbarriers, no block-wide barrier.
+//   warps 0-3          - each owns 16 keys of every stage (Q8_0: 32, as two 16-key sub-tiles)
+//                        and keeps its own online-softmax state; the four warp partials are
+//                        combined once per unit.
 // Math per warp and stage, with keys on the MMA's M dimension so the few GQA rows fill N:
 //   S^T[16 keys x 8r rows] = K[16 x D] . Q^T        (mma.sync m16n8k16, A via ldmatrix)
 //   P^T -> P fragments by movmatrix (register transpose, no shared-memory round trip)
@@ -200,32 +206,6 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void * local, uint32_t rank
     uint32_t r;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(local)), "r"(rank));
     return r;
-}
-
-__device__ __forceinline__ float2 ld_dsmem2(uint32_t addr) {
-    float2 v;
-    asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ float4 ld_dsmem4(uint32_t addr) {
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(addr)
-                 : "memory");
-    return v;
-}
-
-__device__ __forceinline__ float ld_dsmem(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
-}
-
-// all threads of all CTAs in the cluster; release/acquire orders shared-memory writes
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void st_dsmem2(uint32_t addr, float2 v) {
