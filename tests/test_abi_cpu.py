@@ -115,3 +115,42 @@ def test_descriptor_helpers_roundtrip():
     b = np.zeros((2, 3, 136), dtype=np.uint8)
     t = ggml.from_numpy(b, ggml.GGML_TYPE_Q8_0)
     assert list(t.ne) == [128, 3, 2, 1] and list(t.nb) == [34, 136, 408, 816]
+
+
+def _status(fn, *args, **kw):
+    with pytest.raises(mm3fa.MM3FAError) as e:
+        fn(*args, **kw)
+    return e.value.status
+
+
+def test_prologue_entry_points_reject_before_touching_the_device():
+    F32, F16, Q8 = ggml.GGML_TYPE_F32, ggml.GGML_TYPE_F16, ggml.GGML_TYPE_Q8_0
+    D, H, Hkv, N, S = 128, 32, 8, 2, 64
+    q = ggml.make(F32, [D, H, N, 1], 0x1000)
+    k = ggml.make(F32, [D, Hkv, N, 1], 0x2000)
+    v = ggml.make(F32, [D, Hkv, N, 1], 0x3000)
+    kc = ggml.make(F16, [D, 512, Hkv, N], 0x4000)
+    vc = ggml.make(F16, [D, 512, Hkv, N], 0x5000)
+    qo = ggml.make(F32, [D, H, N, 1], 0x6000)
+    args = lambda **o: [o.get("q", q), o.get("k", k), v, 0x7000, 0x7100, 1e-6, 0x7200, 1e6, 0x7300,
+                        o.get("kc", kc), vc, qo]
+    assert _status(mm3fa.decode_prologue, q, k, v, 0, 0x7100, 1e-6, 0x7200, 1e6, 0x7300, kc, vc, qo) == mm3fa.ERR_NULL
+    assert _status(mm3fa.decode_prologue, *args(kc=ggml.make(F32, [D, 512, Hkv, N], 0x4000))) == mm3fa.ERR_TYPE
+    assert _status(mm3fa.decode_prologue, *args(kc=ggml.make(Q8, [D, 512, Hkv, N], 0x4000))) == mm3fa.ERR_TYPE  # v F16
+    assert _status(mm3fa.decode_prologue, *args(q=ggml.make(F32, [96, H, N, 1], 0x1000))) == mm3fa.ERR_UNSUPPORTED
+    assert _status(mm3fa.decode_prologue, *args(k=ggml.make(F32, [D, Hkv, N + 1, 1], 0x2000))) == mm3fa.ERR_SHAPE
+    # DiT prologue: [D, H, S, B] in, [D, S, H, B] out
+    qi = ggml.make(F32, [64, 32, S, 2], 0x1000)
+    ko = ggml.make(F16, [64, S, 32, 2], 0x4000)
+    vo = ggml.make(F16, [64, S, 32, 2], 0x5000)
+    assert _status(mm3fa.dit_prologue, qi, qi, qi, 0x7000, 30, 1e4, qi, ko, vo) == mm3fa.ERR_SHAPE  # rot % 4
+    v_heads_first = ggml.make(F16, [64, 32, S, 2], 0x5000)  # v_out not [D, S, H, B]
+    assert _status(mm3fa.dit_prologue, qi, qi, qi, 0x7000, 32, 1e4, qi, ko, v_heads_first) == mm3fa.ERR_SHAPE
+    assert _status(mm3fa.dit_prologue, qi, qi, qi, 0, 32, 1e4, qi, ko, vo) == mm3fa.ERR_NULL
+    assert _status(mm3fa.dit_prologue, qi, qi, qi, 0x7000, 32, 1e4, qi, ko,
+                   ggml.make(Q8, [64, S, 32, 2], 0x5000)) == mm3fa.ERR_TYPE
+    # kv_len attention: the kv_len pointer is required; the operands are checked as usual
+    _, q4, k4, v4, m4, d4 = _decode_descs(n_seq=2, n_kv=128)
+    assert _status(mm3fa.flash_attn_ext_kvlen, q4, k4, v4, m4, 0, 0.1, 0.0, 0.0, d4, 0, 0) == mm3fa.ERR_NULL
+    assert _status(mm3fa.flash_attn_ext_kvlen, q4, k4, v4, m4, 0x8000, 0.1, 0.0, 0.0,
+                   ggml.make(F16, list(d4.ne), 0x1000), 0, 0) == mm3fa.ERR_TYPE
