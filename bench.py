@@ -23,7 +23,8 @@ D=128, F16 causal mask over the 256-padded cache view).  N GPUs: each rank runs 
 
 Printed JSON: value = whole-job algorithmic GB/s of the timed steps (device time, max over
 ranks); e2e = the same through the C ABI with Q/mask copied from pinned host memory and the
-outputs read back every step; roofline = the decode kernel's achieved GB/s vs the measured
+outputs read back every step (copies in chunks of E2E_CHUNK layers on two copy streams,
+overlapping the attention of the other chunks); roofline = the decode kernel's achieved GB/s vs the measured
 HBM copy bandwidth; cpu_baseline = the CPU oracle (ggml convention) on the host cores.
 """
 from __future__ import annotations
@@ -43,6 +44,7 @@ sys.path.insert(0, os.path.join(ROOT, "minimaxmusic.cpp_b200"))
 
 METRIC = "decode attn GB/s & µs/layer (CFG B=2, KV 8K); DiT attn TFLOPS; % roofline"
 N_LAYERS = 36
+E2E_CHUNK = 6      # layers per host<->device copy in the end-to-end measurement
 N_HEAD, N_HEAD_KV, D = 32, 8, 128
 N_KV, MAX_SEQ = 8192, 10240
 FALLBACK_HBM_GBS = 6650.0
@@ -505,11 +507,13 @@ def main() -> None:
 
     # ---- per-layer operands (device resident), in the reference's layouts
     caches, qs, outs = [], [], []
-    for _ in range(n_layers):
+    q_all = torch.empty(n_layers, n_seq, hq, 1, D, device=dev)  # every layer's Q in one buffer
+    for l in range(n_layers):
         kc = (torch.randn(n_seq, hkv, MAX_SEQ, D, generator=g, device=dev) * 0.5).half()
         vc = (torch.randn(n_seq, hkv, MAX_SEQ, D, generator=g, device=dev) * 0.5).half()
         caches.append((kc, vc))
-        qs.append(torch.randn(n_seq, hq, 1, D, generator=g, device=dev))
+        q_all[l].copy_(torch.randn(n_seq, hq, 1, D, generator=g, device=dev))
+        qs.append(q_all[l])
     mask = torch.zeros(n_seq, 1, 1, N_KV, dtype=torch.float16, device=dev)
     outs = torch.empty(n_layers, n_seq, 1, hq, D, device=dev)
     rb = 2 * D
@@ -599,17 +603,42 @@ def main() -> None:
     achieved = layer_bytes(n_seq, hkv, hq) / (avg_launch_us * 1e-6) / 1e9
 
     # ---- end to end through the C ABI: Q/mask from pinned host memory, outputs back to host
-    q_host = [q.cpu().pin_memory() for q in qs]
+    # One pinned buffer per direction (every layer's Q up, every layer's output down), moved in
+    # chunks of E2E_CHUNK layers on two copy streams so that the transfers overlap the attention
+    # of other layers: chunk c's Q is uploaded before its layers run, its outputs go down while
+    # the next chunk computes.
+    q_host = q_all.cpu().pin_memory()
     mask_host = mask.cpu().pin_memory()
     out_host = torch.empty(outs.shape, dtype=torch.float32).pin_memory()
+    up_s, down_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    chunks = [(a, min(a + E2E_CHUNK, n_layers)) for a in range(0, n_layers, E2E_CHUNK)]
     g2 = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g2, stream=stream):
-        mask.copy_(mask_host, non_blocking=True)
-        for l in range(n_layers):
-            qs[l].copy_(q_host[l], non_blocking=True)
-        attention_layers(stream)
-        out_host.copy_(outs, non_blocking=True)
-    h2d = sum(q.numel() * 4 for q in q_host) + mask_host.numel() * 2
+        fork = torch.cuda.Event()
+        stream.record_event(fork)
+        up_s.wait_event(fork)
+        down_s.wait_event(fork)
+        uploaded = []
+        with torch.cuda.stream(up_s):
+            mask.copy_(mask_host, non_blocking=True)
+            for a, b in chunks:
+                q_all[a:b].copy_(q_host[a:b], non_blocking=True)
+                ev = torch.cuda.Event()
+                up_s.record_event(ev)
+                uploaded.append(ev)
+        for (a, b), ev in zip(chunks, uploaded):
+            stream.wait_event(ev)
+            for (qd, kd, vd, md, dd) in descs[a:b]:
+                mm3fa.flash_attn_ext(qd, kd, vd, md, scale, 0.0, 0.0, dd, ws.data_ptr(), ws.numel(), stream.cuda_stream)
+            done = torch.cuda.Event()
+            stream.record_event(done)
+            down_s.wait_event(done)
+            with torch.cuda.stream(down_s):
+                out_host[a:b].copy_(outs[a:b], non_blocking=True)
+        joined = torch.cuda.Event()
+        down_s.record_event(joined)
+        stream.wait_event(joined)
+    h2d = q_host.numel() * 4 + mask_host.numel() * 2
     d2h = out_host.numel() * 4
     for _ in range(args.warmup):
         g2.replay()

@@ -155,6 +155,37 @@ __device__ __forceinline__ float ld_q_elem(const char * p, int type, int e) {
     return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[e]);
 }
 
+// N elements idx(0..N-1) of one Q row as floats (zeros when !valid), the type decided once so
+// that the N loads are independent and in flight together (a type test per element kept the
+// compiler from batching them: one memory latency per element at kernel start).
+template <int N, typename Idx>
+__device__ __forceinline__ void ld_q_elems(float (&x)[N], const char * row, int type, bool valid, Idx idx) {
+    if (!valid) {
+#pragma unroll
+        for (int i = 0; i < N; i++) {
+            x[i] = 0.0f;
+        }
+    } else if (type == KV_F32) {
+        const float * r = reinterpret_cast<const float *>(row);
+#pragma unroll
+        for (int i = 0; i < N; i++) {
+            x[i] = r[idx(i)];
+        }
+    } else if (type == KV_F16) {
+        const __half * r = reinterpret_cast<const __half *>(row);
+#pragma unroll
+        for (int i = 0; i < N; i++) {
+            x[i] = __half2float(r[idx(i)]);
+        }
+    } else {
+        const __nv_bfloat16 * r = reinterpret_cast<const __nv_bfloat16 *>(row);
+#pragma unroll
+        for (int i = 0; i < N; i++) {
+            x[i] = __bfloat162float(r[idx(i)]);
+        }
+    }
+}
+
 // Launch geometry: the n_units * n_kv key positions cut into n_ctas ranges of keys_per_cta.
 struct DecodeGeometry {
     int64_t n_units;        // (q sequence, kv head, row group) triples

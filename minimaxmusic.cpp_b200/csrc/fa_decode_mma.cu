@@ -53,6 +53,7 @@ constexpr int MMA_CONSUMERS = 4;                         // consumer warps
 constexpr int MMA_THREADS   = 32 * (MMA_CONSUMERS + 1);  // + producer warp
 constexpr int MMA_C         = 16 * MMA_CONSUMERS;        // F16/BF16 keys per stage (16 per consumer warp)
 constexpr int MMA_RMAX      = 32;                        // rows per unit in the partial layout
+constexpr int MMA_MAX_CLUSTER = 16;                      // largest cluster (non-portable size)
 
 template <int D, int NT, int NS, bool Q8 = false>
 struct MmaSmem {
@@ -72,7 +73,7 @@ struct MmaSmem {
                                                                                  : (8 * NT * D / 4 + 16) * 16;
     static constexpr int OFF_RED_O  = NS * STAGE;
     static constexpr int OFF_RECV_ML = OFF_RED_O + RED_O_B;           // [source rank][row][2] (m, l)
-    static constexpr int OFF_RED_ML = OFF_RECV_ML + 16 * 8 * NT * 2 * 4;  // [warp][row][2] (m, l)
+    static constexpr int OFF_RED_ML = OFF_RECV_ML + MMA_MAX_CLUSTER * 8 * NT * 2 * 4;  // [warp][row][2] (m, l)
     static constexpr int OFF_BAR    = OFF_RED_ML + MMA_CONSUMERS * 8 * NT * 2 * 4;
     static constexpr int OFF_FLAG   = OFF_BAR + (2 * NS + 1) * 8;  // full[NS], empty[NS], pushed
     static constexpr int TOTAL      = OFF_FLAG + 16 + 1024;   // + alignment slack for the ring
@@ -208,30 +209,31 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void * local, uint32_t rank
     return r;
 }
 
-__device__ __forceinline__ void st_dsmem2(uint32_t addr, float2 v) {
-    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(v.x), "f"(v.y) : "memory");
-}
-
 // Split cluster barrier: every thread arrives once its CTA's mbarriers are initialised; a
-// thread that will touch another CTA's shared memory waits first.
+// thread that will touch another CTA's shared memory waits first.  The arrive is relaxed: the
+// only writes it has to publish are the mbarrier inits, which fence.mbarrier_init already
+// released at cluster scope (a releasing arrive cost ~0.45 us at kernel start).
 __device__ __forceinline__ void cluster_arrive() {
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void cluster_wait() {
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ void st_dsmem4(uint32_t addr, float4 v) {
-    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
-                 "f"(v.w)
+// Asynchronous store into another CTA's shared memory (addresses from mapa) that signals its
+// bytes to the mbarrier `bar` of that CTA: the receiver's phase completes once every expected
+// byte has landed, with no fence or separate arrive on the sending side.
+__device__ __forceinline__ void st_async4(uint32_t addr, float4 v, uint32_t bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+                 "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(bar)
                  : "memory");
 }
 
-// Arrive on an mbarrier of another CTA of the cluster (addr from mapa), releasing at cluster
-// scope the writes this thread has made or observed (the CTA barrier before it).
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+__device__ __forceinline__ void st_async2(uint32_t addr, float2 v, uint32_t bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+                 "f"(v.x), "f"(v.y), "r"(bar)
+                 : "memory");
 }
 
 // Bounded wait on a local mbarrier phase whose arrivals come from other CTAs of the cluster.
@@ -337,7 +339,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], MMA_CONSUMERS);
         }
-        mbar_init(pushed, CLUSTER ? (uint32_t) p.cluster : 1u);
+        mbar_init(pushed, 1u);  // cluster mode: one local arrival plus the pushed bytes
         flag[0] = 0;
         flag[1] = 0;
         fence_mbar_init();
@@ -506,14 +508,13 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                 // the quad's 4 lanes hold the 32 values of one block of row rb: Q8_0-quantize them
                 // as ggml's reference quantizer does (amax over the block, d = amax/127, stored
                 // as f16, q = round(x / d) with the f32 reciprocal of d)
+                // this thread's 8 values of every block, all loaded before the first is used
+                float xq[NBLK * 8];
+                ld_q_elems(xq, qrow, p.q_type, vb,
+                           [&](int i) { return (i >> 3) * QK8_0 + ((i & 7) >> 2) * 16 + 4 * q4 + (i & 3); });
 #pragma unroll
                 for (int b = 0; b < NBLK; b++) {
-                    float x[8];
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        const int d0 = b * QK8_0 + (i >> 2) * 16 + 4 * q4 + (i & 3);
-                        x[i]         = vb ? ld_q_elem(qrow, p.q_type, d0) : 0.0f;
-                    }
+                    const float * x = xq + b * 8;
                     float amax = 0.0f;
 #pragma unroll
                     for (int i = 0; i < 8; i++) {
@@ -542,18 +543,14 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                     dq[nt][b][1]   = __shfl_sync(0xffffffffu, dh, (2 * q4 + 1) << 2);
                 }
             } else {
+                // dims 16 ks + 2 q4 + {0, 1, 8, 9} of every k-step, all loads in flight together
+                float x[KS * 4];
+                ld_q_elems(x, qrow, p.q_type, vb,
+                           [&](int i) { return (i >> 2) * 16 + 2 * q4 + (i & 1) + ((i & 2) << 2); });
 #pragma unroll
                 for (int ks = 0; ks < KS; ks++) {
-                    float x[4] = { 0.f, 0.f, 0.f, 0.f };
-                    if (vb) {
-                        const int d0 = ks * 16 + 2 * q4;
-                        x[0]         = ld_q_elem(qrow, p.q_type, d0);
-                        x[1]         = ld_q_elem(qrow, p.q_type, d0 + 1);
-                        x[2]         = ld_q_elem(qrow, p.q_type, d0 + 8);
-                        x[3]         = ld_q_elem(qrow, p.q_type, d0 + 9);
-                    }
-                    qb[nt][ks][0] = pack2<BF16>(x[0], x[1]);
-                    qb[nt][ks][1] = pack2<BF16>(x[2], x[3]);
+                    qb[nt][ks][0] = pack2<BF16>(x[4 * ks + 0], x[4 * ks + 1]);
+                    qb[nt][ks][1] = pack2<BF16>(x[4 * ks + 2], x[4 * ks + 3]);
                 }
             }
             // softmax state rows: 8*nt + 2*q4 + {0,1}
@@ -618,16 +615,21 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
             named_barrier_consumers();
             // Cluster merge by pushing (reduce-scatter over DSMEM): item (row, 4 dims) number it
             // belongs to rank it % CS.  This CTA combines its 4 warps per item and stores the result
-            // into the owner's receive buffer, and its (m, l) per row into every rank's; then one
-            // thread per rank arrives on that rank's `pushed` barrier.  Each rank waits for the CS
-            // arrivals on its own barrier and merges its items from local memory, so no CTA ever
-            // reads another's memory and no cluster barrier follows.
+            // into the owner's receive buffer, and its (m, l) per row into every rank's, as
+            // asynchronous stores that count their bytes on the receiver's `pushed` barrier.  Each
+            // rank expects the bytes of its share from all CS ranks, waits for them and merges its
+            // items from local memory, so no CTA ever reads another's memory and no fence or
+            // cluster barrier follows.
             const int      CS    = p.cluster;
             const uint32_t rank  = cluster_ctarank();
             const int      total = nrow * (D / 4);
             const int      IPR   = (total + CS - 1) / CS;  // items per rank
             float4 *       rcv_o  = reinterpret_cast<float4 *>(redO);  // [source][IPR]
             float2 *       rcv_ml = reinterpret_cast<float2 *>(smem + L::OFF_RECV_ML);  // [source][8 NT]
+            if (tid == 0) {
+                const int mine = (int) rank < total ? (total - 1 - (int) rank) / CS + 1 : 0;
+                mbar_arrive_expect_tx(pushed, (uint32_t) (CS * (mine * 16 + nrow * 8)));
+            }
             cluster_wait();  // every CTA of the cluster has initialised its barriers
             for (int it4 = tid; it4 < total; it4 += 32 * MMA_CONSUMERS) {
                 const int r = it4 / (D / 4), d = (it4 % (D / 4)) * 4;
@@ -650,17 +652,13 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                     Ls += wt * redML[(w * 8 * NT + r) * 2 + 1];
                 }
                 const uint32_t owner = (uint32_t) (it4 % CS);
-                st_dsmem4(dsmem_addr(&rcv_o[(int) rank * IPR + it4 / CS], owner), O);
+                st_async4(dsmem_addr(&rcv_o[(int) rank * IPR + it4 / CS], owner), O, dsmem_addr(pushed, owner));
                 if (d == 0) {
                     for (int c = 0; c < CS; c++) {
-                        st_dsmem2(dsmem_addr(&rcv_ml[(int) rank * 8 * NT + r], (uint32_t) c), make_float2(M, Ls));
+                        st_async2(dsmem_addr(&rcv_ml[(int) rank * 8 * NT + r], (uint32_t) c), make_float2(M, Ls),
+                                  dsmem_addr(pushed, (uint32_t) c));
                     }
                 }
-            }
-            asm volatile("fence.acq_rel.cluster;" ::: "memory");
-            named_barrier_consumers();
-            if (tid < CS) {
-                mbar_arrive_remote(dsmem_addr(pushed, (uint32_t) tid));
             }
             if (!mbar_wait_cluster_bounded(pushed, 0, global_timer_ns() + p.timeout_ns)) {
                 if (tid == 0) {
@@ -674,22 +672,29 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                     break;
                 }
                 const int r = it4 / (D / 4), d = (it4 % (D / 4)) * 4;
-                float     M = -INFINITY;
-                for (int c = 0; c < CS; c++) {
-                    M = fmaxf(M, rcv_ml[c * 8 * NT + r].x);
+                // all CS sources' (m, l) and partial O loaded before use (unrolled to the largest
+                // cluster, so that the loads are in flight together)
+                float2 ml[MMA_MAX_CLUSTER];
+                float  M = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < MMA_MAX_CLUSTER; c++) {
+                    ml[c] = c < CS ? rcv_ml[c * 8 * NT + r] : make_float2(-INFINITY, 0.0f);
+                    M     = fmaxf(M, ml[c].x);
                 }
                 float4 O  = make_float4(0.f, 0.f, 0.f, 0.f);
                 float  Ls = 0.0f;
                 if (M != -INFINITY) {
-                    for (int c = 0; c < CS; c++) {
-                        const float2 ml = rcv_ml[c * 8 * NT + r];
-                        const float  w  = ml.x == -INFINITY ? 0.0f : exp2f(ml.x - M);
-                        const float4 v  = rcv_o[c * IPR + li];
-                        O.x += w * v.x;
-                        O.y += w * v.y;
-                        O.z += w * v.z;
-                        O.w += w * v.w;
-                        Ls += w * ml.y;
+#pragma unroll
+                    for (int c = 0; c < MMA_MAX_CLUSTER; c++) {
+                        if (c < CS) {
+                            const float  w = ml[c].x == -INFINITY ? 0.0f : exp2f(ml[c].x - M);
+                            const float4 v = rcv_o[c * IPR + li];
+                            O.x += w * v.x;
+                            O.y += w * v.y;
+                            O.z += w * v.z;
+                            O.w += w * v.w;
+                            Ls += w * ml[c].y;
+                        }
                     }
                 }
                 const float inv = Ls > 0.0f ? 1.0f / Ls : 0.0f;
@@ -1425,7 +1430,7 @@ int decode_mma_cluster_size(int D, int kvt, int rows_per_pair, int64_t n_units, 
         cache[key] = 0;
         return 0;
     }
-    int cs = (int) std::min<int64_t>(16, std::max<int64_t>(1, slots / n_units));
+    int cs = (int) std::min<int64_t>(MMA_MAX_CLUSTER, std::max<int64_t>(1, slots / n_units));
     while (cs > 1) {
         const int n = max_active_clusters(fn, cs, smem);
         if ((int64_t) n >= std::min<int64_t>(n_units, (int64_t) slots / cs)) {
