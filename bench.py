@@ -50,7 +50,7 @@ N_KV, MAX_SEQ = 8192, 10240
 FALLBACK_HBM_GBS = 6650.0
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode launch at this workload (ncu capture)
-NCU_KERNEL = "fa_decode_mma_kernel<128,f16,NT=1,cluster,NS=2>"
+NCU_KERNEL = "fa_decode_mma_kernel<128,f16,NT=1,cluster,NS=3>"
 NCU_TRAFFIC_BYTES = 67231232 + 837376
 
 

@@ -672,14 +672,21 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                     break;
                 }
                 const int r = it4 / (D / 4), d = (it4 % (D / 4)) * 4;
-                // all CS sources' (m, l) and partial O loaded before use (unrolled to the largest
-                // cluster, so that the loads are in flight together)
+                // every source's (m, l) and partial O loaded before any is used: unrolled to the
+                // largest cluster with the index clamped (always in bounds, no branches), so that
+                // the loads are in flight together; sources from CS on are skipped in the sums
                 float2 ml[MMA_MAX_CLUSTER];
+                float4 po[MMA_MAX_CLUSTER];
                 float  M = -INFINITY;
 #pragma unroll
                 for (int c = 0; c < MMA_MAX_CLUSTER; c++) {
-                    ml[c] = c < CS ? rcv_ml[c * 8 * NT + r] : make_float2(-INFINITY, 0.0f);
-                    M     = fmaxf(M, ml[c].x);
+                    const int cc = min(c, CS - 1);
+                    ml[c]        = rcv_ml[cc * 8 * NT + r];
+                    po[c]        = rcv_o[cc * IPR + li];
+                }
+#pragma unroll
+                for (int c = 0; c < MMA_MAX_CLUSTER; c++) {
+                    M = c < CS ? fmaxf(M, ml[c].x) : M;
                 }
                 float4 O  = make_float4(0.f, 0.f, 0.f, 0.f);
                 float  Ls = 0.0f;
@@ -688,7 +695,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                     for (int c = 0; c < MMA_MAX_CLUSTER; c++) {
                         if (c < CS) {
                             const float  w = ml[c].x == -INFINITY ? 0.0f : exp2f(ml[c].x - M);
-                            const float4 v = rcv_o[c * IPR + li];
+                            const float4 v = po[c];
                             O.x += w * v.x;
                             O.y += w * v.y;
                             O.z += w * v.z;
@@ -1311,13 +1318,13 @@ void * mma_kernel(int ns, int & smem) {
     return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT, CL, 3, false>);
 }
 
-// F16/BF16 ring depth: 2 stages of 64 keys per CTA (three CTAs, 192 KiB of K/V in flight per
-// SM at D=128; measured 3% faster than 3 stages with two CTAs per SM) or 3 with
-// MM3FA_DECODE_NSTAGE=3.
+// F16/BF16 ring depth: 3 stages of 64 keys per CTA (two CTAs per SM, up to 192 KiB of K/V in
+// flight per SM at D=128; measured 3% faster than 2 stages on the 36-layer decode graph) or 2
+// with MM3FA_DECODE_NSTAGE=2.
 int mma_nstage() {
     static const int ns = [] {
         const char * e = std::getenv("MM3FA_DECODE_NSTAGE");
-        return (e && std::atoi(e) == 3) ? 3 : 2;
+        return (e && std::atoi(e) == 2) ? 2 : 3;
     }();
     return ns;
 }
