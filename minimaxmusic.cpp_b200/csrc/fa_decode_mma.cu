@@ -76,7 +76,10 @@ struct MmaSmem {
     static constexpr int OFF_RED_ML = OFF_RECV_ML + MMA_MAX_CLUSTER * 8 * NT * 2 * 4;  // [warp][row][2] (m, l)
     static constexpr int OFF_BAR    = OFF_RED_ML + MMA_CONSUMERS * 8 * NT * 2 * 4;
     static constexpr int OFF_FLAG   = OFF_BAR + (2 * NS + 1) * 8;  // full[NS], empty[NS], pushed
-    static constexpr int TOTAL      = OFF_FLAG + 16 + 1024;   // + alignment slack for the ring
+    // Q8_0: the quantized Q fragments, [nt][block][lane] x {2 int8x4 words, 2 row scales}
+    static constexpr int OFF_QX     = (OFF_FLAG + 16 + 15) / 16 * 16;
+    static constexpr int QX_B       = Q8 ? NT * (D / QK8_0) * 32 * 16 : 0;
+    static constexpr int TOTAL      = OFF_QX + QX_B + 1024;   // + alignment slack for the ring
 };
 
 // ------------------------------------------------------------------ PTX helpers
@@ -502,14 +505,15 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
             if constexpr (Q8) {
                 // the quad's 4 lanes hold the 32 values of one block of row rb: Q8_0-quantize them
                 // as ggml's reference quantizer does (amax over the block, d = amax/127, stored
-                // as f16, q = round(x / d) with the f32 reciprocal of d)
-                // this thread's 8 values of every block, all loaded before the first is used
-                float xq[NBLK * 8];
-                ld_q_elems(xq, qrow, p.q_type, vb,
-                           [&](int i) { return (i >> 3) * QK8_0 + ((i & 7) >> 2) * 16 + 4 * q4 + (i & 3); });
-#pragma unroll
-                for (int b = 0; b < NBLK; b++) {
-                    const float * x = xq + b * 8;
+                // as f16, q = round(x / d) with the f32 reciprocal of d).  Warp w quantizes block
+                // w (and w + 4, ...) for every lane and stages the fragments in shared memory; the
+                // warps pick all blocks up after the barrier below (one block's dependency chain
+                // per warp instead of NBLK).
+                uint4 * qx = reinterpret_cast<uint4 *>(smem + L::OFF_QX);
+                for (int b = warp; b < NBLK; b += MMA_CONSUMERS) {
+                    float x[8];
+                    ld_q_elems(x, qrow + 0, p.q_type, vb,
+                               [&](int i) { return b * QK8_0 + (i >> 2) * 16 + 4 * q4 + (i & 3); });
                     float amax = 0.0f;
 #pragma unroll
                     for (int i = 0; i < 8; i++) {
@@ -530,12 +534,11 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                         }
                         w[h] = v;
                     }
-                    q8b[nt][b][0] = w[0];
-                    q8b[nt][b][1] = w[1];
                     // C-fragment rows 8*nt + 2*q4 + e live on the quads g4 = 2*q4 + e
-                    const float dh = round_to_f16(d);
-                    dq[nt][b][0]   = __shfl_sync(0xffffffffu, dh, (2 * q4) << 2);
-                    dq[nt][b][1]   = __shfl_sync(0xffffffffu, dh, (2 * q4 + 1) << 2);
+                    const float dh  = round_to_f16(d);
+                    const float dq0 = __shfl_sync(0xffffffffu, dh, (2 * q4) << 2);
+                    const float dq1 = __shfl_sync(0xffffffffu, dh, (2 * q4 + 1) << 2);
+                    qx[(nt * NBLK + b) * 32 + lane] = make_uint4(w[0], w[1], __float_as_uint(dq0), __float_as_uint(dq1));
                 }
             } else {
                 // dims 16 ks + 2 q4 + {0, 1, 8, 9} of every k-step, all loads in flight together
@@ -563,6 +566,22 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                                                   (int64_t) (sq % p.m_ne3) * p.m_nb3
                                               : 0;
             }
+        }
+        if constexpr (Q8) {  // every warp's copy of the fragments the warps staged above
+            named_barrier_consumers();
+            const uint4 * qx = reinterpret_cast<const uint4 *>(smem + L::OFF_QX);
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+                for (int b = 0; b < NBLK; b++) {
+                    const uint4 v = qx[(nt * NBLK + b) * 32 + lane];
+                    q8b[nt][b][0] = v.x;
+                    q8b[nt][b][1] = v.y;
+                    dq[nt][b][0]  = __uint_as_float(v.z);
+                    dq[nt][b][1]  = __uint_as_float(v.w);
+                }
+            }
+            named_barrier_consumers();  // the staging area is free for the next unit's
         }
 #pragma unroll
         for (int m = 0; m < KS; m++) {
