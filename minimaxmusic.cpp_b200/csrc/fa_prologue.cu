@@ -14,10 +14,42 @@
 // scale stored as f16, values round(x / d)).
 #include "fa_prologue.cuh"
 
+#include <cstdlib>
+
 namespace mm3fa {
 
-
 constexpr int PRO_WARPS = 4;
+
+// Both prologue kernels are launched with programmatic stream serialisation (MM3FA_PDL=0 turns
+// it off, as for the attention kernels): their CTAs may start once the previous kernel's CTAs
+// have exited, and wait on the device for its completion before reading anything.
+__device__ __forceinline__ void prologue_dep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+template <typename Kern, typename Params>
+cudaError_t launch_prologue(Kern kern, unsigned blocks, const Params & p, cudaStream_t stream) {
+    static const bool pdl = [] {
+        const char * e = std::getenv("MM3FA_PDL");
+        return !(e && std::atoi(e) == 0);
+    }();
+    cudaLaunchConfig_t  cfg{};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim          = dim3(blocks);
+    cfg.blockDim         = dim3(32 * PRO_WARPS);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream           = stream;
+    cfg.attrs            = attr;
+    cfg.numAttrs         = 0;
+    if (pdl) {
+        attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs                                       = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+
 
 template <int E>
 __device__ __forceinline__ void store_cache_row(char * row, int kvt, const float (&y)[E], int lane) {
@@ -68,6 +100,7 @@ __global__ void __launch_bounds__(32 * PRO_WARPS) decode_prologue_kernel(const P
     const int     lane = threadIdx.x & 31;
     const int     w    = (int) blockIdx.x * PRO_WARPS + (int) (threadIdx.x >> 5);
     const int     per  = p.n_head + 2 * p.n_head_kv;  // vectors per set: q heads, k heads, v heads
+    prologue_dep_wait();
     if (w >= per * p.n_set) {
         return;
     }
@@ -147,6 +180,7 @@ __global__ void __launch_bounds__(32 * PRO_WARPS) dit_prologue_kernel(const DitP
     const int     lane = threadIdx.x & 31;
     const int64_t w    = (int64_t) blockIdx.x * PRO_WARPS + (threadIdx.x >> 5);
     const int64_t nv   = (int64_t) p.n_head * p.n_tok * p.n_batch;
+    prologue_dep_wait();
     if (w >= 3 * nv) {
         return;
     }
@@ -204,15 +238,12 @@ cudaError_t launch_dit_prologue(const DitPrologueParams & p, int D, cudaStream_t
     }
     switch (D) {
         case 64:
-            dit_prologue_kernel<2><<<(unsigned) blocks, 32 * PRO_WARPS, 0, stream>>>(p);
-            break;
+            return launch_prologue(dit_prologue_kernel<2>, (unsigned) blocks, p, stream);
         case 128:
-            dit_prologue_kernel<4><<<(unsigned) blocks, 32 * PRO_WARPS, 0, stream>>>(p);
-            break;
+            return launch_prologue(dit_prologue_kernel<4>, (unsigned) blocks, p, stream);
         default:
             return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 cudaError_t launch_decode_prologue(const PrologueParams & p, int D, cudaStream_t stream) {
@@ -223,18 +254,14 @@ cudaError_t launch_decode_prologue(const PrologueParams & p, int D, cudaStream_t
     }
     switch (D) {
         case 64:
-            decode_prologue_kernel<2><<<(unsigned) blocks, 32 * PRO_WARPS, 0, stream>>>(p);
-            break;
+            return launch_prologue(decode_prologue_kernel<2>, (unsigned) blocks, p, stream);
         case 128:
-            decode_prologue_kernel<4><<<(unsigned) blocks, 32 * PRO_WARPS, 0, stream>>>(p);
-            break;
+            return launch_prologue(decode_prologue_kernel<4>, (unsigned) blocks, p, stream);
         case 256:
-            decode_prologue_kernel<8><<<(unsigned) blocks, 32 * PRO_WARPS, 0, stream>>>(p);
-            break;
+            return launch_prologue(decode_prologue_kernel<8>, (unsigned) blocks, p, stream);
         default:
             return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 }  // namespace mm3fa
