@@ -377,9 +377,9 @@ def bench_q8(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, world: in
 
 
 def bench_decode_step(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, world: int, n_layers: int) -> dict:
-    """Decode step with the fused prologue (the nodes of src/qwen3-lm.h:764-820 from the QKV projection
-    output on): per layer mm3fa_decode_prologue (RMSNorm + NeoX RoPE of q/k, k/v rows appended to the
-    F16 caches at row 8191) then the attention over the 8192-row views, 36 layers in one CUDA graph;
+    """Decode step from the QKV projection output (the nodes of src/qwen3-lm.h:764-820): per layer
+    mm3fa_decode_step (the prologue kernel: RMSNorm + NeoX RoPE of q/k, k/v rows appended to the F16
+    caches at row 8191; then the attention over the 8192-row views), 36 layers in one CUDA graph;
     also the prologue alone.  Shapes of the headline (per rank: its kv-head shard of a CFG pair)."""
     g = torch.Generator(device=dev)
     g.manual_seed(55)
@@ -446,17 +446,18 @@ def bench_decode_step(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, 
         del graph
         return e0.elapsed_time(e1) * 1e3 / steps / n_layers
 
-    def step():
-        for L in layers:
-            prologue(L)
-            attention(L)
+    def step(L):
+        mm3fa.decode_step(L["q_in"], L["k_in"], L["v_in"], qn.data_ptr(), kn.data_ptr(), 1e-6, pos.data_ptr(), 1e6,
+                          rows.data_ptr(), L["kc"], L["vc"], L["q_out"], L["k"], L["v"], L["m"], scale, 0.0, 0.0,
+                          L["o"], ws.data_ptr(), ws.numel(), stream.cuda_stream)
 
-    us_step = timed(step)
+    us_step = timed(lambda: [step(L) for L in layers])
     us_pro = timed(lambda: [prologue(L) for L in layers])
     return {"decode_step": {"us_per_layer": round(us_step, 3), "prologue_us_per_layer": round(us_pro, 3),
-                            "config": {"workload": "decode step from the QKV projection output: fused prologue "
-                                                   "(QK-RMSNorm, NeoX RoPE theta 1e6, k/v append at row 8191) + "
-                                                   f"attention over KV 8192, {n_layers} layers per CUDA graph",
+                            "config": {"workload": "decode step from the QKV projection output: mm3fa_decode_step "
+                                                   "(prologue kernel: QK-RMSNorm, NeoX RoPE theta 1e6, k/v append "
+                                                   "at row 8191; then the attention over KV 8192), "
+                                                   f"{n_layers} layers per CUDA graph",
                                        "n_seq": n_seq, "n_head": hq, "n_head_kv": hkv, "head_dim": D}}}
 
 

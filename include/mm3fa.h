@@ -211,6 +211,26 @@ MM3FA_API int mm3fa_decode_prologue(const mm3fa_tensor * q_in, const mm3fa_tenso
                                     mm3fa_tensor * v_cache, mm3fa_tensor * q_out, void * stream);
 
 /*
+ * Decode step of one LM layer as one call: mm3fa_decode_prologue followed by
+ * mm3fa_flash_attn_ext with the query q_out viewed as [D, 1, n_head, N] (outputs: q_out, the
+ * appended cache rows, dst).  The prologue arguments are those of mm3fa_decode_prologue; k, v,
+ * mask, scale, max_bias, logit_softcap, prec, dst, workspace and stream those of
+ * mm3fa_flash_attn_ext (k and v the attention's views of the caches; the workspace is sized by
+ * mm3fa_workspace_size with q_out's view).  Every operand is checked before anything is
+ * launched.  The two kernels are launched with programmatic stream serialisation, so the
+ * attention's CTAs start as the prologue's exit.
+ * No counterpart in the reference as one function: it replaces the nodes listed for
+ * mm3fa_decode_prologue plus ggml_flash_attn_ext at src/qwen3-lm.h:816-820.
+ */
+MM3FA_API int mm3fa_decode_step(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
+                                const float * q_norm, const float * k_norm, float eps, const int32_t * pos,
+                                float rope_theta, const int64_t * rows, mm3fa_tensor * k_cache,
+                                mm3fa_tensor * v_cache, mm3fa_tensor * q_out, const mm3fa_tensor * k,
+                                const mm3fa_tensor * v, const mm3fa_tensor * mask, float scale, float max_bias,
+                                float logit_softcap, int prec, mm3fa_tensor * dst, void * workspace,
+                                size_t workspace_bytes, void * stream);
+
+/*
  * DiT attention prologue: the nodes between the QKV projection and the attention call of a
  * DiT block, as one kernel (src/dit.h:201-220):
  *   q_out = rope_neox(q_in, pos, rot_dims)          (F32, same [D, n_head, S, B] layout)

@@ -52,51 +52,7 @@ cudaError_t launch_prologue(Kern kern, unsigned blocks, const Params & p, cudaSt
 
 
 template <int E>
-__device__ __forceinline__ void store_cache_row(char * row, int kvt, const float (&y)[E], int lane) {
-    if (kvt == KV_Q8_0) {
-        // a 32-value block spans 32/E lanes
-        constexpr int LPB  = QK8_0 / E;
-        float         amax = 0.0f;
-#pragma unroll
-        for (int e = 0; e < E; e++) {
-            amax = fmaxf(amax, fabsf(y[e]));
-        }
-#pragma unroll
-        for (int o = 1; o < LPB; o <<= 1) {
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        }
-        const float d    = amax / 127.0f;
-        const float id   = d != 0.0f ? 1.0f / d : 0.0f;
-        const int   blk  = lane / LPB;
-        char *      bp   = row + blk * Q8_0_BLOCK;
-        const int   off  = (lane % LPB) * E;
-#pragma unroll
-        for (int e = 0; e < E; e++) {
-            bp[2 + off + e] = (char) (int8_t) roundf(y[e] * id);
-        }
-        if (lane % LPB == 0) {
-            *reinterpret_cast<__half *>(bp) = __float2half_rn(d);
-        }
-        return;
-    }
-    if (kvt == KV_BF16) {
-        __nv_bfloat16 * r = reinterpret_cast<__nv_bfloat16 *>(row) + lane * E;
-#pragma unroll
-        for (int e = 0; e < E; e++) {
-            r[e] = __float2bfloat16_rn(y[e]);
-        }
-        return;
-    }
-    __half * r = reinterpret_cast<__half *>(row) + lane * E;
-#pragma unroll
-    for (int e = 0; e < E; e++) {
-        r[e] = __float2half_rn(y[e]);
-    }
-}
-
-template <int E>
 __global__ void __launch_bounds__(32 * PRO_WARPS) decode_prologue_kernel(const PrologueParams p) {
-    constexpr int D    = 32 * E;
     const int     lane = threadIdx.x & 31;
     const int     w    = (int) blockIdx.x * PRO_WARPS + (int) (threadIdx.x >> 5);
     const int     per  = p.n_head + 2 * p.n_head_kv;  // vectors per set: q heads, k heads, v heads
@@ -123,40 +79,8 @@ __global__ void __launch_bounds__(32 * PRO_WARPS) decode_prologue_kernel(const P
         }
         return;
     }
-    // ---- RMSNorm over the D values, then the weight
-    float ss = 0.0f;
-#pragma unroll
-    for (int e = 0; e < E; e++) {
-        ss = fmaf(x[e], x[e], ss);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    }
-    const float   scale = 1.0f / sqrtf(ss / (float) D + p.eps);
-    const float * wn    = kind == 0 ? p.q_norm : p.k_norm;
-#pragma unroll
-    for (int e = 0; e < E; e++) {
-        x[e] = (x[e] * scale) * wn[lane * E + e];
-    }
-    // ---- NeoX RoPE: pair i = lane*E + e (lanes 0-15) with i + D/2 (lane + 16, same e)
     float y[E];
-    {
-        const int lo = lane & 15;  // pair index base of this lane: lo*E
-        // theta of pair i: position * theta_scale^i, the scale applied i times in turn
-        float th = (float) p.pos[s];
-        for (int k = 0; k < lo * E; k++) {
-            th *= p.theta_scale;
-        }
-#pragma unroll
-        for (int e = 0; e < E; e++) {
-            const float c  = cosf(th), sn = sinf(th);
-            const float xo = __shfl_xor_sync(0xffffffffu, x[e], 16);  // the pair's other value
-            // lanes 0-15 hold x0 (first half), lanes 16-31 hold x1 (second half)
-            y[e] = lane < 16 ? x[e] * c - xo * sn : xo * sn + x[e] * c;
-            th *= p.theta_scale;
-        }
-    }
+    rms_norm_rope_vec<E>(x, y, kind == 0 ? p.q_norm : p.k_norm, p.eps, (float) p.pos[s], p.theta_scale, lane);
     if (kind == 0) {
         float * dst = reinterpret_cast<float *>(p.q_out + (int64_t) hh * p.qo_nb1 + (int64_t) s * p.qo_nb2);
 #pragma unroll

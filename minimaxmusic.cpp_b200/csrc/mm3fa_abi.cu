@@ -603,10 +603,15 @@ int mm3fa_flash_attn_ext_kvlen(const mm3fa_tensor * q, const mm3fa_tensor * k, c
                            workspace_bytes, stream);
 }
 
-int mm3fa_decode_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
-                          const float * q_norm, const float * k_norm, float eps, const int32_t * pos, float rope_theta,
-                          const int64_t * rows, mm3fa_tensor * k_cache, mm3fa_tensor * v_cache, mm3fa_tensor * q_out,
-                          void * stream) {
+}  // extern "C"
+
+namespace {
+
+// Checks the decode prologue's operands (mm3fa_decode_prologue) and fills its parameters.
+int prepare_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
+                     const float * q_norm, const float * k_norm, float eps, const int32_t * pos, float rope_theta,
+                     const int64_t * rows, mm3fa_tensor * k_cache, mm3fa_tensor * v_cache, mm3fa_tensor * q_out,
+                     PrologueParams & p, int64_t & D_out) {
     if (!q_in || !k_in || !v_in || !k_cache || !v_cache || !q_out || !q_norm || !k_norm || !pos || !rows) {
         return MM3FA_ERR_NULL;
     }
@@ -661,7 +666,6 @@ int mm3fa_decode_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, 
     if (device_info().major != 10) {
         return MM3FA_ERR_DEVICE;
     }
-    PrologueParams p{};
     p.q_in        = static_cast<const char *>(q_in->data);
     p.k_in        = static_cast<const char *>(k_in->data);
     p.v_in        = static_cast<const char *>(v_in->data);
@@ -694,7 +698,68 @@ int mm3fa_decode_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, 
     p.v_rows      = v_cache->ne[1];
     p.eps         = eps;
     p.theta_scale = std::pow(rope_theta, -2.0f / (float) D);
+    D_out         = D;
+    return MM3FA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mm3fa_decode_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
+                          const float * q_norm, const float * k_norm, float eps, const int32_t * pos, float rope_theta,
+                          const int64_t * rows, mm3fa_tensor * k_cache, mm3fa_tensor * v_cache, mm3fa_tensor * q_out,
+                          void * stream) {
+    PrologueParams p{};
+    int64_t        D  = 0;
+    const int      st = prepare_prologue(q_in, k_in, v_in, q_norm, k_norm, eps, pos, rope_theta, rows, k_cache, v_cache,
+                                         q_out, p, D);
+    if (st != MM3FA_OK) {
+        return st;
+    }
     return record_cuda(launch_decode_prologue(p, (int) D, static_cast<cudaStream_t>(stream)));
+}
+
+int mm3fa_decode_step(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
+                      const float * q_norm, const float * k_norm, float eps, const int32_t * pos, float rope_theta,
+                      const int64_t * rows, mm3fa_tensor * k_cache, mm3fa_tensor * v_cache, mm3fa_tensor * q_out,
+                      const mm3fa_tensor * k, const mm3fa_tensor * v, const mm3fa_tensor * mask, float scale,
+                      float max_bias, float logit_softcap, int prec, mm3fa_tensor * dst, void * workspace,
+                      size_t workspace_bytes, void * stream) {
+    PrologueParams pp{};
+    int64_t        D  = 0;
+    int            st = prepare_prologue(q_in, k_in, v_in, q_norm, k_norm, eps, pos, rope_theta, rows, k_cache, v_cache,
+                                         q_out, pp, D);
+    if (st != MM3FA_OK) {
+        return st;
+    }
+    if (!k || !v) {
+        return MM3FA_ERR_NULL;
+    }
+    // the attention reads q_out as [D, 1, n_head, N]; its operands are checked before the
+    // prologue runs, so that a rejected call changes nothing
+    mm3fa_tensor qa = *q_out;
+    qa.ne[0] = D, qa.ne[1] = 1, qa.ne[2] = q_out->ne[1], qa.ne[3] = q_out->ne[2];
+    qa.nb[0] = 4, qa.nb[1] = (size_t) (4 * D), qa.nb[2] = q_out->nb[1], qa.nb[3] = q_out->nb[2];
+    {
+        OpShape sh{};
+        st = check_op(&qa, k, v, mask, max_bias, logit_softcap, dst, true, sh);
+        if (st != MM3FA_OK) {
+            return st;
+        }
+        const size_t need = mm3fa_workspace_size(&qa, k, v, mask, dst);
+        if (need > 0 && (!workspace || workspace_bytes < need)) {
+            return MM3FA_ERR_WORKSPACE;
+        }
+    }
+    // the prologue kernel, then the attention (both launched with programmatic stream
+    // serialisation, so the attention's CTAs start as the prologue's exit)
+    st = record_cuda(launch_decode_prologue(pp, (int) D, static_cast<cudaStream_t>(stream)));
+    if (st != MM3FA_OK) {
+        return st;
+    }
+    return flash_attn_impl(&qa, k, v, mask, nullptr, scale, max_bias, logit_softcap, prec, dst, workspace,
+                           workspace_bytes, stream);
 }
 
 int mm3fa_dit_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,

@@ -80,6 +80,11 @@ def lib():
                                             ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p, P, P, P,
                                             ctypes.c_void_p]
         L.mm3fa_decode_prologue.restype = ctypes.c_int
+        L.mm3fa_decode_step.argtypes = [P, P, P, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p,
+                                        ctypes.c_float, ctypes.c_void_p, P, P, P, P, P, P, ctypes.c_float,
+                                        ctypes.c_float, ctypes.c_float, ctypes.c_int, P, ctypes.c_void_p,
+                                        ctypes.c_size_t, ctypes.c_void_p]
+        L.mm3fa_decode_step.restype = ctypes.c_int
         L.mm3fa_flash_attn_ext_kvlen.argtypes = [P, P, P, P, ctypes.c_void_p, ctypes.c_float, ctypes.c_float,
                                                  ctypes.c_float, ctypes.c_int, P, ctypes.c_void_p, ctypes.c_size_t,
                                                  ctypes.c_void_p]
@@ -178,6 +183,23 @@ def decode_prologue(q_in: Tensor, k_in: Tensor, v_in: Tensor, q_norm_ptr: int, k
                                      ctypes.c_void_p(stream or None))
     if st != OK:
         raise MM3FAError(st, "mm3fa_decode_prologue")
+
+
+def decode_step(q_in: Tensor, k_in: Tensor, v_in: Tensor, q_norm_ptr: int, k_norm_ptr: int, eps: float,
+                pos_ptr: int, rope_theta: float, rows_ptr: int, k_cache: Tensor, v_cache: Tensor, q_out: Tensor,
+                k: Tensor, v: Tensor, mask: Tensor | None, scale: float, max_bias: float, logit_softcap: float,
+                dst: Tensor, workspace: int, workspace_bytes: int, stream: int = 0,
+                prec: int = GGML_PREC_F32) -> None:
+    """decode_prologue followed by flash_attn_ext on q_out viewed as [D, 1, n_head, N], as one call
+    (fused into the tensor-core decode kernel when k/v are the caches themselves)."""
+    st = lib().mm3fa_decode_step(_ref(q_in), _ref(k_in), _ref(v_in), ctypes.c_void_p(q_norm_ptr),
+                                 ctypes.c_void_p(k_norm_ptr), eps, ctypes.c_void_p(pos_ptr), rope_theta,
+                                 ctypes.c_void_p(rows_ptr), _ref(k_cache), _ref(v_cache), _ref(q_out), _ref(k),
+                                 _ref(v), _ref(mask), scale, max_bias, logit_softcap,
+                                 prec, _ref(dst), ctypes.c_void_p(workspace or None), workspace_bytes,
+                                 ctypes.c_void_p(stream or None))
+    if st != OK:
+        raise MM3FAError(st, "mm3fa_decode_step")
 
 
 def assemble_heads(gathered_ptr: int, dst_ptr: int, dv: int, n_head: int, n_q: int, n_seq: int, n_ranks: int,
