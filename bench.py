@@ -307,10 +307,10 @@ def bench_dense(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, world:
 def bench_q8(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, world: int, n_layers: int) -> dict:
     """Q8_0 KV-cache decode (benchmark config 3: config 1 at KV 8192 with Q8_0 K/V, int8 ~U[-127,127],
     fp16 scales ~U[0.001,0.02]), as a 36-layer step of independent caches in one CUDA graph; each
-    rank holds its kv-head shard of its own CFG pair, like the F16 line."""
+    rank holds its kv-head shard of `world` CFG pairs, like the F16 line (16 units per rank)."""
     g = torch.Generator(device=dev)
     g.manual_seed(77)
-    n_seq, hkv, hq = 2, N_HEAD_KV // world, N_HEAD // world
+    n_seq, hkv, hq = 2 * world, N_HEAD_KV // world, N_HEAD // world  # per-rank work fixed as N grows
     nblk = D // 32
     rb = nblk * 34
 
@@ -380,10 +380,10 @@ def bench_decode_step(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, 
     """Decode step from the QKV projection output (the nodes of src/qwen3-lm.h:764-820): per layer
     mm3fa_decode_step (the prologue kernel: RMSNorm + NeoX RoPE of q/k, k/v rows appended to the F16
     caches at row 8191; then the attention over the 8192-row views), 36 layers in one CUDA graph;
-    also the prologue alone.  Shapes of the headline (per rank: its kv-head shard of a CFG pair)."""
+    also the prologue alone.  Shapes of the headline (per rank: its kv-head shard of `world` CFG pairs)."""
     g = torch.Generator(device=dev)
     g.manual_seed(55)
-    n_seq, hkv, hq = 2, N_HEAD_KV // world, N_HEAD // world
+    n_seq, hkv, hq = 2 * world, N_HEAD_KV // world, N_HEAD // world  # per-rank work fixed as N grows
     row = N_KV - 1
     keep, layers = [], []
     mask = torch.zeros(n_seq, 1, 1, N_KV, dtype=torch.float16, device=dev)
