@@ -80,6 +80,8 @@ struct MmaSmem {
     static constexpr int OFF_QX     = (OFF_FLAG + 16 + 15) / 16 * 16;
     static constexpr int QX_B       = Q8 ? NT * (D / QK8_0) * 32 * 16 : 0;
     static constexpr int TOTAL      = OFF_QX + QX_B + 1024;   // + alignment slack for the ring
+    // the cluster merge parks the 4 warps' O fragments ([warp][8 NT rows][D + 4] floats) in the ring
+    static_assert(MMA_CONSUMERS * 8 * NT * (D + 4) * 4 <= NS * STAGE, "merge staging exceeds the ring");
 };
 
 // ------------------------------------------------------------------ PTX helpers
@@ -599,7 +601,10 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
         if constexpr (CLUSTER) {
             // one unit per CTA, so the ring is free: each warp parks its raw O fragments there,
             // then all consumer threads combine the 4 warps per (row, 4 dims) in one pass
-            float * o4 = reinterpret_cast<float *>(smem);  // [warp][8 NT rows][D]
+            // [warp][8 NT rows][OD]: rows padded by 4 floats so that the fragment stores of one
+            // warp (rows 2 q4, dims g4 + 16 m) fall in 32 different banks
+            constexpr int OD = D + 4;
+            float *       o4 = reinterpret_cast<float *>(smem);
             named_barrier_consumers();  // every warp is done reading the ring
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
@@ -619,11 +624,11 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                 for (int m = 0; m < KS; m++) {
                     const int r  = nt * 8 + 2 * q4;
                     const int d  = acc_dim(m, 0), d1 = acc_dim(m, 1);
-                    float *   ow = o4 + (size_t) warp * 8 * NT * D;
-                    ow[r * D + d]        = acc[m][nt][0];
-                    ow[(r + 1) * D + d]  = acc[m][nt][1];
-                    ow[r * D + d1]       = acc[m][nt][2];
-                    ow[(r + 1) * D + d1] = acc[m][nt][3];
+                    float *   ow = o4 + (size_t) warp * 8 * NT * OD;
+                    ow[r * OD + d]        = acc[m][nt][0];
+                    ow[(r + 1) * OD + d]  = acc[m][nt][1];
+                    ow[r * OD + d1]       = acc[m][nt][2];
+                    ow[(r + 1) * OD + d1] = acc[m][nt][3];
                 }
             }
             named_barrier_consumers();
@@ -658,7 +663,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
 #pragma unroll
                 for (int w = 0; w < MMA_CONSUMERS; w++) {
                     const float  wt = mw[w] == -INFINITY ? 0.0f : exp2f(mw[w] - M);
-                    const float4 v  = *reinterpret_cast<const float4 *>(o4 + ((size_t) w * 8 * NT + r) * D + d);
+                    const float4 v  = *reinterpret_cast<const float4 *>(o4 + ((size_t) w * 8 * NT + r) * OD + d);
                     O.x += wt * v.x;
                     O.y += wt * v.y;
                     O.z += wt * v.z;
