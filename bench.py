@@ -51,7 +51,7 @@ FALLBACK_HBM_GBS = 6650.0
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode launch at this workload (ncu capture)
 NCU_KERNEL = "fa_decode_mma_kernel<128,f16,NT=1,cluster,NS=3>"
-NCU_TRAFFIC_BYTES = 67225600 + 615936
+NCU_TRAFFIC_BYTES = 67225600 + 466432
 
 
 def layer_bytes(n_seq: int, n_head_kv: int, n_head: int) -> int:
