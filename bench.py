@@ -25,7 +25,7 @@ Printed JSON: value = whole-job algorithmic GB/s of the timed steps (device time
 ranks); e2e = the same through the C ABI with Q/mask copied from pinned host memory and the
 outputs read back every step (copies in chunks of E2E_CHUNK layers on two copy streams,
 overlapping the attention of the other chunks); roofline = the decode kernel's achieved GB/s vs the measured
-HBM copy bandwidth; cpu_baseline = the CPU oracle (ggml convention) on the host cores.
+HBM copy bandwidth; cpu_baseline = the CPU oracle (ggml-cpu algorithm) on the host cores.
 """
 from __future__ import annotations
 
@@ -151,11 +151,11 @@ def cpu_baseline(seconds: float = 10.0) -> dict:
     cases = [workloads.decode_case(n_seq=2, n_kv=N_KV, max_seq=N_KV, kv_std=0.5, seed=1000 + i)
              for i in range(n_distinct)]
     descs = [(c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), c.mask.host_desc(), c.scale) for c in cases]
-    oracle.flash_attn_ext(*descs[0], mode=oracle.MODE_GGML, threads=threads)  # warm
+    oracle.flash_attn_ext(*descs[0], mode=oracle.MODE_F32ACC, threads=threads)  # warm
     t0 = time.perf_counter()
     n = 0
     while True:
-        oracle.flash_attn_ext(*descs[n % n_distinct], mode=oracle.MODE_GGML, threads=threads)
+        oracle.flash_attn_ext(*descs[n % n_distinct], mode=oracle.MODE_F32ACC, threads=threads)
         n += 1
         if time.perf_counter() - t0 >= seconds:
             break
@@ -163,7 +163,7 @@ def cpu_baseline(seconds: float = 10.0) -> dict:
     b = layer_bytes(2, N_HEAD_KV, N_HEAD)
     return {"value": round(b * n / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{n} decode-attention layers (B=2, KV 8192, 32q/8kv, D=128, F16 K/V) cycling over "
-                      f"{n_distinct} distinct caches, {dt:.1f} s, oracle ggml-convention mode",
+                      f"{n_distinct} distinct caches, {dt:.1f} s, oracle F32-accumulation mode",
             "us_per_layer": round(dt / n * 1e6, 1)}
 
 
@@ -185,7 +185,7 @@ def run_reference(args) -> None:
 
     def step():
         for d in descs:
-            oracle.flash_attn_ext(*d, mode=oracle.MODE_GGML, threads=threads)
+            oracle.flash_attn_ext(*d, mode=oracle.MODE_F32ACC, threads=threads)
 
     for _ in range(args.warmup):
         step()
@@ -206,7 +206,7 @@ def run_reference(args) -> None:
                    "n_seq": 2, "n_kv": N_KV, "n_head": N_HEAD, "n_head_kv": N_HEAD_KV, "head_dim": D,
                    "kv_type": "f16", "us_per_layer": round(us_layer, 1)},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{n_layers_per_step} distinct layers per step, oracle ggml-convention mode "
+                         "sample": f"{n_layers_per_step} distinct layers per step, oracle F32-accumulation mode "
                                    "(ggml, the reference's implementation, is absent from the reference tree)"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

@@ -132,14 +132,34 @@ MM3FA_API int mm3fa_flash_attn_ext_kvlen(const mm3fa_tensor * q, const mm3fa_ten
  *   - Returns MM3FA_ERR_SCRATCH_LIMIT, enqueuing nothing, when the operands need more scratch
  *     than the buffer holds (mm3fa_workspace_size > MM3FA_NOALLOC_SCRATCH_BYTES).
  *   - The first call on a device looks up the buffer's device address (cudaGetSymbolAddress)
- *     with that device current; make that first call before any stream capture.
- *   - Each call clears the buffer's counters on `stream` and allocates nothing.  All calls on a
- *     device share the buffer: calls that can overlap on the GPU (unordered streams) race.
+ *     with that device current; make that first call before any stream capture.  The address
+ *     is cached per device and CUDA context; after cudaDeviceReset the next call looks it up
+ *     again (so again outside capture).
+ *   - Each call clears the arrival counters its operands use on `stream` and allocates
+ *     nothing.  The status word is not cleared: a bounded device wait that expired inside a
+ *     call stays recorded until mm3fa_noalloc_status reads it.  All calls on a device share the
+ *     buffer: calls that can overlap on the GPU (unordered streams) race.
  * Replaces: nothing - it has no counterpart in the reference.
  */
 MM3FA_API int mm3fa_flash_attn_ext_noalloc(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
                                            const mm3fa_tensor * mask, float scale, float max_bias,
                                            float logit_softcap, int prec, mm3fa_tensor * dst, void * stream);
+
+/*
+ * mm3fa_workspace_status for the built-in buffer of mm3fa_flash_attn_ext_noalloc on the current
+ * device: MM3FA_OK, or MM3FA_ERR_TIMEOUT (status cleared) when a bounded wait of an earlier
+ * no-allocation call expired; *status_out gets the raw bits.  Synchronises `stream`.
+ * Replaces: nothing - it has no counterpart in the reference.
+ */
+MM3FA_API int mm3fa_noalloc_status(void * stream, uint32_t * status_out);
+
+/*
+ * mm3fa_selftest_bounded_wait on the built-in buffer of mm3fa_flash_attn_ext_noalloc: a wait that
+ * nothing satisfies expires after timeout_us and is recorded in that buffer's status word, so
+ * that tests can check mm3fa_noalloc_status without faulting or hanging the GPU.
+ * Replaces: nothing - it has no counterpart in the reference.
+ */
+MM3FA_API int mm3fa_noalloc_selftest_bounded_wait(uint32_t timeout_us, void * stream);
 
 /*
  * Bytes of device workspace mm3fa_flash_attn_ext needs for these operands on the current

@@ -490,6 +490,37 @@ size_t mm3fa_workspace_size(const mm3fa_tensor * q, const mm3fa_tensor * k, cons
 
 }  // extern "C"
 
+namespace mm3fa {
+
+// Bytes right after the status word that must be zero when a call with these operands starts:
+// the decode kernels' per-unit arrival counters (one u32 per unit, the region rounded up to
+// 256 bytes).  The dense kernel's mask-block flags need nothing here: launch_dense clears
+// them on the stream itself.  Sized, like mm3fa_workspace_size, for every decode variant the
+// operands could take.  Used by the no-allocation entry point.
+size_t workspace_counter_bytes(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                               const mm3fa_tensor * mask, const mm3fa_tensor * dst) {
+    OpShape s{};
+    if (check_op(q, k, v, mask, 0.0f, 0.0f, dst, false, s) != MM3FA_OK || s.n_kv == 0 || s.n_q == 0 ||
+        s.n_head == 0 || s.n_seq == 0) {
+        return 0;
+    }
+    size_t    cnt  = 0;
+    const int rows = s.ratio * (int) s.n_q;
+    for (Variant var : { V_SIMT_BULK, V_SIMT_COPY, V_MMA_8, V_MMA_16 }) {
+        if (var == V_MMA_8 && !(rows <= 8 && decode_mma_eligible((int) s.D, s.kvt, rows))) {
+            continue;
+        }
+        if (var == V_MMA_16 && !(rows > 8 && decode_mma_eligible((int) s.D, s.kvt, rows))) {
+            continue;
+        }
+        const DecodeGeometry g = geometry_for(s, var);
+        cnt                    = std::max(cnt, ((size_t) g.n_units * 4 + 255) / 256 * 256);
+    }
+    return cnt;
+}
+
+}  // namespace mm3fa
+
 namespace {
 
 // The operator with an optional device array of per-sequence key counts (kv_len[s]: q sequence

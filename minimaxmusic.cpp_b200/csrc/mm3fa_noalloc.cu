@@ -1,5 +1,5 @@
 // mm3fa_noalloc.cu - mm3fa_flash_attn_ext_noalloc: the attention call for callers that
-// cannot allocate device memory.
+// cannot allocate device memory, and mm3fa_noalloc_status, which reads its status word.
 //
 // Some hosts of this operator are not allowed to call cudaMalloc at the point where they
 // run attention: a ggml backend whose buffers were all sized up front by ggml_gallocr, an
@@ -11,20 +11,33 @@
 // The buffer is the file-scope device array below, MM3FA_NOALLOC_SCRATCH_BYTES in size.  Every
 // GPU that loads the library holds one copy of it until the process exits.  Host code must not
 // pass the array's name to a kernel (on the host it only names a stand-in); the device address
-// is looked up once per device with cudaGetSymbolAddress on the first call made while that
-// device is current, so that first call should happen before any stream capture.
+// is looked up with cudaGetSymbolAddress on the first call made while a device (more exactly:
+// a CUDA context) is current, so that first call should happen before any stream capture.  The
+// address is cached per device together with the context it was looked up in, and looked up
+// again when the device's current context is a different one (after cudaDeviceReset).
 //
-// All calls on a device share the one buffer and it keeps the last call's contents; the
-// counters the kernel needs at zero are cleared (cudaMemsetAsync on the caller's stream) at the
-// start of every call.  Two calls that can run at the same time on the GPU - different streams
-// without ordering between them - race on the buffer and produce wrong results.
+// Layout (the workspace layout of mm3fa_flash_attn_ext): a 256-byte status word, then the
+// decode kernels' per-unit arrival counters, then partial results.  Every call clears the
+// counter region its operands use (cudaMemsetAsync on the caller's stream) and nothing else;
+// the status word is left as it is so that a bounded wait that expired inside a call stays
+// visible until mm3fa_noalloc_status reads and clears it.  All calls on a device share the one
+// buffer and it keeps the last call's contents.  Two calls that can run at the same time on
+// the GPU - different streams without ordering between them - race on the buffer and produce
+// wrong results.
 #include "../../include/mm3fa.h"
 #include "fa_common.cuh"
 #include "fa_decode.cuh"
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
+
+namespace mm3fa {
+// defined in mm3fa_abi.cu: bytes after the status word a call needs zeroed
+size_t workspace_counter_bytes(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                               const mm3fa_tensor * mask, const mm3fa_tensor * dst);
+}  // namespace mm3fa
 
 namespace {
 
@@ -32,10 +45,33 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[MM3FA_NOALLOC_S
 
 constexpr int MAX_DEVICES = 64;
 
-// Device address of g_noalloc_scratch on the current device (looked up once per device).
-cudaError_t scratch_address(void ** out) {
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+
+// The current CUDA context, or nullptr when it cannot be queried.
+CUcontext current_context() {
+    static CtxGetCurrentFn fn = [] {
+        void *                          p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return (CtxGetCurrentFn) nullptr;
+        }
+        return reinterpret_cast<CtxGetCurrentFn>(p);
+    }();
+    CUcontext c = nullptr;
+    if (fn && fn(&c) != CUDA_SUCCESS) {
+        c = nullptr;
+    }
+    return c;
+}
+
+// Device address of g_noalloc_scratch in the current device's context.  The first lookup in a
+// context also clears the status word (on `stream`), so every context starts from "no error".
+cudaError_t scratch_address(void ** out, cudaStream_t stream) {
     static std::mutex mu;
     static void *     addr[MAX_DEVICES] = {};
+    static CUcontext  ctx[MAX_DEVICES]  = {};
     int               dev               = 0;
     cudaError_t       e                 = cudaGetDevice(&dev);
     if (e != cudaSuccess) {
@@ -45,13 +81,22 @@ cudaError_t scratch_address(void ** out) {
         return cudaErrorInvalidDevice;
     }
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    CUcontext                   cur = current_context();  // nullptr before the device's first use
+    if (!cur || !addr[dev] || ctx[dev] != cur) {
+        // the lookup also creates the device's primary context when none is current yet
         void * p = nullptr;
         e        = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) {
             return e;
         }
-        addr[dev] = p;
+        cur = current_context();
+        if (!addr[dev] || ctx[dev] != cur) {
+            if ((e = cudaMemsetAsync(p, 0, mm3fa::WS_STATUS_BYTES, stream)) != cudaSuccess) {
+                return e;
+            }
+            addr[dev] = p;
+            ctx[dev]  = cur;
+        }
     }
     *out = addr[dev];
     return cudaSuccess;
@@ -73,18 +118,18 @@ int mm3fa_flash_attn_ext_noalloc(const mm3fa_tensor * q, const mm3fa_tensor * k,
     if (need > (size_t) MM3FA_NOALLOC_SCRATCH_BYTES) {
         return MM3FA_ERR_SCRATCH_LIMIT;
     }
-    void *      scratch = nullptr;
-    cudaError_t e       = scratch_address(&scratch);
+    cudaStream_t cs      = static_cast<cudaStream_t>(stream);
+    void *       scratch = nullptr;
+    cudaError_t  e       = scratch_address(&scratch, cs);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return MM3FA_ERR_CUDA;
     }
-    // The status word and the per-unit arrival counters must start at zero.  They sit at the
-    // front of the workspace and take at most 512 + need/4096 bytes (every unit also reserves
-    // >= 16 KiB of partial results), so for need <= the scratch size the first 64 KiB hold them.
-    const size_t zero_bytes = need < (size_t) 65536 ? need : (size_t) 65536;
-    if (zero_bytes > 0) {
-        e = cudaMemsetAsync(scratch, 0, zero_bytes, static_cast<cudaStream_t>(stream));
+    // the arrival counters of this call's decode geometry must start at zero (earlier calls
+    // may have used the region for partial results); the status word is kept
+    const size_t counters = mm3fa::workspace_counter_bytes(q, k, v, mask, dst);
+    if (counters > 0) {
+        e = cudaMemsetAsync(static_cast<char *>(scratch) + mm3fa::WS_STATUS_BYTES, 0, counters, cs);
         if (e != cudaSuccess) {
             cudaGetLastError();
             return MM3FA_ERR_CUDA;
@@ -92,6 +137,29 @@ int mm3fa_flash_attn_ext_noalloc(const mm3fa_tensor * q, const mm3fa_tensor * k,
     }
     return mm3fa_flash_attn_ext(q, k, v, mask, scale, max_bias, logit_softcap, prec, dst, scratch,
                                 (size_t) MM3FA_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+int mm3fa_noalloc_status(void * stream, uint32_t * status_out) {
+    if (!status_out) {
+        return MM3FA_ERR_NULL;
+    }
+    void *      scratch = nullptr;
+    cudaError_t e       = scratch_address(&scratch, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return MM3FA_ERR_CUDA;
+    }
+    return mm3fa_workspace_status(scratch, stream, status_out);
+}
+
+int mm3fa_noalloc_selftest_bounded_wait(uint32_t timeout_us, void * stream) {
+    void *      scratch = nullptr;
+    cudaError_t e       = scratch_address(&scratch, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return MM3FA_ERR_CUDA;
+    }
+    return mm3fa_selftest_bounded_wait(scratch, timeout_us, stream);
 }
 
 }  // extern "C"

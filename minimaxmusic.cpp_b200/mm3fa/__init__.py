@@ -76,6 +76,10 @@ def lib():
         L.mm3fa_flash_attn_ext_noalloc.argtypes = [P, P, P, P, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                                    ctypes.c_int, P, ctypes.c_void_p]
         L.mm3fa_flash_attn_ext_noalloc.restype = ctypes.c_int
+        L.mm3fa_noalloc_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]
+        L.mm3fa_noalloc_status.restype = ctypes.c_int
+        L.mm3fa_noalloc_selftest_bounded_wait.argtypes = [ctypes.c_uint32, ctypes.c_void_p]
+        L.mm3fa_noalloc_selftest_bounded_wait.restype = ctypes.c_int
         L.mm3fa_decode_prologue.argtypes = [P, P, P, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float,
                                             ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p, P, P, P,
                                             ctypes.c_void_p]
@@ -150,6 +154,14 @@ def flash_attn_ext_noalloc(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None,
                                             prec, _ref(dst), ctypes.c_void_p(stream or None))
     if st != OK:
         raise MM3FAError(st, "mm3fa_flash_attn_ext_noalloc")
+
+
+def noalloc_status(stream: int = 0) -> tuple[int, int]:
+    """(status, raw bits) of the built-in no-allocation buffer's status word, read and cleared
+    (MM3FA_ERR_TIMEOUT when a bounded wait of an earlier no-allocation call expired)."""
+    raw = ctypes.c_uint32(0)
+    st = lib().mm3fa_noalloc_status(ctypes.c_void_p(stream or None), ctypes.byref(raw))
+    return st, raw.value
 
 
 def flash_attn_ext_kvlen(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None, kv_len_ptr: int, scale: float,

@@ -18,17 +18,29 @@
 // It is cross-checked against torch SDPA in float64 and, for Q8_0, against gguf-py 0.19.0's
 // numpy codec (tests/test_oracle.py).
 //
-// Two modes:
-//   ORC_EXACT  (0): double accumulation everywhere, Q used at full precision: ground truth.
-//   ORC_GGML   (1): ggml's CPU convention - Q rounded to K's vec-dot type before the dot
-//                   (F16/BF16 rounding, or Q8_0 quantization when K is Q8_0), F32 scores,
-//                   one-pass F32 online softmax, F32 V accumulation.
+// Three modes:
+//   ORC_EXACT    (0): double accumulation everywhere, Q used at full precision: ground truth.
+//   ORC_F32ACC   (1): Q rounded to K's vec-dot type before the dot (F16/BF16 rounding, or
+//                     Q8_0 quantization when K is Q8_0), F32 scores, one-pass F32 online
+//                     softmax, F32 V accumulation: the precision the callers ask for with
+//                     ggml_flash_attn_ext_set_prec(GGML_PREC_F32) (src/qwen3-lm.h:435,820,
+//                     src/dit.h:222).  This is the parity bar of the GPU kernels.
+//   ORC_GGML_CPU (2): ggml's CPU kernel as published in ggml-cpu (the one-row-at-a-time
+//                     flash_attn_ext_f16 loop: Q converted to K's vec_dot_type, kq_vec_dot,
+//                     expf online softmax), which keeps the V accumulator in F16 when V is F16
+//                     (ggml_vec_mad_f16: y <- f16(y + v*p), ggml_vec_scale_f16 on a new
+//                     maximum) and in F32 otherwise (V converted with to_float).  ggml-cpu
+//                     ignores the F32 precision request, so this is what the reference's
+//                     CPU backend would compute; with F16 V it is less accurate than
+//                     ORC_F32ACC (one f16 rounding per key of the accumulated sum).
 //
 // Formats restated from their published definitions:
 //   * IEEE 754 binary16 / bfloat16 conversions (round to nearest even);
 //   * ggml Q8_0: blocks of 32 values = fp16 scale d + 32 int8 q, value = d*q; quantizer
-//     d = max|x|/127, q = roundf(x/d) (gguf-py quants.py Q8_0 follows the same recipe);
+//     d = max|x|/127, id = 1/d, q = roundf(x*id) (gguf-py quants.py Q8_0 follows the
+//     same recipe);
 //   * ALiBi slopes for max_bias > 0 (Press et al.; ggml's n_head_log2 split into m0/m1).
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdint>
@@ -51,7 +63,7 @@ typedef struct orc_tensor {
 } orc_tensor;
 
 enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q8_0 = 8, ORC_BF16 = 30 };
-enum { ORC_EXACT = 0, ORC_GGML = 1 };
+enum { ORC_EXACT = 0, ORC_F32ACC = 1, ORC_GGML_CPU = 2 };
 enum { QK8_0 = 32, Q8_0_BLOCK_BYTES = 34 };
 
 // ---------------------------------------------------------------- scalar formats
@@ -222,7 +234,7 @@ float orc_alibi_slope(int h, int n_head, float max_bias) {
     return h < n_head_log2 ? std::pow(m0, (float) (h + 1)) : std::pow(m1, (float) (2 * (h - n_head_log2) + 1));
 }
 
-// ---------------------------------------------------------------- dot / axpy kernels (ggml mode)
+// ---------------------------------------------------------------- vector kernels
 
 static inline float dot_f32(const float * a, const float * b, int64_t n) {
     float acc[8] = { 0, 0, 0, 0, 0, 0, 0, 0 };
@@ -238,6 +250,34 @@ static inline float dot_f32(const float * a, const float * b, int64_t n) {
     }
     return s;
 }
+
+// float64 dot of two float rows (four independent partial sums)
+static inline double dot_f64_scalar(const float * a, const float * b, int64_t n) {
+    double  acc[4] = { 0, 0, 0, 0 };
+    int64_t i      = 0;
+    for (; i + 4 <= n; i += 4) {
+        for (int l = 0; l < 4; l++) {
+            acc[l] += (double) a[i + l] * (double) b[i + l];
+        }
+    }
+    double s = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    for (; i < n; i++) {
+        s += (double) a[i] * (double) b[i];
+    }
+    return s;
+}
+
+static inline void axpy_f64_scalar(double * y, const float * x, double a, int64_t n) {
+    for (int64_t i = 0; i < n; i++) {
+        y[i] += a * (double) x[i];
+    }
+}
+
+// One step of the F16 accumulator of ggml's CPU kernel (ggml_vec_mad_f16): y <- f16(y + x*v),
+// the product and sum formed in F32 with one rounding (FMA), then rounded to F16.
+static inline void mad_f16_scalar(uint16_t * y, const uint16_t * x, float v, int64_t n);
+// ggml_vec_scale_f16: y <- f16(y * v)
+static inline void scale_f16_scalar(uint16_t * y, float v, int64_t n);
 
 #if defined(__x86_64__)
 __attribute__((target("avx2,fma,f16c"))) static float dot_f32_f16_avx2(const float * a, const uint16_t * b,
@@ -274,11 +314,114 @@ __attribute__((target("avx2,fma,f16c"))) static void axpy_f16_avx2(float * y, co
     }
 }
 
+__attribute__((target("avx2,fma,f16c"))) static void mad_f16_avx2(uint16_t * y, const uint16_t * x, float v,
+                                                                    int64_t n) {
+    const __m256 vv = _mm256_set1_ps(v);
+    int64_t      i  = 0;
+    for (; i + 8 <= n; i += 8) {
+        __m256 xv = _mm256_cvtph_ps(_mm_loadu_si128((const __m128i *) (x + i)));
+        __m256 yv = _mm256_cvtph_ps(_mm_loadu_si128((const __m128i *) (y + i)));
+        yv        = _mm256_fmadd_ps(xv, vv, yv);
+        _mm_storeu_si128((__m128i *) (y + i), _mm256_cvtps_ph(yv, _MM_FROUND_TO_NEAREST_INT));
+    }
+    mad_f16_scalar(y + i, x + i, v, n - i);
+}
+
+__attribute__((target("avx2,fma,f16c"))) static void scale_f16_avx2(uint16_t * y, float v, int64_t n) {
+    const __m256 vv = _mm256_set1_ps(v);
+    int64_t      i  = 0;
+    for (; i + 8 <= n; i += 8) {
+        __m256 yv = _mm256_cvtph_ps(_mm_loadu_si128((const __m128i *) (y + i)));
+        _mm_storeu_si128((__m128i *) (y + i), _mm256_cvtps_ph(_mm256_mul_ps(yv, vv), _MM_FROUND_TO_NEAREST_INT));
+    }
+    scale_f16_scalar(y + i, v, n - i);
+}
+
+__attribute__((target("avx2,fma"))) static double dot_f64_avx2(const float * a, const float * b, int64_t n) {
+    __m256d acc0 = _mm256_setzero_pd(), acc1 = _mm256_setzero_pd();
+    int64_t i    = 0;
+    for (; i + 8 <= n; i += 8) {
+        acc0 = _mm256_fmadd_pd(_mm256_cvtps_pd(_mm_loadu_ps(a + i)), _mm256_cvtps_pd(_mm_loadu_ps(b + i)), acc0);
+        acc1 = _mm256_fmadd_pd(_mm256_cvtps_pd(_mm_loadu_ps(a + i + 4)), _mm256_cvtps_pd(_mm_loadu_ps(b + i + 4)),
+                               acc1);
+    }
+    acc0      = _mm256_add_pd(acc0, acc1);
+    double t[4];
+    _mm256_storeu_pd(t, acc0);
+    double s = (t[0] + t[1]) + (t[2] + t[3]);
+    for (; i < n; i++) {
+        s += (double) a[i] * (double) b[i];
+    }
+    return s;
+}
+
+__attribute__((target("avx2,fma"))) static void axpy_f64_avx2(double * y, const float * x, double a, int64_t n) {
+    const __m256d va = _mm256_set1_pd(a);
+    int64_t       i  = 0;
+    for (; i + 4 <= n; i += 4) {
+        _mm256_storeu_pd(y + i, _mm256_fmadd_pd(va, _mm256_cvtps_pd(_mm_loadu_ps(x + i)), _mm256_loadu_pd(y + i)));
+    }
+    for (; i < n; i++) {
+        y[i] += a * (double) x[i];
+    }
+}
+
 static const bool g_has_avx2 = __builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma") &&
                                __builtin_cpu_supports("f16c");
 #else
 static const bool g_has_avx2 = false;
 #endif
+
+static inline void mad_f16_scalar(uint16_t * y, const uint16_t * x, float v, int64_t n) {
+    for (int64_t i = 0; i < n; i++) {
+        y[i] = orc_f32_to_f16(std::fmaf(g_f16_table[x[i]], v, g_f16_table[y[i]]));
+    }
+}
+
+static inline void scale_f16_scalar(uint16_t * y, float v, int64_t n) {
+    for (int64_t i = 0; i < n; i++) {
+        y[i] = orc_f32_to_f16(g_f16_table[y[i]] * v);
+    }
+}
+
+static inline void mad_f16(uint16_t * y, const uint16_t * x, float v, int64_t n) {
+#if defined(__x86_64__)
+    if (g_has_avx2) {
+        mad_f16_avx2(y, x, v, n);
+        return;
+    }
+#endif
+    mad_f16_scalar(y, x, v, n);
+}
+
+static inline void scale_f16(uint16_t * y, float v, int64_t n) {
+#if defined(__x86_64__)
+    if (g_has_avx2) {
+        scale_f16_avx2(y, v, n);
+        return;
+    }
+#endif
+    scale_f16_scalar(y, v, n);
+}
+
+static inline double dot_f64(const float * a, const float * b, int64_t n) {
+#if defined(__x86_64__)
+    if (g_has_avx2) {
+        return dot_f64_avx2(a, b, n);
+    }
+#endif
+    return dot_f64_scalar(a, b, n);
+}
+
+static inline void axpy_f64(double * y, const float * x, double a, int64_t n) {
+#if defined(__x86_64__)
+    if (g_has_avx2) {
+        axpy_f64_avx2(y, x, a, n);
+        return;
+    }
+#endif
+    axpy_f64_scalar(y, x, a, n);
+}
 
 // Q8_0 x Q8_0 dot: per block int32 sum times the product of both fp16 scales.
 static float dot_q8_0(const uint8_t * a, const uint8_t * b, int64_t n) {
@@ -321,18 +464,43 @@ static int64_t type_row_bytes(int type, int64_t n) {
     }
 }
 
+// Per-thread scratch.  The exact mode converts the K and V slab of one (kv head, kv sequence)
+// to float once and reuses it for every query row of that slab the thread takes.
+struct orc_scratch {
+    std::vector<float>    qf, kf, vf, accf;
+    std::vector<double>   accd, sc;
+    std::vector<uint8_t>  qq;
+    std::vector<uint16_t> q16, acc16;
+    std::vector<float>    kslab, vslab;
+    int64_t               slab_kh = -1, slab_ks = -1;
+};
+
+static void load_slab(const orc_job & J, int64_t kh, int64_t ks, orc_scratch & W) {
+    if (W.slab_kh == kh && W.slab_ks == ks) {
+        return;
+    }
+    const int64_t D = J.k->ne[0], DV = J.v->ne[0], n_kv = J.k->ne[1];
+    W.kslab.resize((size_t) (n_kv * D));
+    W.vslab.resize((size_t) (n_kv * DV));
+    for (int64_t j = 0; j < n_kv; j++) {
+        row_to_f32(J.k->type, elem_ptr(J.k, j, kh, ks), W.kslab.data() + j * D, D);
+        row_to_f32(J.v->type, elem_ptr(J.v, j, kh, ks), W.vslab.data() + j * DV, DV);
+    }
+    W.slab_kh = kh;
+    W.slab_ks = ks;
+}
+
 // One query row (i, h, s) of the operator.
-static void run_row(const orc_job & J, int64_t i, int64_t h, int64_t s, std::vector<float> & qf,
-                    std::vector<float> & kf, std::vector<float> & vf, std::vector<double> & accd,
-                    std::vector<float> & accf, std::vector<uint8_t> & qq, std::vector<uint16_t> & q16) {
+static void run_row(const orc_job & J, int64_t i, int64_t h, int64_t s, orc_scratch & W) {
     const orc_tensor *q = J.q, *k = J.k, *v = J.v, *mask = J.mask;
     const int64_t     D = q->ne[0], DV = v->ne[0], n_kv = k->ne[1];
     const int64_t     n_head = q->ne[2];
     const int64_t     kh     = h / (q->ne[2] / k->ne[2]);
     const int64_t     ks     = s / (q->ne[3] / k->ne[3]);
     const float       slope  = orc_alibi_slope((int) h, (int) n_head, J.max_bias);
+    float *           qf     = W.qf.data();
 
-    row_to_f32(q->type, elem_ptr(q, i, h, s), qf.data(), D);
+    row_to_f32(q->type, elem_ptr(q, i, h, s), qf, D);
     const uint8_t * mrow = nullptr;
     if (mask) {
         mrow = (const uint8_t *) mask->data + i * mask->nb[1] + (h % mask->ne[2]) * mask->nb[2] +
@@ -354,61 +522,64 @@ static void run_row(const orc_job & J, int64_t i, int64_t h, int64_t s, std::vec
     float *dst_row = (float *) ((uint8_t *) J.dst->data + h * J.dst->nb[1] + i * J.dst->nb[2] + s * J.dst->nb[3]);
 
     if (J.mode == ORC_EXACT) {
-        // two-pass softmax in double: scores, max, exp-sum, weighted V
-        std::vector<double> sc((size_t) n_kv);
-        double              mx = -INFINITY;
+        // two-pass softmax in double over the float slab: scores, max, exp-sum, weighted V
+        load_slab(J, kh, ks, W);
+        double * sc = W.sc.data();
+        double   mx = -INFINITY;
         for (int64_t j = 0; j < n_kv; j++) {
-            row_to_f32(k->type, elem_ptr(k, j, kh, ks), kf.data(), D);
-            double dot = 0.0;
-            for (int64_t d = 0; d < D; d++) {
-                dot += (double) qf[d] * (double) kf[d];
+            const float mv = mask_at(j);
+            if (mv == -INFINITY) {
+                sc[j] = -INFINITY;
+                continue;
             }
-            double sv = dot * (double) J.scale;
+            double sv = dot_f64(qf, W.kslab.data() + j * D, D) * (double) J.scale;
             if (J.softcap != 0.0f) {
                 sv = (double) J.softcap * std::tanh(sv / (double) J.softcap);
             }
-            sv += (double) slope * (double) mask_at(j);
-            sc[(size_t) j] = sv;
+            sv += (double) slope * (double) mv;
+            sc[j] = sv;
             if (sv > mx) {
                 mx = sv;
             }
         }
-        std::fill(accd.begin(), accd.end(), 0.0);
+        double * accd = W.accd.data();
+        std::fill(accd, accd + DV, 0.0);
         double sum = 0.0;
         if (mx != -INFINITY) {
             for (int64_t j = 0; j < n_kv; j++) {
-                if (sc[(size_t) j] == -INFINITY) {
+                if (sc[j] == -INFINITY) {
                     continue;
                 }
-                const double p = std::exp(sc[(size_t) j] - mx);
+                const double p = std::exp(sc[j] - mx);
                 sum += p;
-                row_to_f32(v->type, elem_ptr(v, j, kh, ks), vf.data(), DV);
-                for (int64_t d = 0; d < DV; d++) {
-                    accd[(size_t) d] += p * (double) vf[d];
-                }
+                axpy_f64(accd, W.vslab.data() + j * DV, p, DV);
             }
         }
         for (int64_t d = 0; d < DV; d++) {
-            dst_row[d] = sum > 0.0 ? (float) (accd[(size_t) d] / sum) : 0.0f;
+            dst_row[d] = sum > 0.0 ? (float) (accd[d] / sum) : 0.0f;
         }
         return;
     }
 
-    // ggml convention: Q rounded to K's vec-dot type, F32 online softmax.
+    // F32ACC and GGML_CPU: Q rounded to K's vec-dot type, F32 scores, one-pass online softmax.
+    const bool  acc16     = J.mode == ORC_GGML_CPU && v->type == ORC_F16;
     const float scale_eff = J.softcap != 0.0f ? J.scale / J.softcap : J.scale;
     if (k->type == ORC_F16) {
         for (int64_t d = 0; d < D; d++) {
-            q16[(size_t) d] = orc_f32_to_f16(qf[d]);
-            qf[d]           = g_f16_table[q16[(size_t) d]];
+            W.q16[(size_t) d] = orc_f32_to_f16(qf[d]);
+            qf[d]             = g_f16_table[W.q16[(size_t) d]];
         }
     } else if (k->type == ORC_BF16) {
         for (int64_t d = 0; d < D; d++) {
             qf[d] = orc_bf16_to_f32(orc_f32_to_bf16(qf[d]));
         }
     } else if (k->type == ORC_Q8_0) {
-        orc_q8_0_quantize_row(qf.data(), qq.data(), D);
+        orc_q8_0_quantize_row(qf, W.qq.data(), D);
     }
-    std::fill(accf.begin(), accf.end(), 0.0f);
+    float *    accf = W.accf.data();
+    uint16_t * a16  = W.acc16.data();
+    std::fill(accf, accf + DV, 0.0f);
+    std::fill(a16, a16 + DV, (uint16_t) 0);
     float M = -INFINITY, S = 0.0f;
     for (int64_t j = 0; j < n_kv; j++) {
         const float mv = mask_at(j);
@@ -418,16 +589,16 @@ static void run_row(const orc_job & J, int64_t i, int64_t h, int64_t s, std::vec
         const uint8_t * kp = elem_ptr(k, j, kh, ks);
         float           dot;
         if (k->type == ORC_Q8_0) {
-            dot = dot_q8_0(qq.data(), kp, D);
+            dot = dot_q8_0(W.qq.data(), kp, D);
         } else if (k->type == ORC_F16 && g_has_avx2) {
 #if defined(__x86_64__)
-            dot = dot_f32_f16_avx2(qf.data(), (const uint16_t *) kp, D);
+            dot = dot_f32_f16_avx2(qf, (const uint16_t *) kp, D);
 #else
             dot = 0.0f;
 #endif
         } else {
-            row_to_f32(k->type, kp, kf.data(), D);
-            dot = dot_f32(qf.data(), kf.data(), D);
+            row_to_f32(k->type, kp, W.kf.data(), D);
+            dot = dot_f32(qf, W.kf.data(), D);
         }
         float sv = dot * scale_eff;
         if (J.softcap != 0.0f) {
@@ -441,30 +612,39 @@ static void run_row(const orc_job & J, int64_t i, int64_t h, int64_t s, std::vec
         if (sv > M) {
             ms = M == -INFINITY ? 0.0f : std::exp(M - sv);
             M  = sv;
-            if (ms != 1.0f) {
+            if (acc16) {
+                scale_f16(a16, ms, DV);
+            } else if (ms != 1.0f) {
                 for (int64_t d = 0; d < DV; d++) {
-                    accf[(size_t) d] *= ms;
+                    accf[d] *= ms;
                 }
             }
         } else {
             vs = std::exp(sv - M);
         }
         const uint8_t * vp = elem_ptr(v, j, kh, ks);
-        if (v->type == ORC_F16 && g_has_avx2) {
+        if (acc16) {
+            mad_f16(a16, (const uint16_t *) vp, vs, DV);
+        } else if (v->type == ORC_F16 && g_has_avx2) {
 #if defined(__x86_64__)
-            axpy_f16_avx2(accf.data(), (const uint16_t *) vp, vs, DV);
+            axpy_f16_avx2(accf, (const uint16_t *) vp, vs, DV);
 #endif
         } else {
-            row_to_f32(v->type, vp, vf.data(), DV);
+            row_to_f32(v->type, vp, W.vf.data(), DV);
             for (int64_t d = 0; d < DV; d++) {
-                accf[(size_t) d] += vs * vf[d];
+                accf[d] += vs * W.vf[(size_t) d];
             }
         }
         S = S * ms + vs;
     }
+    if (acc16) {
+        for (int64_t d = 0; d < DV; d++) {
+            accf[d] = g_f16_table[a16[d]];
+        }
+    }
     const float inv = S > 0.0f ? 1.0f / S : 0.0f;
     for (int64_t d = 0; d < DV; d++) {
-        dst_row[d] = accf[(size_t) d] * inv;
+        dst_row[d] = accf[d] * inv;
     }
 }
 
@@ -474,6 +654,9 @@ int orc_flash_attn_ext(const orc_tensor * q, const orc_tensor * k, const orc_ten
     init_tables();
     if (!q || !k || !v || !dst) {
         return 1;
+    }
+    if (mode != ORC_EXACT && mode != ORC_F32ACC && mode != ORC_GGML_CPU) {
+        return 4;
     }
     if (q->ne[0] != k->ne[0] || k->ne[1] != v->ne[1] || k->ne[2] != v->ne[2] || k->ne[3] != v->ne[3]) {
         return 3;
@@ -499,25 +682,35 @@ int orc_flash_attn_ext(const orc_tensor * q, const orc_tensor * k, const orc_ten
         n_threads = 1;
     }
     if ((int64_t) n_threads > n_rows) {
-        n_threads = (int) n_rows;
+        n_threads = (int) std::max<int64_t>(n_rows, 1);
     }
+    // rows are handed out in chunks of consecutive rows (i fastest, then h, then s), so a
+    // thread's rows mostly share one (kv head, kv sequence) slab
+    const int64_t        chunk = std::max<int64_t>(1, std::min<int64_t>(64, n_rows / ((int64_t) n_threads * 8)));
     std::atomic<int64_t> next{ 0 };
     auto                 worker = [&]() {
-        const int64_t         D = q->ne[0], DV = v->ne[0];
-        std::vector<float>    qf((size_t) D), kf((size_t) D), vf((size_t) DV), accf((size_t) DV);
-        std::vector<double>   accd((size_t) DV);
-        std::vector<uint8_t>  qq((size_t) (D / QK8_0 + 1) * Q8_0_BLOCK_BYTES);
-        std::vector<uint16_t> q16((size_t) D);
+        const int64_t D = q->ne[0], DV = v->ne[0];
+        orc_scratch   W;
+        W.qf.resize((size_t) D);
+        W.kf.resize((size_t) D);
+        W.vf.resize((size_t) DV);
+        W.accf.resize((size_t) DV);
+        W.accd.resize((size_t) DV);
+        W.acc16.resize((size_t) DV);
+        W.sc.resize((size_t) std::max<int64_t>(k->ne[1], 1));
+        W.qq.resize((size_t) (D / QK8_0 + 1) * Q8_0_BLOCK_BYTES);
+        W.q16.resize((size_t) D);
         for (;;) {
-            const int64_t r = next.fetch_add(1);
-            if (r >= n_rows) {
+            const int64_t r0 = next.fetch_add(chunk);
+            if (r0 >= n_rows) {
                 break;
             }
-            // row order: i fastest, then h, then s (matches the query tensor's order)
-            const int64_t i = r % q->ne[1];
-            const int64_t h = (r / q->ne[1]) % q->ne[2];
-            const int64_t s = r / (q->ne[1] * q->ne[2]);
-            run_row(J, i, h, s, qf, kf, vf, accd, accf, qq, q16);
+            for (int64_t r = r0; r < std::min(n_rows, r0 + chunk); r++) {
+                const int64_t i = r % q->ne[1];
+                const int64_t h = (r / q->ne[1]) % q->ne[2];
+                const int64_t s = r / (q->ne[1] * q->ne[2]);
+                run_row(J, i, h, s, W);
+            }
         }
     };
     if (n_threads == 1) {

@@ -22,7 +22,8 @@ sys.path.insert(0, os.path.join(ROOT, "minimaxmusic.cpp_b200"))
 from mm3fa import ggml  # noqa: E402  (descriptor layout shared with the C ABI)
 
 MODE_EXACT = 0
-MODE_GGML = 1
+MODE_F32ACC = 1
+MODE_GGML_CPU = 2
 
 _lib = None
 

@@ -7,12 +7,15 @@ from the reference tree, so no reference-produced vectors exist.  Each fixture i
 stores seeded operands (in the exact ggml layouts the reference uses, see
 mm3fa/workloads.py) with three independently computed results:
 
-  out_exact  - the CPU oracle in exact mode (float64 accumulation)
-  out_ggml   - the CPU oracle in ggml-convention mode (Q rounded to K's vec-dot type)
-  out_torch  - torch.nn.functional.scaled_dot_product_attention in float64 on the
-               dequantized operands (only where no softcap/ALiBi is involved)
+  out_exact     - the CPU oracle in exact mode (float64 accumulation)
+  out_f32acc    - the CPU oracle in F32-accumulation mode (Q rounded to K's vec-dot type,
+                  F32 softmax and V sums: the precision set_prec(F32) asks for)
+  out_ggml_cpu  - the CPU oracle's restatement of ggml's CPU kernel (F16 V accumulator when
+                  V is F16)
+  out_torch     - torch.nn.functional.scaled_dot_product_attention in float64 on the
+                  dequantized operands (only where no softcap/ALiBi is involved)
 
-Tests check that the oracle still reproduces out_exact / out_ggml bit for bit and that
+Tests check that the oracle still reproduces the three oracle outputs bit for bit and that
 out_exact agrees with out_torch, and the GPU tests compare the CUDA path against them.
 """
 from __future__ import annotations
@@ -86,8 +89,9 @@ def save(name, c):
     qd, kd, vd = c.q.host_desc(), c.k.host_desc(), c.v.host_desc()
     md = c.mask.host_desc() if c.mask is not None else None
     ex = oracle.flash_attn_ext(qd, kd, vd, md, c.scale, c.max_bias, c.softcap, oracle.MODE_EXACT, threads=1)
-    gg = oracle.flash_attn_ext(qd, kd, vd, md, c.scale, c.max_bias, c.softcap, oracle.MODE_GGML, threads=1)
-    arrays = dict(out_exact=ex, out_ggml=gg)
+    f32 = oracle.flash_attn_ext(qd, kd, vd, md, c.scale, c.max_bias, c.softcap, oracle.MODE_F32ACC, threads=1)
+    cpu = oracle.flash_attn_ext(qd, kd, vd, md, c.scale, c.max_bias, c.softcap, oracle.MODE_GGML_CPU, threads=1)
+    arrays = dict(out_exact=ex, out_f32acc=f32, out_ggml_cpu=cpu)
     if c.softcap == 0.0 and c.max_bias == 0.0:
         arrays["out_torch"] = torch_reference(c)
     for tag, op in (("q", c.q), ("k", c.k), ("v", c.v), ("mask", c.mask)):

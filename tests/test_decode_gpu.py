@@ -1,9 +1,12 @@
 """Parity of the CUDA decode path (through the C ABI) against the CPU oracle.
 
 Tolerance (north star, F32 output): max-abs <= 2e-3 and cosine >= 0.99999 against the
-oracle's ggml-convention mode, i.e. ggml's own CPU arithmetic.  Against the exact (float64)
-oracle the same bound holds for F16/BF16 K; for Q8_0 K the ggml convention itself quantizes
-Q to 8 bits, so the exact comparison uses max-abs <= 5e-3, cosine >= 0.9999.
+oracle's F32-accumulation mode (Q rounded to K's vec-dot type, F32 softmax and V sums: the
+precision set_prec(F32) asks for).  Against the exact (float64) oracle the same bound holds for
+F16/BF16 K; for Q8_0 K the convention itself quantizes Q to 8 bits, so the exact comparison
+uses max-abs <= 5e-3, cosine >= 0.9999.  Against the restatement of ggml's CPU kernel, whose
+F16 V accumulator is itself ~5e-4 / cos 0.9999 from exact math at KV 8192, the bound is
+relative (gpu_util.check_three_ways).
 """
 import os
 
@@ -13,7 +16,7 @@ import torch
 
 import mm3fa
 import oracle
-from gpu_util import assert_close, cosine, run_gpu, run_oracle
+from gpu_util import assert_close, check_three_ways, cosine, run_gpu, run_oracle
 from mm3fa import ggml, workloads
 from test_oracle import GOLDEN_FILES, _load_golden
 
@@ -36,17 +39,11 @@ def kernel(request, monkeypatch):
 
 
 def check(c, dev, exact_abs=2e-3, exact_cos=0.99999):
-    """GPU vs the ggml-convention oracle at the north-star tolerance; GPU vs the exact oracle
-    at (exact_abs, exact_cos), widened to the ggml convention's own distance from exact math
-    when that is larger (Q8_0 with a handful of keys: Q's 8-bit rounding moves the weights)."""
+    """GPU vs the three oracle modes (gpu_util.check_three_ways): the F32-accumulation oracle at
+    the north-star tolerance, the exact oracle at (exact_abs, exact_cos), and ggml's CPU kernel
+    (F16 V accumulator) relative to the F32-accumulation mode's own distance from it."""
     got = run_gpu(c, dev)
-    gg = run_oracle(c, oracle.MODE_GGML)
-    ex = run_oracle(c, oracle.MODE_EXACT)
-    assert_close(got, gg, what=f"{c.name} vs ggml-convention oracle")
-    conv_abs = float(np.abs(gg - ex).max()) if ex.size else 0.0
-    conv_cos = cosine(gg, ex)
-    assert_close(got, ex, max(exact_abs, 1.25 * conv_abs), min(exact_cos, conv_cos - 1e-6),
-                 what=f"{c.name} vs exact oracle")
+    check_three_ways(got, c, exact_abs, exact_cos)
     return got
 
 
@@ -195,7 +192,7 @@ def test_workspace_reuse_is_stable(kernel, cuda_device):
 def test_golden_fixtures_on_gpu(kernel, cuda_device, path):
     c, z = _load_golden(path)
     got = run_gpu(c, cuda_device)
-    assert_close(got, z["out_ggml"], what="vs golden ggml-convention")
+    assert_close(got, z["out_f32acc"], what="vs golden F32-accumulation")
     loose = c.k.gtype == Q8
     assert_close(got, z["out_exact"], 5e-3 if loose else 2e-3, 0.9999 if loose else 0.99999, what="vs golden exact")
 
@@ -264,7 +261,7 @@ def test_kv_len_equals_length_mask(kernel, cuda_device, kvt):
             bf = torch.from_numpy(op.storage.astype(np.float32)).to(torch.bfloat16).view(torch.int16).numpy()
             setattr(c, name, workloads.Operand(bf.view(np.uint16), BF16, op.ne, op.nb))
     got = run_gpu_kvlen(c, cuda_device, kv_len)
-    ref = run_oracle(length_mask_case(c, kv_len), oracle.MODE_GGML)
+    ref = run_oracle(length_mask_case(c, kv_len), oracle.MODE_F32ACC)
     assert_close(got, ref, what="kv_len vs length mask")
 
 
@@ -278,7 +275,7 @@ def test_kv_len_with_mask_multirow_and_edges(kernel, cuda_device):
     for s in range(4):
         m[s, :, :, max(0, min(kv_len[s], 1024)):] = -np.inf
     c.mask = workloads.Operand(m, F16, c.mask.ne, c.mask.nb)
-    ref = run_oracle(c, oracle.MODE_GGML)
+    ref = run_oracle(c, oracle.MODE_F32ACC)
     assert_close(got, ref, what="kv_len + mask vs oracle")
     assert np.all(got[0] == 0)
 
@@ -319,3 +316,112 @@ def test_depth_decoder_d256_q8_0(cuda_device):
 def test_decode_d256_long_kv(cuda_device):
     """D = 256 over several 32-key stages and the stream-K split (GQA 4, F16 cache view)."""
     check(workloads.decode_case(n_seq=2, n_kv=700, D=256, n_head=8, n_head_kv=2, seed=80), cuda_device)
+
+
+# ---------------------------------------------------------------- bit-exact single-key rows
+
+def single_key_case(kvt, n_kv: int, seed: int):
+    """CFG decode where each row sees exactly one key (key 0; the others, if any, masked -inf).
+    softmax over one score is exactly 1, so the result must be V's row 0 converted to F32 bit
+    for bit: f16/bf16 -> f32, or the Q8_0 dequantization d * q (an exact product in F32)."""
+    c = workloads.decode_case(n_seq=2, n_kv=n_kv, n_head=32, n_head_kv=8, seed=seed,
+                              kv_type=Q8 if kvt == Q8 else F16)
+    if kvt == BF16:
+        for name in ("k", "v"):
+            op = getattr(c, name)
+            bf = torch.from_numpy(op.storage.astype(np.float32)).to(torch.bfloat16).view(torch.int16).numpy()
+            setattr(c, name, workloads.Operand(bf.view(np.uint16), BF16, op.ne, op.nb))
+    c.mask.storage[..., 1:] = -np.inf
+    return c
+
+
+def v_row0_f32(c) -> np.ndarray:
+    """V row 0 of every (sequence, kv head) as F32, broadcast to the result [n_seq, 1, H, D]."""
+    st = c.v.storage  # [n_seq, Hkv, max_seq, row]
+    if c.v.gtype == Q8:
+        rows = oracle.q8_0_dequantize(st[:, :, 0])
+    elif c.v.gtype == BF16:
+        rows = (st[:, :, 0].astype(np.uint32) << 16).view(np.float32)
+    else:
+        rows = st[:, :, 0].astype(np.float32)
+    ratio = c.q.ne[2] // c.v.ne[2]
+    return np.repeat(rows, ratio, axis=1)[:, None]
+
+
+@pytest.mark.parametrize("kvt", [F16, BF16, Q8])
+@pytest.mark.parametrize("n_kv", [1, 2, 256])
+def test_single_visible_key_is_bit_exact(kernel, cuda_device, kvt, n_kv):
+    """One visible key: out == V row 0 exactly (for Q8_0 this pins the in-kernel dequantization
+    d * q bit for bit).  n_kv = 1 runs the element-copy path for Q8_0 (136-byte rows are not
+    16-byte multiples), n_kv = 2 and 256 the bulk-copied tensor-core path with masked keys."""
+    c = single_key_case(kvt, n_kv, seed=500 + n_kv + kvt)
+    got = run_gpu(c, cuda_device)
+    want = v_row0_f32(c)
+    assert got.shape == want.shape
+    assert np.array_equal(got, want), f"max |diff| {np.abs(got - want).max():.3e}"
+
+
+# ---------------------------------------------------------------- benchmark config 2, large end
+
+@pytest.mark.parametrize("n_seq,n_kv", [(8, 8192), (8, 16384)])
+def test_config2_large_end_full_output(kernel, cuda_device, n_seq, n_kv):
+    """config 2 at batch 8 (4 CFG pairs) and KV 8192 / 16384 (K/V ~ N(0, 0.25)), every output row
+    checked against the three oracle modes."""
+    check(workloads.decode_case(n_seq=n_seq, n_kv=n_kv, max_seq=n_kv, kv_std=0.5, seed=45 + n_kv // 1024),
+          cuda_device)
+
+
+def test_config2_36_layer_graph_n8_kv8192(cuda_device):
+    """The bench's step at config 2's batch 8: 36 independent layers (F16 caches [128, 10240, 8, 8]
+    viewed at KV 8192) captured once in a CUDA graph and replayed twice.  Every layer's replayed
+    output equals its eager call bit for bit, and three layers are checked against the oracle."""
+    dev = cuda_device
+    L, N, Hkv, H, D, n_kv, max_seq = 36, 8, 8, 32, 128, 8192, 10240
+    g = torch.Generator(device=dev)
+    g.manual_seed(4242)
+    F32 = ggml.GGML_TYPE_F32
+    rb = 2 * D
+    nb = [2, rb, rb * max_seq, rb * max_seq * Hkv]
+    mask = torch.zeros(N, 1, 1, n_kv, dtype=torch.float16, device=dev)
+    layers = []
+    for _ in range(L):
+        kc = (torch.randn(N, Hkv, max_seq, D, generator=g, device=dev) * 0.5).half()
+        vc = (torch.randn(N, Hkv, max_seq, D, generator=g, device=dev) * 0.5).half()
+        q = torch.randn(N, H, 1, D, generator=g, device=dev)
+        o = torch.full((N, 1, H, D), float("nan"), device=dev)
+        descs = (ggml.make(F32, [D, 1, H, N], q.data_ptr()), ggml.make(F16, [D, n_kv, Hkv, N], kc.data_ptr(), nb),
+                 ggml.make(F16, [D, n_kv, Hkv, N], vc.data_ptr(), list(nb)),
+                 ggml.make(F16, [n_kv, 1, 1, N], mask.data_ptr()), ggml.make(F32, [D, H, 1, N], o.data_ptr()))
+        layers.append(((kc, vc, q, o), descs))
+    ws = mm3fa.Workspace(dev)
+    s = torch.cuda.Stream(device=dev)
+
+    def step():
+        for _, (qd, kd, vd, md, dd) in layers:
+            mm3fa.run(qd, kd, vd, md, dd, 1.0 / np.sqrt(D), 0.0, 0.0, ws, stream=s)
+
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.synchronize(dev)
+    eager = [t[3].cpu().numpy() for t, _ in layers]
+    for t, _ in layers:
+        t[3].fill_(float("nan"))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        step()
+    for _ in range(2):
+        with torch.cuda.stream(s):
+            graph.replay()
+    torch.cuda.synchronize(dev)
+    for l, (t, _) in enumerate(layers):
+        assert np.array_equal(t[3].cpu().numpy(), eager[l]), f"layer {l}: graph replay differs from the eager call"
+    for l in (0, 17, 35):
+        kc, vc, q, _ = layers[l][0]
+        qn, kn, vn, mn = (x.cpu().numpy() for x in (q, kc, vc, mask))
+        c = workloads.Case(f"cfg2-layer{l}", workloads.Operand(qn, F32, [D, 1, H, N], ggml.contiguous_nb(F32, [D, 1, H, N])),
+                           workloads.Operand(kn, F16, [D, n_kv, Hkv, N], nb),
+                           workloads.Operand(vn, F16, [D, n_kv, Hkv, N], list(nb)),
+                           workloads.Operand(mn, F16, [n_kv, 1, 1, N], ggml.contiguous_nb(F16, [n_kv, 1, 1, N])),
+                           1.0 / np.sqrt(D))
+        check_three_ways(eager[l], c)
+    del graph

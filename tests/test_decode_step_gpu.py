@@ -85,7 +85,7 @@ def step_case(dev, kvt, rows, n_kv=1024, max_seq=1100, seed=0):
     kdh = ggml.make(kvt, [D, n_kv, Hkv, N], kh.ctypes.data, cnb)
     vdh = ggml.make(kvt, [D, n_kv, Hkv, N], vh.ctypes.data, list(cnb))
     mdh = ggml.make(F16, [n_kv, 1, 1, N], mh.ctypes.data)
-    ref = oracle.flash_attn_ext(qdh, kdh, vdh, mdh, scale, 0.0, 0.0, oracle.MODE_GGML)
+    ref = oracle.flash_attn_ext(qdh, kdh, vdh, mdh, scale, 0.0, 0.0, oracle.MODE_F32ACC)
     return fused, split, ref
 
 

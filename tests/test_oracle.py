@@ -142,7 +142,7 @@ def test_ggml_mode_within_tolerance_of_exact():
     c = workloads.decode_case(n_seq=2, n_kv=512, seed=26)
     args = (c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), c.mask.host_desc(), c.scale)
     ex = oracle.flash_attn_ext(*args, mode=oracle.MODE_EXACT)
-    gg = oracle.flash_attn_ext(*args, mode=oracle.MODE_GGML)
+    gg = oracle.flash_attn_ext(*args, mode=oracle.MODE_F32ACC)
     assert np.abs(ex - gg).max() < 2e-3
     cos = (ex * gg).sum() / np.sqrt((ex * ex).sum() * (gg * gg).sum())
     assert cos > 0.99999
@@ -151,7 +151,7 @@ def test_ggml_mode_within_tolerance_of_exact():
 def test_fully_masked_rows_are_zero():
     c = workloads.decode_case(n_seq=2, n_kv=64, n_head=4, n_head_kv=1, seed=27)
     c.mask.storage[0, 0, 0, :] = -np.inf  # sequence 0 sees nothing
-    for mode in (oracle.MODE_EXACT, oracle.MODE_GGML):
+    for mode in (oracle.MODE_EXACT, oracle.MODE_F32ACC):
         out = oracle.flash_attn_ext(c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), c.mask.host_desc(), c.scale,
                                     mode=mode)
         assert np.all(out[0] == 0.0) and np.all(np.isfinite(out[1])) and np.abs(out[1]).sum() > 0
@@ -186,7 +186,8 @@ def test_oracle_reproduces_golden(path):
     md = c.mask.host_desc() if c.mask is not None else None
     args = (c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), md, c.scale, c.max_bias, c.softcap)
     assert np.array_equal(oracle.flash_attn_ext(*args, mode=oracle.MODE_EXACT, threads=1), z["out_exact"])
-    assert np.array_equal(oracle.flash_attn_ext(*args, mode=oracle.MODE_GGML, threads=1), z["out_ggml"])
+    assert np.array_equal(oracle.flash_attn_ext(*args, mode=oracle.MODE_F32ACC, threads=1), z["out_f32acc"])
+    assert np.array_equal(oracle.flash_attn_ext(*args, mode=oracle.MODE_GGML_CPU, threads=1), z["out_ggml_cpu"])
     if "out_torch" in z:
         np.testing.assert_allclose(z["out_exact"], z["out_torch"], atol=1e-6, rtol=0)
 
@@ -209,3 +210,84 @@ def test_prologue_restatement_against_float64():
     assert np.abs(r - ref2).max() <= 2e-5
     # position 0 is the identity
     assert np.array_equal(r[0], y[0])
+
+
+# ---------------------------------------------------------------- ggml's CPU kernel (F16 accumulator)
+
+def _np_ggml_cpu_f16acc(c) -> np.ndarray:
+    """numpy statement of ggml-cpu's one-row flash_attn_ext loop for F16 K/V (independent of the
+    oracle's C code): Q rounded to f16, F32 dot, expf online softmax, V accumulated in f16 with
+    one f32 FMA per key (y <- f16(fma(v, p, y))) and f16(y * ms) on a new maximum."""
+    D, n_q, H, n_seq = c.q.ne
+    Hk, n_kv = c.k.ne[2], c.k.ne[1]
+    q = c.q.storage.reshape(n_seq, H, n_q, D)
+    k = c.k.storage.reshape(n_seq, Hk, -1, D)[:, :, :n_kv]
+    v = c.v.storage.reshape(n_seq, Hk, -1, D)[:, :, :n_kv]
+    m = c.mask.storage.reshape(n_seq, -1, n_kv) if c.mask is not None else None
+    out = np.zeros((n_seq, n_q, H, D), np.float32)
+    for s in range(n_seq):
+        for h in range(H):
+            kh = h // (H // Hk)
+            for i in range(n_q):
+                qf = q[s, h, i].astype(np.float16).astype(np.float32)
+                acc = np.zeros(D, np.float16)
+                M, S = -np.inf, np.float32(0)
+                for j in range(n_kv):
+                    mv = np.float32(m[s, i, j]) if m is not None else np.float32(0)
+                    if mv == -np.inf:
+                        continue
+                    sv = np.float32(np.float32(qf @ k[s, kh, j].astype(np.float32)) * np.float32(c.scale)) + mv
+                    ms, vs = np.float32(1), np.float32(1)
+                    if sv > M:
+                        ms = np.float32(0) if M == -np.inf else np.float32(np.exp(np.float32(M - sv)))
+                        M = sv
+                        acc = (acc.astype(np.float32) * ms).astype(np.float16)
+                    else:
+                        vs = np.float32(np.exp(np.float32(sv - M)))
+                    # f32 FMA emulated in float64 (the f16 x f32 product is exact there)
+                    y = (v[s, kh, j].astype(np.float64) * np.float64(vs) + acc.astype(np.float64)).astype(np.float32)
+                    acc = y.astype(np.float16)
+                    S = np.float32(S * ms + vs)
+                out[s, i, h] = acc.astype(np.float32) * (np.float32(1) / S if S > 0 else np.float32(0))
+    return out
+
+
+def test_ggml_cpu_mode_matches_numpy_restatement():
+    c = workloads.decode_case(n_seq=2, n_kv=300, n_head=4, n_head_kv=2, n_q=2, kv_len=[300, 171], seed=91)
+    got = oracle.flash_attn_ext(c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), c.mask.host_desc(), c.scale,
+                                mode=oracle.MODE_GGML_CPU, threads=2)
+    ref = _np_ggml_cpu_f16acc(c)
+    # the float64 emulation of the f32 FMA can differ from fmaf by one f32 rounding, rarely
+    # moving one f16 rounding of the accumulator; the outputs agree to a fraction of an f16 ulp
+    assert np.abs(got - ref).max() <= 2e-4 * np.abs(ref).max()
+    # and the F16 accumulator is measurably coarser than the F32 one
+    f32 = oracle.flash_attn_ext(c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), c.mask.host_desc(), c.scale,
+                                mode=oracle.MODE_F32ACC, threads=2)
+    assert np.abs(got - f32).max() > 1e-6
+
+
+def test_ggml_cpu_mode_equals_f32_mode_without_f16_v():
+    """ggml's CPU kernel accumulates in F32 unless V is F16, so for Q8_0 (and BF16) V the two
+    modes are the same computation."""
+    c = workloads.decode_case(n_seq=2, n_kv=256, n_head=8, n_head_kv=2, kv_type=ggml.GGML_TYPE_Q8_0, seed=92)
+    a = oracle.flash_attn_ext(c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), c.mask.host_desc(), c.scale,
+                              mode=oracle.MODE_GGML_CPU, threads=2)
+    b = oracle.flash_attn_ext(c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), c.mask.host_desc(), c.scale,
+                              mode=oracle.MODE_F32ACC, threads=2)
+    assert np.array_equal(a, b)
+
+
+def test_exact_mode_threading_is_deterministic():
+    """The exact mode's per-thread slab cache gives the same bits for any thread count."""
+    c = workloads.prefill_case(n_seq=1, S=80, n_head=8, n_head_kv=2, kv_pos=30, seed=93)
+    a = oracle.flash_attn_ext(c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), c.mask.host_desc(), c.scale,
+                              mode=oracle.MODE_EXACT, threads=1)
+    b = oracle.flash_attn_ext(c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), c.mask.host_desc(), c.scale,
+                              mode=oracle.MODE_EXACT, threads=7)
+    assert np.array_equal(a, b)
+
+
+def test_oracle_rejects_unknown_mode():
+    c = workloads.decode_case(n_seq=1, n_kv=8, n_head=2, n_head_kv=1, seed=94)
+    with pytest.raises(ValueError):
+        oracle.flash_attn_ext(c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), c.mask.host_desc(), c.scale, mode=9)

@@ -3,8 +3,10 @@ of ggml's rms_norm, mul, rope_ext (NEOX) and set_rows as src/qwen3-lm.h:764-800 
 and of the attention call that follows it on the updated caches.
 
 Tolerances: q_out (F32) within 1e-4 absolute (float32 arithmetic on both sides; cos/sin may
-differ in the last bit); cache rows within one unit of the cache type's rounding (F16/BF16: one
-ulp of the value; Q8_0: one quantum d of the block); every other cache row bit-identical; the
+differ in the last bit); k cache rows within one unit of the cache type's rounding (F16/BF16:
+one ulp of the value; Q8_0: one quantum d of the block), because k is normed and rotated in
+float32 on both sides first; v cache rows (a plain set_rows conversion of the same F32 input)
+bit-identical, as is every other cache row; the
 attention output at the north-star bound (max-abs 2e-3, cosine 0.99999) against the oracle run
 on the oracle's own prologue results.
 """
@@ -111,7 +113,12 @@ def test_prologue_matches_oracle(cuda_device, kvt, D):
         for s in range(r["N"]):
             touched[s, :, r["rows"][s]] = True
         assert np.array_equal(got[~touched], before[~touched]), f"{name}: rows other than the new one changed"
-        check_rows_close(got[touched], ref[touched], kvt, name)
+        if name == "vc":
+            # v goes into the cache with no arithmetic before set_rows: the F16/BF16 cast and the
+            # Q8_0 quantization of identical F32 input must give identical bytes
+            assert np.array_equal(got[touched], ref[touched]), "v rows: set_rows conversion not bit-exact"
+        else:
+            check_rows_close(got[touched], ref[touched], kvt, name)
 
 
 def test_prologue_row_out_of_range_is_not_written(cuda_device):
@@ -154,7 +161,7 @@ def test_prologue_then_attention(cuda_device, kvt):
         kd = ggml.make(kvt, [D, n_kv, Hkv, N], kc.ctypes.data, cnb)
         vd = ggml.make(kvt, [D, n_kv, Hkv, N], vc.ctypes.data, list(cnb))
         md = ggml.make(F16, [n_kv, 1, 1, N], mask.ctypes.data)
-        return oracle.flash_attn_ext(qd, kd, vd, md, 1.0 / np.sqrt(D), 0.0, 0.0, oracle.MODE_GGML)
+        return oracle.flash_attn_ext(qd, kd, vd, md, 1.0 / np.sqrt(D), 0.0, 0.0, oracle.MODE_F32ACC)
 
     got = attend(r["q"], r["kc"], r["vc"], True)
     ref = attend(r["q_ref"], r["kc_ref"], r["vc_ref"], False)
@@ -213,7 +220,7 @@ def test_dit_prologue_real_dit_shapes(cuda_device, out_t):
     ref = oracle.flash_attn_ext(ggml.make(F32, [D, S, H, B], qh.ctypes.data, qv),
                                 ggml.make(out_t, [D, S, H, B], kh.ctypes.data, kvnb),
                                 ggml.make(out_t, [D, S, H, B], vh.ctypes.data, list(kvnb)), None,
-                                1.0 / np.sqrt(D), 0.0, 0.0, oracle.MODE_GGML)
+                                1.0 / np.sqrt(D), 0.0, 0.0, oracle.MODE_F32ACC)
     assert_close(out.cpu().numpy(), ref, what="DiT prologue + attention vs oracle")
 
 

@@ -78,3 +78,44 @@ def test_noalloc_rejects_operands_beyond_its_scratch(cuda_device):
     assert e.value.status == mm3fa.ERR_SCRATCH_LIMIT
     torch.cuda.synchronize()
     assert torch.all(out == 0)
+
+
+def test_noalloc_dense_kernel_after_decode_calls(cuda_device):
+    """A causal prefill (the tensor-core kernel, whose mask-block flags also live in the scratch)
+    run twice through the built-in buffer right after the decode calls above left their partial
+    results in it, compared with the workspace entry point."""
+    from gpu_util import run_gpu
+
+    c = workloads.prefill_case(n_seq=2, S=200, n_head=8, n_head_kv=2, kv_pos=37, seed=41)
+    ref = run_gpu(c, cuda_device)
+    t, d = _device_operands(c, cuda_device)
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):
+        out = torch.full(c.dst_shape(), float("nan"), device=cuda_device)
+        mm3fa.flash_attn_ext_noalloc(d["q"], d["k"], d["v"], d["mask"], c.scale, 0.0, 0.0,
+                                     mm3fa.dst_desc(d["q"], d["v"], out.data_ptr()), stream)
+        torch.cuda.synchronize()
+        assert_close(out.cpu().numpy(), ref, what="noalloc dense vs workspace entry point")
+
+
+def test_noalloc_status_reports_an_expired_wait(cuda_device):
+    """A bounded wait that expires inside the built-in buffer's user is visible through
+    mm3fa_noalloc_status (once), and later no-allocation calls are still correct."""
+    stream = torch.cuda.current_stream().cuda_stream
+    st, raw = mm3fa.noalloc_status(stream)
+    assert st == mm3fa.OK and raw == 0
+    assert mm3fa.lib().mm3fa_noalloc_selftest_bounded_wait(20000, ctypes.c_void_p(stream)) == mm3fa.OK
+    st, raw = mm3fa.noalloc_status(stream)
+    assert st == mm3fa.ERR_TIMEOUT and raw & 1
+    st, raw = mm3fa.noalloc_status(stream)
+    assert st == mm3fa.OK and raw == 0
+    from gpu_util import run_gpu
+
+    c = workloads.decode_case(n_seq=2, n_kv=1024, seed=42)
+    t, d = _device_operands(c, cuda_device)
+    out = torch.full(c.dst_shape(), float("nan"), device=cuda_device)
+    mm3fa.flash_attn_ext_noalloc(d["q"], d["k"], d["v"], d["mask"], c.scale, 0.0, 0.0,
+                                 mm3fa.dst_desc(d["q"], d["v"], out.data_ptr()), stream)
+    torch.cuda.synchronize()
+    assert_close(out.cpu().numpy(), run_gpu(c, cuda_device), what="noalloc after a reported timeout")
+    assert mm3fa.noalloc_status(stream) == (mm3fa.OK, 0)
