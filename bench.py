@@ -49,17 +49,19 @@ N_HEAD, N_HEAD_KV, D = 32, 8, 128
 N_KV, MAX_SEQ = 8192, 10240
 FALLBACK_HBM_GBS = 6650.0
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one decode launch at this workload (ncu capture)
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode launch at this workload, from the ncu
+# capture summarised in profiles/ (re-captured whenever the kernel changes)
 NCU_KERNEL = "fa_decode_mma_kernel<128,f16,NT=1,cluster,NS=3>"
 NCU_TRAFFIC_BYTES = 67225600 + 466432
+NCU_TRAFFIC_SOURCE = "profiles/fa_decode_mma_kernel_cfg2_b2_kv8192.md (one ncu launch, 36-layer step)"
 
 
-def layer_bytes(n_seq: int, n_head_kv: int, n_head: int) -> int:
-    """Algorithmic bytes of one decode-attention call: K+V once, Q, mask, out."""
-    kv = 2 * n_seq * n_head_kv * N_KV * D * 2
+def layer_bytes(n_seq: int, n_head_kv: int, n_head: int, n_kv: int = N_KV) -> int:
+    """Algorithmic bytes of one decode-attention call: K+V once, Q, mask, out (this rank's heads)."""
+    kv = 2 * n_seq * n_head_kv * n_kv * D * 2
     q = n_seq * n_head * D * 4
     out = n_seq * n_head * D * 4
-    mask = n_seq * N_KV * 2
+    mask = n_seq * n_kv * 2
     return kv + q + out + mask
 
 
@@ -139,9 +141,24 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
+def _cpu_layers_per_s(oracle, descs, threads: int, seconds: float) -> tuple[int, float]:
+    """Runs the ggml-CPU restatement over `descs` in turn for about `seconds`."""
+    oracle.flash_attn_ext(*descs[0], mode=oracle.MODE_GGML_CPU, threads=threads)  # warm
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        oracle.flash_attn_ext(*descs[n % len(descs)], mode=oracle.MODE_GGML_CPU, threads=threads)
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    return n, time.perf_counter() - t0
+
+
 def cpu_baseline(seconds: float = 10.0) -> dict:
-    """The CPU oracle (ggml convention: Q rounded to F16, F32 online softmax) on all host cores,
-    over distinct layers of the same shape, for about `seconds`."""
+    """The oracle's restatement of ggml's CPU flash_attn_ext kernel (Q rounded to F16, expf online
+    softmax, F16 V accumulator) on all host cores and on half of them (the reference's own CPU
+    thread count, hardware_concurrency / 2, src/backend.h:28-31), over distinct layers of the
+    headline shape, about `seconds` each."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle  # test infrastructure: the timed CPU baseline only
     from mm3fa import workloads
@@ -151,26 +168,25 @@ def cpu_baseline(seconds: float = 10.0) -> dict:
     cases = [workloads.decode_case(n_seq=2, n_kv=N_KV, max_seq=N_KV, kv_std=0.5, seed=1000 + i)
              for i in range(n_distinct)]
     descs = [(c.q.host_desc(), c.k.host_desc(), c.v.host_desc(), c.mask.host_desc(), c.scale) for c in cases]
-    oracle.flash_attn_ext(*descs[0], mode=oracle.MODE_F32ACC, threads=threads)  # warm
-    t0 = time.perf_counter()
-    n = 0
-    while True:
-        oracle.flash_attn_ext(*descs[n % n_distinct], mode=oracle.MODE_F32ACC, threads=threads)
-        n += 1
-        if time.perf_counter() - t0 >= seconds:
-            break
-    dt = time.perf_counter() - t0
     b = layer_bytes(2, N_HEAD_KV, N_HEAD)
+    n, dt = _cpu_layers_per_s(oracle, descs, threads, seconds)
+    half = max(1, threads // 2)
+    n2, dt2 = _cpu_layers_per_s(oracle, descs, half, seconds / 2)
     return {"value": round(b * n / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{n} decode-attention layers (B=2, KV 8192, 32q/8kv, D=128, F16 K/V) cycling over "
-                      f"{n_distinct} distinct caches, {dt:.1f} s, oracle F32-accumulation mode",
-            "us_per_layer": round(dt / n * 1e6, 1)}
+                      f"{n_distinct} distinct caches, {dt:.1f} s, oracle restatement of ggml's CPU kernel "
+                      "(F16 V accumulator)",
+            "us_per_layer": round(dt / n * 1e6, 1),
+            "half_cores": {"cores": half, "value": round(b * n2 / dt2 / 1e9, 3), "unit": "GB/s",
+                           "us_per_layer": round(dt2 / n2 * 1e6, 1),
+                           "note": "hardware_concurrency/2, the reference's CPU thread count (src/backend.h:28-31)"}}
 
 
 def run_reference(args) -> None:
     """--impl reference: the reference's CPU implementation of the path.  ggml (the
-    reference's implementation) is absent from its tree, so this times the CPU oracle port
-    on the same workload, all host threads, rank 0 only."""
+    reference's implementation) is absent from its tree, so this times the CPU oracle's
+    restatement of ggml's CPU flash_attn_ext kernel (F16 V accumulator) on the same workload,
+    all host threads, rank 0 only."""
     if int(os.environ.get("RANK", "0")) != 0:
         return
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -185,7 +201,7 @@ def run_reference(args) -> None:
 
     def step():
         for d in descs:
-            oracle.flash_attn_ext(*d, mode=oracle.MODE_F32ACC, threads=threads)
+            oracle.flash_attn_ext(*d, mode=oracle.MODE_GGML_CPU, threads=threads)
 
     for _ in range(args.warmup):
         step()
@@ -206,17 +222,28 @@ def run_reference(args) -> None:
                    "n_seq": 2, "n_kv": N_KV, "n_head": N_HEAD, "n_head_kv": N_HEAD_KV, "head_dim": D,
                    "kv_type": "f16", "us_per_layer": round(us_layer, 1)},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{n_layers_per_step} distinct layers per step, oracle F32-accumulation mode "
-                                   "(ggml, the reference's implementation, is absent from the reference tree)"},
+                         "sample": f"{n_layers_per_step} distinct layers per step, oracle restatement of ggml's "
+                                   "CPU kernel (ggml, the reference's implementation, is absent from the reference "
+                                   "tree)"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def bench_dense(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, world: int, local: int) -> dict:
-    """DiT (config 5) and causal prefill (config 4) attention on the tensor-core kernel."""
+def bench_dense(torch, dist, mm3fa, ggml, dev, stream, steps: int, warmup: int, world: int, rank: int,
+                local: int) -> dict:
+    """DiT (config 5) and causal prefill (config 4) attention on the tensor-core kernel.
+
+    N GPUs: the DiT job grows to N CFG pairs (B = 2N) and rank r computes pair r, all 16 heads
+    (weak scaling); a second line keeps the B = 2 job and splits its 32 (batch x head) units over
+    the ranks (strong scaling).  The prefill job grows to 2N sequences, split by kv head.  Every
+    call is followed by mm3fa_allgather_heads (NCCL), as to_out / o_proj need every head."""
+    from mm3fa import exchange as xch, sharding
+
     g = torch.Generator(device=dev)
-    g.manual_seed(99)
+    g.manual_seed(99 + rank)
+    comm = xch.nccl_comm(dist, dev) if world > 1 else 0
+    F32, F16 = ggml.GGML_TYPE_F32, ggml.GGML_TYPE_F16
 
     def rms(x):
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)
@@ -225,83 +252,170 @@ def bench_dense(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, world:
         q = rms(torch.randn(B, S, H, Dh, generator=g, device=dev))           # [D, H, S, B] storage
         k = rms(torch.randn(B, H, S, Dh, generator=g, device=dev)).half()    # [D, S, H, B] contiguous
         v = torch.randn(B, H, S, Dh, generator=g, device=dev).half()
-        o = torch.empty(B, S, H, Dh, device=dev)
-        qd = ggml.make(ggml.GGML_TYPE_F32, [Dh, S, H, B], q.data_ptr(), [4, 4 * Dh * H, 4 * Dh, 4 * Dh * H * S])
-        kd = ggml.make(ggml.GGML_TYPE_F16, [Dh, S, H, B], k.data_ptr())
-        vd = ggml.make(ggml.GGML_TYPE_F16, [Dh, S, H, B], v.data_ptr())
-        dd = ggml.make(ggml.GGML_TYPE_F32, [Dh, H, S, B], o.data_ptr())
-        return (q, k, v, o), (qd, kd, vd, None, dd)
+        qd = ggml.make(F32, [Dh, S, H, B], q.data_ptr(), [4, 4 * Dh * H, 4 * Dh, 4 * Dh * H * S])
+        kd = ggml.make(F16, [Dh, S, H, B], k.data_ptr())
+        vd = ggml.make(F16, [Dh, S, H, B], v.data_ptr())
+        return (q, k, v), (qd, kd, vd)
 
-    def timed(calls, n_calls_per_step, flops_per_call, ws):
-        def step():
+    def timed(calls, exchange_fn, n_calls_per_step, flops_per_call, ws):
+        """calls: [(q, k, v, mask, dst descriptors, scale)]; exchange_fn(s) after each call or None."""
+        def step(with_exchange=True):
             for (qd, kd, vd, md, dd), sc in calls:
                 mm3fa.flash_attn_ext(qd, kd, vd, md, sc, 0.0, 0.0, dd, ws.data_ptr(), ws.numel(), stream.cuda_stream)
+                if with_exchange and exchange_fn is not None:
+                    exchange_fn(stream)
 
-        with torch.cuda.stream(stream):
-            step()
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            step()
-        with torch.cuda.stream(stream):
-            for _ in range(warmup):
-                graph.replay()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(local) as clk:
-            stream.record_event(e0)
-            with torch.cuda.stream(stream):  # replay() launches on the current stream
-                for _ in range(steps):
-                    graph.replay()
-            stream.record_event(e1)
+        res = {}
+        for tag, ex in (("with_exchange", True), ("attention_only", False)):
+            if tag == "attention_only" and exchange_fn is None:
+                break
+            with torch.cuda.stream(stream):
+                step(ex)
             torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / steps
-        del graph
-        us_call = ms * 1e3 / n_calls_per_step
-        return us_call, flops_per_call / (us_call * 1e-6) / 1e12, clk.summary()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step(ex)
+            with ClockSampler(local) as clk:
+                ms = timed_replays(torch, dist, graph, stream, steps, warmup, world)
+            del graph
+            us_call = ms * 1e3 / n_calls_per_step
+            res[tag] = (us_call, flops_per_call / (us_call * 1e-6) / 1e12, clk.summary())
+        return res
 
     burst, sustained, src = measured_tensor_peaks()
     out = {}
     # ---- DiT: 24 blocks of one flow step, 4 operand sets (each ~192 MB > L2) cycled
     B, S, H, Dh = 2, 4096, 16, 128
-    sets = [dit_set(B, S, H, Dh) for _ in range(4)]
-    ws = torch.zeros(1 << 20, dtype=torch.uint8, device=dev)
-    calls = [(sets[i % 4][1], 1.0 / math.sqrt(Dh)) for i in range(24)]
     fl = 4.0 * Dh * S * S * H * B
-    us, tf, clocks = timed(calls, 24, fl, ws)
+    sets = [dit_set(B, S, H, Dh) for _ in range(4)]
+    full = torch.empty(B * world, S, H, Dh, device=dev)  # the whole job's result ([D, H, S, 2N])
+    slice_bytes = B * S * H * Dh * 4
+    dd = ggml.make(F32, [Dh, H, S, B], full.data_ptr() + rank * slice_bytes)  # this rank's pair, in place
+    ws = torch.zeros(1 << 20, dtype=torch.uint8, device=dev)
+    calls = [((*sets[i % 4][1], None, dd), 1.0 / math.sqrt(Dh)) for i in range(24)]
+    ex = (lambda s_: mm3fa.allgather_heads(full.data_ptr() + rank * slice_bytes, 0, full.data_ptr(), Dh, H, S,
+                                           B * world, world, comm, s_.cuda_stream)) if world > 1 else None
+    r = timed(calls, ex, 24, fl, ws)
+    us, tf, clocks = r["with_exchange"]
     out["dit"] = {"tflops": round(tf * world, 1), "tflops_per_gpu": round(tf, 1), "us_per_call": round(us, 2),
                   "clocks": clocks,
                   "config": {"workload": "DiT self-attention, benchmark config 5, 24 blocks per step",
-                             "batch_per_gpu": B, "seq": S, "heads": H, "head_dim": Dh, "mask": None,
-                             "l2": "4 operand sets cycled, each > L2"},
-                  "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": sustained, "unit": "TFLOP/s",
-                               "frac": round(tf / sustained, 4), "peak_kind": "bf16_tflops_sustained",
-                               "frac_of_burst": round(tf / burst, 4), "peak_source": src,
-                               "kernel": "fa_dense_kernel<128,f16>", "traffic": 134490000 + 37360000,
-                               "flops_per_launch": fl}}
+                             "batch_per_gpu": B, "global_batch": B * world, "seq": S, "heads": H, "head_dim": Dh,
+                             "mask": None, "l2": "4 operand sets cycled, each > L2",
+                             "exchange": "all-gather of the result after every call (mm3fa_allgather_heads)"
+                                         if world > 1 else "none (1 GPU)"},
+                  "roofline": {"bound": "tensor", "achieved": round(r.get("attention_only", r["with_exchange"])[1], 1),
+                               "peak": burst, "unit": "TFLOP/s",
+                               "frac": round(r.get("attention_only", r["with_exchange"])[1] / burst, 4),
+                               "peak_kind": "bf16_tflops (burst: the timed region is a fraction of a second)",
+                               "frac_of_sustained": round(r.get("attention_only", r["with_exchange"])[1] / sustained,
+                                                          4),
+                               "peak_source": src, "kernel": "fa_dense_kernel<128,f16>",
+                               "traffic": 134490000 + 37360000, "flops_per_launch": fl}}
+    if "attention_only" in r:
+        out["dit"]["attention_only_us_per_call"] = round(r["attention_only"][0], 2)
+        out["dit"]["attention_only_tflops"] = round(r["attention_only"][1] * world, 1)
+    del full, calls
+    if world > 1:
+        # strong scaling: the B = 2 job's 32 (batch x head) units over the ranks
+        s0, s1, h0, h1, ss = sharding.unit_slice(B, H, rank, world)
+        sl, hl = s1 - s0, h1 - h0
+        direct = world // ss == 1
+        full2 = torch.empty(B, S, H, Dh, device=dev)
+        gath = None if direct else torch.empty(world, sl, S, hl, Dh, device=dev)
+        sptr = full2.data_ptr() + rank * sl * S * H * Dh * 4 if direct else gath[rank].data_ptr()
+        dd2 = ggml.make(F32, [Dh, hl, S, sl], sptr)
+        calls2 = []
+        for i in range(24):
+            qd, kd, vd = sets[i % 4][1]
+            view = lambda t: ggml.make(t.type, [Dh, S, hl, sl], t.data + h0 * t.nb[2] + s0 * t.nb[3], list(t.nb))
+            calls2.append(((view(qd), view(kd), view(vd), None, dd2), 1.0 / math.sqrt(Dh)))
+        ex2 = lambda s_: mm3fa.allgather_heads(sptr, 0 if direct else gath.data_ptr(), full2.data_ptr(), Dh, H, S, B,
+                                               ss, comm, s_.cuda_stream)
+        r2 = timed(calls2, ex2, 24, fl, ws)
+        out["dit_strong"] = {"tflops_job": round(r2["with_exchange"][1], 1), "us_per_call": round(r2["with_exchange"][0], 2),
+                             "attention_only_us_per_call": round(r2["attention_only"][0], 2),
+                             "attention_only_tflops_job": round(r2["attention_only"][1], 1),
+                             "units_per_gpu": sl * hl, "config": {"global_batch": B, "heads": H, "seq": S,
+                                                                  "seq_split": ss, "scaling": "strong"}}
+        del full2, gath, calls2
     del sets
-    # ---- causal prefill: 2 x 1024 tokens, 32q / 8kv, cache view padded to 256
-    Sp, Hq, Hkv, pad = 1024, 32, 8, 256
+    torch.cuda.empty_cache()
+    # ---- causal prefill: 2 x 1024 tokens per GPU (the job: 2N sequences), 32q / 8kv, cache view padded to 256
+    Sp, Hq, Hkv, pad = 1024, N_HEAD // world, N_HEAD_KV // world, 256
+    nsp = 2 * world
     n_kv = -(-Sp // pad) * pad
-    q = rms(torch.randn(2, Sp, Hq, Dh, generator=g, device=dev))
-    kc = rms(torch.randn(2, Hkv, n_kv, Dh, generator=g, device=dev)).half()
-    vc = torch.randn(2, Hkv, n_kv, Dh, generator=g, device=dev).half()
-    o = torch.empty(2, Sp, Hq, Dh, device=dev)
+    q = rms(torch.randn(nsp, Sp, Hq, Dh, generator=g, device=dev))
+    kc = rms(torch.randn(nsp, Hkv, n_kv, Dh, generator=g, device=dev)).half()
+    vc = torch.randn(nsp, Hkv, n_kv, Dh, generator=g, device=dev).half()
     mask = torch.triu(torch.full((Sp, n_kv), float("-inf"), device=dev), diagonal=1).half()
-    qd = ggml.make(ggml.GGML_TYPE_F32, [Dh, Sp, Hq, 2], q.data_ptr(), [4, 4 * Dh * Hq, 4 * Dh, 4 * Dh * Hq * Sp])
-    kd = ggml.make(ggml.GGML_TYPE_F16, [Dh, n_kv, Hkv, 2], kc.data_ptr())
-    vd = ggml.make(ggml.GGML_TYPE_F16, [Dh, n_kv, Hkv, 2], vc.data_ptr())
-    md = ggml.make(ggml.GGML_TYPE_F16, [n_kv, Sp, 1, 1], mask.data_ptr())
-    dd = ggml.make(ggml.GGML_TYPE_F32, [Dh, Hq, Sp, 2], o.data_ptr())
-    need = mm3fa.workspace_size(qd, kd, vd, md, dd)
+    gath = torch.empty(world, nsp, Sp, Hq, Dh, device=dev)
+    fullp = torch.empty(nsp, Sp, N_HEAD, Dh, device=dev) if world > 1 else None
+    qd = ggml.make(F32, [Dh, Sp, Hq, nsp], q.data_ptr(), [4, 4 * Dh * Hq, 4 * Dh, 4 * Dh * Hq * Sp])
+    kd = ggml.make(F16, [Dh, n_kv, Hkv, nsp], kc.data_ptr())
+    vd = ggml.make(F16, [Dh, n_kv, Hkv, nsp], vc.data_ptr())
+    md = ggml.make(F16, [n_kv, Sp, 1, 1], mask.data_ptr())
+    ddp = ggml.make(F32, [Dh, Hq, Sp, nsp], gath[rank].data_ptr())
+    need = mm3fa.workspace_size(qd, kd, vd, md, ddp)
     ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
-    flp = 4.0 * Dh * (Sp * (Sp + 1) / 2) * Hq * 2
-    us, tf, clocks = timed([((qd, kd, vd, md, dd), 1.0 / math.sqrt(Dh))], 1, flp, ws)
+    flp = 4.0 * Dh * (Sp * (Sp + 1) / 2) * Hq * nsp
+    exp_ = (lambda s_: mm3fa.allgather_heads(gath[rank].data_ptr(), gath.data_ptr(), fullp.data_ptr(), Dh, N_HEAD, Sp,
+                                             nsp, 1, comm, s_.cuda_stream)) if world > 1 else None
+    r = timed([((qd, kd, vd, md, ddp), 1.0 / math.sqrt(Dh))], exp_, 1, flp, ws)
+    us, tf, clocks = r["with_exchange"]
+    tf_k = r.get("attention_only", r["with_exchange"])[1]
     out["prefill"] = {"tflops": round(tf * world, 1), "tflops_per_gpu": round(tf, 1), "us_per_call": round(us, 2),
-                      "frac_of_sustained": round(tf / sustained, 4), "clocks": clocks,
-                      "config": {"workload": "causal LM prefill, benchmark config 4", "n_seq": 2, "tokens": Sp,
-                                 "n_head": Hq, "n_head_kv": Hkv, "head_dim": Dh, "n_kv_view": n_kv}}
+                      "frac_of_burst": round(tf_k / burst, 4), "frac_of_sustained": round(tf_k / sustained, 4),
+                      "clocks": clocks,
+                      "config": {"workload": "causal LM prefill, benchmark config 4", "n_seq": nsp, "tokens": Sp,
+                                 "n_head": N_HEAD, "n_head_kv": N_HEAD_KV, "head_dim": Dh, "n_kv_view": n_kv,
+                                 "parallelism": f"kv-head shard x{world}"
+                                                + (", all-gather after the call" if world > 1 else "")}}
+    if "attention_only" in r:
+        out["prefill"]["attention_only_us_per_call"] = round(r["attention_only"][0], 2)
     return out
+
+
+SWEEP_BATCH = (2, 4, 8)
+SWEEP_KV = (512, 2048, 8192, 16384)
+
+
+def bench_sweep(torch, dist, mm3fa, ggml, dev, stream, steps: int, warmup: int, world: int, rank: int,
+                n_layers: int) -> dict:
+    """Benchmark config 2 as a sweep: batch 2/4/8 (CFG pairs) x KV 512/2048/8192/16384, 36 independent
+    F16 layers (caches [128, max(10240, KV), 8, batch], K/V ~ N(0, 0.25)) per CUDA graph.  With N GPUs
+    each point keeps its batch, rank r computes kv heads [8r/N, 8(r+1)/N) and the heads are exchanged
+    after every layer (fused peer stores + device wait), so the per-layer time is the sharded time of
+    the fixed job (strong scaling of the point)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(31 + rank)
+    peak, src = measured_peaks()
+    points = []
+    for B in SWEEP_BATCH:
+        for kv in SWEEP_KV:
+            st = DecodeStack(torch, dist, mm3fa, ggml, dev, g, B, kv, n_layers, world, rank, "p2p")
+            with torch.cuda.stream(stream):
+                st.step(stream)
+            torch.cuda.synchronize()
+            graph = st.capture(stream)
+            us_layer = timed_replays(torch, dist, graph, stream, steps, warmup, world) * 1e3 / n_layers
+            del graph
+            algo = st.layer_bytes()
+            gbs = algo / (us_layer * 1e-6) / 1e9
+            points.append({"n_seq": B, "n_kv": kv, "us_per_layer": round(us_layer, 3), "GBps": round(gbs, 1),
+                           "GBps_job": round(gbs * world, 1), "frac": round(gbs / peak, 4),
+                           "bytes_per_layer_per_gpu": algo})
+            torch.cuda.synchronize()
+            st.close()
+            del st
+            torch.cuda.empty_cache()
+    return {"sweep": {"points": points, "peak": peak, "peak_source": src, "unit": "GB/s",
+                      "config": {"workload": "benchmark config 2: 36-layer decode attention, batch x KV sweep",
+                                 "n_layers": n_layers, "n_head": N_HEAD // world, "n_head_kv": N_HEAD_KV // world,
+                                 "head_dim": D, "kv_type": "f16",
+                                 "parallelism": f"kv-head shard x{world} of each point"
+                                                + (", per-layer fused exchange" if world > 1 else ""),
+                                 "l2": "inputs > L2 (36 layers of caches per point)"}}}
 
 
 def bench_q8(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, world: int, n_layers: int) -> dict:
@@ -461,6 +575,157 @@ def bench_decode_step(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, 
                                        "n_seq": n_seq, "n_head": hq, "n_head_kv": hkv, "head_dim": D}}}
 
 
+class DecodeStack:
+    """n_layers independent F16 decode-attention layers of one (batch, KV) point in the reference's
+    cache layout ([128, max_seq, 8, batch] viewed at KV), this rank's kv-head shard of it, with the
+    per-layer head exchange the model needs: layer l's o_proj consumes every head of layer l's
+    result before layer l+1 starts (src/qwen3-lm.h:732, 823-827).
+
+    world == 1: plain attention into [L, B, 1, 32, D].  world > 1, exchange "p2p": the attention
+    kernel stores its rows into every rank's buffer (mm3fa_flash_attn_ext_peers) and the next layer
+    waits on the device (mm3fa_peer_wait); "nccl": mm3fa_allgather_heads after every layer."""
+
+    def __init__(self, torch, dist, mm3fa, ggml, dev, gen, B: int, kv: int, n_layers: int, world: int, rank: int,
+                 mode: str = "p2p", max_seq: int | None = None):
+        from mm3fa import exchange as xch
+
+        self.torch, self.mm3fa, self.world, self.rank, self.mode = torch, mm3fa, world, rank, mode
+        self.B, self.kv, self.L = B, kv, n_layers
+        self.hkv, self.hq = N_HEAD_KV // world, N_HEAD // world
+        hkv, hq = self.hkv, self.hq
+        max_seq = max_seq or max(MAX_SEQ, kv)
+        rb = 2 * D
+        nb = [2, rb, rb * max_seq, rb * max_seq * hkv]
+        self.caches = []
+        self.q_all = torch.empty(n_layers, B, hq, 1, D, device=dev)  # every layer's Q in one buffer
+        for l in range(n_layers):
+            kc = (torch.randn(B, hkv, max_seq, D, generator=gen, device=dev) * 0.5).half()
+            vc = (torch.randn(B, hkv, max_seq, D, generator=gen, device=dev) * 0.5).half()
+            self.caches.append((kc, vc))
+            self.q_all[l].copy_(torch.randn(B, hq, 1, D, generator=gen, device=dev))
+        self.mask = torch.zeros(B, 1, 1, kv, dtype=torch.float16, device=dev)
+        self.pb = None
+        F32, F16 = ggml.GGML_TYPE_F32, ggml.GGML_TYPE_F16
+        layer_out = B * N_HEAD * D * 4
+        if world == 1:
+            self.full = torch.empty(n_layers, B, 1, N_HEAD, D, device=dev)
+            dst_ptr = [self.full[l].data_ptr() for l in range(n_layers)]
+        elif mode == "p2p":
+            self.pb = xch.PeerBuffers(torch, dist, dev, layer_out, n_layers)
+            assert self.pb.slot_bytes == layer_out
+            self.full = self.pb.result(0, (n_layers, B, 1, N_HEAD, D))  # slots are contiguous
+            dst_ptr = [self.pb.result_ptr(l) + rank * hq * D * 4 for l in range(n_layers)]
+        else:
+            self.comm = xch.nccl_comm(dist, dev)
+            self.gathered = torch.empty(n_layers, world, B, 1, hq, D, device=dev)
+            self.full = torch.empty(n_layers, B, 1, N_HEAD, D, device=dev)
+            dst_ptr = [self.gathered[l, rank].data_ptr() for l in range(n_layers)]
+        # this rank's heads of each layer's result: [D, hq, 1, B] with the strides of the whole
+        # [D, 32, 1, B] result (world == 1, p2p) or the contiguous slice (nccl)
+        dnb = [4, 4 * D, 4 * D * hq, 4 * D * hq] if (world > 1 and mode == "nccl") else \
+            [4, 4 * D, 4 * D * N_HEAD, 4 * D * N_HEAD]
+        self.descs = []
+        for l in range(n_layers):
+            kc, vc = self.caches[l]
+            self.descs.append((ggml.make(F32, [D, 1, hq, B], self.q_all[l].data_ptr()),
+                               ggml.make(F16, [D, kv, hkv, B], kc.data_ptr(), nb),
+                               ggml.make(F16, [D, kv, hkv, B], vc.data_ptr(), list(nb)),
+                               ggml.make(F16, [kv, 1, 1, B], self.mask.data_ptr()),
+                               ggml.make(F32, [D, hq, 1, B], dst_ptr[l], dnb)))
+        need = mm3fa.workspace_size(*self.descs[0][:4], self.descs[0][4])
+        self.ws = torch.zeros(max(need, 4096), dtype=torch.uint8, device=dev)
+        self.scale = 1.0 / math.sqrt(D)
+
+    def layer(self, l: int, s, exchange: bool = True) -> int:
+        """Enqueues layer l (attention, then the exchange when asked); returns its launches."""
+        mm3fa, (qd, kd, vd, md, dd) = self.mm3fa, self.descs[l]
+        ws = (self.ws.data_ptr(), self.ws.numel())
+        if self.world > 1 and exchange and self.mode == "p2p":
+            mm3fa.flash_attn_ext_peers(qd, kd, vd, md, self.scale, 0.0, 0.0, dd, *ws, self.pb.peers[l], l,
+                                       s.cuda_stream)
+            mm3fa.peer_wait(self.pb.peers[l], l, self.pb.targets.data_ptr(), ws[0], s.cuda_stream)
+            return 2
+        mm3fa.flash_attn_ext(qd, kd, vd, md, self.scale, 0.0, 0.0, dd, *ws, s.cuda_stream)
+        if self.world > 1 and exchange:
+            g = self.gathered[l]
+            mm3fa.allgather_heads(g[self.rank].data_ptr(), g.data_ptr(), self.full[l].data_ptr(), D, N_HEAD, 1, self.B,
+                                  1, self.comm, s.cuda_stream)
+            return 2
+        return 1
+
+    def step(self, s, exchange: bool = True, layers=None) -> int:
+        return sum(self.layer(l, s, exchange) for l in (range(self.L) if layers is None else layers))
+
+    def capture(self, s, exchange: bool = True):
+        torch = self.torch
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            self.step(s, exchange)
+        return graph
+
+    def layer_bytes(self) -> int:
+        return layer_bytes(self.B, self.hkv, self.hq, self.kv)
+
+    def close(self):
+        if self.pb is not None:
+            self.pb.close()
+
+
+def timed_replays(torch, dist, graph, stream, steps: int, warmup: int, world: int, clk=None) -> float:
+    """ms per replay of `graph`, device time (CUDA events on `stream`), max over ranks, with a
+    barrier and a synchronize on both sides of the timed replays."""
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    stream.record_event(e0)
+    with torch.cuda.stream(stream):
+        for _ in range(steps):
+            graph.replay()
+    stream.record_event(e1)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1)], device=stream.device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item()) / steps
+
+
+def bench_strong(torch, dist, mm3fa, ggml, dev, stream, steps: int, warmup: int, world: int, rank: int,
+                 n_layers: int) -> dict:
+    """Strong scaling of fixed decode jobs over the GPUs: the headline point (B=2, KV 8192) and
+    config 2's large end (B=8, KV 16384), each a 36-layer step whose 8 kv heads are split over the
+    ranks, with the fused per-layer head exchange (world > 1)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(77 + rank)
+    peak, src = measured_peaks()
+    out = {}
+    for name, B, kv in (("b2_kv8192", 2, 8192), ("b8_kv16384", 8, 16384)):
+        st = DecodeStack(torch, dist, mm3fa, ggml, dev, g, B, kv, n_layers, world, rank, "p2p")
+        with torch.cuda.stream(stream):
+            st.step(stream)
+        torch.cuda.synchronize()
+        graph = st.capture(stream)
+        ms = timed_replays(torch, dist, graph, stream, steps, warmup, world)
+        del graph
+        job = layer_bytes(B, N_HEAD_KV, N_HEAD, kv) * n_layers
+        out[name] = {"n_seq": B, "n_kv": kv, "us_per_layer": round(ms * 1e3 / n_layers, 3),
+                     "GBps_job": round(job / (ms * 1e-3) / 1e9, 1),
+                     "frac_of_n_gpus_x_peak": round(job / (ms * 1e-3) / 1e9 / (peak * world), 4),
+                     "exchange": "fused peer stores + device wait per layer" if world > 1 else "none (1 GPU)"}
+        torch.cuda.synchronize()
+        st.close()
+        del st
+        torch.cuda.empty_cache()
+    return {"strong": {"points": out, "peak_per_gpu": peak, "peak_source": src, "n_layers": n_layers,
+                       "scaling": "strong (fixed job, kv heads split over the ranks)"}}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -472,6 +737,10 @@ def main() -> None:
     ap.add_argument("--no-dense", action="store_true", help="skip the DiT / prefill (tensor-core) lines")
     ap.add_argument("--no-q8", action="store_true", help="skip the Q8_0 KV-cache decode line (config 3)")
     ap.add_argument("--no-step", action="store_true", help="skip the decode-step line (fused prologue + attention)")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the config 2 sweep (batch x KV)")
+    ap.add_argument("--no-strong", action="store_true", help="skip the strong-scaling lines")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="per-layer head exchange of the headline at N > 1 (the other is timed beside it)")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers per step (36 = the LM; fewer only for small ncu captures)")
     args = ap.parse_args()
@@ -500,117 +769,70 @@ def main() -> None:
     if N_HEAD_KV % world:
         raise SystemExit(f"{N_HEAD_KV} kv heads do not shard over {world} GPUs")
 
-    n_seq = 2 * world                 # N CFG pairs
-    hkv = N_HEAD_KV // world          # kv heads held by this rank
-    hq = N_HEAD // world              # query heads computed by this rank
+    n_seq = 2 * world                 # N CFG pairs: weak scaling, 16 (sequence, kv head) pairs per GPU
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
-
-    # ---- per-layer operands (device resident), in the reference's layouts
-    caches, qs, outs = [], [], []
-    q_all = torch.empty(n_layers, n_seq, hq, 1, D, device=dev)  # every layer's Q in one buffer
-    for l in range(n_layers):
-        kc = (torch.randn(n_seq, hkv, MAX_SEQ, D, generator=g, device=dev) * 0.5).half()
-        vc = (torch.randn(n_seq, hkv, MAX_SEQ, D, generator=g, device=dev) * 0.5).half()
-        caches.append((kc, vc))
-        q_all[l].copy_(torch.randn(n_seq, hq, 1, D, generator=g, device=dev))
-        qs.append(q_all[l])
-    mask = torch.zeros(n_seq, 1, 1, N_KV, dtype=torch.float16, device=dev)
-    outs = torch.empty(n_layers, n_seq, 1, hq, D, device=dev)
-    rb = 2 * D
-    kv_nb = [2, rb, rb * MAX_SEQ, rb * MAX_SEQ * hkv]
-    descs = []
-    for l in range(n_layers):
-        kc, vc = caches[l]
-        qd = ggml.make(ggml.GGML_TYPE_F32, [D, 1, hq, n_seq], qs[l].data_ptr())
-        kd = ggml.make(ggml.GGML_TYPE_F16, [D, N_KV, hkv, n_seq], kc.data_ptr(), kv_nb)
-        vd = ggml.make(ggml.GGML_TYPE_F16, [D, N_KV, hkv, n_seq], vc.data_ptr(), kv_nb)
-        md = ggml.make(ggml.GGML_TYPE_F16, [N_KV, 1, 1, n_seq], mask.data_ptr())
-        dd = ggml.make(ggml.GGML_TYPE_F32, [D, hq, 1, n_seq], outs[l].data_ptr())
-        descs.append((qd, kd, vd, md, dd))
-    scale = 1.0 / math.sqrt(D)
-    ws_bytes = mm3fa.workspace_size(*descs[0][:4], descs[0][4])
-    ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
-    gathered = torch.empty(world, n_layers, n_seq, 1, hq, D, device=dev) if world > 1 else None
-    final = torch.empty(n_layers * n_seq, 1, N_HEAD, D, device=dev) if world > 1 else None
-
     stream = torch.cuda.Stream(device=dev)
-    ev_k0, ev_k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st = DecodeStack(torch, dist, mm3fa, ggml, dev, g, n_seq, N_KV, n_layers, world, rank, args.exchange, MAX_SEQ)
+    hkv, hq = st.hkv, st.hq
 
-    def attention_layers(s):
-        for (qd, kd, vd, md, dd) in descs:
-            mm3fa.flash_attn_ext(qd, kd, vd, md, scale, 0.0, 0.0, dd, ws.data_ptr(), ws.numel(), s.cuda_stream)
-
-    def exchange(s):
-        if world > 1:
-            dist.all_gather_into_tensor(gathered.view(-1), outs.view(-1))
-            mm3fa.assemble_heads(gathered.data_ptr(), final.data_ptr(), D, N_HEAD, 1, n_layers * n_seq, world,
-                                 s.cuda_stream)
-
-    # capture the 36 attention launches once: the reference replays its decode graph the same way
+    # capture the step once: the reference replays its decode graph the same way
     with torch.cuda.stream(stream):
-        attention_layers(stream)  # first call sets kernel attributes outside capture
-        exchange(stream)
+        st.step(stream)  # first calls set kernel attributes outside capture
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        attention_layers(stream)
-    launches_per_step = n_layers + (1 if world > 1 else 0)
+    graph = st.capture(stream)
+    launches_per_step = n_layers * (2 if world > 1 else 1)
+    graph_attn = st.capture(stream, exchange=False) if world > 1 else graph
 
-    def step():
-        with torch.cuda.stream(stream):
-            graph.replay()
-            exchange(stream)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-
-    # ---- timed region (device time, CUDA events on the launching stream)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    kern_ms = []
+    # ---- timed region (device time, CUDA events on the launching stream, max over ranks)
     with ClockSampler(local) as clk:
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        stream.record_event(e0)
-        for _ in range(args.steps):
-            stream.record_event(ev_k0)
-            with torch.cuda.stream(stream):
-                graph.replay()
-            stream.record_event(ev_k1)
-            with torch.cuda.stream(stream):
-                exchange(stream)
-            ev_k1.synchronize()
-            kern_ms.append(ev_k0.elapsed_time(ev_k1))
-        stream.record_event(e1)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
+        ms_per_step = timed_replays(torch, dist, graph, stream, args.steps, args.warmup, world)
     clocks = clk.summary()
-    t_ms = e0.elapsed_time(e1)
-    t = torch.tensor([t_ms], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    t_ms = float(t.item())
-    ms_per_step = t_ms / args.steps
-    per_rank_bytes = layer_bytes(n_seq, hkv, hq) * n_layers
+    per_rank_bytes = st.layer_bytes() * n_layers
     job_bytes = per_rank_bytes * world
-    value = job_bytes * args.steps / (t_ms * 1e-3) / 1e9
+    value = job_bytes / (ms_per_step * 1e-3) / 1e9
 
-    # ---- roofline of the decode kernel (average launch inside the captured step)
-    avg_launch_us = statistics.median(kern_ms) * 1e3 / n_layers
+    # ---- roofline of the decode kernel: its average launch in the attention-only graph
+    ms_attn = timed_replays(torch, dist, graph_attn, stream, args.steps, args.warmup, world)
+    avg_launch_us = ms_attn * 1e3 / n_layers
     peak, peak_src = measured_peaks()
-    achieved = layer_bytes(n_seq, hkv, hq) / (avg_launch_us * 1e-6) / 1e9
+    achieved = st.layer_bytes() / (avg_launch_us * 1e-6) / 1e9
+    xinfo = None
+    if world > 1:
+        # the other exchange form, timed the same way (same shapes, its own buffers)
+        other = "nccl" if args.exchange == "p2p" else "p2p"
+        g_o = torch.Generator(device=dev)
+        g_o.manual_seed(4321 + rank)
+        st_o = DecodeStack(torch, dist, mm3fa, ggml, dev, g_o, n_seq, N_KV, n_layers, world, rank, other, MAX_SEQ)
+        with torch.cuda.stream(stream):
+            st_o.step(stream)
+        torch.cuda.synchronize()
+        graph_o = st_o.capture(stream)
+        ms_o = timed_replays(torch, dist, graph_o, stream, args.steps, args.warmup, world)
+        del graph_o
+        torch.cuda.synchronize()
+        st_o.close()
+        del st_o
+        torch.cuda.empty_cache()
+        us = {args.exchange: ms_per_step * 1e3 / n_layers, other: ms_o * 1e3 / n_layers}
+        xinfo = {"per_layer": True, "mode": args.exchange,
+                 "us_per_layer": {"attention_only": round(avg_launch_us, 3), "p2p": round(us["p2p"], 3),
+                                  "nccl": round(us["nccl"], 3)},
+                 "exchange_us_per_layer": {"p2p": round(us["p2p"] - avg_launch_us, 3),
+                                           "nccl": round(us["nccl"] - avg_launch_us, 3)},
+                 "p2p": "mm3fa_flash_attn_ext_peers (rows stored into every rank's buffer over NVLink from the "
+                        "decode kernel's merge) + mm3fa_peer_wait (device-side bounded wait) per layer",
+                 "nccl": "mm3fa_flash_attn_ext + mm3fa_allgather_heads (ncclAllGather + permute) per layer"}
 
     # ---- end to end through the C ABI: Q/mask from pinned host memory, outputs back to host
-    # One pinned buffer per direction (every layer's Q up, every layer's output down), moved in
-    # chunks of E2E_CHUNK layers on two copy streams so that the transfers overlap the attention
-    # of other layers: chunk c's Q is uploaded before its layers run, its outputs go down while
+    # One pinned buffer per direction (every layer's Q up, every layer's whole result down), moved
+    # in chunks of E2E_CHUNK layers on two copy streams so that the transfers overlap the attention
+    # of other layers: chunk c's Q is uploaded before its layers run, its results go down while
     # the next chunk computes.
+    q_all, mask, full = st.q_all, st.mask, st.full
     q_host = q_all.cpu().pin_memory()
     mask_host = mask.cpu().pin_memory()
-    out_host = torch.empty(outs.shape, dtype=torch.float32).pin_memory()
+    out_host = torch.empty(full.shape, dtype=torch.float32).pin_memory()
     up_s, down_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
     chunks = [(a, min(a + E2E_CHUNK, n_layers)) for a in range(0, n_layers, E2E_CHUNK)]
     g2 = torch.cuda.CUDAGraph()
@@ -629,21 +851,20 @@ def main() -> None:
                 uploaded.append(ev)
         for (a, b), ev in zip(chunks, uploaded):
             stream.wait_event(ev)
-            for (qd, kd, vd, md, dd) in descs[a:b]:
-                mm3fa.flash_attn_ext(qd, kd, vd, md, scale, 0.0, 0.0, dd, ws.data_ptr(), ws.numel(), stream.cuda_stream)
+            st.step(stream, layers=range(a, b))
             done = torch.cuda.Event()
             stream.record_event(done)
             down_s.wait_event(done)
             with torch.cuda.stream(down_s):
-                out_host[a:b].copy_(outs[a:b], non_blocking=True)
+                out_host[a:b].copy_(full[a:b], non_blocking=True)
         joined = torch.cuda.Event()
         down_s.record_event(joined)
         stream.wait_event(joined)
-    h2d = q_host.numel() * 4 + mask_host.numel() * 2
-    d2h = out_host.numel() * 4
+    h2d = (q_host.numel() * 4 + mask_host.numel() * 2) * world
+    d2h = out_host.numel() * 4 * world
     for _ in range(args.warmup):
-        g2.replay()
-        exchange(stream)
+        with torch.cuda.stream(stream):
+            g2.replay()
         stream.synchronize()
     if world > 1:
         dist.barrier()
@@ -652,7 +873,6 @@ def main() -> None:
     for _ in range(args.steps):
         with torch.cuda.stream(stream):
             g2.replay()
-            exchange(stream)
         stream.synchronize()  # the step's result is read on the host every step
     stream.record_event(f1)
     torch.cuda.synchronize()
@@ -660,8 +880,12 @@ def main() -> None:
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = job_bytes * args.steps / (float(te.item()) * 1e-3) / 1e9
+    del g2
+    if graph_attn is not graph:
+        del graph_attn
 
-    dense = None if args.no_dense else bench_dense(torch, mm3fa, ggml, dev, stream, args.steps, args.warmup, world, local)
+    dense = None if args.no_dense else bench_dense(torch, dist, mm3fa, ggml, dev, stream, args.steps, args.warmup,
+                                                   world, rank, local)
     if dense is not None and world > 1:
         dist.barrier()
     q8 = None if args.no_q8 else bench_q8(torch, mm3fa, ggml, dev, stream, args.steps, args.warmup, world, n_layers)
@@ -671,6 +895,13 @@ def main() -> None:
                                                         n_layers)
     if dstep is not None and world > 1:
         dist.barrier()
+
+    sweep = None if args.no_sweep else bench_sweep(torch, dist, mm3fa, ggml, dev, stream, args.steps, args.warmup,
+                                                   world, rank, n_layers)
+    if sweep is not None and world > 1:
+        dist.barrier()
+    strong = None if args.no_strong else bench_strong(torch, dist, mm3fa, ggml, dev, stream, args.steps,
+                                                      args.warmup, world, rank, n_layers)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -686,14 +917,15 @@ def main() -> None:
                                    "(F16 cache views [128, 8192, 8, B] of [128, 10240, 8, B])",
                        "global_batch": n_seq, "n_kv": N_KV, "n_layers": n_layers, "n_head": N_HEAD,
                        "n_head_kv": N_HEAD_KV, "head_dim": D, "parallelism": f"kv-head shard x{world}",
+                       "exchange": (f"per layer ({args.exchange})" if world > 1 else "none (1 GPU)"),
                        "l2": "inputs > L2 (36 x 84 MB caches)",
                        "us_per_layer": round(ms_per_step * 1e3 / n_layers, 3),
-                       "bytes_per_layer_per_gpu": layer_bytes(n_seq, hkv, hq)},
+                       "bytes_per_layer_per_gpu": st.layer_bytes()},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
-                         "traffic": NCU_TRAFFIC_BYTES, "kernel": NCU_KERNEL,
+                         "traffic": NCU_TRAFFIC_BYTES, "traffic_source": NCU_TRAFFIC_SOURCE, "kernel": NCU_KERNEL,
                          "avg_launch_us": round(avg_launch_us, 3)},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
@@ -704,11 +936,21 @@ def main() -> None:
             line.update(q8)
         if dstep is not None:
             line.update(dstep)
+        if sweep is not None:
+            line.update(sweep)
+        if strong is not None:
+            line.update(strong)
+        if xinfo is not None:
+            line["exchange"] = xinfo
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
 
-    del graph, g2
+    del graph
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    st.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

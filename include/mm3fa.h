@@ -71,6 +71,7 @@ enum mm3fa_status {
     MM3FA_ERR_TIMEOUT     = 9,  /* a bounded device-side wait expired                     */
     MM3FA_ERR_DEVICE      = 10, /* current device is not an sm_100 part                   */
     MM3FA_ERR_SCRATCH_LIMIT = 11, /* needs more scratch than MM3FA_NOALLOC_SCRATCH_BYTES  */
+    MM3FA_ERR_COMM        = 12, /* NCCL missing, or a collective / IPC call failed        */
 };
 
 /* Size of the fixed device scratch buffer behind mm3fa_flash_attn_ext_noalloc (8 MiB). */
@@ -280,6 +281,101 @@ MM3FA_API int mm3fa_dit_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor *
  */
 MM3FA_API int mm3fa_assemble_heads(const float * gathered, float * dst, int64_t dv, int64_t n_head, int64_t n_q,
                          int64_t n_seq, int n_ranks, void * stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Multi-GPU head exchange.  With the kv heads (decode, prefill) or the (sequence, head) units
+ * (DiT) partitioned over G ranks, one process per GPU, each rank computes a slice of the ggml
+ * result [Dv, n_head, n_q, n_seq]; the o_proj / to_out that follows the attention needs every
+ * head of its rows, so the slices are exchanged after every attention call.  Two forms:
+ *   - mm3fa_allgather_heads: one NCCL all-gather (the caller's communicator) + a permute;
+ *   - mm3fa_flash_attn_ext_peers + mm3fa_peer_wait: the decode kernel stores its result rows
+ *     straight into every rank's result buffer over NVLink (CUDA IPC mappings) and signals a
+ *     counter, and the consumer waits for the counter on the device (bounded).
+ * ------------------------------------------------------------------------------------------ */
+
+/* Most ranks a head exchange spans (one node). */
+#define MM3FA_MAX_RANKS 8
+
+/*
+ * All-gathers the result slices of G ranks over a NCCL communicator and writes the whole ggml
+ * result on every rank.  The ranks split the sequences into seq_split groups and the heads into
+ * G / seq_split groups; rank r = (sequence group) * (G / seq_split) + (head group) holds
+ *   slice     F32 contiguous [Dv, n_head*seq_split/G, n_q, n_seq/seq_split]: its sequences'
+ *             rows for its heads (the decode kernel's dst when it runs on the rank's shard)
+ * and gets
+ *   dst       F32 contiguous [Dv, n_head, n_q, n_seq] (may not overlap slice unless slice ==
+ *             gathered + r * slice elements, the in-place form)
+ *   gathered  F32 scratch of G slices, or NULL when the gathered order is already ggml's (each
+ *             rank holds whole sequences: G / seq_split == 1; or a single row: n_q * n_seq /
+ *             seq_split == 1 with seq_split == 1); then NCCL writes dst directly.
+ * KV-head sharding of the LM is seq_split = 1; (batch x head) sharding of the DiT with G <= B is
+ * seq_split = G, with G > B seq_split = B.  nccl_comm is an ncclComm_t of G ranks (e.g. from
+ * ncclCommInitRank, or the one torch.distributed made); the library loads libnccl.so.2 at the
+ * first call (the copy already in the process when there is one).
+ * Replaces: nothing in the reference (one device): the exchange that turns the sharded attention
+ *           into the [n_head*Dv, n_q, n_seq] input of the o_proj at src/qwen3-lm.h:823-827 (and
+ *           of to_out after src/dit.h:221-226).
+ */
+MM3FA_API int mm3fa_allgather_heads(const float * slice, float * gathered, float * dst, int64_t dv, int64_t n_head,
+                                    int64_t n_q, int64_t n_seq, int seq_split, void * nccl_comm, void * stream);
+
+/* Every rank's exchange buffers as mapped into this process (see mm3fa_ipc_open). */
+typedef struct mm3fa_peers {
+    int32_t    n_ranks;                  /* G, 2 .. MM3FA_MAX_RANKS */
+    int32_t    rank;                     /* this process's rank */
+    void *     dst[MM3FA_MAX_RANKS];     /* rank i's whole result buffer (16-byte aligned); dst[rank] is ours */
+    uint32_t * flags[MM3FA_MAX_RANKS];   /* rank i's arrival counters (one u32 per slot, zeroed once) */
+} mm3fa_peers;
+
+/*
+ * mm3fa_flash_attn_ext on this rank's shard, with the head exchange fused into the kernel: dst
+ * is this rank's slice as a view of its own result buffer peers->dst[rank] (e.g. heads
+ * [r*H/G, (r+1)*H/G) of [Dv, H, n_q, n_seq]); every result row is stored at the same offset in
+ * every rank's buffer as well (plain stores over NVLink while other CTAs still compute), and when
+ * the whole grid is done, counter `slot` of every other rank is incremented (release, system
+ * scope).  kv_len may be NULL (as mm3fa_flash_attn_ext) or a device array (as _kvlen).  Only the
+ * tensor-core decode kernel's cluster split carries the exchange (<= 16 query rows per (sequence,
+ * kv head), F16/BF16/Q8_0 caches it can stream, 16-byte aligned rows): other shapes return
+ * MM3FA_ERR_UNSUPPORTED and enqueue nothing, as does max_bias != 0 (ALiBi slopes follow the
+ * global head index, which a shard's descriptors do not carry; the reference passes 0).  Peer
+ * memory is only ever written, by plain stores and one atomic per rank; nothing loads from it.
+ * Replaces: the attention node of src/qwen3-lm.h:816-820 plus its exchange (see above).
+ */
+MM3FA_API int mm3fa_flash_attn_ext_peers(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                                         const mm3fa_tensor * mask, const int32_t * kv_len, float scale,
+                                         float max_bias, float logit_softcap, int prec, mm3fa_tensor * dst,
+                                         void * workspace, size_t workspace_bytes, const mm3fa_peers * peers,
+                                         int slot, void * stream);
+
+/*
+ * Device-side wait of the consumer of a fused exchange: enqueues on `stream` one thread that
+ * waits (acquire, system scope) until this rank's counter `slot` has grown by n_ranks - 1 since
+ * the previous wait on that slot, i.e. until every other rank's slice of the latest
+ * mm3fa_flash_attn_ext_peers call on the slot is in this rank's buffer; kernels enqueued after
+ * it read the whole result.  targets: device u32 per slot, zeroed once with the counters, private
+ * to this rank.  The wait is bounded (MM3FA_WAIT_TIMEOUT_MS, 2 s by default); on expiry it sets
+ * the workspace status word (mm3fa_workspace_status reports MM3FA_ERR_TIMEOUT) and returns.
+ * Replaces: nothing in the reference (see above).
+ */
+MM3FA_API int mm3fa_peer_wait(const mm3fa_peers * peers, int slot, uint32_t * targets, void * workspace,
+                              void * stream);
+
+/* CUDA IPC handle of a device buffer: the allocation's handle plus the buffer's offset in it. */
+typedef struct mm3fa_ipc_handle {
+    unsigned char handle[64];
+    uint64_t      offset;
+} mm3fa_ipc_handle;
+
+/*
+ * Host helpers for building mm3fa_peers across processes: mm3fa_ipc_export fills a handle for a
+ * device buffer (cudaIpcGetMemHandle of the allocation that holds it); the caller moves the
+ * handles between its processes by any means; mm3fa_ipc_open maps another process's buffer into
+ * this one (cudaIpcOpenMemHandle, peer access enabled) and mm3fa_ipc_close unmaps it.
+ * Replaces: nothing in the reference (see above).
+ */
+MM3FA_API int mm3fa_ipc_export(const void * dev_ptr, mm3fa_ipc_handle * out);
+MM3FA_API int mm3fa_ipc_open(const mm3fa_ipc_handle * h, void ** dev_ptr_out);
+MM3FA_API int mm3fa_ipc_close(void * dev_ptr);
 
 #ifdef __cplusplus
 }

@@ -3,7 +3,8 @@
 Usage: python minimaxmusic.cpp_b200/build.py [--force] [--verbose]
 
 The library is written next to this file (lib/libmm3fa.so) so it travels with the source
-tree; it statically links the CUDA runtime and has no torch dependency.
+tree; it statically links the CUDA runtime and has no torch dependency.  NCCL is not linked:
+the multi-GPU exchange loads libnccl.so.2 at run time (nccl.h supplies only the types).
 """
 from __future__ import annotations
 
@@ -19,7 +20,8 @@ LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libmm3fa.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["mm3fa_abi.cu", "fa_decode.cu", "fa_decode_mma.cu", "fa_dense_sm100.cu", "fa_prologue.cu", "mm3fa_noalloc.cu"]
+SOURCES = ["mm3fa_abi.cu", "fa_decode.cu", "fa_decode_mma.cu", "fa_dense_sm100.cu", "fa_prologue.cu", "mm3fa_noalloc.cu",
+           "mm3fa_exchange.cu"]
 HEADERS = ["fa_common.cuh", "fa_decode.cuh", "fa_dense.cuh", "fa_prologue.cuh"]
 
 NVCC_FLAGS = [
@@ -66,7 +68,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     with concurrent.futures.ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
         objs = list(ex.map(compile_one, SOURCES))
     tmp = LIB + ".tmp"
-    cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp, *objs]
+    cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp, *objs, "-ldl"]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)

@@ -272,6 +272,33 @@ __device__ __forceinline__ void pdl_wait() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// ---- head exchange over peer memory.  Called by all consumer threads of every CTA after its
+// result rows (local and peer copies) are stored: each thread fences its stores at system scope,
+// the CTA counts itself on the workspace's arrival word, and the grid's last CTA resets the word
+// and adds 1, with release semantics at system scope, to every peer's arrival counter.  A peer
+// that has seen the counter grow with acquire semantics (mm3fa_peer_wait) sees every row.
+__device__ __forceinline__ void red_add_release_sys(uint32_t * a, uint32_t v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void peer_exchange_arrive(const DecodeParams & p, int tid) {
+    __threadfence_system();
+    named_barrier_consumers();
+    if (tid == 0) {
+        const uint32_t old = atomicAdd(&p.status[WS_PEER_ARRIVE], 1u);
+        if (old + 1u == gridDim.x) {
+            p.status[WS_PEER_ARRIVE] = 0u;  // the next call starts from zero
+            __threadfence_system();
+#pragma unroll
+            for (int i = 0; i < MAX_PEERS; i++) {
+                if (i < p.n_peers) {
+                    red_add_release_sys(p.peer_flag[i], 1u);
+                }
+            }
+        }
+    }
+}
+
 // byte offset of (key row j, 16-byte chunk c) inside one 128-byte-swizzled TMA box
 __device__ __forceinline__ uint32_t swz(int j, int c) {
     return (uint32_t) (j * 128 + ((c ^ (j & 7)) << 4));
@@ -730,13 +757,25 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                 float *     out = reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 + (int64_t) i * p.d_nb2 +
                                                         (int64_t) u_sq * p.d_nb3) + d;
                 if (p.dst_vec) {
-                    *reinterpret_cast<float4 *>(out) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+                    const float4 r4                  = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+                    *reinterpret_cast<float4 *>(out) = r4;
+                    // head exchange over peer memory: the same row into every peer's result
+                    // buffer (plain 16-byte stores over NVLink; the host guarantees dst_vec)
+#pragma unroll
+                    for (int pp = 0; pp < MAX_PEERS; pp++) {
+                        if (pp < p.n_peers) {
+                            *reinterpret_cast<float4 *>(reinterpret_cast<char *>(out) + p.peer_delta[pp]) = r4;
+                        }
+                    }
                 } else {
                     out[0] = O.x * inv;
                     out[1] = O.y * inv;
                     out[2] = O.z * inv;
                     out[3] = O.w * inv;
                 }
+            }
+            if (p.n_peers > 0) {
+                peer_exchange_arrive(p, tid);
             }
             return;
         } else {

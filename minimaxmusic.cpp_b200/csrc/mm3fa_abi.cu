@@ -445,6 +445,8 @@ const char * mm3fa_status_string(int st) {
             return "device is not sm_100";
         case MM3FA_ERR_SCRATCH_LIMIT:
             return "operands need more scratch than the built-in no-allocation buffer holds";
+        case MM3FA_ERR_COMM:
+            return "NCCL unavailable, or a collective or CUDA IPC call failed";
         default:
             return "unknown status";
     }
@@ -528,7 +530,8 @@ namespace {
 // whatever the row count: they skip (cluster split) or mask (stream-K split) the keys past it.
 int flash_attn_impl(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v, const mm3fa_tensor * mask,
                     const int32_t * kv_len, float scale, float max_bias, float logit_softcap, int prec,
-                    mm3fa_tensor * dst, void * workspace, size_t workspace_bytes, void * stream) {
+                    mm3fa_tensor * dst, void * workspace, size_t workspace_bytes, void * stream,
+                    const mm3fa_peers * peers = nullptr, int slot = 0) {
     if (prec != MM3FA_PREC_DEFAULT && prec != MM3FA_PREC_F32) {
         return MM3FA_ERR_UNSUPPORTED;
     }
@@ -550,7 +553,7 @@ int flash_attn_impl(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_
                                               (int64_t) dst->nb[1], (int64_t) dst->nb[2], (int64_t) dst->nb[3]);
         return record_cuda(cudaGetLastError());
     }
-    if (!kv_len && use_dense(s, mask)) {
+    if (!kv_len && !peers && use_dense(s, mask)) {
         return run_dense(s, q, k, v, mask, scale, max_bias, logit_softcap, dst, workspace, workspace_bytes,
                          wait_timeout_ns(), cs);
     }
@@ -606,8 +609,27 @@ int flash_attn_impl(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_
         const int cluster = pref == 1 ? 0
                                       : decode_mma_cluster_size((int) s.D, s.kvt, p.rows_per_pair, g.n_units,
                                                                 device_info().sms);
+        if (peers) {
+            // the exchange lives in the cluster merge's 16-byte result stores
+            if (cluster == 0 || !p.dst_vec) {
+                return MM3FA_ERR_UNSUPPORTED;
+            }
+            int n = 0;
+            for (int r = 0; r < peers->n_ranks; r++) {
+                if (r != peers->rank) {
+                    p.peer_delta[n] = static_cast<const char *>(peers->dst[r]) -
+                                      static_cast<const char *>(peers->dst[peers->rank]);
+                    p.peer_flag[n]  = peers->flags[r] + slot;
+                    n++;
+                }
+            }
+            p.n_peers = n;
+        }
         return record_cuda(
             launch_decode_mma(p, g, (int) s.D, s.kvt, s.n_head_kv, s.n_seq_k, cluster, workspace, cs));
+    }
+    if (peers) {
+        return MM3FA_ERR_UNSUPPORTED;
     }
     return record_cuda(launch_decode(p, g, (int) s.D, s.kvt, s.bulk, workspace, cs));
 }
@@ -621,6 +643,43 @@ int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const m
                          mm3fa_tensor * dst, void * workspace, size_t workspace_bytes, void * stream) {
     return flash_attn_impl(q, k, v, mask, nullptr, scale, max_bias, logit_softcap, prec, dst, workspace,
                            workspace_bytes, stream);
+}
+
+int mm3fa_flash_attn_ext_peers(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                               const mm3fa_tensor * mask, const int32_t * kv_len, float scale, float max_bias,
+                               float logit_softcap, int prec, mm3fa_tensor * dst, void * workspace,
+                               size_t workspace_bytes, const mm3fa_peers * peers, int slot, void * stream) {
+    if (!peers) {
+        return MM3FA_ERR_NULL;
+    }
+    if (peers->n_ranks < 2 || peers->n_ranks > MM3FA_MAX_RANKS || peers->rank < 0 || peers->rank >= peers->n_ranks ||
+        slot < 0) {
+        return MM3FA_ERR_SHAPE;
+    }
+    for (int r = 0; r < peers->n_ranks; r++) {
+        if (!peers->dst[r] || !peers->flags[r]) {
+            return MM3FA_ERR_NULL;
+        }
+        if (!aligned(peers->dst[r], 16) || !aligned(peers->flags[r], 4)) {
+            return MM3FA_ERR_ALIGN;
+        }
+    }
+    if (!dst || !dst->data) {
+        return MM3FA_ERR_NULL;
+    }
+    // dst must be a view into this rank's own result buffer, 16-byte aligned like the others
+    if (static_cast<const char *>(dst->data) < static_cast<const char *>(peers->dst[peers->rank])) {
+        return MM3FA_ERR_SHAPE;
+    }
+    if (!workspace) {
+        return MM3FA_ERR_WORKSPACE;
+    }
+    // ALiBi slopes depend on the global head index, which a shard's descriptors do not carry
+    if (max_bias != 0.0f) {
+        return MM3FA_ERR_UNSUPPORTED;
+    }
+    return flash_attn_impl(q, k, v, mask, kv_len, scale, max_bias, logit_softcap, prec, dst, workspace,
+                           workspace_bytes, stream, peers, slot);
 }
 
 int mm3fa_flash_attn_ext_kvlen(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,

@@ -28,6 +28,20 @@ OK = 0
 ERR_NULL, ERR_TYPE, ERR_SHAPE, ERR_STRIDE, ERR_ALIGN = 1, 2, 3, 4, 5
 ERR_WORKSPACE, ERR_CUDA, ERR_UNSUPPORTED, ERR_TIMEOUT, ERR_DEVICE = 6, 7, 8, 9, 10
 ERR_SCRATCH_LIMIT = 11
+ERR_COMM = 12
+
+MAX_RANKS = 8
+
+
+class Peers(ctypes.Structure):
+    """struct mm3fa_peers: every rank's result buffer and arrival counters, mapped here."""
+    _fields_ = [("n_ranks", ctypes.c_int32), ("rank", ctypes.c_int32), ("dst", ctypes.c_void_p * MAX_RANKS),
+                ("flags", ctypes.c_void_p * MAX_RANKS)]
+
+
+class IpcHandle(ctypes.Structure):
+    """struct mm3fa_ipc_handle."""
+    _fields_ = [("handle", ctypes.c_ubyte * 64), ("offset", ctypes.c_uint64)]
 
 # size of the fixed scratch buffer behind flash_attn_ext_noalloc (MM3FA_NOALLOC_SCRATCH_BYTES)
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -96,6 +110,21 @@ def lib():
         L.mm3fa_dit_prologue.argtypes = [P, P, P, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, P, P, P,
                                          ctypes.c_void_p]
         L.mm3fa_dit_prologue.restype = ctypes.c_int
+        vp, i64 = ctypes.c_void_p, ctypes.c_int64
+        L.mm3fa_allgather_heads.argtypes = [vp, vp, vp, i64, i64, i64, i64, ctypes.c_int, vp, vp]
+        L.mm3fa_allgather_heads.restype = ctypes.c_int
+        L.mm3fa_flash_attn_ext_peers.argtypes = [P, P, P, P, vp, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                                 ctypes.c_int, P, vp, ctypes.c_size_t, ctypes.POINTER(Peers),
+                                                 ctypes.c_int, vp]
+        L.mm3fa_flash_attn_ext_peers.restype = ctypes.c_int
+        L.mm3fa_peer_wait.argtypes = [ctypes.POINTER(Peers), ctypes.c_int, vp, vp, vp]
+        L.mm3fa_peer_wait.restype = ctypes.c_int
+        L.mm3fa_ipc_export.argtypes = [vp, ctypes.POINTER(IpcHandle)]
+        L.mm3fa_ipc_export.restype = ctypes.c_int
+        L.mm3fa_ipc_open.argtypes = [ctypes.POINTER(IpcHandle), ctypes.POINTER(ctypes.c_void_p)]
+        L.mm3fa_ipc_open.restype = ctypes.c_int
+        L.mm3fa_ipc_close.argtypes = [vp]
+        L.mm3fa_ipc_close.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -258,3 +287,60 @@ def run(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None, dst: Tensor, scale
     ptr, cap = ws.get(nbytes)
     s = stream if stream is not None else torch.cuda.current_stream()
     flash_attn_ext(q, k, v, mask, scale, max_bias, logit_softcap, dst, ptr, cap, s.cuda_stream)
+
+
+# ---------------------------------------------------------------- multi-GPU head exchange
+
+def allgather_heads(slice_ptr: int, gathered_ptr: int, dst_ptr: int, dv: int, n_head: int, n_q: int, n_seq: int,
+                    seq_split: int, nccl_comm: int, stream: int = 0) -> None:
+    """mm3fa_allgather_heads: every rank's result slice gathered over NCCL into the whole
+    [Dv, n_head, n_q, n_seq] result (gathered_ptr: G-slice scratch, or 0 when not needed)."""
+    st = lib().mm3fa_allgather_heads(ctypes.c_void_p(slice_ptr), ctypes.c_void_p(gathered_ptr or None),
+                                     ctypes.c_void_p(dst_ptr), dv, n_head, n_q, n_seq, seq_split,
+                                     ctypes.c_void_p(nccl_comm or None), ctypes.c_void_p(stream or None))
+    if st != OK:
+        raise MM3FAError(st, "mm3fa_allgather_heads")
+
+
+def flash_attn_ext_peers(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None, scale: float, max_bias: float,
+                         logit_softcap: float, dst: Tensor, workspace: int, workspace_bytes: int, peers: Peers,
+                         slot: int, stream: int = 0, kv_len_ptr: int = 0, prec: int = GGML_PREC_F32) -> None:
+    """Attention on this rank's shard with the head exchange fused into the kernel: result rows
+    go to every rank's buffer (peers.dst) and counter `slot` of every other rank is bumped."""
+    st = lib().mm3fa_flash_attn_ext_peers(_ref(q), _ref(k), _ref(v), _ref(mask), ctypes.c_void_p(kv_len_ptr or None),
+                                          scale, max_bias, logit_softcap, prec, _ref(dst),
+                                          ctypes.c_void_p(workspace or None), workspace_bytes, ctypes.byref(peers),
+                                          slot, ctypes.c_void_p(stream or None))
+    if st != OK:
+        raise MM3FAError(st, "mm3fa_flash_attn_ext_peers")
+
+
+def peer_wait(peers: Peers, slot: int, targets_ptr: int, workspace: int, stream: int = 0) -> None:
+    """Device-side bounded wait until every other rank's slice of call `slot` has arrived."""
+    st = lib().mm3fa_peer_wait(ctypes.byref(peers), slot, ctypes.c_void_p(targets_ptr or None),
+                               ctypes.c_void_p(workspace or None), ctypes.c_void_p(stream or None))
+    if st != OK:
+        raise MM3FAError(st, "mm3fa_peer_wait")
+
+
+def ipc_export(ptr: int) -> bytes:
+    h = IpcHandle()
+    st = lib().mm3fa_ipc_export(ctypes.c_void_p(ptr or None), ctypes.byref(h))
+    if st != OK:
+        raise MM3FAError(st, "mm3fa_ipc_export")
+    return bytes(ctypes.string_at(ctypes.addressof(h), ctypes.sizeof(h)))
+
+
+def ipc_open(blob: bytes) -> int:
+    h = IpcHandle.from_buffer_copy(blob)
+    out = ctypes.c_void_p()
+    st = lib().mm3fa_ipc_open(ctypes.byref(h), ctypes.byref(out))
+    if st != OK:
+        raise MM3FAError(st, "mm3fa_ipc_open")
+    return int(out.value)
+
+
+def ipc_close(ptr: int) -> None:
+    st = lib().mm3fa_ipc_close(ctypes.c_void_p(ptr or None))
+    if st != OK:
+        raise MM3FAError(st, "mm3fa_ipc_close")

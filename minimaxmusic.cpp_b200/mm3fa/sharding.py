@@ -56,3 +56,29 @@ def assemble_heads_np(gathered: np.ndarray, world: int) -> np.ndarray:
     """
     g = np.asarray(gathered)
     return np.ascontiguousarray(g.transpose(1, 2, 0, 3, 4).reshape(g.shape[1], g.shape[2], -1, g.shape[4]))
+
+
+def unit_slice(n_seq: int, n_head: int, rank: int, world: int) -> tuple[int, int, int, int, int]:
+    """(batch x head) sharding of the DiT (and of any call by sequence and head): the ranks split
+    the sequences into seq_split = min(world, n_seq) groups and the heads into world / seq_split
+    groups.  Returns (s0, s1, h0, h1, seq_split): rank r = sg * (world / seq_split) + hg owns
+    sequences [s0, s1) and heads [h0, h1), in the rank order mm3fa_allgather_heads gathers."""
+    seq_split = min(world, n_seq)
+    if world % seq_split or n_seq % seq_split:
+        raise ValueError(f"{n_seq} sequences do not split over {world} ranks")
+    hs = world // seq_split
+    if n_head % hs:
+        raise ValueError(f"{n_head} heads do not split over {hs} head groups")
+    sg, hg = rank // hs, rank % hs
+    sl, hl = n_seq // seq_split, n_head // hs
+    return sg * sl, (sg + 1) * sl, hg * hl, (hg + 1) * hl, seq_split
+
+
+def allgather_scatter_np(gathered: np.ndarray, seq_split: int) -> np.ndarray:
+    """numpy statement of mm3fa_allgather_heads' permute: gathered (G, n_seq/ss, n_q, H/hs, Dv) in
+    rank order r = sg * hs + hg -> the ggml result (n_seq, n_q, H, Dv)."""
+    g = np.asarray(gathered)
+    G, sl, n_q, hl, dv = g.shape
+    hs = G // seq_split
+    x = g.reshape(seq_split, hs, sl, n_q, hl, dv).transpose(0, 2, 3, 1, 4, 5)
+    return np.ascontiguousarray(x.reshape(seq_split * sl, n_q, hs * hl, dv))

@@ -154,3 +154,54 @@ def test_prologue_entry_points_reject_before_touching_the_device():
     assert _status(mm3fa.flash_attn_ext_kvlen, q4, k4, v4, m4, 0, 0.1, 0.0, 0.0, d4, 0, 0) == mm3fa.ERR_NULL
     assert _status(mm3fa.flash_attn_ext_kvlen, q4, k4, v4, m4, 0x8000, 0.1, 0.0, 0.0,
                    ggml.make(F16, list(d4.ne), 0x1000), 0, 0) == mm3fa.ERR_TYPE
+
+
+def test_exchange_entry_points_reject_before_touching_the_device():
+    """mm3fa_allgather_heads / _flash_attn_ext_peers / _peer_wait / IPC helpers: argument checks
+    that need neither a GPU nor NCCL."""
+    L = mm3fa.lib()
+    vp = ctypes.c_void_p
+    # allgather: null pointers, bad split, null communicator
+    assert L.mm3fa_allgather_heads(None, None, vp(0x2000), 128, 32, 1, 2, 1, vp(0x9000), None) == mm3fa.ERR_NULL
+    assert L.mm3fa_allgather_heads(vp(0x1000), None, vp(0x2000), 128, 32, 1, 2, 1, None, None) == mm3fa.ERR_NULL
+    assert L.mm3fa_allgather_heads(vp(0x1000), None, vp(0x2000), 128, 32, 1, 3, 2, vp(0x9000), None) == \
+        mm3fa.ERR_SHAPE
+    assert L.mm3fa_allgather_heads(vp(0x1000), None, vp(0x2000), 128, 32, 1, 2, 0, vp(0x9000), None) == \
+        mm3fa.ERR_SHAPE
+    assert L.mm3fa_allgather_heads(vp(0x1002), None, vp(0x2000), 128, 32, 1, 2, 1, vp(0x9000), None) == \
+        mm3fa.ERR_ALIGN
+    # fused exchange: peers table checks
+    _, q4, k4, v4, m4, d4 = _decode_descs(n_seq=2, n_kv=128)
+    peers = mm3fa.Peers()
+    peers.n_ranks, peers.rank = 1, 0
+    st = lambda pr, **kw: _status(mm3fa.flash_attn_ext_peers, q4, k4, v4, m4, 0.1, kw.get("max_bias", 0.0), 0.0, d4,
+                                  0x8000, 4096, pr, kw.get("slot", 0))
+    assert st(peers) == mm3fa.ERR_SHAPE  # one rank
+    peers.n_ranks, peers.rank = 2, 2
+    assert st(peers) == mm3fa.ERR_SHAPE  # rank out of range
+    peers.rank = 1
+    assert st(peers) == mm3fa.ERR_NULL  # buffers missing
+    for r in range(2):
+        peers.dst[r] = 0x100000 * (r + 1)
+        peers.flags[r] = 0x900000 + 0x1000 * r
+    assert st(peers, slot=-1) == mm3fa.ERR_SHAPE
+    peers.dst[1] = 0x200008
+    assert st(peers) == mm3fa.ERR_ALIGN
+    peers.dst[1] = (d4.data + 0x100000) & ~15
+    assert st(peers) == mm3fa.ERR_SHAPE  # dst is not a view into this rank's own buffer
+    peers.dst[1] = d4.data & ~15
+    assert st(peers, max_bias=8.0) == mm3fa.ERR_UNSUPPORTED  # ALiBi needs the global head index
+    assert L.mm3fa_flash_attn_ext_peers(ctypes.byref(q4), ctypes.byref(k4), ctypes.byref(v4), ctypes.byref(m4), None,
+                                        0.1, 0.0, 0.0, 10, ctypes.byref(d4), vp(0x8000), 4096, None, 0, None) == \
+        mm3fa.ERR_NULL
+    # wait: table and targets
+    assert L.mm3fa_peer_wait(ctypes.byref(peers), 0, None, vp(0x8000), None) == mm3fa.ERR_NULL
+    bad = mm3fa.Peers()
+    bad.n_ranks, bad.rank = 9, 0
+    assert L.mm3fa_peer_wait(ctypes.byref(bad), 0, vp(0x7000), vp(0x8000), None) == mm3fa.ERR_SHAPE
+    # IPC helpers
+    h = mm3fa.IpcHandle()
+    assert L.mm3fa_ipc_export(None, ctypes.byref(h)) == mm3fa.ERR_NULL
+    assert L.mm3fa_ipc_open(None, ctypes.byref(ctypes.c_void_p())) == mm3fa.ERR_NULL
+    assert L.mm3fa_ipc_close(None) == mm3fa.ERR_NULL
+    assert ctypes.sizeof(mm3fa.Peers) == 8 + 8 * 8 * 2 and ctypes.sizeof(mm3fa.IpcHandle) == 72

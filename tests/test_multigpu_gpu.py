@@ -1,0 +1,176 @@
+"""The multi-GPU head exchange on 2 (or more) GPUs, one process per GPU over NCCL.
+
+Each rank computes its shard of a CFG decode call (kv heads [8r/G, 8(r+1)/G)) and of a DiT call
+((batch x head) units), and the slices are exchanged through the C ABI:
+  * mm3fa_allgather_heads (NCCL all-gather of torch's communicator + the permute);
+  * mm3fa_flash_attn_ext_peers + mm3fa_peer_wait (the decode kernel stores its rows into every
+    rank's buffer over NVLink, the consumer waits on the device), over several slots and a
+    reused slot.
+The exchanged result must equal, bit for bit, the slices computed one by one on rank 0's GPU
+with the plain entry point (the exchange is a copy), and match the oracle at the north-star
+bound.  Skipped on a box with fewer than 2 GPUs.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _descs(torch, ggml, c, dev, keep):
+    d = {}
+    for n in ("q", "k", "v", "mask"):
+        op = getattr(c, n)
+        if op is None:
+            d[n] = None
+            continue
+        t = torch.from_numpy(np.ascontiguousarray(op.storage)).to(dev)
+        keep.append(t)
+        d[n] = op.device_desc(t)
+    return d
+
+
+def _rank_main(rank, world, port, out_dir):
+    import datetime
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for p in (os.path.join(root, "minimaxmusic.cpp_b200"), os.path.join(root, "oracle")):
+        sys.path.insert(0, p)
+    import torch.distributed as dist
+
+    import mm3fa
+    from mm3fa import exchange, ggml, sharding, workloads
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    s = torch.cuda.current_stream(dev)
+    comm = exchange.nccl_comm(dist, dev)
+    keep = []
+    F32 = ggml.GGML_TYPE_F32
+
+    # ---------------- CFG decode, kv-head sharding (seq_split = 1)
+    c = workloads.decode_case(n_seq=4, n_kv=2048, max_seq=2304, seed=900)  # the same operands on every rank
+    d = _descs(torch, ggml, c, dev, keep)
+    H, D, n_seq = c.q.ne[2], c.q.ne[0], c.q.ne[3]
+    hl = H // world
+    qs, ks, vs, ms = sharding.shard_operands(d["q"], d["k"], d["v"], d["mask"], rank, world)
+    ws = mm3fa.Workspace(dev)
+    # NCCL form: the slice is computed in place at its rank's position of the gather buffer
+    gathered = torch.full((world, n_seq, 1, hl, D), float("nan"), device=dev)
+    full_nccl = torch.full((n_seq, 1, H, D), float("nan"), device=dev)
+    mm3fa.run(qs, ks, vs, ms, mm3fa.dst_desc(qs, vs, gathered[rank].data_ptr()), c.scale, ws=ws)
+    mm3fa.allgather_heads(gathered[rank].data_ptr(), gathered.data_ptr(), full_nccl.data_ptr(), D, H, 1, n_seq, 1, comm,
+                          s.cuda_stream)
+    # fused form: 3 slots, then slot 0 again (the wait's target moves on per use)
+    pb = exchange.PeerBuffers(torch, dist, dev, n_seq * H * D * 4, 3)
+    wsz = mm3fa.workspace_size(qs, ks, vs, ms, mm3fa.dst_desc(qs, vs, 0))
+    wsb = torch.zeros(max(wsz, 4096), dtype=torch.uint8, device=dev)
+    peer_out = []
+    for slot in (0, 1, 2, 0):
+        res = pb.result(slot, (n_seq, 1, H, D))
+        view = ggml.make(F32, [D, hl, 1, n_seq], res.data_ptr() + rank * hl * D * 4, [4, 4 * D, 4 * D * H, 4 * D * H])
+        mm3fa.flash_attn_ext_peers(qs, ks, vs, ms, c.scale, 0.0, 0.0, view, wsb.data_ptr(), wsb.numel(),
+                                   pb.peers[slot], slot, s.cuda_stream)
+        mm3fa.peer_wait(pb.peers[slot], slot, pb.targets.data_ptr(), wsb.data_ptr(), s.cuda_stream)
+        peer_out.append(res.clone())
+    torch.cuda.synchronize(dev)
+    st, raw = mm3fa.workspace_status(wsb.data_ptr(), s.cuda_stream)
+    out = {"decode_nccl": full_nccl.cpu().numpy(), "decode_peer": np.stack([p.cpu().numpy() for p in peer_out]),
+           "decode_status": np.array([st, raw])}
+    if rank == 0:
+        # every shard alone on this GPU with the plain entry point, assembled on the host
+        parts = []
+        for r in range(world):
+            q_, k_, v_, m_ = sharding.shard_operands(d["q"], d["k"], d["v"], d["mask"], r, world)
+            o = torch.full((n_seq, 1, hl, D), float("nan"), device=dev)
+            mm3fa.run(q_, k_, v_, m_, mm3fa.dst_desc(q_, v_, o.data_ptr()), c.scale, ws=ws)
+            parts.append(o.cpu().numpy())
+        out["decode_ref"] = sharding.assemble_heads_np(np.stack(parts), world)
+
+    # ---------------- DiT, (batch x head) sharding through mm3fa_allgather_heads
+    cd = workloads.dit_case(B=2, S=300, H=8, D=64, seed=901)
+    dd = _descs(torch, ggml, cd, dev, keep)
+    B, S, Hd, Dd = 2, 300, 8, 64
+
+    def shard(r):
+        s0, s1, h0, h1, ss = sharding.unit_slice(B, Hd, r, world)
+        q, k, v = dd["q"], dd["k"], dd["v"]
+        qv = ggml.make(q.type, [Dd, S, h1 - h0, s1 - s0], q.data + h0 * q.nb[2] + s0 * q.nb[3], list(q.nb))
+        kv = ggml.make(k.type, [Dd, S, h1 - h0, s1 - s0], k.data + h0 * k.nb[2] + s0 * k.nb[3], list(k.nb))
+        vv = ggml.make(v.type, [Dd, S, h1 - h0, s1 - s0], v.data + h0 * v.nb[2] + s0 * v.nb[3], list(v.nb))
+        return qv, kv, vv, (s1 - s0, h1 - h0, ss)
+
+    qv, kv, vv, (sl, hd, ss) = shard(rank)
+    g2 = torch.full((world, sl, S, hd, Dd), float("nan"), device=dev)
+    full_dit = torch.full((B, S, Hd, Dd), float("nan"), device=dev)
+    mm3fa.run(qv, kv, vv, None, mm3fa.dst_desc(qv, vv, g2[rank].data_ptr()), cd.scale, ws=ws)
+    mm3fa.allgather_heads(g2[rank].data_ptr(), g2.data_ptr(), full_dit.data_ptr(), Dd, Hd, S, B, ss, comm,
+                          s.cuda_stream)
+    torch.cuda.synchronize(dev)
+    out["dit_nccl"] = full_dit.cpu().numpy()
+    if rank == 0:
+        parts = []
+        for r in range(world):
+            q_, k_, v_, (sl_, hd_, ss_) = shard(r)
+            o = torch.full((sl_, S, hd_, Dd), float("nan"), device=dev)
+            mm3fa.run(q_, k_, v_, None, mm3fa.dst_desc(q_, v_, o.data_ptr()), cd.scale, ws=ws)
+            parts.append(o.cpu().numpy())
+        out["dit_ref"] = sharding.allgather_scatter_np(np.stack(parts), ss)
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **out)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    pb.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.fixture(scope="module")
+def exchange_results(tmp_path_factory):
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    import torch.multiprocessing as mp
+
+    out = str(tmp_path_factory.mktemp("exchange"))
+    mp.start_processes(_rank_main, args=(WORLD, _free_port(), out), nprocs=WORLD, join=True, start_method="spawn")
+    return [dict(np.load(os.path.join(out, f"rank{r}.npz"))) for r in range(WORLD)]
+
+
+def test_nccl_exchange_is_the_shards_bit_for_bit(exchange_results):
+    ref = exchange_results[0]["decode_ref"]
+    for r, res in enumerate(exchange_results):
+        assert np.array_equal(res["decode_nccl"], ref), f"rank {r}: decode all-gather differs"
+        assert np.array_equal(res["dit_nccl"], exchange_results[0]["dit_ref"]), f"rank {r}: DiT all-gather differs"
+
+
+def test_fused_peer_exchange_is_the_shards_bit_for_bit(exchange_results):
+    import mm3fa
+
+    ref = exchange_results[0]["decode_ref"]
+    for r, res in enumerate(exchange_results):
+        assert tuple(res["decode_status"]) == (mm3fa.OK, 0), f"rank {r}: a peer wait expired"
+        for k in range(res["decode_peer"].shape[0]):
+            assert np.array_equal(res["decode_peer"][k], ref), f"rank {r}: peer exchange call {k} differs"
+
+
+def test_exchanged_results_match_the_oracle(exchange_results):
+    from gpu_util import check_three_ways
+    from mm3fa import workloads
+
+    check_three_ways(exchange_results[0]["decode_nccl"], workloads.decode_case(n_seq=4, n_kv=2048, max_seq=2304,
+                                                                               seed=900))
+    check_three_ways(exchange_results[1]["dit_nccl"], workloads.dit_case(B=2, S=300, H=8, D=64, seed=901))

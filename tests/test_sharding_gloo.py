@@ -84,3 +84,27 @@ def test_assemble_heads_np_layout():
     full = sharding.assemble_heads_np(x, G)
     for r in range(G):
         np.testing.assert_array_equal(full[:, :, r * (H // G):(r + 1) * (H // G)], x[r])
+
+
+@pytest.mark.parametrize("world,n_seq,n_head", [(2, 2, 16), (4, 2, 16), (8, 2, 16), (4, 8, 32), (8, 4, 32)])
+def test_unit_slices_and_gather_permute_rebuild_the_result(world, n_seq, n_head):
+    """(batch x head) sharding: the ranks' slices, gathered in rank order and permuted as
+    mm3fa_allgather_heads does, are exactly the unsharded result."""
+    rng = np.random.default_rng(world * 100 + n_seq)
+    n_q, dv = 3, 4
+    full = rng.standard_normal((n_seq, n_q, n_head, dv)).astype(np.float32)
+    slices, ss = [], None
+    for r in range(world):
+        s0, s1, h0, h1, ss = sharding.unit_slice(n_seq, n_head, r, world)
+        slices.append(full[s0:s1, :, h0:h1])
+    got = sharding.allgather_scatter_np(np.stack(slices), ss)
+    assert np.array_equal(got, full)
+    if ss == 1:  # KV-head sharding is the special case seq_split = 1
+        assert np.array_equal(got, sharding.assemble_heads_np(np.stack(slices), world))
+
+
+def test_unit_slice_rejects_uneven_splits():
+    with pytest.raises(ValueError):
+        sharding.unit_slice(2, 15, 0, 4)
+    with pytest.raises(ValueError):
+        sharding.unit_slice(3, 16, 0, 2)
