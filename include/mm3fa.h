@@ -14,7 +14,9 @@
  * size of one row of ne[0]/32 blocks of 34 bytes.
  *
  *   q    [D,  n_q,  n_head,    n_seq ]   F32 (F16/BF16 accepted)
- *   k    [D,  n_kv, n_head_kv, n_seq_k]  F16, BF16 or Q8_0 (may be a strided view of a cache)
+ *   k    [D,  n_kv, n_head_kv, n_seq_k]  F16, BF16, Q8_0 or F32 (may be a strided view of a cache;
+ *                                         F32 K/V - the depth decoder's F32 attention - run on
+ *                                         the CUDA-core decode kernel)
  *   v    [Dv, n_kv, n_head_kv, n_seq_k]  same type family as k
  *   mask [n_kv, >=n_q, m2, m3] F16 or NULL; broadcast over heads (h % m2) and sequences (s % m3)
  *   dst  [Dv, n_head, n_q, n_seq] F32 -- heads BEFORE query rows, exactly as ggml's result
@@ -250,6 +252,32 @@ MM3FA_API int mm3fa_decode_step(const mm3fa_tensor * q_in, const mm3fa_tensor * 
                                 const mm3fa_tensor * v, const mm3fa_tensor * mask, float scale, float max_bias,
                                 float logit_softcap, int prec, mm3fa_tensor * dst, void * workspace,
                                 size_t workspace_bytes, void * stream);
+
+/* Flags of mm3fa_decode_prologue_ex / mm3fa_decode_step_ex. */
+enum mm3fa_prologue_flags {
+    /* v is clamped to [-65504, 65504] before its conversion to the cache type (NaN passes
+     * through): the ggml_clamp the reference inserts with --clamp-fp16 (src/qwen3-lm.h:779-782) */
+    MM3FA_PROLOGUE_CLAMP_FP16 = 1,
+};
+
+/*
+ * mm3fa_decode_prologue / mm3fa_decode_step with flags (enum mm3fa_prologue_flags; unknown bits
+ * return MM3FA_ERR_UNSUPPORTED).  The plain entry points are these with flags = 0.
+ * Replaces: as mm3fa_decode_prologue / mm3fa_decode_step, plus the ggml_clamp node of
+ *           src/qwen3-lm.h:779-782 when MM3FA_PROLOGUE_CLAMP_FP16 is set.
+ */
+MM3FA_API int mm3fa_decode_prologue_ex(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in,
+                                       const mm3fa_tensor * v_in, const float * q_norm, const float * k_norm,
+                                       float eps, const int32_t * pos, float rope_theta, const int64_t * rows,
+                                       mm3fa_tensor * k_cache, mm3fa_tensor * v_cache, mm3fa_tensor * q_out,
+                                       uint32_t flags, void * stream);
+MM3FA_API int mm3fa_decode_step_ex(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
+                                   const float * q_norm, const float * k_norm, float eps, const int32_t * pos,
+                                   float rope_theta, const int64_t * rows, mm3fa_tensor * k_cache,
+                                   mm3fa_tensor * v_cache, mm3fa_tensor * q_out, const mm3fa_tensor * k,
+                                   const mm3fa_tensor * v, const mm3fa_tensor * mask, float scale, float max_bias,
+                                   float logit_softcap, int prec, mm3fa_tensor * dst, void * workspace,
+                                   size_t workspace_bytes, uint32_t flags, void * stream);
 
 /*
  * DiT attention prologue: the nodes between the QKV projection and the attention call of a

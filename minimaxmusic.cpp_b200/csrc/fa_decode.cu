@@ -20,9 +20,10 @@
 // counts.  Layouts whose strides break the 16-byte rule of bulk copies take a cooperative
 // element-copy path instead (same math).
 //
-// Math (ggml convention, F32 accumulation): Q is rounded to K's vec-dot type first (F16,
-// BF16, or quantized to Q8_0 blocks when K is Q8_0, whose dot is then an exact int8 dot per
-// block times both fp16 scales).  Scores s = scale * q.k (then softcap), + slope_h * mask,
+// Math (F32 accumulation): Q is rounded to K's vec-dot type first (F16, BF16, or quantized to
+// Q8_0 blocks when K is Q8_0, whose dot is then an exact int8 dot per block times both fp16
+// scales; F32 K keeps Q as it is).  F32 K/V (the depth decoder's manual attention,
+// src/depth-decoder.h:210-219, is F32 throughout) use this kernel only.  Scores s = scale * q.k (then softcap), + slope_h * mask,
 // kept in log2 units; one-pass online softmax per stage; V accumulated in F32 (Q8_0 V is
 // dequantized exactly in registers as fp16(d) * int8).
 #include "fa_decode.cuh"
@@ -37,8 +38,28 @@ constexpr int DEC_RMAX    = 32;   // query rows per unit
 
 template <int D, int KVT>
 struct KvRow {
-    static constexpr int BYTES = KVT == KV_Q8_0 ? D / QK8_0 * Q8_0_BLOCK : 2 * D;
+    static constexpr int BYTES = KVT == KV_Q8_0 ? D / QK8_0 * Q8_0_BLOCK : (KVT == KV_F32 ? 4 * D : 2 * D);
 };
+
+// 8 consecutive K or V elements of an F16, BF16 or F32 row in shared memory (16-byte aligned
+// for 16-bit types, 32-byte for F32) as floats.
+template <int KVT>
+__device__ __forceinline__ void lds8(const char * p, float (&x)[8]) {
+    if constexpr (KVT == KV_F32) {
+        const float4 a = *reinterpret_cast<const float4 *>(p);
+        const float4 b = *reinterpret_cast<const float4 *>(p + 16);
+        x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+    } else {
+        const uint4    raw   = *reinterpret_cast<const uint4 *>(p);
+        const uint32_t rw[4] = { raw.x, raw.y, raw.z, raw.w };
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            const float2 f = KVT == KV_F16 ? h2_to_f2(rw[w]) : bf2_to_f2(rw[w]);
+            x[2 * w]       = f.x;
+            x[2 * w + 1]   = f.y;
+        }
+    }
+}
 
 template <int D, int KVT, int C, int NSTAGE>
 struct DecodeSmem {
@@ -409,15 +430,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) fa_decode_kernel(const DecodeP
                 }
 #pragma unroll
                 for (int c = 0; c < NCH; c++) {
-                    const uint4 raw = *reinterpret_cast<const uint4 *>(krow + 128 * c + 16 * ls);
-                    float       kf[8];
-                    const uint32_t rw[4] = { raw.x, raw.y, raw.z, raw.w };
-#pragma unroll
-                    for (int w = 0; w < 4; w++) {
-                        const float2 f = KVT == KV_F16 ? h2_to_f2(rw[w]) : bf2_to_f2(rw[w]);
-                        kf[2 * w]      = f.x;
-                        kf[2 * w + 1]  = f.y;
-                    }
+                    // elements [64c + 8ls, 64c + 8ls + 8) of the key row
+                    float kf[8];
+                    lds8<KVT>(krow + (KVT == KV_F32 ? 4 : 2) * (64 * c + 8 * ls), kf);
 #pragma unroll
                     for (int rr = 0; rr < 4; rr++) {
 #pragma unroll
@@ -530,14 +545,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) fa_decode_kernel(const DecodeP
                         vf[e]          = d * (float) b;
                     }
                 } else {
-                    const uint4    raw   = *reinterpret_cast<const uint4 *>(vrow + 16 * dg);
-                    const uint32_t rw[4] = { raw.x, raw.y, raw.z, raw.w };
-#pragma unroll
-                    for (int w = 0; w < 4; w++) {
-                        const float2 f = KVT == KV_F16 ? h2_to_f2(rw[w]) : bf2_to_f2(rw[w]);
-                        vf[2 * w]      = f.x;
-                        vf[2 * w + 1]  = f.y;
-                    }
+                    lds8<KVT>(vrow + (KVT == KV_F32 ? 32 : 16) * dg, vf);
                 }
 #pragma unroll
                 for (int rr = 0; rr < 4; rr++) {
@@ -584,9 +592,10 @@ struct DecodeConfig {
 
 template <int D, int KVT, bool BULK>
 static void * decode_kernel_ptr(int & smem, int & C) {
-    // D = 256 (the depth decoder's heads): 32-key stages, 2 deep, to stay within shared memory
+    // D = 256 (the depth decoder's heads): 32-key stages, 2 deep, to stay within shared memory;
+    // F32 K/V (rows twice as long) 2 deep as well
     constexpr int CC     = D == 256 ? 32 : ((D == 64 && KVT != KV_Q8_0) ? 128 : 64);
-    constexpr int NSTAGE = D == 256 ? 2 : 4;
+    constexpr int NSTAGE = (D == 256 || KVT == KV_F32) ? 2 : 4;
     smem                 = DecodeSmem<D, KVT, CC, NSTAGE>::TOTAL;
     C                    = CC;
     return reinterpret_cast<void *>(&fa_decode_kernel<D, KVT, CC, NSTAGE, BULK>);
@@ -606,6 +615,9 @@ static void * select_decode_kernel(int D, int kvt, bool bulk, int & smem, int & 
     MM3FA_SEL(256, KV_F16)
     MM3FA_SEL(256, KV_BF16)
     MM3FA_SEL(256, KV_Q8_0)
+    MM3FA_SEL(64, KV_F32)
+    MM3FA_SEL(128, KV_F32)
+    MM3FA_SEL(256, KV_F32)
 #undef MM3FA_SEL
     return nullptr;
 }

@@ -221,9 +221,14 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 // strides that a TMA tensor map can express.
 bool        decode_mma_eligible(int D, int kvt, int rows_per_pair);
 int         decode_mma_ctas_per_sm(int D, int kvt, int rows_per_pair);
-// Thread-block cluster size for the cluster mode (0 = use the stream-K split).
-int         decode_mma_cluster_size(int D, int kvt, int rows_per_pair, int64_t n_units, int n_sms);
+// Launch plan of the cluster mode: CTAs per thread-block cluster (0 = use the stream-K split) and
+// the K/V ring depth of the instance.
+struct MmaPlan {
+    int cluster;
+    int nstage;
+};
+MmaPlan     decode_mma_plan(int D, int kvt, int rows_per_pair, int64_t n_units, int n_sms);
 cudaError_t launch_decode_mma(DecodeParams p, const DecodeGeometry & g, int D, int kvt, int64_t n_head_kv,
-                              int64_t n_seq_k, int cluster, void * workspace, cudaStream_t stream);
+                              int64_t n_seq_k, MmaPlan plan, void * workspace, cudaStream_t stream);
 
 }  // namespace mm3fa

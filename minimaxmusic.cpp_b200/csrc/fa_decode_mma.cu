@@ -273,18 +273,19 @@ __device__ __forceinline__ void pdl_wait() {
 }
 
 // ---- head exchange over peer memory.  Called by all consumer threads of every CTA after its
-// result rows (local and peer copies) are stored: each thread fences its stores at system scope,
-// the CTA counts itself on the workspace's arrival word, and the grid's last CTA resets the word
-// and adds 1, with release semantics at system scope, to every peer's arrival counter.  A peer
-// that has seen the counter grow with acquire semantics (mm3fa_peer_wait) sees every row.
+// result rows (local and peer copies) are stored: the consumer barrier orders every thread's
+// stores before thread 0's system-scope fence (release is cumulative over that barrier), thread 0
+// counts the CTA on the workspace's arrival word, and the grid's last CTA resets the word, fences
+// again and adds 1, with release semantics at system scope, to every peer's arrival counter.  A
+// peer that has seen the counter grow with acquire semantics (mm3fa_peer_wait) sees every row.
 __device__ __forceinline__ void red_add_release_sys(uint32_t * a, uint32_t v) {
     asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ void peer_exchange_arrive(const DecodeParams & p, int tid) {
-    __threadfence_system();
     named_barrier_consumers();
     if (tid == 0) {
+        __threadfence_system();
         const uint32_t old = atomicAdd(&p.status[WS_PEER_ARRIVE], 1u);
         if (old + 1u == gridDim.x) {
             p.status[WS_PEER_ARRIVE] = 0u;  // the next call starts from zero
@@ -1366,28 +1367,30 @@ void * mma_kernel(int ns, int & smem) {
     if constexpr (Q8) {
         smem = MmaSmem<D, NT, Q8_NSTAGE, true>::TOTAL;
         return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, false, NT, CL, Q8_NSTAGE, true>);
+    } else {
+        if (ns == 2) {
+            smem = MmaSmem<D, NT, 2>::TOTAL;
+            return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT, CL, 2, false>);
+        }
+        smem = MmaSmem<D, NT, 3>::TOTAL;
+        return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT, CL, 3, false>);
     }
-    if (ns == 2) {
-        smem = MmaSmem<D, NT, 2>::TOTAL;
-        return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT, CL, 2, false>);
-    }
-    smem = MmaSmem<D, NT, 3>::TOTAL;
-    return reinterpret_cast<void *>(&fa_decode_mma_kernel<D, BF16, NT, CL, 3, false>);
 }
 
 // F16/BF16 ring depth: 3 stages of 64 keys per CTA (two CTAs per SM, up to 192 KiB of K/V in
 // flight per SM at D=128; measured 3% faster than 2 stages on the 36-layer decode graph) or 2
-// with MM3FA_DECODE_NSTAGE=2.
-int mma_nstage() {
+// with MM3FA_DECODE_NSTAGE=2.  A 4-stage ring at one CTA per SM (so that the headline's 16
+// clusters of 9 CTAs sit one per SM instead of 13-CTA clusters two per SM) measured 19.9 against
+// 14.6 us per layer: one CTA's 4 consumer warps do not keep an SM's share of HBM in flight.
+int mma_nstage_forced() {
     static const int ns = [] {
         const char * e = std::getenv("MM3FA_DECODE_NSTAGE");
-        return (e && std::atoi(e) == 2) ? 2 : 3;
+        return (e && std::atoi(e) == 2) ? 2 : 0;
     }();
     return ns;
 }
 
-void * select_mma_kernel(int D, int kvt, int nt, bool cluster, int & smem) {
-    const int  ns   = mma_nstage();
+void * select_mma_kernel(int D, int kvt, int nt, bool cluster, int & smem, int ns = 3) {
     const bool bf16 = kvt == KV_BF16, q8 = kvt == KV_Q8_0;
 #define MM3FA_SELM(DD, BB, QQ, NN)                                                                 \
     if (D == DD && bf16 == BB && q8 == QQ && nt == NN) {                                           \
@@ -1448,7 +1451,7 @@ bool decode_mma_eligible(int D, int kvt, int rows_per_pair) {
 
 int decode_mma_ctas_per_sm(int D, int kvt, int rows_per_pair) {
     int    smem = 0;
-    void * fn   = select_mma_kernel(D, kvt, rows_per_pair <= 8 ? 1 : 2, false, smem);
+    void * fn   = select_mma_kernel(D, kvt, rows_per_pair <= 8 ? 1 : 2, false, smem, mma_nstage_forced() == 2 ? 2 : 3);
     if (!fn) {
         return 0;
     }
@@ -1461,27 +1464,33 @@ int decode_mma_ctas_per_sm(int D, int kvt, int rows_per_pair) {
     return nb;
 }
 
-// Cluster size for `n_units` units on a device with n_sms SMs: the largest size <= 16 with
-// n_units * cs <= the cluster kernel's resident CTAs whose clusters all fit at once (0, the
-// stream-K split, only when no cluster fits).  The cluster instance's
-// own occupancy counts (it needs fewer registers than the stream-K one).  Cached per
-// (device, kernel, units).
-int decode_mma_cluster_size(int D, int kvt, int rows_per_pair, int64_t n_units, int n_sms) {
+// Launch plan of the cluster split for `n_units` units on a device with n_sms SMs: the largest
+// cluster size <= 16 (MM3FA_DECODE_CS caps it) with n_units * cs <= the cluster kernel's resident
+// CTAs whose clusters all fit at once (0, the stream-K split, only when no cluster fits).  The
+// cluster instance's own occupancy counts (it needs fewer registers than the stream-K one).
+// Cached per (device, kernel, units).
+MmaPlan decode_mma_plan(int D, int kvt, int rows_per_pair, int64_t n_units, int n_sms) {
     const int nt  = rows_per_pair <= 8 ? 1 : 2;
+    const int ns  = kvt == KV_Q8_0 ? Q8_NSTAGE : (mma_nstage_forced() == 2 ? 2 : 3);
     int       dev = 0;
     cudaGetDevice(&dev);
-    static std::mutex                                   mu;
-    static std::map<std::tuple<int, int, int, int, int, int64_t>, int> cache;
-    std::lock_guard<std::mutex>                         lock(mu);
+    static std::mutex                                                   mu;
+    static std::map<std::tuple<int, int, int, int, int, int64_t>, MmaPlan> cache;
+    std::lock_guard<std::mutex>                                         lock(mu);
     const auto key = std::make_tuple(dev, D, kvt, nt, n_sms, n_units);
     auto       it  = cache.find(key);
     if (it != cache.end()) {
         return it->second;
     }
+    static const int cs_cap = [] {
+        const char * e = std::getenv("MM3FA_DECODE_CS");
+        const int    v = e ? std::atoi(e) : 0;
+        return (v >= 1 && v <= MMA_MAX_CLUSTER) ? v : MMA_MAX_CLUSTER;
+    }();
     int    smem = 0;
-    void * fn   = select_mma_kernel(D, kvt, nt, true, smem);
+    void * fn   = select_mma_kernel(D, kvt, nt, true, smem, ns);
     if (!fn || n_units <= 0) {
-        return 0;
+        return MmaPlan{ 0, ns };
     }
     cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     int per_sm = 0;
@@ -1494,7 +1503,7 @@ int decode_mma_cluster_size(int D, int kvt, int rows_per_pair, int64_t n_units, 
     // measured 2.3-2.5x faster than the stream-K split over all SMs (36-layer graphs at 2-8
     // units: 10.4-11.6 against 26-27 us per layer), whose last-arriver merge of many partials
     // dominates; stream-K stays available through MM3FA_DECODE_SPLIT=streamk.
-    int cs = (int) std::min<int64_t>(MMA_MAX_CLUSTER, std::max<int64_t>(1, slots / n_units));
+    int cs = (int) std::min<int64_t>(cs_cap, std::max<int64_t>(1, slots / n_units));
     while (cs > 1) {
         const int n = max_active_clusters(fn, cs, smem);
         if ((int64_t) n >= std::min<int64_t>(n_units, (int64_t) slots / cs)) {
@@ -1502,16 +1511,19 @@ int decode_mma_cluster_size(int D, int kvt, int rows_per_pair, int64_t n_units, 
         }
         cs--;
     }
-    cache[key] = cs;
-    return cs;
+    const MmaPlan plan{ cs, ns };
+    cache[key] = plan;
+    return plan;
 }
 
 cudaError_t launch_decode_mma(DecodeParams p, const DecodeGeometry & g, int D, int kvt, int64_t n_head_kv,
-                              int64_t n_seq_k, int cluster, void * workspace, cudaStream_t stream) {
-    const bool bf16 = kvt == KV_BF16;
-    const int  nt   = p.rows_per_pair <= 8 ? 1 : 2;
-    int        smem = 0;
-    void *     fn   = select_mma_kernel(D, kvt, nt, cluster > 0, smem);
+                              int64_t n_seq_k, MmaPlan plan, void * workspace, cudaStream_t stream) {
+    const bool bf16    = kvt == KV_BF16;
+    const int  nt      = p.rows_per_pair <= 8 ? 1 : 2;
+    const int  cluster = plan.cluster;
+    int        smem    = 0;
+    const int  ns      = cluster > 0 ? plan.nstage : (mma_nstage_forced() == 2 ? 2 : 3);
+    void *     fn      = select_mma_kernel(D, kvt, nt, cluster > 0, smem, ns);
     if (!fn) {
         return cudaErrorInvalidValue;
     }

@@ -72,7 +72,13 @@ __global__ void __launch_bounds__(32 * PRO_WARPS) decode_prologue_kernel(const P
         x[e] = reinterpret_cast<const float *>(src)[lane * E + e];
     }
     const int64_t r_dst = p.rows[s];
-    if (kind == 2) {  // v: conversion only
+    if (kind == 2) {  // v: conversion only (clamped first with --clamp-fp16, src/qwen3-lm.h:779-782)
+        if (p.clamp_v) {
+#pragma unroll
+            for (int e = 0; e < E; e++) {
+                x[e] = x[e] > 65504.0f ? 65504.0f : (x[e] < -65504.0f ? -65504.0f : x[e]);
+            }
+        }
         if (r_dst >= 0 && r_dst < p.v_rows) {
             char * row = p.v_cache + r_dst * p.vc_nb1 + (int64_t) hh * p.vc_nb2 + (int64_t) s * p.vc_nb3;
             store_cache_row<E>(row, p.kvt, x, lane);

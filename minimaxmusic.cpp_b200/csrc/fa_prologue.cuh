@@ -132,6 +132,7 @@ struct PrologueParams {
     int             n_head, n_head_kv, n_set;
     int64_t         k_rows, v_rows;  // rows of each cache slice: a row index outside is not written
     float           eps, theta_scale;
+    int             clamp_v;  // v clamped to [-65504, 65504] before the cache conversion (NaN kept)
 };
 
 // D = 64, 128 or 256; one warp per q, k and v head vector of every set.

@@ -86,12 +86,13 @@ enum Variant { V_SIMT_BULK = 0, V_SIMT_COPY = 1, V_MMA_8 = 2, V_MMA_16 = 3 };
 
 int ctas_per_sm_cached(int D, int kvt, Variant var) {
     static std::mutex mu;
-    static int        cache[64][2][3][4];  // [dev][D==128][type idx][variant]
+    static int        cache[64][3][4][4];  // [dev][D 64/128/256][type idx][variant]
     int               dev = 0;
     cudaGetDevice(&dev);
-    const int ti = kvt == MM3FA_TYPE_F16 ? 0 : (kvt == MM3FA_TYPE_BF16 ? 1 : 2);
+    const int ti = kvt == MM3FA_TYPE_F16 ? 0 : (kvt == MM3FA_TYPE_BF16 ? 1 : (kvt == MM3FA_TYPE_Q8_0 ? 2 : 3));
+    const int di = D == 64 ? 0 : (D == 128 ? 1 : 2);
     std::lock_guard<std::mutex> lock(mu);
-    int & c = cache[dev & 63][D == 128][ti][var];
+    int & c = cache[dev & 63][di][ti][var];
     if (c == 0) {
         c = var >= V_MMA_8 ? decode_mma_ctas_per_sm(D, kvt, var == V_MMA_8 ? 8 : 16)
                            : decode_ctas_per_sm(D, kvt, var == V_SIMT_BULK);
@@ -172,7 +173,8 @@ int check_op(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor 
     if (q->type != MM3FA_TYPE_F32 && q->type != MM3FA_TYPE_F16 && q->type != MM3FA_TYPE_BF16) {
         return MM3FA_ERR_TYPE;
     }
-    if (k->type != MM3FA_TYPE_F16 && k->type != MM3FA_TYPE_BF16 && k->type != MM3FA_TYPE_Q8_0) {
+    if (k->type != MM3FA_TYPE_F16 && k->type != MM3FA_TYPE_BF16 && k->type != MM3FA_TYPE_Q8_0 &&
+        k->type != MM3FA_TYPE_F32) {
         return MM3FA_ERR_TYPE;
     }
     if (v->type != k->type || dst->type != MM3FA_TYPE_F32 || (mask && mask->type != MM3FA_TYPE_F16)) {
@@ -222,8 +224,10 @@ int check_op(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor 
         (int64_t) dst->nb[0] != 4 || (mask && mask->nb[0] != 2)) {
         return MM3FA_ERR_STRIDE;
     }
+    const uint64_t kva = k->type == MM3FA_TYPE_F32 ? 4 : 2;  // K/V element alignment
     for (int i = 1; i < 4; i++) {
-        if (q->nb[i] % (uint64_t) qe || k->nb[i] % 2 || v->nb[i] % 2 || dst->nb[i] % 4 || (mask && mask->nb[i] % 2)) {
+        if (q->nb[i] % (uint64_t) qe || k->nb[i] % kva || v->nb[i] % kva || dst->nb[i] % 4 ||
+            (mask && mask->nb[i] % 2)) {
             return MM3FA_ERR_STRIDE;
         }
     }
@@ -232,7 +236,7 @@ int check_op(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor 
         return MM3FA_ERR_STRIDE;
     }
     if (check_data) {
-        if (!aligned(q->data, (uintptr_t) qe) || !aligned(k->data, 2) || !aligned(v->data, 2) ||
+        if (!aligned(q->data, (uintptr_t) qe) || !aligned(k->data, kva) || !aligned(v->data, kva) ||
             !aligned(dst->data, 4) || (mask && !aligned(mask->data, 2))) {
             return MM3FA_ERR_ALIGN;
         }
@@ -606,9 +610,9 @@ int flash_attn_impl(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_
     p.kv_len     = kv_len;
     if (var >= V_MMA_8) {
         const int pref    = decode_mma_mode_preference();
-        const int cluster = pref == 1 ? 0
-                                      : decode_mma_cluster_size((int) s.D, s.kvt, p.rows_per_pair, g.n_units,
-                                                                device_info().sms);
+        MmaPlan   plan    = pref == 1 ? MmaPlan{ 0, 3 }
+                                      : decode_mma_plan((int) s.D, s.kvt, p.rows_per_pair, g.n_units, device_info().sms);
+        const int cluster = plan.cluster;
         if (peers) {
             // the exchange lives in the cluster merge's 16-byte result stores
             if (cluster == 0 || !p.dst_vec) {
@@ -626,7 +630,7 @@ int flash_attn_impl(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_
             p.n_peers = n;
         }
         return record_cuda(
-            launch_decode_mma(p, g, (int) s.D, s.kvt, s.n_head_kv, s.n_seq_k, cluster, workspace, cs));
+            launch_decode_mma(p, g, (int) s.D, s.kvt, s.n_head_kv, s.n_seq_k, plan, workspace, cs));
     }
     if (peers) {
         return MM3FA_ERR_UNSUPPORTED;
@@ -701,7 +705,10 @@ namespace {
 int prepare_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
                      const float * q_norm, const float * k_norm, float eps, const int32_t * pos, float rope_theta,
                      const int64_t * rows, mm3fa_tensor * k_cache, mm3fa_tensor * v_cache, mm3fa_tensor * q_out,
-                     PrologueParams & p, int64_t & D_out) {
+                     uint32_t flags, PrologueParams & p, int64_t & D_out) {
+    if (flags & ~(uint32_t) MM3FA_PROLOGUE_CLAMP_FP16) {
+        return MM3FA_ERR_UNSUPPORTED;
+    }
     if (!q_in || !k_in || !v_in || !k_cache || !v_cache || !q_out || !q_norm || !k_norm || !pos || !rows) {
         return MM3FA_ERR_NULL;
     }
@@ -788,6 +795,7 @@ int prepare_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const
     p.v_rows      = v_cache->ne[1];
     p.eps         = eps;
     p.theta_scale = std::pow(rope_theta, -2.0f / (float) D);
+    p.clamp_v     = (flags & MM3FA_PROLOGUE_CLAMP_FP16) ? 1 : 0;
     D_out         = D;
     return MM3FA_OK;
 }
@@ -796,30 +804,38 @@ int prepare_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const
 
 extern "C" {
 
-int mm3fa_decode_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
-                          const float * q_norm, const float * k_norm, float eps, const int32_t * pos, float rope_theta,
-                          const int64_t * rows, mm3fa_tensor * k_cache, mm3fa_tensor * v_cache, mm3fa_tensor * q_out,
-                          void * stream) {
+int mm3fa_decode_prologue_ex(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
+                             const float * q_norm, const float * k_norm, float eps, const int32_t * pos,
+                             float rope_theta, const int64_t * rows, mm3fa_tensor * k_cache, mm3fa_tensor * v_cache,
+                             mm3fa_tensor * q_out, uint32_t flags, void * stream) {
     PrologueParams p{};
     int64_t        D  = 0;
     const int      st = prepare_prologue(q_in, k_in, v_in, q_norm, k_norm, eps, pos, rope_theta, rows, k_cache, v_cache,
-                                         q_out, p, D);
+                                         q_out, flags, p, D);
     if (st != MM3FA_OK) {
         return st;
     }
     return record_cuda(launch_decode_prologue(p, (int) D, static_cast<cudaStream_t>(stream)));
 }
 
-int mm3fa_decode_step(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
-                      const float * q_norm, const float * k_norm, float eps, const int32_t * pos, float rope_theta,
-                      const int64_t * rows, mm3fa_tensor * k_cache, mm3fa_tensor * v_cache, mm3fa_tensor * q_out,
-                      const mm3fa_tensor * k, const mm3fa_tensor * v, const mm3fa_tensor * mask, float scale,
-                      float max_bias, float logit_softcap, int prec, mm3fa_tensor * dst, void * workspace,
-                      size_t workspace_bytes, void * stream) {
+int mm3fa_decode_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
+                          const float * q_norm, const float * k_norm, float eps, const int32_t * pos, float rope_theta,
+                          const int64_t * rows, mm3fa_tensor * k_cache, mm3fa_tensor * v_cache, mm3fa_tensor * q_out,
+                          void * stream) {
+    return mm3fa_decode_prologue_ex(q_in, k_in, v_in, q_norm, k_norm, eps, pos, rope_theta, rows, k_cache, v_cache,
+                                    q_out, 0u, stream);
+}
+
+int mm3fa_decode_step_ex(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
+                         const float * q_norm, const float * k_norm, float eps, const int32_t * pos, float rope_theta,
+                         const int64_t * rows, mm3fa_tensor * k_cache, mm3fa_tensor * v_cache, mm3fa_tensor * q_out,
+                         const mm3fa_tensor * k, const mm3fa_tensor * v, const mm3fa_tensor * mask, float scale,
+                         float max_bias, float logit_softcap, int prec, mm3fa_tensor * dst, void * workspace,
+                         size_t workspace_bytes, uint32_t flags, void * stream) {
     PrologueParams pp{};
     int64_t        D  = 0;
     int            st = prepare_prologue(q_in, k_in, v_in, q_norm, k_norm, eps, pos, rope_theta, rows, k_cache, v_cache,
-                                         q_out, pp, D);
+                                         q_out, flags, pp, D);
     if (st != MM3FA_OK) {
         return st;
     }
@@ -850,6 +866,17 @@ int mm3fa_decode_step(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, cons
     }
     return flash_attn_impl(&qa, k, v, mask, nullptr, scale, max_bias, logit_softcap, prec, dst, workspace,
                            workspace_bytes, stream);
+}
+
+int mm3fa_decode_step(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,
+                      const float * q_norm, const float * k_norm, float eps, const int32_t * pos, float rope_theta,
+                      const int64_t * rows, mm3fa_tensor * k_cache, mm3fa_tensor * v_cache, mm3fa_tensor * q_out,
+                      const mm3fa_tensor * k, const mm3fa_tensor * v, const mm3fa_tensor * mask, float scale,
+                      float max_bias, float logit_softcap, int prec, mm3fa_tensor * dst, void * workspace,
+                      size_t workspace_bytes, void * stream) {
+    return mm3fa_decode_step_ex(q_in, k_in, v_in, q_norm, k_norm, eps, pos, rope_theta, rows, k_cache, v_cache, q_out,
+                                k, v, mask, scale, max_bias, logit_softcap, prec, dst, workspace, workspace_bytes, 0u,
+                                stream);
 }
 
 int mm3fa_dit_prologue(const mm3fa_tensor * q_in, const mm3fa_tensor * k_in, const mm3fa_tensor * v_in,

@@ -16,6 +16,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <type_traits>
 #include <cstring>
 #include <mutex>
 
@@ -66,19 +67,28 @@ bool aligned(const void * p, uintptr_t a) {
 }
 
 // gathered[r][s_l][i][h_l][d] (rank r = sequence group sg * HS + head group hg) -> the ggml result
-// dst[s][i][h][d] with s = sg * SL + s_l, h = hg * HL + h_l.
-__global__ void scatter_gathered_kernel(const float * __restrict__ gathered, float * __restrict__ dst, int64_t dv,
-                                        int64_t n_head, int64_t n_q, int64_t n_seq, int seq_split, int head_split) {
-    const int64_t hl = n_head / head_split, sl = n_seq / seq_split;
-    const int64_t total = dv * n_head * n_q * n_seq;
-    for (int64_t o = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; o < total;
-         o += (int64_t) gridDim.x * blockDim.x) {
-        const int64_t d = o % dv;
-        const int64_t h = (o / dv) % n_head;
-        const int64_t i = (o / (dv * n_head)) % n_q;
-        const int64_t s = o / (dv * n_head * n_q);
-        const int64_t r = (s / sl) * head_split + h / hl;
-        dst[o]          = gathered[(((r * sl + s % sl) * n_q + i) * hl + h % hl) * dv + d];
+// dst[s][i][h][d] with s = sg * SL + s_l, h = hg * HL + h_l.  One block row per (sequence, query
+// row) of dst (grid y, strided past 65535), threads over its n_head * dv values as float4 (VEC) or
+// floats, so the index arithmetic is a few 32-bit divisions per thread.
+template <bool VEC>
+__global__ void scatter_gathered_kernel(const float * __restrict__ gathered, float * __restrict__ dst, int dv, int n_head,
+                                        int n_q, int64_t n_rows, int sl, int head_split) {
+    using T         = typename std::conditional<VEC, float4, float>::type;
+    constexpr int W = VEC ? 4 : 1;
+    const int     dw = dv / W;               // vectors per head row
+    const int     hl = n_head / head_split;
+    const int     per_row = n_head * dw;
+    const T *     src = reinterpret_cast<const T *>(gathered);
+    T *           out = reinterpret_cast<T *>(dst);
+    for (int64_t row = blockIdx.y; row < n_rows; row += gridDim.y) {
+        const int64_t s = row / n_q;
+        const int     i = (int) (row % n_q);
+        const int64_t sg = s / sl, s_l = s % sl;
+        for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < per_row; c += gridDim.x * blockDim.x) {
+            const int     h = c / dw, d = c % dw;
+            const int64_t r = sg * head_split + h / hl;
+            out[row * per_row + c] = src[(((r * sl + s_l) * n_q + i) * hl + h % hl) * dw + d];
+        }
     }
 }
 
@@ -198,10 +208,21 @@ int mm3fa_allgather_heads(const float * slice, float * gathered, float * dst, in
     if (direct) {
         return MM3FA_OK;
     }
-    const int64_t total  = dv * n_head * n_q * n_seq;
-    const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 8);
-    scatter_gathered_kernel<<<(unsigned) blocks, 256, 0, cs>>>(gathered, dst, dv, n_head, n_q, n_seq, seq_split,
-                                                                head_split);
+    if (dv * n_head > (int64_t) 1 << 30 || n_q > (int64_t) 1 << 30) {
+        return MM3FA_ERR_UNSUPPORTED;
+    }
+    const bool    vec     = dv % 4 == 0 && aligned(gathered, 16) && aligned(dst, 16);
+    const int64_t per_row = dv * n_head / (vec ? 4 : 1);
+    const dim3    grid((unsigned) std::min<int64_t>((per_row + 255) / 256, 64),
+                       (unsigned) std::min<int64_t>(n_q * n_seq, 65535));
+    const int     sl = (int) (n_seq / seq_split);
+    if (vec) {
+        scatter_gathered_kernel<true><<<grid, 256, 0, cs>>>(gathered, dst, (int) dv, (int) n_head, (int) n_q,
+                                                             n_q * n_seq, sl, head_split);
+    } else {
+        scatter_gathered_kernel<false><<<grid, 256, 0, cs>>>(gathered, dst, (int) dv, (int) n_head, (int) n_q,
+                                                              n_q * n_seq, sl, head_split);
+    }
     return cuda_status(cudaGetLastError());
 }
 

@@ -98,11 +98,16 @@ def lib():
                                             ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p, P, P, P,
                                             ctypes.c_void_p]
         L.mm3fa_decode_prologue.restype = ctypes.c_int
+        L.mm3fa_decode_prologue_ex.argtypes = L.mm3fa_decode_prologue.argtypes[:-1] + [ctypes.c_uint32,
+                                                                                        ctypes.c_void_p]
+        L.mm3fa_decode_prologue_ex.restype = ctypes.c_int
         L.mm3fa_decode_step.argtypes = [P, P, P, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p,
                                         ctypes.c_float, ctypes.c_void_p, P, P, P, P, P, P, ctypes.c_float,
                                         ctypes.c_float, ctypes.c_float, ctypes.c_int, P, ctypes.c_void_p,
                                         ctypes.c_size_t, ctypes.c_void_p]
         L.mm3fa_decode_step.restype = ctypes.c_int
+        L.mm3fa_decode_step_ex.argtypes = L.mm3fa_decode_step.argtypes[:-1] + [ctypes.c_uint32, ctypes.c_void_p]
+        L.mm3fa_decode_step_ex.restype = ctypes.c_int
         L.mm3fa_flash_attn_ext_kvlen.argtypes = [P, P, P, P, ctypes.c_void_p, ctypes.c_float, ctypes.c_float,
                                                  ctypes.c_float, ctypes.c_int, P, ctypes.c_void_p, ctypes.c_size_t,
                                                  ctypes.c_void_p]
@@ -213,15 +218,19 @@ def dit_prologue(q_in: Tensor, k_in: Tensor, v_in: Tensor, pos_ptr: int, rot_dim
         raise MM3FAError(st, "mm3fa_dit_prologue")
 
 
+PROLOGUE_CLAMP_FP16 = 1  # MM3FA_PROLOGUE_CLAMP_FP16: clamp v to +-65504 before the cache conversion
+
+
 def decode_prologue(q_in: Tensor, k_in: Tensor, v_in: Tensor, q_norm_ptr: int, k_norm_ptr: int, eps: float,
                     pos_ptr: int, rope_theta: float, rows_ptr: int, k_cache: Tensor, v_cache: Tensor, q_out: Tensor,
-                    stream: int = 0) -> None:
+                    stream: int = 0, flags: int = 0) -> None:
     """Fused decode prologue (RMSNorm + NeoX RoPE of q and k, append of the new k/v rows into the caches);
-    pointers are device addresses (q_norm/k_norm F32 [D], pos int32 [N], rows int64 [N])."""
-    st = lib().mm3fa_decode_prologue(_ref(q_in), _ref(k_in), _ref(v_in), ctypes.c_void_p(q_norm_ptr),
-                                     ctypes.c_void_p(k_norm_ptr), eps, ctypes.c_void_p(pos_ptr), rope_theta,
-                                     ctypes.c_void_p(rows_ptr), _ref(k_cache), _ref(v_cache), _ref(q_out),
-                                     ctypes.c_void_p(stream or None))
+    pointers are device addresses (q_norm/k_norm F32 [D], pos int32 [N], rows int64 [N]).
+    flags: PROLOGUE_CLAMP_FP16 adds the reference's --clamp-fp16 clamp of v."""
+    st = lib().mm3fa_decode_prologue_ex(_ref(q_in), _ref(k_in), _ref(v_in), ctypes.c_void_p(q_norm_ptr),
+                                        ctypes.c_void_p(k_norm_ptr), eps, ctypes.c_void_p(pos_ptr), rope_theta,
+                                        ctypes.c_void_p(rows_ptr), _ref(k_cache), _ref(v_cache), _ref(q_out), flags,
+                                        ctypes.c_void_p(stream or None))
     if st != OK:
         raise MM3FAError(st, "mm3fa_decode_prologue")
 
@@ -230,15 +239,15 @@ def decode_step(q_in: Tensor, k_in: Tensor, v_in: Tensor, q_norm_ptr: int, k_nor
                 pos_ptr: int, rope_theta: float, rows_ptr: int, k_cache: Tensor, v_cache: Tensor, q_out: Tensor,
                 k: Tensor, v: Tensor, mask: Tensor | None, scale: float, max_bias: float, logit_softcap: float,
                 dst: Tensor, workspace: int, workspace_bytes: int, stream: int = 0,
-                prec: int = GGML_PREC_F32) -> None:
+                prec: int = GGML_PREC_F32, flags: int = 0) -> None:
     """decode_prologue followed by flash_attn_ext on q_out viewed as [D, 1, n_head, N], as one call
-    (fused into the tensor-core decode kernel when k/v are the caches themselves)."""
-    st = lib().mm3fa_decode_step(_ref(q_in), _ref(k_in), _ref(v_in), ctypes.c_void_p(q_norm_ptr),
-                                 ctypes.c_void_p(k_norm_ptr), eps, ctypes.c_void_p(pos_ptr), rope_theta,
-                                 ctypes.c_void_p(rows_ptr), _ref(k_cache), _ref(v_cache), _ref(q_out), _ref(k),
-                                 _ref(v), _ref(mask), scale, max_bias, logit_softcap,
-                                 prec, _ref(dst), ctypes.c_void_p(workspace or None), workspace_bytes,
-                                 ctypes.c_void_p(stream or None))
+    (two kernels on the stream, the attention's CTAs starting as the prologue's exit)."""
+    st = lib().mm3fa_decode_step_ex(_ref(q_in), _ref(k_in), _ref(v_in), ctypes.c_void_p(q_norm_ptr),
+                                    ctypes.c_void_p(k_norm_ptr), eps, ctypes.c_void_p(pos_ptr), rope_theta,
+                                    ctypes.c_void_p(rows_ptr), _ref(k_cache), _ref(v_cache), _ref(q_out), _ref(k),
+                                    _ref(v), _ref(mask), scale, max_bias, logit_softcap,
+                                    prec, _ref(dst), ctypes.c_void_p(workspace or None), workspace_bytes, flags,
+                                    ctypes.c_void_p(stream or None))
     if st != OK:
         raise MM3FAError(st, "mm3fa_decode_step")
 

@@ -136,13 +136,24 @@ def rope_neox(x: np.ndarray, pos: np.ndarray, theta: float, n_dims: int | None =
     return out
 
 
+def clamp_fp16(x: np.ndarray) -> np.ndarray:
+    """ggml_clamp(v, -65504, 65504) as the reference inserts it with --clamp-fp16
+    (src/qwen3-lm.h:779-782): values beyond the F16 range saturate, NaN passes through."""
+    x = np.asarray(x, dtype=np.float32)
+    return np.where(x > np.float32(65504), np.float32(65504),
+                    np.where(x < np.float32(-65504), np.float32(-65504), x)).astype(np.float32)
+
+
 def decode_prologue(q_in: np.ndarray, k_in: np.ndarray, v_in: np.ndarray, q_norm: np.ndarray, k_norm: np.ndarray,
-                    eps: float, pos: np.ndarray, theta: float) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+                    eps: float, pos: np.ndarray, theta: float,
+                    clamp_v: bool = False) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
     """(q_out, k_new, v_new) in F32: q_in [N, H, D], k_in/v_in [N, Hkv, D]; the caller converts
-    k_new / v_new to the cache type (f32_to_f16_bits, q8_0_quantize) as set_rows does."""
+    k_new / v_new to the cache type (f32_to_f16_bits, q8_0_quantize) as set_rows does.  clamp_v:
+    the --clamp-fp16 clamp of v before that conversion."""
     q = rope_neox(rms_norm_mul(q_in, q_norm, eps), pos, theta)
     k = rope_neox(rms_norm_mul(k_in, k_norm, eps), pos, theta)
-    return q, k, np.asarray(v_in, dtype=np.float32)
+    v = np.asarray(v_in, dtype=np.float32)
+    return q, k, (clamp_fp16(v) if clamp_v else v)
 
 
 def alibi_slope(h: int, n_head: int, max_bias: float) -> float:

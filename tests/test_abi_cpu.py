@@ -77,7 +77,7 @@ def test_supports_rejections():
     _, q, k, v, m, d = _decode_descs(n_seq=2, n_kv=128)
     assert mm3fa.supports(None, k, v, m, d) == mm3fa.ERR_NULL
     bad = ggml.make(ggml.GGML_TYPE_F32, list(k.ne), k.data, [4, 512, 512 * 128, 512 * 128 * 8])
-    assert mm3fa.supports(q, bad, v, m, d) == mm3fa.ERR_TYPE  # F32 K
+    assert mm3fa.supports(q, bad, v, m, d) == mm3fa.ERR_TYPE  # F32 K with F16 V
     assert mm3fa.supports(q, k, v, m, ggml.make(ggml.GGML_TYPE_F16, list(d.ne), 0x1000)) == mm3fa.ERR_TYPE
     wrong_dst = ggml.make(ggml.GGML_TYPE_F32, [128, 1, 32, 2], 0x1000)  # rows before heads
     assert mm3fa.supports(q, k, v, m, wrong_dst) == mm3fa.ERR_SHAPE

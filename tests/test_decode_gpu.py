@@ -425,3 +425,39 @@ def test_config2_36_layer_graph_n8_kv8192(cuda_device):
                            1.0 / np.sqrt(D))
         check_three_ways(eager[l], c)
     del graph
+
+
+# ---------------------------------------------------------------- F32 K/V (the depth decoder's attention)
+
+def depth_decoder_f32_case(S: int, B: int, seed: int):
+    """The depth decoder's attention exactly as src/depth-decoder.h:205-219 forms it: q, k and v are the
+    F32 [D, Nh, S, B] projections viewed as [D, S, Nh, B] (ggml_permute 0,2,1,3: token stride D*Nh*4,
+    head stride D*4), D = 256, 16 heads, causal; as a flash_attn_ext call with a causal F16 mask."""
+    D, H = 256, 16
+    rng = np.random.default_rng(seed)
+    ops = []
+    for sc in (1.0, 0.5, 0.5):
+        x = (rng.standard_normal((B, S, H, D)) * sc).astype(np.float32)  # [D, Nh, S, B] storage
+        ops.append(workloads.Operand(x, ggml.GGML_TYPE_F32, [D, S, H, B], [4, 4 * D * H, 4 * D, 4 * D * H * S]))
+    m = np.triu(np.full((S, S), -np.inf, dtype=np.float32), k=1).astype(np.float16)
+    mop = workloads.Operand(m, F16, [S, S, 1, 1], ggml.contiguous_nb(F16, [S, S, 1, 1]))
+    return workloads.Case("depth-f32", ops[0], ops[1], ops[2], mop, 1.0 / np.sqrt(D))
+
+
+@pytest.mark.parametrize("S,B", [(1, 2), (5, 4), (8, 2), (8, 16)])
+def test_depth_decoder_f32_kv(cuda_device, S, B):
+    """F32 K/V in the reference's permuted views (element-copy path): no numerics change against the
+    F32 manual attention the reference runs."""
+    check(depth_decoder_f32_case(S, B, seed=700 + S * B), cuda_device)
+
+
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_f32_kv_contiguous_long(kernel, cuda_device, D):
+    """F32 caches with packed rows (bulk copies), several stages and the stream-K split, GQA 4."""
+    c = workloads.decode_case(n_seq=2, n_kv=700, D=D, n_head=8, n_head_kv=2, seed=710 + D)
+    for name in ("k", "v"):
+        op = getattr(c, name)
+        st = op.storage.astype(np.float32)
+        setattr(c, name, workloads.Operand(st, ggml.GGML_TYPE_F32, op.ne,
+                                           [4, 4 * D, 4 * D * st.shape[2], 4 * D * st.shape[2] * st.shape[1]]))
+    check(c, cuda_device)

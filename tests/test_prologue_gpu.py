@@ -50,12 +50,13 @@ def cache_to_f32(b: np.ndarray, kvt: int) -> np.ndarray:
     return oracle.q8_0_dequantize(b)
 
 
-def run_case(dev, kvt, D, N=2, H=8, Hkv=2, max_seq=300, pos=(123, 8191), rows=(123, 250), seed=0):
+def run_case(dev, kvt, D, N=2, H=8, Hkv=2, max_seq=300, pos=(123, 8191), rows=(123, 250), seed=0, v_in=None,
+             flags=0):
     rng = np.random.default_rng(seed)
     eps, theta = 1e-6, 1e6
     q_in = (rng.standard_normal((N, H, D)) * 3).astype(np.float32)
     k_in = (rng.standard_normal((N, Hkv, D)) * 2).astype(np.float32)
-    v_in = rng.standard_normal((N, Hkv, D)).astype(np.float32)
+    v_in = rng.standard_normal((N, Hkv, D)).astype(np.float32) if v_in is None else v_in
     q_norm = (1 + 0.2 * rng.standard_normal(D)).astype(np.float32)
     k_norm = (1 + 0.2 * rng.standard_normal(D)).astype(np.float32)
     pos = np.array(pos, dtype=np.int32)
@@ -76,10 +77,11 @@ def run_case(dev, kvt, D, N=2, H=8, Hkv=2, max_seq=300, pos=(123, 8191), rows=(1
     kcd, vcd = mk(kvt, [D, max_seq, Hkv, N], dkc, cnb), mk(kvt, [D, max_seq, Hkv, N], dvc, list(cnb))
     qod = mk(F32, [D, H, N, 1], dqo)
     mm3fa.decode_prologue(qd, kd, vd, dqn.data_ptr(), dkn.data_ptr(), eps, dpos.data_ptr(), theta, drows.data_ptr(),
-                          kcd, vcd, qod, torch.cuda.current_stream(dev).cuda_stream)
+                          kcd, vcd, qod, torch.cuda.current_stream(dev).cuda_stream, flags=flags)
     torch.cuda.synchronize(dev)
 
-    q_ref, k_ref, v_ref = oracle.decode_prologue(q_in, k_in, v_in, q_norm, k_norm, eps, pos, theta)
+    q_ref, k_ref, v_ref = oracle.decode_prologue(q_in, k_in, v_in, q_norm, k_norm, eps, pos, theta,
+                                                 clamp_v=bool(flags & mm3fa.PROLOGUE_CLAMP_FP16))
     kc_ref, vc_ref = kc0.copy(), vc0.copy()
     for s in range(N):
         if 0 <= rows[s] < max_seq:
@@ -247,3 +249,35 @@ def test_dit_prologue_full_rotation_d128(cuda_device):
     k_ref = oracle.rope_neox(x[1].reshape(B * S, H, D), np.tile(pos, B), 1e4).reshape(B, S, H, D)
     check_rows_close(dko.cpu().view(torch.int16).numpy().view(np.uint16),
                      to_cache_bytes(k_ref.transpose(0, 2, 1, 3), F16), F16, "k_out")
+
+
+@pytest.mark.parametrize("kvt", [F16, BF16, Q8])
+def test_prologue_clamp_fp16(cuda_device, kvt):
+    """--clamp-fp16 (src/qwen3-lm.h:779-782): v values beyond the F16 range saturate at +-65504 before
+    the cache conversion (NaN passes through); without the flag they round to +-inf in an F16 cache.
+    The v rows must equal the oracle's clamp-then-convert bit for bit."""
+    N, Hkv, D = 2, 2, 128
+    rng = np.random.default_rng(60 + kvt)
+    v = rng.standard_normal((N, Hkv, D)).astype(np.float32)
+    v[0, 0, :4] = [1e5, -7e4, 65519.0, -3e38]
+    v[1, 1, 5] = np.nan if kvt != Q8 else 2e5  # a NaN would poison its whole Q8_0 block scale
+    for flags in (mm3fa.PROLOGUE_CLAMP_FP16, 0):
+        r = run_case(cuda_device, kvt, D, N=N, Hkv=Hkv, v_in=v.copy(), flags=flags, seed=61)
+        got, ref = r["vc"], r["vc_ref"]
+        for s_ in range(N):
+            row = r["rows"][s_]
+            g, w = got[s_, :, row], ref[s_, :, row]
+            if kvt == Q8:
+                assert np.array_equal(g, w), f"flags={flags} set {s_}: v rows differ"
+            else:
+                # bit-identical values; a NaN may carry a different payload on each side
+                gf, wf = cache_to_f32(g, kvt), cache_to_f32(w, kvt)
+                both_nan = np.isnan(gf) & np.isnan(wf)
+                assert np.array_equal(g[~both_nan], w[~both_nan]), f"flags={flags} set {s_}: v rows differ"
+                assert np.array_equal(np.isnan(gf), np.isnan(wf))
+        if kvt == F16:
+            vals = oracle.f16_bits_to_f32(got[0, 0, r["rows"][0], :4])
+            if flags:
+                assert list(vals) == [65504.0, -65504.0, 65504.0, -65504.0]
+            else:
+                assert np.isinf(vals[0]) and np.isinf(vals[1])
