@@ -582,8 +582,9 @@ class DecodeStack:
     result before layer l+1 starts (src/qwen3-lm.h:732, 823-827).
 
     world == 1: plain attention into [L, B, 1, 32, D].  world > 1, exchange "p2p": the attention
-    kernel stores its rows into every rank's buffer (mm3fa_flash_attn_ext_peers) and the next layer
-    waits on the device (mm3fa_peer_wait); "nccl": mm3fa_allgather_heads after every layer."""
+    kernel also stores its values into every other rank's receive buffer as {value, epoch} words
+    (mm3fa_flash_attn_ext_peers) and the next layer starts after this rank's wait-and-unpack
+    kernel (mm3fa_peer_wait); "nccl": mm3fa_allgather_heads after every layer."""
 
     def __init__(self, torch, dist, mm3fa, ggml, dev, gen, B: int, kv: int, n_layers: int, world: int, rank: int,
                  mode: str = "p2p", max_seq: int | None = None):
@@ -611,10 +612,10 @@ class DecodeStack:
             self.full = torch.empty(n_layers, B, 1, N_HEAD, D, device=dev)
             dst_ptr = [self.full[l].data_ptr() for l in range(n_layers)]
         elif mode == "p2p":
-            self.pb = xch.PeerBuffers(torch, dist, dev, layer_out, n_layers)
-            assert self.pb.slot_bytes == layer_out
-            self.full = self.pb.result(0, (n_layers, B, 1, N_HEAD, D))  # slots are contiguous
-            dst_ptr = [self.pb.result_ptr(l) + rank * hq * D * 4 for l in range(n_layers)]
+            self.pb = xch.PeerBuffers(torch, dist, dev, B * hq * D, n_layers)
+            self.full = torch.empty(n_layers, B, 1, N_HEAD, D, device=dev)
+            dst_ptr = [self.full[l].data_ptr() + rank * hq * D * 4 for l in range(n_layers)]
+            self.results = [ggml.make(F32, [D, N_HEAD, 1, B], self.full[l].data_ptr()) for l in range(n_layers)]
         else:
             self.comm = xch.nccl_comm(dist, dev)
             self.gathered = torch.empty(n_layers, world, B, 1, hq, D, device=dev)
@@ -641,9 +642,10 @@ class DecodeStack:
         mm3fa, (qd, kd, vd, md, dd) = self.mm3fa, self.descs[l]
         ws = (self.ws.data_ptr(), self.ws.numel())
         if self.world > 1 and exchange and self.mode == "p2p":
-            mm3fa.flash_attn_ext_peers(qd, kd, vd, md, self.scale, 0.0, 0.0, dd, *ws, self.pb.peers[l], l,
+            ep = self.pb.epochs.data_ptr()
+            mm3fa.flash_attn_ext_peers(qd, kd, vd, md, self.scale, 0.0, 0.0, dd, *ws, self.pb.peers, l, ep,
                                        s.cuda_stream)
-            mm3fa.peer_wait(self.pb.peers[l], l, self.pb.targets.data_ptr(), ws[0], s.cuda_stream)
+            mm3fa.peer_wait(self.pb.peers, l, ep, self.results[l], ws[0], s.cuda_stream)
             return 2
         mm3fa.flash_attn_ext(qd, kd, vd, md, self.scale, 0.0, 0.0, dd, *ws, s.cuda_stream)
         if self.world > 1 and exchange:
@@ -820,8 +822,9 @@ def main() -> None:
                                   "nccl": round(us["nccl"], 3)},
                  "exchange_us_per_layer": {"p2p": round(us["p2p"] - avg_launch_us, 3),
                                            "nccl": round(us["nccl"] - avg_launch_us, 3)},
-                 "p2p": "mm3fa_flash_attn_ext_peers (rows stored into every rank's buffer over NVLink from the "
-                        "decode kernel's merge) + mm3fa_peer_wait (device-side bounded wait) per layer",
+                 "p2p": "mm3fa_flash_attn_ext_peers (values stored as {value, epoch} words into every rank's "
+                        "receive buffer over NVLink from the decode kernel's merge, no fences) + mm3fa_peer_wait "
+                        "(device-side bounded wait and unpack) per layer",
                  "nccl": "mm3fa_flash_attn_ext + mm3fa_allgather_heads (ncclAllGather + permute) per layer"}
 
     # ---- end to end through the C ABI: Q/mask from pinned host memory, outputs back to host

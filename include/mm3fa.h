@@ -347,46 +347,51 @@ MM3FA_API int mm3fa_assemble_heads(const float * gathered, float * dst, int64_t 
 MM3FA_API int mm3fa_allgather_heads(const float * slice, float * gathered, float * dst, int64_t dv, int64_t n_head,
                                     int64_t n_q, int64_t n_seq, int seq_split, void * nccl_comm, void * stream);
 
-/* Every rank's exchange buffers as mapped into this process (see mm3fa_ipc_open). */
+/* Every rank's receive buffer as mapped into this process (see mm3fa_ipc_open).  Slot s of a
+ * receive buffer (recv_slot_bytes from s * recv_slot_bytes on) holds two halves, selected by the
+ * parity of the call's epoch, of n_ranks source regions of 8 * V bytes each, V = the values of one
+ * rank's result slice; a value is the 8-byte word {float bits, epoch}.  Zero-fill the buffers
+ * once, before the first call. */
 typedef struct mm3fa_peers {
-    int32_t    n_ranks;                  /* G, 2 .. MM3FA_MAX_RANKS */
-    int32_t    rank;                     /* this process's rank */
-    void *     dst[MM3FA_MAX_RANKS];     /* rank i's whole result buffer (16-byte aligned); dst[rank] is ours */
-    uint32_t * flags[MM3FA_MAX_RANKS];   /* rank i's arrival counters (one u32 per slot, zeroed once) */
+    int32_t  n_ranks;                 /* G, 2 .. MM3FA_MAX_RANKS */
+    int32_t  rank;                    /* this process's rank */
+    void *   recv[MM3FA_MAX_RANKS];   /* rank i's receive buffer (16-byte aligned); recv[rank] is ours */
+    uint64_t recv_slot_bytes;         /* >= 2 * n_ranks * 8 * V, a multiple of 16 */
 } mm3fa_peers;
 
 /*
- * mm3fa_flash_attn_ext on this rank's shard, with the head exchange fused into the kernel: dst
- * is this rank's slice as a view of its own result buffer peers->dst[rank] (e.g. heads
- * [r*H/G, (r+1)*H/G) of [Dv, H, n_q, n_seq]); every result row is stored at the same offset in
- * every rank's buffer as well (plain stores over NVLink while other CTAs still compute), and when
- * the whole grid is done, counter `slot` of every other rank is incremented (release, system
- * scope).  kv_len may be NULL (as mm3fa_flash_attn_ext) or a device array (as _kvlen).  Only the
- * tensor-core decode kernel's cluster split carries the exchange (<= 16 query rows per (sequence,
- * kv head), F16/BF16/Q8_0 caches it can stream, 16-byte aligned rows): other shapes return
- * MM3FA_ERR_UNSUPPORTED and enqueue nothing, as does max_bias != 0 (ALiBi slopes follow the
- * global head index, which a shard's descriptors do not carry; the reference passes 0).  Peer
- * memory is only ever written, by plain stores and one atomic per rank; nothing loads from it.
+ * mm3fa_flash_attn_ext on this rank's shard, with the head exchange fused into the kernel: dst is
+ * this rank's slice of the result (e.g. heads [r*H/G, (r+1)*H/G) of [Dv, H, n_q, n_seq], as a view
+ * of this rank's whole result buffer), and every result value is also stored, while other CTAs
+ * still compute, into each other rank's receive buffer (slot `slot`, this rank's source region)
+ * as {value, epoch} with epoch = epochs[slot] + 1 - plain volatile stores over NVLink, no fences,
+ * no flags.  epochs: device u32 per slot, zeroed once, private to this rank, advanced only by
+ * mm3fa_peer_wait.  kv_len may be NULL (as mm3fa_flash_attn_ext) or a device array (as _kvlen).
+ * Only the tensor-core decode kernel's cluster split carries the exchange (<= 16 query rows per
+ * (sequence, kv head), F16/BF16/Q8_0 caches it can stream, 16-byte aligned contiguous rows):
+ * other shapes return MM3FA_ERR_UNSUPPORTED and enqueue nothing, as does max_bias != 0 (ALiBi
+ * slopes follow the global head index, which a shard's descriptors do not carry; the reference
+ * passes 0).  Peer memory is only ever written; nothing loads from it.
  * Replaces: the attention node of src/qwen3-lm.h:816-820 plus its exchange (see above).
  */
 MM3FA_API int mm3fa_flash_attn_ext_peers(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
                                          const mm3fa_tensor * mask, const int32_t * kv_len, float scale,
                                          float max_bias, float logit_softcap, int prec, mm3fa_tensor * dst,
                                          void * workspace, size_t workspace_bytes, const mm3fa_peers * peers,
-                                         int slot, void * stream);
+                                         int slot, const uint32_t * epochs, void * stream);
 
 /*
- * Device-side wait of the consumer of a fused exchange: enqueues on `stream` one thread that
- * waits (acquire, system scope) until this rank's counter `slot` has grown by n_ranks - 1 since
- * the previous wait on that slot, i.e. until every other rank's slice of the latest
- * mm3fa_flash_attn_ext_peers call on the slot is in this rank's buffer; kernels enqueued after
- * it read the whole result.  targets: device u32 per slot, zeroed once with the counters, private
- * to this rank.  The wait is bounded (MM3FA_WAIT_TIMEOUT_MS, 2 s by default); on expiry it sets
+ * The consumer's side of the fused exchange, enqueued on `stream` after this rank's
+ * mm3fa_flash_attn_ext_peers call on `slot`: waits on the device until every other rank's values
+ * of that call (epoch epochs[slot] + 1) are in this rank's receive buffer, writes them into
+ * `result` - this rank's whole result [Dv, n_head, n_q, n_seq] F32, rank i's slice being heads
+ * [i*n_head/G, (i+1)*n_head/G) - and advances epochs[slot].  Kernels enqueued after it read the
+ * whole result.  Each wait is bounded (MM3FA_WAIT_TIMEOUT_MS, 2 s by default); on expiry it sets
  * the workspace status word (mm3fa_workspace_status reports MM3FA_ERR_TIMEOUT) and returns.
  * Replaces: nothing in the reference (see above).
  */
-MM3FA_API int mm3fa_peer_wait(const mm3fa_peers * peers, int slot, uint32_t * targets, void * workspace,
-                              void * stream);
+MM3FA_API int mm3fa_peer_wait(const mm3fa_peers * peers, int slot, uint32_t * epochs, mm3fa_tensor * result,
+                              void * workspace, void * stream);
 
 /* CUDA IPC handle of a device buffer: the allocation's handle plus the buffer's offset in it. */
 typedef struct mm3fa_ipc_handle {

@@ -21,7 +21,7 @@ constexpr uint32_t ST_TIMEOUT = 1u;  // status bit: a bounded wait expired
 
 // Workspace layout shared by host and device (byte offsets from the workspace base).
 constexpr size_t WS_STATUS_BYTES = 256;  // [0]: status bits, [1]: where the wait gave up
-constexpr int    WS_PEER_ARRIVE  = 8;    // status[8]: CTAs of a peer-exchange call done (reset by the last)
+constexpr int    WS_PEER_ARRIVE  = 8;    // status[8]: CTAs of a peer-exchange wait done (reset by the last)
 constexpr int    MAX_PEERS       = 7;    // other ranks a head exchange over peer memory can write to
 
 // ------------------------------------------------------------------ PTX wrappers
@@ -157,12 +157,15 @@ struct DecodeParams {
     int          dst_vec;        // dst rows start 16-byte aligned: 16-byte stores
     int          mask_tma;       // mask rows staged by TMA with K/V (cluster mode)
     const int *  kv_len;         // device [n_seq]: q sequence s sees keys [0, kv_len[s]) (null: all)
-    // head exchange over peer memory (cluster mode only): every result row is also stored at
-    // dst + peer_delta[i] (rank i's buffer, mapped into this process) for i < n_peers, and the
-    // grid's last CTA then adds 1 to each peer_flag[i] with release semantics at system scope
-    int          n_peers;
-    int64_t      peer_delta[MAX_PEERS];
-    uint32_t *   peer_flag[MAX_PEERS];
+    // head exchange over peer memory (cluster mode only): every result value, at linear index e
+    // of this rank's result view [Dv, n_head, n_q, n_seq], is also stored into each peer's
+    // receive buffer as the 8-byte word {value, epoch} at peer_ll[i] + (epoch & 1) * ll_parity
+    // + 8 * e (16-byte volatile stores, no fence), epoch = *epoch_ptr + 1 (the calls on this slot
+    // so far, advanced by the receiver's wait kernel)
+    int             n_peers;
+    char *          peer_ll[MAX_PEERS];
+    int64_t         ll_parity;
+    const uint32_t *epoch_ptr;
     // workspace
     uint32_t *   status;
     uint32_t *   counters;

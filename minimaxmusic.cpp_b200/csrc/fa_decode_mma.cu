@@ -272,32 +272,17 @@ __device__ __forceinline__ void pdl_wait() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
-// ---- head exchange over peer memory.  Called by all consumer threads of every CTA after its
-// result rows (local and peer copies) are stored: the consumer barrier orders every thread's
-// stores before thread 0's system-scope fence (release is cumulative over that barrier), thread 0
-// counts the CTA on the workspace's arrival word, and the grid's last CTA resets the word, fences
-// again and adds 1, with release semantics at system scope, to every peer's arrival counter.  A
-// peer that has seen the counter grow with acquire semantics (mm3fa_peer_wait) sees every row.
-__device__ __forceinline__ void red_add_release_sys(uint32_t * a, uint32_t v) {
-    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ void peer_exchange_arrive(const DecodeParams & p, int tid) {
-    named_barrier_consumers();
-    if (tid == 0) {
-        __threadfence_system();
-        const uint32_t old = atomicAdd(&p.status[WS_PEER_ARRIVE], 1u);
-        if (old + 1u == gridDim.x) {
-            p.status[WS_PEER_ARRIVE] = 0u;  // the next call starts from zero
-            __threadfence_system();
-#pragma unroll
-            for (int i = 0; i < MAX_PEERS; i++) {
-                if (i < p.n_peers) {
-                    red_add_release_sys(p.peer_flag[i], 1u);
-                }
-            }
-        }
-    }
+// ---- head exchange over peer memory: 4 result values at linear index e (a multiple of 4) of this
+// rank's result view go to each peer's receive buffer as 8-byte words {value, epoch}, two 16-byte
+// volatile stores (each 8-byte half is single-copy atomic, so a word whose epoch matches carries
+// its value: no fence and no flag are needed; the receiver polls the words themselves).
+__device__ __forceinline__ void st_ll4(char * dst, float4 v, uint32_t epoch) {
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(__float_as_uint(v.x)),
+                 "r"(epoch), "r"(__float_as_uint(v.y)), "r"(epoch)
+                 : "memory");
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(dst + 16), "r"(__float_as_uint(v.z)),
+                 "r"(epoch), "r"(__float_as_uint(v.w)), "r"(epoch)
+                 : "memory");
 }
 
 // byte offset of (key row j, 16-byte chunk c) inside one 128-byte-swizzled TMA box
@@ -760,12 +745,17 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                 if (p.dst_vec) {
                     const float4 r4                  = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
                     *reinterpret_cast<float4 *>(out) = r4;
-                    // head exchange over peer memory: the same row into every peer's result
-                    // buffer (plain 16-byte stores over NVLink; the host guarantees dst_vec)
+                    if (p.n_peers > 0) {
+                        // head exchange over peer memory: the 4 values into every peer's receive
+                        // buffer as {value, epoch} words (the host guarantees dst_vec)
+                        const uint32_t epoch = *p.epoch_ptr + 1u;
+                        const int64_t  e = d + (int64_t) D * (h + (int64_t) p.n_head * (i + (int64_t) p.n_q * u_sq));
+                        const int64_t  off = (int64_t) (epoch & 1u) * p.ll_parity + 8 * e;
 #pragma unroll
-                    for (int pp = 0; pp < MAX_PEERS; pp++) {
-                        if (pp < p.n_peers) {
-                            *reinterpret_cast<float4 *>(reinterpret_cast<char *>(out) + p.peer_delta[pp]) = r4;
+                        for (int pp = 0; pp < MAX_PEERS; pp++) {
+                            if (pp < p.n_peers) {
+                                st_ll4(p.peer_ll[pp] + off, r4, epoch);
+                            }
                         }
                     }
                 } else {
@@ -774,9 +764,6 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                     out[2] = O.z * inv;
                     out[3] = O.w * inv;
                 }
-            }
-            if (p.n_peers > 0) {
-                peer_exchange_arrive(p, tid);
             }
             return;
         } else {

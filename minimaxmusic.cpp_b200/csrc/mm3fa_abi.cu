@@ -535,7 +535,7 @@ namespace {
 int flash_attn_impl(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v, const mm3fa_tensor * mask,
                     const int32_t * kv_len, float scale, float max_bias, float logit_softcap, int prec,
                     mm3fa_tensor * dst, void * workspace, size_t workspace_bytes, void * stream,
-                    const mm3fa_peers * peers = nullptr, int slot = 0) {
+                    const mm3fa_peers * peers = nullptr, int slot = 0, const uint32_t * epochs = nullptr) {
     if (prec != MM3FA_PREC_DEFAULT && prec != MM3FA_PREC_F32) {
         return MM3FA_ERR_UNSUPPORTED;
     }
@@ -618,16 +618,22 @@ int flash_attn_impl(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_
             if (cluster == 0 || !p.dst_vec) {
                 return MM3FA_ERR_UNSUPPORTED;
             }
+            const int64_t vals   = s.DV * s.n_head * s.n_q * s.n_seq;  // this rank's slice
+            const int64_t region = 8 * vals;
+            if ((uint64_t) (2 * peers->n_ranks * region) > peers->recv_slot_bytes) {
+                return MM3FA_ERR_WORKSPACE;
+            }
             int n = 0;
             for (int r = 0; r < peers->n_ranks; r++) {
                 if (r != peers->rank) {
-                    p.peer_delta[n] = static_cast<const char *>(peers->dst[r]) -
-                                      static_cast<const char *>(peers->dst[peers->rank]);
-                    p.peer_flag[n]  = peers->flags[r] + slot;
+                    p.peer_ll[n] = static_cast<char *>(peers->recv[r]) + (uint64_t) slot * peers->recv_slot_bytes +
+                                   (uint64_t) peers->rank * region;
                     n++;
                 }
             }
-            p.n_peers = n;
+            p.n_peers   = n;
+            p.ll_parity = (int64_t) peers->n_ranks * region;
+            p.epoch_ptr = epochs + slot;
         }
         return record_cuda(
             launch_decode_mma(p, g, (int) s.D, s.kvt, s.n_head_kv, s.n_seq_k, plan, workspace, cs));
@@ -652,28 +658,32 @@ int mm3fa_flash_attn_ext(const mm3fa_tensor * q, const mm3fa_tensor * k, const m
 int mm3fa_flash_attn_ext_peers(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
                                const mm3fa_tensor * mask, const int32_t * kv_len, float scale, float max_bias,
                                float logit_softcap, int prec, mm3fa_tensor * dst, void * workspace,
-                               size_t workspace_bytes, const mm3fa_peers * peers, int slot, void * stream) {
-    if (!peers) {
+                               size_t workspace_bytes, const mm3fa_peers * peers, int slot, const uint32_t * epochs,
+                               void * stream) {
+    if (!peers || !epochs) {
         return MM3FA_ERR_NULL;
     }
     if (peers->n_ranks < 2 || peers->n_ranks > MM3FA_MAX_RANKS || peers->rank < 0 || peers->rank >= peers->n_ranks ||
-        slot < 0) {
+        slot < 0 || peers->recv_slot_bytes % 16 != 0) {
         return MM3FA_ERR_SHAPE;
     }
     for (int r = 0; r < peers->n_ranks; r++) {
-        if (!peers->dst[r] || !peers->flags[r]) {
+        if (!peers->recv[r]) {
             return MM3FA_ERR_NULL;
         }
-        if (!aligned(peers->dst[r], 16) || !aligned(peers->flags[r], 4)) {
+        if (!aligned(peers->recv[r], 16)) {
             return MM3FA_ERR_ALIGN;
         }
+    }
+    if (!aligned(epochs, 4)) {
+        return MM3FA_ERR_ALIGN;
     }
     if (!dst || !dst->data) {
         return MM3FA_ERR_NULL;
     }
-    // dst must be a view into this rank's own result buffer, 16-byte aligned like the others
-    if (static_cast<const char *>(dst->data) < static_cast<const char *>(peers->dst[peers->rank])) {
-        return MM3FA_ERR_SHAPE;
+    // the receivers index values by their position in a contiguous [Dv, n_head, n_q, n_seq] slice
+    if (dst->nb[0] != 4 || dst->nb[1] % 16 != 0) {
+        return MM3FA_ERR_STRIDE;
     }
     if (!workspace) {
         return MM3FA_ERR_WORKSPACE;
@@ -683,7 +693,7 @@ int mm3fa_flash_attn_ext_peers(const mm3fa_tensor * q, const mm3fa_tensor * k, c
         return MM3FA_ERR_UNSUPPORTED;
     }
     return flash_attn_impl(q, k, v, mask, kv_len, scale, max_bias, logit_softcap, prec, dst, workspace,
-                           workspace_bytes, stream, peers, slot);
+                           workspace_bytes, stream, peers, slot, epochs);
 }
 
 int mm3fa_flash_attn_ext_kvlen(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,

@@ -92,35 +92,84 @@ __global__ void scatter_gathered_kernel(const float * __restrict__ gathered, flo
     }
 }
 
-// ---------------------------------------------------------------- fused exchange: the consumer's wait
+// ---------------------------------------------------------------- fused exchange: the consumer's side
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t * a) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+__device__ __forceinline__ uint4 ld_volatile_v4(const char * a) {
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(a)
+                 : "memory");
     return v;
 }
 
-// One thread: waits until *flag has passed *target + expect (wrap-safe), then moves *target
-// there.  Launched with programmatic stream serialisation: griddepcontrol.wait first, so that this
-// kernel completes only after the kernel before it (whose results the next kernel also reads).
-__global__ void peer_wait_kernel(const uint32_t * flag, uint32_t * target, uint32_t expect, uint32_t * status,
-                                 uint64_t timeout_ns) {
+// Unpacks every other rank's slice of the latest call on a slot from this rank's receive buffer
+// into the whole result.  Item t = (source s', value pair j): the 16-byte line {v0, epoch, v1,
+// epoch} of values 2j, 2j+1 of source rank r (r != self), polled until both epochs match (bounded),
+// then written to result at (d, r*hl + h_l, i, seq).  The last CTA to finish advances the slot's
+// epoch.  Launched with programmatic stream serialisation: griddepcontrol.wait first, so the
+// attention call before it (which read the epoch) has completed.
+struct UnpackParams {
+    const char * recv;     // this rank's receive buffer, slot base
+    char *       result;   // this rank's whole result [Dv, H, n_q, n_seq]
+    int64_t      nb1, nb2, nb3;
+    int64_t      parity;   // bytes of one parity half of the slot
+    int64_t      region;   // bytes of one source region
+    int64_t      vals;     // values of one slice (Dv * hl * n_q * n_seq)
+    int          dv, hl, n_q, n_ranks, rank;
+    uint32_t *   epoch;    // &epochs[slot]
+    uint32_t *   status;   // workspace status word; status[WS_PEER_ARRIVE] counts finished CTAs
+    uint64_t     timeout_ns;
+};
+
+__global__ void __launch_bounds__(256) peer_unpack_kernel(const UnpackParams p) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (threadIdx.x != 0) {
-        return;
-    }
-    const uint32_t t        = *target + expect;
-    const uint64_t deadline = mm3fa::global_timer_ns() + timeout_ns;
-    uint32_t       spins    = 0;
-    while ((int32_t) (ld_acquire_sys(flag) - t) < 0) {
-        if ((++spins & 63u) == 0 && mm3fa::global_timer_ns() > deadline) {
-            atomicOr(&status[0], mm3fa::ST_TIMEOUT);
-            atomicExch(&status[1], 0xfffffff0u);  // where: the peer-exchange wait
+    const uint32_t e      = *p.epoch + 1u;
+    const int64_t  pairs  = p.vals / 2;
+    const int64_t  items  = pairs * (p.n_ranks - 1);
+    const char *   base   = p.recv + (int64_t) (e & 1u) * p.parity;
+    const uint64_t dl     = mm3fa::global_timer_ns() + p.timeout_ns;
+    bool           failed = false;
+    for (int64_t t = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; t < items && !failed;
+         t += (int64_t) gridDim.x * blockDim.x) {
+        const int     sp = (int) (t / pairs);
+        const int     r  = sp < p.rank ? sp : sp + 1;  // source rank (this rank skipped)
+        const int64_t j  = t % pairs;
+        const char *  line = base + r * p.region + 16 * j;
+        uint4         w    = ld_volatile_v4(line);
+        uint32_t      spins = 0;
+        while (w.y != e || w.w != e) {
+            if ((++spins & 63u) == 0 && mm3fa::global_timer_ns() > dl) {
+                atomicOr(&p.status[0], mm3fa::ST_TIMEOUT);
+                atomicExch(&p.status[1], 0xfffffff0u);  // where: the peer-exchange wait
+                failed = true;
+                break;
+            }
+            __nanosleep(32);
+            w = ld_volatile_v4(line);
+        }
+        if (failed) {
             break;
         }
-        __nanosleep(64);
+        const int64_t v0  = 2 * j;  // d, h_l, i, seq of the pair's first value (dv is even)
+        const int     d   = (int) (v0 % p.dv);
+        const int64_t rest = v0 / p.dv;
+        const int     h_l = (int) (rest % p.hl);
+        const int64_t rest2 = rest / p.hl;
+        const int     i   = (int) (rest2 % p.n_q);
+        const int64_t sq  = rest2 / p.n_q;
+        float * dst = reinterpret_cast<float *>(p.result + (int64_t) (r * p.hl + h_l) * p.nb1 + (int64_t) i * p.nb2 +
+                                                sq * p.nb3) + d;
+        *reinterpret_cast<float2 *>(dst) = make_float2(__uint_as_float(w.x), __uint_as_float(w.z));
     }
-    *target = t;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t old = atomicAdd(&p.status[mm3fa::WS_PEER_ARRIVE], 1u);
+        if (old + 1u == gridDim.x) {
+            p.status[mm3fa::WS_PEER_ARRIVE] = 0u;
+            *p.epoch                        = e;
+        }
+    }
 }
 
 int cuda_status(cudaError_t e) {
@@ -226,26 +275,59 @@ int mm3fa_allgather_heads(const float * slice, float * gathered, float * dst, in
     return cuda_status(cudaGetLastError());
 }
 
-int mm3fa_peer_wait(const mm3fa_peers * peers, int slot, uint32_t * targets, void * workspace, void * stream) {
-    if (!peers || !targets || !workspace) {
+int mm3fa_peer_wait(const mm3fa_peers * peers, int slot, uint32_t * epochs, mm3fa_tensor * result, void * workspace,
+                    void * stream) {
+    if (!peers || !epochs || !workspace || !result || !result->data) {
         return MM3FA_ERR_NULL;
     }
     if (peers->n_ranks < 2 || peers->n_ranks > MM3FA_MAX_RANKS || peers->rank < 0 || peers->rank >= peers->n_ranks ||
-        slot < 0 || !peers->flags[peers->rank]) {
+        slot < 0 || !peers->recv[peers->rank]) {
         return MM3FA_ERR_SHAPE;
     }
+    if (result->type != MM3FA_TYPE_F32) {
+        return MM3FA_ERR_TYPE;
+    }
+    const int64_t dv = result->ne[0], H = result->ne[1], n_q = result->ne[2], n_seq = result->ne[3];
+    if (dv <= 0 || dv % 2 || H <= 0 || H % peers->n_ranks || n_q <= 0 || n_seq <= 0 || dv > 4096 || H > 65535 ||
+        n_q > 65535 || n_seq > 65535) {
+        return MM3FA_ERR_SHAPE;
+    }
+    if (result->nb[0] != 4 || result->nb[1] % 8 || result->nb[2] % 8 || result->nb[3] % 8 ||
+        !aligned(result->data, 8)) {
+        return MM3FA_ERR_STRIDE;
+    }
+    UnpackParams p{};
+    p.hl      = (int) (H / peers->n_ranks);
+    p.vals    = dv * p.hl * n_q * n_seq;
+    p.region  = 8 * p.vals;
+    p.parity  = (int64_t) peers->n_ranks * p.region;
+    if ((uint64_t) (2 * p.parity) > peers->recv_slot_bytes) {
+        return MM3FA_ERR_WORKSPACE;
+    }
+    p.recv       = static_cast<const char *>(peers->recv[peers->rank]) + (uint64_t) slot * peers->recv_slot_bytes;
+    p.result     = static_cast<char *>(result->data);
+    p.nb1        = (int64_t) result->nb[1];
+    p.nb2        = (int64_t) result->nb[2];
+    p.nb3        = (int64_t) result->nb[3];
+    p.dv         = (int) dv;
+    p.n_q        = (int) n_q;
+    p.n_ranks    = peers->n_ranks;
+    p.rank       = peers->rank;
+    p.epoch      = epochs + slot;
+    p.status     = static_cast<uint32_t *>(workspace);
+    p.timeout_ns = wait_timeout_ns();
+    const int64_t items  = p.vals / 2 * (p.n_ranks - 1);
+    const int     blocks = (int) std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256, 148));
     cudaLaunchConfig_t  cfg{};
     cudaLaunchAttribute attr[1];
-    cfg.gridDim                                        = dim3(1);
-    cfg.blockDim                                       = dim3(32);
+    cfg.gridDim                                        = dim3((unsigned) blocks);
+    cfg.blockDim                                       = dim3(256);
     cfg.stream                                         = static_cast<cudaStream_t>(stream);
     attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs                                          = attr;
     cfg.numAttrs                                       = 1;
-    return cuda_status(cudaLaunchKernelEx(&cfg, peer_wait_kernel, (const uint32_t *) (peers->flags[peers->rank] + slot),
-                                          targets + slot, (uint32_t) (peers->n_ranks - 1),
-                                          static_cast<uint32_t *>(workspace), wait_timeout_ns()));
+    return cuda_status(cudaLaunchKernelEx(&cfg, peer_unpack_kernel, p));
 }
 
 int mm3fa_ipc_export(const void * dev_ptr, mm3fa_ipc_handle * out) {

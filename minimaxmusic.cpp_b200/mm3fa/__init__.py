@@ -34,9 +34,9 @@ MAX_RANKS = 8
 
 
 class Peers(ctypes.Structure):
-    """struct mm3fa_peers: every rank's result buffer and arrival counters, mapped here."""
-    _fields_ = [("n_ranks", ctypes.c_int32), ("rank", ctypes.c_int32), ("dst", ctypes.c_void_p * MAX_RANKS),
-                ("flags", ctypes.c_void_p * MAX_RANKS)]
+    """struct mm3fa_peers: every rank's receive buffer mapped here, and the bytes of one slot."""
+    _fields_ = [("n_ranks", ctypes.c_int32), ("rank", ctypes.c_int32), ("recv", ctypes.c_void_p * MAX_RANKS),
+                ("recv_slot_bytes", ctypes.c_uint64)]
 
 
 class IpcHandle(ctypes.Structure):
@@ -120,9 +120,9 @@ def lib():
         L.mm3fa_allgather_heads.restype = ctypes.c_int
         L.mm3fa_flash_attn_ext_peers.argtypes = [P, P, P, P, vp, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                                  ctypes.c_int, P, vp, ctypes.c_size_t, ctypes.POINTER(Peers),
-                                                 ctypes.c_int, vp]
+                                                 ctypes.c_int, vp, vp]
         L.mm3fa_flash_attn_ext_peers.restype = ctypes.c_int
-        L.mm3fa_peer_wait.argtypes = [ctypes.POINTER(Peers), ctypes.c_int, vp, vp, vp]
+        L.mm3fa_peer_wait.argtypes = [ctypes.POINTER(Peers), ctypes.c_int, vp, P, vp, vp]
         L.mm3fa_peer_wait.restype = ctypes.c_int
         L.mm3fa_ipc_export.argtypes = [vp, ctypes.POINTER(IpcHandle)]
         L.mm3fa_ipc_export.restype = ctypes.c_int
@@ -313,20 +313,22 @@ def allgather_heads(slice_ptr: int, gathered_ptr: int, dst_ptr: int, dv: int, n_
 
 def flash_attn_ext_peers(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None, scale: float, max_bias: float,
                          logit_softcap: float, dst: Tensor, workspace: int, workspace_bytes: int, peers: Peers,
-                         slot: int, stream: int = 0, kv_len_ptr: int = 0, prec: int = GGML_PREC_F32) -> None:
-    """Attention on this rank's shard with the head exchange fused into the kernel: result rows
-    go to every rank's buffer (peers.dst) and counter `slot` of every other rank is bumped."""
+                         slot: int, epochs_ptr: int, stream: int = 0, kv_len_ptr: int = 0,
+                         prec: int = GGML_PREC_F32) -> None:
+    """Attention on this rank's shard with the head exchange fused into the kernel: the result values
+    also go, as {value, epoch} words, into every other rank's receive buffer (slot `slot`)."""
     st = lib().mm3fa_flash_attn_ext_peers(_ref(q), _ref(k), _ref(v), _ref(mask), ctypes.c_void_p(kv_len_ptr or None),
                                           scale, max_bias, logit_softcap, prec, _ref(dst),
                                           ctypes.c_void_p(workspace or None), workspace_bytes, ctypes.byref(peers),
-                                          slot, ctypes.c_void_p(stream or None))
+                                          slot, ctypes.c_void_p(epochs_ptr or None), ctypes.c_void_p(stream or None))
     if st != OK:
         raise MM3FAError(st, "mm3fa_flash_attn_ext_peers")
 
 
-def peer_wait(peers: Peers, slot: int, targets_ptr: int, workspace: int, stream: int = 0) -> None:
-    """Device-side bounded wait until every other rank's slice of call `slot` has arrived."""
-    st = lib().mm3fa_peer_wait(ctypes.byref(peers), slot, ctypes.c_void_p(targets_ptr or None),
+def peer_wait(peers: Peers, slot: int, epochs_ptr: int, result: Tensor, workspace: int, stream: int = 0) -> None:
+    """Device-side bounded wait for every other rank's slice of the latest call on `slot`, unpacked
+    into `result` (this rank's whole [Dv, n_head, n_q, n_seq] result); advances epochs[slot]."""
+    st = lib().mm3fa_peer_wait(ctypes.byref(peers), slot, ctypes.c_void_p(epochs_ptr or None), _ref(result),
                                ctypes.c_void_p(workspace or None), ctypes.c_void_p(stream or None))
     if st != OK:
         raise MM3FAError(st, "mm3fa_peer_wait")

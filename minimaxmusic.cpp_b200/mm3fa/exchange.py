@@ -6,11 +6,13 @@ Two forms, both behind the C ABI (include/mm3fa.h):
 * NCCL: `nccl_comm` returns the ncclComm_t of torch's process group, which
   mm3fa_allgather_heads takes; the library calls ncclAllGather on it and permutes the
   rank-major gather into the ggml result.
-* Peer memory: `PeerBuffers` gives every rank one device allocation holding its whole result
-  buffers (one per slot, e.g. per layer) and its arrival counters, exports it with CUDA IPC
-  (mm3fa_ipc_export), swaps the handles with the other ranks and maps theirs
-  (mm3fa_ipc_open).  mm3fa_flash_attn_ext_peers then stores each rank's result rows into all
-  the buffers from inside the attention kernel and mm3fa_peer_wait is the consumer's wait.
+* Peer memory: `PeerBuffers` gives every rank one zero-filled receive buffer (one slot per
+  exchange site, e.g. per layer), exports it with CUDA IPC (mm3fa_ipc_export), swaps the handles
+  with the other ranks and maps theirs (mm3fa_ipc_open).  mm3fa_flash_attn_ext_peers then
+  stores each rank's result values as {value, epoch} words into the other ranks' receive
+  buffers from inside the attention kernel (no fences: a matching epoch validates its value),
+  and mm3fa_peer_wait is the consumer's kernel: it waits for the words of the current epoch and
+  unpacks them into the local result.
 
 The reference runs on one device (src/backend.h:123); this is the exchange step of the
 head-sharded layout the o_proj consumes (src/qwen3-lm.h:823-827).
@@ -31,56 +33,35 @@ def _round_up(x: int, a: int) -> int:
 
 
 class PeerBuffers:
-    """n_slots result buffers of slot_bytes each plus n_slots u32 arrival counters per rank, in one
-    allocation, mapped into every rank's process.
+    """Receive buffers of the fused exchange: n_slots slots per rank, each holding two parity halves
+    of `world` source regions of 8 * slice_values bytes ({value, epoch} words), in one zero-filled
+    allocation per rank that every other rank maps; plus this rank's epoch counters (one u32 per
+    slot, zero).  Collective: every rank constructs it at the same point, with the same arguments."""
 
-    Collective: every rank constructs it at the same point, with the same arguments."""
-
-    def __init__(self, torch, dist, device, slot_bytes: int, n_slots: int):
+    def __init__(self, torch, dist, device, slice_values: int, n_slots: int):
         self.torch = torch
         self.world = dist.get_world_size()
         self.rank = dist.get_rank()
         if not 2 <= self.world <= mm3fa.MAX_RANKS:
             raise ValueError(f"peer exchange spans 2..{mm3fa.MAX_RANKS} ranks, not {self.world}")
         self.n_slots = n_slots
-        self.slot_bytes = _round_up(slot_bytes, 256)
-        self.flags_off = self.slot_bytes * n_slots
-        total = self.flags_off + _round_up(4 * n_slots, 256)
-        # zero-filled: the counters start at 0 (the result area need not)
-        self.buf = torch.zeros(total, dtype=torch.uint8, device=device)
-        self.targets = torch.zeros(n_slots, dtype=torch.int32, device=device)
-        handle = mm3fa.ipc_export(self.buf.data_ptr())
+        self.slot_bytes = _round_up(2 * self.world * 8 * slice_values, 256)
+        self.recv = torch.zeros(self.slot_bytes * n_slots, dtype=torch.uint8, device=device)
+        self.epochs = torch.zeros(n_slots, dtype=torch.int32, device=device)
+        handle = mm3fa.ipc_export(self.recv.data_ptr())
         handles = [None] * self.world
         dist.all_gather_object(handles, handle)
         self.bases = []
         for r in range(self.world):
-            self.bases.append(self.buf.data_ptr() if r == self.rank else mm3fa.ipc_open(handles[r]))
-        # every rank's zeroed counters are in place before any rank's kernel writes to them
+            self.bases.append(self.recv.data_ptr() if r == self.rank else mm3fa.ipc_open(handles[r]))
+        # every rank's zeroed buffer is in place before any rank's kernel writes into it
         torch.cuda.synchronize(device)
         dist.barrier()
-        self.peers = []
-        for s in range(n_slots):
-            p = mm3fa.Peers()
-            p.n_ranks, p.rank = self.world, self.rank
-            for r in range(self.world):
-                p.dst[r] = self.bases[r] + s * self.slot_bytes
-                p.flags[r] = self.bases[r] + self.flags_off
-            self.peers.append(p)
-
-    def result_ptr(self, slot: int) -> int:
-        """This rank's whole result buffer of `slot`."""
-        return self.buf.data_ptr() + slot * self.slot_bytes
-
-    def result(self, slot: int, shape, dtype=None):
-        """This rank's result buffer of `slot` as a torch tensor view (F32 by default)."""
-        torch = self.torch
-        dtype = dtype or torch.float32
-        n = 1
-        for d in shape:
-            n *= d
-        esz = torch.tensor([], dtype=dtype).element_size()
-        off = slot * self.slot_bytes
-        return self.buf[off:off + n * esz].view(dtype).view(*shape)
+        self.peers = mm3fa.Peers()
+        self.peers.n_ranks, self.peers.rank = self.world, self.rank
+        for r in range(self.world):
+            self.peers.recv[r] = self.bases[r]
+        self.peers.recv_slot_bytes = self.slot_bytes
 
     def close(self):
         """Unmaps the other ranks' buffers (collective: call on every rank, after all use)."""

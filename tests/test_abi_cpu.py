@@ -175,33 +175,43 @@ def test_exchange_entry_points_reject_before_touching_the_device():
     peers = mm3fa.Peers()
     peers.n_ranks, peers.rank = 1, 0
     st = lambda pr, **kw: _status(mm3fa.flash_attn_ext_peers, q4, k4, v4, m4, 0.1, kw.get("max_bias", 0.0), 0.0, d4,
-                                  0x8000, 4096, pr, kw.get("slot", 0))
+                                  0x8000, 4096, pr, kw.get("slot", 0), kw.get("epochs", 0x7000))
     assert st(peers) == mm3fa.ERR_SHAPE  # one rank
     peers.n_ranks, peers.rank = 2, 2
     assert st(peers) == mm3fa.ERR_SHAPE  # rank out of range
     peers.rank = 1
     assert st(peers) == mm3fa.ERR_NULL  # buffers missing
     for r in range(2):
-        peers.dst[r] = 0x100000 * (r + 1)
-        peers.flags[r] = 0x900000 + 0x1000 * r
+        peers.recv[r] = 0x100000 * (r + 1)
+    peers.recv_slot_bytes = 1 << 20
     assert st(peers, slot=-1) == mm3fa.ERR_SHAPE
-    peers.dst[1] = 0x200008
+    assert st(peers, epochs=0) == mm3fa.ERR_NULL
+    assert st(peers, epochs=0x7002) == mm3fa.ERR_ALIGN
+    peers.recv[1] = 0x200008
     assert st(peers) == mm3fa.ERR_ALIGN
-    peers.dst[1] = (d4.data + 0x100000) & ~15
-    assert st(peers) == mm3fa.ERR_SHAPE  # dst is not a view into this rank's own buffer
-    peers.dst[1] = d4.data & ~15
+    peers.recv[1] = 0x200000
+    peers.recv_slot_bytes = 1000
+    assert st(peers) == mm3fa.ERR_SHAPE  # slot size not a multiple of 16
+    peers.recv_slot_bytes = 1 << 20
     assert st(peers, max_bias=8.0) == mm3fa.ERR_UNSUPPORTED  # ALiBi needs the global head index
     assert L.mm3fa_flash_attn_ext_peers(ctypes.byref(q4), ctypes.byref(k4), ctypes.byref(v4), ctypes.byref(m4), None,
-                                        0.1, 0.0, 0.0, 10, ctypes.byref(d4), vp(0x8000), 4096, None, 0, None) == \
-        mm3fa.ERR_NULL
-    # wait: table and targets
-    assert L.mm3fa_peer_wait(ctypes.byref(peers), 0, None, vp(0x8000), None) == mm3fa.ERR_NULL
+                                        0.1, 0.0, 0.0, 10, ctypes.byref(d4), vp(0x8000), 4096, None, 0, vp(0x7000),
+                                        None) == mm3fa.ERR_NULL
+    # wait: table, epochs, result
+    res = ggml.make(ggml.GGML_TYPE_F32, [128, 32, 1, 2], 0x300000)
+    assert L.mm3fa_peer_wait(ctypes.byref(peers), 0, None, ctypes.byref(res), vp(0x8000), None) == mm3fa.ERR_NULL
     bad = mm3fa.Peers()
     bad.n_ranks, bad.rank = 9, 0
-    assert L.mm3fa_peer_wait(ctypes.byref(bad), 0, vp(0x7000), vp(0x8000), None) == mm3fa.ERR_SHAPE
+    assert L.mm3fa_peer_wait(ctypes.byref(bad), 0, vp(0x7000), ctypes.byref(res), vp(0x8000), None) == mm3fa.ERR_SHAPE
+    odd = ggml.make(ggml.GGML_TYPE_F32, [128, 31, 1, 2], 0x300000)  # heads do not split over 2 ranks
+    assert L.mm3fa_peer_wait(ctypes.byref(peers), 0, vp(0x7000), ctypes.byref(odd), vp(0x8000), None) == \
+        mm3fa.ERR_SHAPE
+    peers.recv_slot_bytes = 1024  # smaller than 2 ranks x 2 parities x the slice's words
+    assert L.mm3fa_peer_wait(ctypes.byref(peers), 0, vp(0x7000), ctypes.byref(res), vp(0x8000), None) == \
+        mm3fa.ERR_WORKSPACE
     # IPC helpers
     h = mm3fa.IpcHandle()
     assert L.mm3fa_ipc_export(None, ctypes.byref(h)) == mm3fa.ERR_NULL
     assert L.mm3fa_ipc_open(None, ctypes.byref(ctypes.c_void_p())) == mm3fa.ERR_NULL
     assert L.mm3fa_ipc_close(None) == mm3fa.ERR_NULL
-    assert ctypes.sizeof(mm3fa.Peers) == 8 + 8 * 8 * 2 and ctypes.sizeof(mm3fa.IpcHandle) == 72
+    assert ctypes.sizeof(mm3fa.Peers) == 8 + 8 * 8 + 8 and ctypes.sizeof(mm3fa.IpcHandle) == 72

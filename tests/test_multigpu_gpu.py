@@ -3,9 +3,9 @@
 Each rank computes its shard of a CFG decode call (kv heads [8r/G, 8(r+1)/G)) and of a DiT call
 ((batch x head) units), and the slices are exchanged through the C ABI:
   * mm3fa_allgather_heads (NCCL all-gather of torch's communicator + the permute);
-  * mm3fa_flash_attn_ext_peers + mm3fa_peer_wait (the decode kernel stores its rows into every
-    rank's buffer over NVLink, the consumer waits on the device), over several slots and a
-    reused slot.
+  * mm3fa_flash_attn_ext_peers + mm3fa_peer_wait (the decode kernel stores its values as
+    {value, epoch} words into every other rank's receive buffer over NVLink, the consumer's
+    kernel waits for them and unpacks them), over several slots and both epoch parities.
 The exchanged result must equal, bit for bit, the slices computed one by one on rank 0's GPU
 with the plain entry point (the exchange is a copy), and match the oracle at the north-star
 bound.  Skipped on a box with fewer than 2 GPUs.
@@ -76,18 +76,20 @@ def _rank_main(rank, world, port, out_dir):
     mm3fa.run(qs, ks, vs, ms, mm3fa.dst_desc(qs, vs, gathered[rank].data_ptr()), c.scale, ws=ws)
     mm3fa.allgather_heads(gathered[rank].data_ptr(), gathered.data_ptr(), full_nccl.data_ptr(), D, H, 1, n_seq, 1, comm,
                           s.cuda_stream)
-    # fused form: 3 slots, then slot 0 again (the wait's target moves on per use)
-    pb = exchange.PeerBuffers(torch, dist, dev, n_seq * H * D * 4, 3)
+    # fused form: 3 slots, then slots 0 and 1 again (both epoch parities of a slot), each call into
+    # a NaN-filled result so that every value the exchange misses would show
+    pb = exchange.PeerBuffers(torch, dist, dev, n_seq * hl * D, 3)
     wsz = mm3fa.workspace_size(qs, ks, vs, ms, mm3fa.dst_desc(qs, vs, 0))
     wsb = torch.zeros(max(wsz, 4096), dtype=torch.uint8, device=dev)
     peer_out = []
-    for slot in (0, 1, 2, 0):
-        res = pb.result(slot, (n_seq, 1, H, D))
+    for slot in (0, 1, 2, 0, 1):
+        res = torch.full((n_seq, 1, H, D), float("nan"), device=dev)
         view = ggml.make(F32, [D, hl, 1, n_seq], res.data_ptr() + rank * hl * D * 4, [4, 4 * D, 4 * D * H, 4 * D * H])
         mm3fa.flash_attn_ext_peers(qs, ks, vs, ms, c.scale, 0.0, 0.0, view, wsb.data_ptr(), wsb.numel(),
-                                   pb.peers[slot], slot, s.cuda_stream)
-        mm3fa.peer_wait(pb.peers[slot], slot, pb.targets.data_ptr(), wsb.data_ptr(), s.cuda_stream)
-        peer_out.append(res.clone())
+                                   pb.peers, slot, pb.epochs.data_ptr(), s.cuda_stream)
+        mm3fa.peer_wait(pb.peers, slot, pb.epochs.data_ptr(), ggml.make(F32, [D, H, 1, n_seq], res.data_ptr()),
+                        wsb.data_ptr(), s.cuda_stream)
+        peer_out.append(res)
     torch.cuda.synchronize(dev)
     st, raw = mm3fa.workspace_status(wsb.data_ptr(), s.cuda_stream)
     out = {"decode_nccl": full_nccl.cpu().numpy(), "decode_peer": np.stack([p.cpu().numpy() for p in peer_out]),
