@@ -10,22 +10,26 @@ F32 Q, zero F16 mask, scale 1/sqrt(128).  Synthetic seeded data; K/V ~ N(0, 0.5^
 Inputs are larger than L2 (36 x 84 MB of cache), so no L2 flush is needed.
 
 N GPUs: KV-head sharding, weak scaling.  Rank r holds kv heads [8r/N, 8(r+1)/N) of the
-caches of 2N sequences (N CFG pairs), i.e. the same bytes per GPU as N=1; after the 36
-layers one NCCL all-gather moves every rank's head slices and mm3fa_assemble_heads
-rebuilds the ggml [128, 32, 1, 2N] outputs.
+caches of 2N sequences (N CFG pairs), i.e. the same bytes per GPU as N=1, and the heads are
+exchanged after every layer, as the o_proj of each layer needs them (--exchange p2p: the fused
+peer-store exchange in the decode kernel + the consumer's wait-and-unpack kernel; nccl: an
+all-gather per layer; the other form is timed beside it).  "strong" splits fixed jobs over the
+GPUs instead, "sweep" measures config 2 point by point.
 
 The same line carries the dense (tensor-core) side of the metric: "dit" times benchmark config 5
 (DiT bidirectional attention, B=2 CFG x S=4096 x 16 heads x D=128, F32 Q permuted view, F16
 K/V, no mask) as one flow step of 24 blocks per timed step, cycling 4 operand sets so every call
 reads its inputs from HBM; "prefill" times config 4 (2 x 1024-token causal prefill, 32q/8kv,
-D=128, F16 causal mask over the 256-padded cache view).  N GPUs: each rank runs its own
-(CFG batch x head) shard of the same per-GPU size (weak scaling, no collective).
+D=128, F16 causal mask over the 256-padded cache view); at N GPUs both grow with N and gather
+their results after every call.  "q8_decode" is config 3, "decode_step" the fused prologue +
+attention, "depth" the depth decoder's F32 attention of one frame.
 
 Printed JSON: value = whole-job algorithmic GB/s of the timed steps (device time, max over
 ranks); e2e = the same through the C ABI with Q/mask copied from pinned host memory and the
-outputs read back every step (copies in chunks of E2E_CHUNK layers on two copy streams,
-overlapping the attention of the other chunks); roofline = the decode kernel's achieved GB/s vs the measured
-HBM copy bandwidth; cpu_baseline = the CPU oracle (ggml-cpu algorithm) on the host cores.
+outputs read back every step (copies on two copy streams in uneven chunks, E2E_UP / E2E_DOWN,
+overlapping the attention of other layers); roofline = the decode kernel's achieved GB/s vs the
+measured HBM copy bandwidth; cpu_baseline = the oracle's restatement of ggml's CPU kernel on the
+host cores (all of them, and half).
 """
 from __future__ import annotations
 
@@ -44,7 +48,12 @@ sys.path.insert(0, os.path.join(ROOT, "minimaxmusic.cpp_b200"))
 
 METRIC = "decode attn GB/s & µs/layer (CFG B=2, KV 8K); DiT attn TFLOPS; % roofline"
 N_LAYERS = 36
-E2E_CHUNK = 6      # layers per host<->device copy in the end-to-end measurement
+# host<->device copies of the end-to-end measurement: Q uploads gate the layers they feed (each
+# gate is an event wait in the graph, which also breaks the programmatic launch edge between two
+# decode kernels, so there are few), results go down in chunks while later layers compute; the
+# first upload and the last download are one layer each, so little copying is left exposed
+E2E_UP = (1, 7)           # upload boundaries: Q[0:1], Q[1:8], Q[8:L]
+E2E_DOWN = (8, 16, 24, 32, 35)  # download boundaries: out[0:8], ..., out[32:35], out[35:L]
 N_HEAD, N_HEAD_KV, D = 32, 8, 128
 N_KV, MAX_SEQ = 8192, 10240
 FALLBACK_HBM_GBS = 6650.0
@@ -418,6 +427,52 @@ def bench_sweep(torch, dist, mm3fa, ggml, dev, stream, steps: int, warmup: int, 
                                  "l2": "inputs > L2 (36 layers of caches per point)"}}}
 
 
+def bench_depth(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int) -> dict:
+    """The depth decoder's attention for one LM frame (src/depth-decoder.h:196-221, 249-253, 466): 7
+    autoregressive steps over S = 2..8 codebook positions (no KV cache: each step attends over the
+    whole prefix), 4 layers each, 16 heads x 256, CFG batch 2, F32 q/k/v as the reference's permuted
+    [256, S, 16, 2] views of the [256, 16, S, 2] projections, causal F16 mask; 28 calls per frame in
+    one CUDA graph on the CUDA-core decode kernel (F32 K/V).  Latency-bound: reported in us."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(66)
+    Dd, H, B, L = 256, 16, 2, 4
+    F32, F16 = ggml.GGML_TYPE_F32, ggml.GGML_TYPE_F16
+    keep, calls = [], []
+    for S in range(2, 9):
+        mask = torch.triu(torch.full((S, S), float("-inf"), device=dev), diagonal=1).half()
+        keep.append(mask)
+        for _ in range(L):
+            q, k, v = (torch.randn(B, S, H, Dd, generator=g, device=dev) * sc for sc in (1.0, 0.5, 0.5))
+            o = torch.empty(B, S, H, Dd, device=dev)
+            keep += [q, k, v, o]
+            nb = [4, 4 * Dd * H, 4 * Dd, 4 * Dd * H * S]
+            calls.append((ggml.make(F32, [Dd, S, H, B], q.data_ptr(), nb), ggml.make(F32, [Dd, S, H, B], k.data_ptr(), nb),
+                          ggml.make(F32, [Dd, S, H, B], v.data_ptr(), nb), ggml.make(F16, [S, S, 1, 1], mask.data_ptr()),
+                          ggml.make(F32, [Dd, H, S, B], o.data_ptr())))
+    need = max(mm3fa.workspace_size(*c[:4], c[4]) for c in calls)
+    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
+    scale = 1.0 / math.sqrt(Dd)
+
+    def step():
+        for (qd, kd, vd, md, dd) in calls:
+            mm3fa.flash_attn_ext(qd, kd, vd, md, scale, 0.0, 0.0, dd, ws.data_ptr(), ws.numel(), stream.cuda_stream)
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    ms = timed_replays(torch, None, graph, stream, steps, warmup, 1)
+    del graph
+    return {"depth": {"us_per_frame": round(ms * 1e3, 2), "us_per_call": round(ms * 1e3 / len(calls), 3),
+                      "calls_per_frame": len(calls),
+                      "config": {"workload": "depth decoder attention of one frame: 7 steps (S = 2..8) x 4 layers, "
+                                             "16 heads x 256, CFG batch 2, F32 K/V permuted views, causal",
+                                 "kernel": "fa_decode_kernel<256,f32,C=32,NSTAGE=2,copy> (element copies: "
+                                           "the views' rows are not contiguous)"}}}
+
+
 def bench_q8(torch, mm3fa, ggml, dev, stream, steps: int, warmup: int, world: int, n_layers: int) -> dict:
     """Q8_0 KV-cache decode (benchmark config 3: config 1 at KV 8192 with Q8_0 K/V, int8 ~U[-127,127],
     fp16 scales ~U[0.001,0.02]), as a 36-layer step of independent caches in one CUDA graph; each
@@ -741,6 +796,7 @@ def main() -> None:
     ap.add_argument("--no-step", action="store_true", help="skip the decode-step line (fused prologue + attention)")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config 2 sweep (batch x KV)")
     ap.add_argument("--no-strong", action="store_true", help="skip the strong-scaling lines")
+    ap.add_argument("--no-depth", action="store_true", help="skip the depth-decoder attention line")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="per-layer head exchange of the headline at N > 1 (the other is timed beside it)")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
@@ -829,37 +885,46 @@ def main() -> None:
 
     # ---- end to end through the C ABI: Q/mask from pinned host memory, outputs back to host
     # One pinned buffer per direction (every layer's Q up, every layer's whole result down), moved
-    # in chunks of E2E_CHUNK layers on two copy streams so that the transfers overlap the attention
-    # of other layers: chunk c's Q is uploaded before its layers run, its results go down while
-    # the next chunk computes.
+    # in chunks (E2E_UP, E2E_DOWN) on two copy streams so that the transfers overlap the attention
+    # of other layers: an upload chunk's Q arrives before its first layer runs, a download chunk's
+    # results go down while later layers compute.
     q_all, mask, full = st.q_all, st.mask, st.full
     q_host = q_all.cpu().pin_memory()
     mask_host = mask.cpu().pin_memory()
     out_host = torch.empty(full.shape, dtype=torch.float32).pin_memory()
     up_s, down_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-    chunks = [(a, min(a + E2E_CHUNK, n_layers)) for a in range(0, n_layers, E2E_CHUNK)]
+
+    def spans(bounds):
+        cuts = [0] + [b for b in bounds if 0 < b < n_layers] + [n_layers]
+        return [(a, b) for a, b in zip(cuts[:-1], cuts[1:]) if b > a]
+
+    ups, downs = spans(E2E_UP), spans(E2E_DOWN)
     g2 = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g2, stream=stream):
         fork = torch.cuda.Event()
         stream.record_event(fork)
         up_s.wait_event(fork)
         down_s.wait_event(fork)
-        uploaded = []
+        uploaded = {}
         with torch.cuda.stream(up_s):
             mask.copy_(mask_host, non_blocking=True)
-            for a, b in chunks:
+            for a, b in ups:
                 q_all[a:b].copy_(q_host[a:b], non_blocking=True)
                 ev = torch.cuda.Event()
                 up_s.record_event(ev)
-                uploaded.append(ev)
-        for (a, b), ev in zip(chunks, uploaded):
-            stream.wait_event(ev)
-            st.step(stream, layers=range(a, b))
-            done = torch.cuda.Event()
-            stream.record_event(done)
-            down_s.wait_event(done)
-            with torch.cuda.stream(down_s):
-                out_host[a:b].copy_(full[a:b], non_blocking=True)
+                uploaded[a] = ev
+        down_end = {b: a for a, b in downs}
+        for l in range(n_layers):
+            if l in uploaded:
+                stream.wait_event(uploaded[l])
+            st.step(stream, layers=[l])
+            if l + 1 in down_end:
+                a = down_end[l + 1]
+                done = torch.cuda.Event()
+                stream.record_event(done)
+                down_s.wait_event(done)
+                with torch.cuda.stream(down_s):
+                    out_host[a:l + 1].copy_(full[a:l + 1], non_blocking=True)
         joined = torch.cuda.Event()
         down_s.record_event(joined)
         stream.wait_event(joined)
@@ -899,6 +964,9 @@ def main() -> None:
     if dstep is not None and world > 1:
         dist.barrier()
 
+    depth = None if args.no_depth else bench_depth(torch, mm3fa, ggml, dev, stream, args.steps, args.warmup)
+    if world > 1:
+        dist.barrier()
     sweep = None if args.no_sweep else bench_sweep(torch, dist, mm3fa, ggml, dev, stream, args.steps, args.warmup,
                                                    world, rank, n_layers)
     if sweep is not None and world > 1:
@@ -943,6 +1011,8 @@ def main() -> None:
             line.update(sweep)
         if strong is not None:
             line.update(strong)
+        if depth is not None:
+            line.update(depth)
         if xinfo is not None:
             line["exchange"] = xinfo
         if cpu is not None:
