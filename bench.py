@@ -61,7 +61,7 @@ FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode launch at this workload, from the ncu
 # capture summarised in profiles/ (re-captured whenever the kernel changes)
 NCU_KERNEL = "fa_decode_mma_kernel<128,f16,NT=1,cluster,NS=3>"
-NCU_TRAFFIC_BYTES = 67225600 + 466432
+NCU_TRAFFIC_BYTES = 67227136 + 437760
 NCU_TRAFFIC_SOURCE = "profiles/fa_decode_mma_kernel_cfg2_b2_kv8192.md (one ncu launch, 36-layer step)"
 
 

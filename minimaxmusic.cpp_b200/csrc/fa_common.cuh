@@ -155,6 +155,7 @@ struct DecodeParams {
     int          max_slots;      // partial slots per unit
     int          cluster;        // CTAs per thread-block cluster (tensor-core cluster mode)
     int          dst_vec;        // dst rows start 16-byte aligned: 16-byte stores
+    int          kv_vec;         // every K and V row starts 16-byte aligned (element copies in 16 B)
     int          mask_tma;       // mask rows staged by TMA with K/V (cluster mode)
     const int *  kv_len;         // device [n_seq]: q sequence s sees keys [0, kv_len[s]) (null: all)
     // head exchange over peer memory (cluster mode only): every result value, at linear index e

@@ -94,6 +94,34 @@ __device__ __forceinline__ void lds_bytes(const char * row, int off, uint32_t (&
     }
 }
 
+// Copies rows [j0, j0 + n) of a K and a V slab (row stride nbk / nbv) into the stage, W words of
+// type T per row, every thread loading up to 4 words of each before it stores them.
+template <typename T, int W>
+__device__ __forceinline__ void copy_rows(const char * sk, const char * sv, const char * srck, const char * srcv,
+                                          int j0, int n, int64_t nbk, int64_t nbv, int tid) {
+    const int total = n * W;
+    for (int base = tid; base < total; base += 4 * DEC_THREADS) {
+        T a[4], b[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int idx = base + u * DEC_THREADS;
+            if (idx < total) {
+                const int j = idx / W, w = idx % W;
+                a[u]        = reinterpret_cast<const T *>(srck + (int64_t) (j0 + j) * nbk)[w];
+                b[u]        = reinterpret_cast<const T *>(srcv + (int64_t) (j0 + j) * nbv)[w];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int idx = base + u * DEC_THREADS;
+            if (idx < total) {
+                reinterpret_cast<T *>(const_cast<char *>(sk))[idx] = a[u];
+                reinterpret_cast<T *>(const_cast<char *>(sv))[idx] = b[u];
+            }
+        }
+    }
+}
+
 template <int D, int KVT, int C, int NSTAGE, bool BULK>
 __global__ void __launch_bounds__(DEC_THREADS, 1) fa_decode_kernel(const DecodeParams p) {
     using L               = DecodeSmem<D, KVT, C, NSTAGE>;
@@ -375,16 +403,15 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) fa_decode_kernel(const DecodeP
                 break;
             }
         } else {
-            // cooperative element copy (strides that bulk copies cannot express)
+            // cooperative element copy (strides that bulk copies cannot express): 16-byte words
+            // when every row start is 16-byte aligned, else 2-byte words; each thread issues its
+            // loads of a round together before storing them (one memory latency per round)
             const char * srck = kv_base(unit, p.k, p.k_nb2, p.k_nb3);
             const char * srcv = kv_base(unit, p.v, p.v_nb2, p.v_nb3);
-            constexpr int HW  = ROW / 2;
-            for (int idx = tid; idx < n * HW; idx += DEC_THREADS) {
-                const int j = idx / HW, w = idx % HW;
-                reinterpret_cast<uint16_t *>(const_cast<char *>(sk))[j * HW + w] =
-                    reinterpret_cast<const uint16_t *>(srck + (int64_t) (j0 + j) * p.k_nb1)[w];
-                reinterpret_cast<uint16_t *>(const_cast<char *>(sv))[j * HW + w] =
-                    reinterpret_cast<const uint16_t *>(srcv + (int64_t) (j0 + j) * p.v_nb1)[w];
+            if (ROW % 16 == 0 && p.kv_vec) {
+                copy_rows<uint4, ROW / 16>(sk, sv, srck, srcv, j0, n, p.k_nb1, p.v_nb1, tid);
+            } else {
+                copy_rows<uint16_t, ROW / 2>(sk, sv, srck, srcv, j0, n, p.k_nb1, p.v_nb1, tid);
             }
             __syncthreads();
         }
@@ -647,9 +674,16 @@ DecodeGeometry decode_geometry(int n_seq, int n_head_kv, int ratio, int n_q, int
     const int64_t total = g.n_units * (int64_t) n_kv;
     const int64_t slots = (int64_t) std::max(1, n_sms) * std::max(1, ctas_per_sm);
     int64_t W           = (total + slots - 1) / slots;
-    W                   = std::max<int64_t>(W, 64);
-    const int64_t q     = std::max(16, key_align);
-    W                   = (W + q - 1) / q * q;
+    if (n_kv < 64) {
+        // short units (the depth decoder's S <= 8 steps, short prefixes): one CTA per whole unit,
+        // so they all run at once and no partials are merged (a floor of 64 keys put several
+        // units in sequence into one CTA)
+        W = std::max(n_kv, 1);
+    } else {
+        W             = std::max<int64_t>(W, 64);
+        const int64_t q = std::max(16, key_align);
+        W             = (W + q - 1) / q * q;
+    }
     g.keys_per_cta      = W;
     g.n_ctas            = total > 0 ? (total + W - 1) / W : 0;
     g.max_slots         = (int) ((n_kv + W - 1) / W + 1);

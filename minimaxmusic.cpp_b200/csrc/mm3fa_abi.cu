@@ -607,6 +607,7 @@ int flash_attn_impl(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_
     p.m1        = std::pow(2.0f, -max_bias / 2.0f / (float) n_head_log2);
     p.timeout_ns = wait_timeout_ns();
     p.dst_vec    = rows_vec16(dst);
+    p.kv_vec     = rows_vec16(k) && rows_vec16(v);
     p.kv_len     = kv_len;
     if (var >= V_MMA_8) {
         const int pref    = decode_mma_mode_preference();

@@ -8,7 +8,8 @@ Each rank computes its shard of a CFG decode call (kv heads [8r/G, 8(r+1)/G)) an
     kernel waits for them and unpacks them), over several slots and both epoch parities.
 The exchanged result must equal, bit for bit, the slices computed one by one on rank 0's GPU
 with the plain entry point (the exchange is a copy), and match the oracle at the north-star
-bound.  Skipped on a box with fewer than 2 GPUs.
+bound.  Runs on MM3FA_TEST_GPUS ranks (2 by default; 4 and 8 split the heads further); skipped on
+a box with fewer GPUs.
 """
 import os
 import socket
@@ -19,7 +20,7 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-WORLD = 2
+WORLD = int(os.environ.get("MM3FA_TEST_GPUS", "2"))
 
 
 def _free_port() -> int:
