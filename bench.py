@@ -937,12 +937,12 @@ def main() -> None:
     if world > 1:
         dist.barrier()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    stream.record_event(f0)
-    for _ in range(args.steps):
-        with torch.cuda.stream(stream):
+    with torch.cuda.stream(stream):
+        stream.record_event(f0)
+        for _ in range(args.steps):
             g2.replay()
-        stream.synchronize()  # the step's result is read on the host every step
-    stream.record_event(f1)
+            stream.synchronize()  # the step's result is read on the host every step
+        stream.record_event(f1)
     torch.cuda.synchronize()
     te = torch.tensor([f0.elapsed_time(f1)], device=dev)
     if world > 1:
