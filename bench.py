@@ -19,9 +19,12 @@ GPUs instead, "sweep" measures config 2 point by point.
 The same line carries the dense (tensor-core) side of the metric: "dit" times benchmark config 5
 (DiT bidirectional attention, B=2 CFG x S=4096 x 16 heads x D=128, F32 Q permuted view, F16
 K/V, no mask) as one flow step of 24 blocks per timed step, cycling 4 operand sets so every call
-reads its inputs from HBM; "prefill" times config 4 (2 x 1024-token causal prefill, 32q/8kv,
-D=128, F16 causal mask over the 256-padded cache view); at N GPUs both grow with N and gather
-their results after every call.  "q8_decode" is config 3, "decode_step" the fused prologue +
+reads its inputs from HBM; "dit_real" the same at the real model's shape (B=2 x S=690 x 32 heads x
+D=64, 8 operand sets cycled); "prefill" times config 4 (2 x 1024-token causal prefill, 32q/8kv,
+D=128, F16 causal mask over the 256-padded cache view).  At N GPUs the jobs grow with N: the DiT
+by CFG pairs (every head of a pair on one rank: no exchange needed; "dit_strong" splits the B=2
+job's heads over the ranks and all-gathers after every call), the prefill by sequences split by kv
+head, all-gathered after every call.  "q8_decode" is config 3, "decode_step" the fused prologue +
 attention, "depth" the depth decoder's F32 attention of one frame.
 
 Printed JSON: value = whole-job algorithmic GB/s of the timed steps (device time, max over
@@ -244,9 +247,10 @@ def bench_dense(torch, dist, mm3fa, ggml, dev, stream, steps: int, warmup: int, 
     """DiT (config 5) and causal prefill (config 4) attention on the tensor-core kernel.
 
     N GPUs: the DiT job grows to N CFG pairs (B = 2N) and rank r computes pair r, all 16 heads
-    (weak scaling); a second line keeps the B = 2 job and splits its 32 (batch x head) units over
-    the ranks (strong scaling).  The prefill job grows to 2N sequences, split by kv head.  Every
-    call is followed by mm3fa_allgather_heads (NCCL), as to_out / o_proj need every head."""
+    (weak scaling, no exchange needed); a second line keeps the B = 2 job and splits its 32
+    (batch x head) units over the ranks (strong scaling), each call followed by
+    mm3fa_allgather_heads (NCCL), as to_out needs every head of its rows.  The prefill job grows to
+    2N sequences, split by kv head, with the same all-gather after the call (o_proj)."""
     from mm3fa import exchange as xch, sharding
 
     g = torch.Generator(device=dev)
@@ -293,38 +297,38 @@ def bench_dense(torch, dist, mm3fa, ggml, dev, stream, steps: int, warmup: int, 
 
     burst, sustained, src = measured_tensor_peaks()
     out = {}
-    # ---- DiT: 24 blocks of one flow step, 4 operand sets (each ~192 MB > L2) cycled
+    def dit_line(B, S, H, Dh, n_sets, workload, l2):
+        """24 blocks of one flow step over n_sets operand sets cycled (the sets together > L2).  At N GPUs
+        the job is N CFG pairs and the (batch x head) units split by whole sequences (seq_split = N): rank
+        r computes every head of pair r, so the head-concatenated output that to_out reads is local and
+        no exchange is needed (the head-split exchange is the strong line's)."""
+        fl = 4.0 * Dh * S * S * H * B
+        sets = [dit_set(B, S, H, Dh) for _ in range(n_sets)]
+        res = torch.empty(B, S, H, Dh, device=dev)  # this rank's pair ([D, H, S, B])
+        dd = ggml.make(F32, [Dh, H, S, B], res.data_ptr())
+        ws = torch.zeros(1 << 20, dtype=torch.uint8, device=dev)
+        calls = [((*sets[i % n_sets][1], None, dd), 1.0 / math.sqrt(Dh)) for i in range(24)]
+        us, tf, clocks = timed(calls, None, 24, fl, ws)["with_exchange"]
+        line = {"tflops": round(tf * world, 1), "tflops_per_gpu": round(tf, 1), "us_per_call": round(us, 2),
+                "clocks": clocks,
+                "config": {"workload": workload, "batch_per_gpu": B, "global_batch": B * world, "seq": S, "heads": H,
+                           "head_dim": Dh, "mask": None, "l2": l2,
+                           "exchange": "none needed: every head of a rank's CFG pair is local" if world > 1
+                                       else "none (1 GPU)"},
+                "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": burst, "unit": "TFLOP/s",
+                             "frac": round(tf / burst, 4),
+                             "peak_kind": "bf16_tflops (burst: the timed region is a fraction of a second)",
+                             "frac_of_sustained": round(tf / sustained, 4), "peak_source": src,
+                             "kernel": f"fa_dense_kernel<{Dh},f16>", "flops_per_launch": fl}}
+        del res, calls
+        return line, sets
+
+    # ---- DiT, benchmark config 5: 4 operand sets (each ~192 MB > L2) cycled
     B, S, H, Dh = 2, 4096, 16, 128
     fl = 4.0 * Dh * S * S * H * B
-    sets = [dit_set(B, S, H, Dh) for _ in range(4)]
-    full = torch.empty(B * world, S, H, Dh, device=dev)  # the whole job's result ([D, H, S, 2N])
-    slice_bytes = B * S * H * Dh * 4
-    dd = ggml.make(F32, [Dh, H, S, B], full.data_ptr() + rank * slice_bytes)  # this rank's pair, in place
-    ws = torch.zeros(1 << 20, dtype=torch.uint8, device=dev)
-    calls = [((*sets[i % 4][1], None, dd), 1.0 / math.sqrt(Dh)) for i in range(24)]
-    ex = (lambda s_: mm3fa.allgather_heads(full.data_ptr() + rank * slice_bytes, 0, full.data_ptr(), Dh, H, S,
-                                           B * world, world, comm, s_.cuda_stream)) if world > 1 else None
-    r = timed(calls, ex, 24, fl, ws)
-    us, tf, clocks = r["with_exchange"]
-    out["dit"] = {"tflops": round(tf * world, 1), "tflops_per_gpu": round(tf, 1), "us_per_call": round(us, 2),
-                  "clocks": clocks,
-                  "config": {"workload": "DiT self-attention, benchmark config 5, 24 blocks per step",
-                             "batch_per_gpu": B, "global_batch": B * world, "seq": S, "heads": H, "head_dim": Dh,
-                             "mask": None, "l2": "4 operand sets cycled, each > L2",
-                             "exchange": "all-gather of the result after every call (mm3fa_allgather_heads)"
-                                         if world > 1 else "none (1 GPU)"},
-                  "roofline": {"bound": "tensor", "achieved": round(r.get("attention_only", r["with_exchange"])[1], 1),
-                               "peak": burst, "unit": "TFLOP/s",
-                               "frac": round(r.get("attention_only", r["with_exchange"])[1] / burst, 4),
-                               "peak_kind": "bf16_tflops (burst: the timed region is a fraction of a second)",
-                               "frac_of_sustained": round(r.get("attention_only", r["with_exchange"])[1] / sustained,
-                                                          4),
-                               "peak_source": src, "kernel": "fa_dense_kernel<128,f16>",
-                               "traffic": 134490000 + 37360000, "flops_per_launch": fl}}
-    if "attention_only" in r:
-        out["dit"]["attention_only_us_per_call"] = round(r["attention_only"][0], 2)
-        out["dit"]["attention_only_tflops"] = round(r["attention_only"][1] * world, 1)
-    del full, calls
+    out["dit"], sets = dit_line(B, S, H, Dh, 4, "DiT self-attention, benchmark config 5, 24 blocks per step",
+                                "4 operand sets cycled, each > L2")
+    out["dit"]["roofline"]["traffic"] = 134490000 + 37360000
     if world > 1:
         # strong scaling: the B = 2 job's 32 (batch x head) units over the ranks
         s0, s1, h0, h1, ss = sharding.unit_slice(B, H, rank, world)
@@ -341,13 +345,19 @@ def bench_dense(torch, dist, mm3fa, ggml, dev, stream, steps: int, warmup: int, 
             calls2.append(((view(qd), view(kd), view(vd), None, dd2), 1.0 / math.sqrt(Dh)))
         ex2 = lambda s_: mm3fa.allgather_heads(sptr, 0 if direct else gath.data_ptr(), full2.data_ptr(), Dh, H, S, B,
                                                ss, comm, s_.cuda_stream)
-        r2 = timed(calls2, ex2, 24, fl, ws)
+        r2 = timed(calls2, ex2, 24, fl, torch.zeros(1 << 20, dtype=torch.uint8, device=dev))
         out["dit_strong"] = {"tflops_job": round(r2["with_exchange"][1], 1), "us_per_call": round(r2["with_exchange"][0], 2),
                              "attention_only_us_per_call": round(r2["attention_only"][0], 2),
                              "attention_only_tflops_job": round(r2["attention_only"][1], 1),
                              "units_per_gpu": sl * hl, "config": {"global_batch": B, "heads": H, "seq": S,
                                                                   "seq_split": ss, "scaling": "strong"}}
         del full2, gath, calls2
+    del sets
+    torch.cuda.empty_cache()
+    # ---- the real DiT's attention (src/dit.h:201-222: 32 heads x 64, 690 tokens per CFG pair member), 8
+    # operand sets of 22.6 MB cycled so that the 24 calls read from HBM
+    out["dit_real"], sets = dit_line(2, 690, 32, 64, 8, "DiT self-attention at the real model's shape, 24 blocks "
+                                     "per step", "8 operand sets cycled, together > L2")
     del sets
     torch.cuda.empty_cache()
     # ---- causal prefill: 2 x 1024 tokens per GPU (the job: 2N sequences), 32q / 8kv, cache view padded to 256

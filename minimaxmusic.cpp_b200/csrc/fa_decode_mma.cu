@@ -1368,7 +1368,10 @@ void * mma_kernel(int ns, int & smem) {
 // flight per SM at D=128; measured 3% faster than 2 stages on the 36-layer decode graph) or 2
 // with MM3FA_DECODE_NSTAGE=2.  A 4-stage ring at one CTA per SM (so that the headline's 16
 // clusters of 9 CTAs sit one per SM instead of 13-CTA clusters two per SM) measured 19.9 against
-// 14.6 us per layer: one CTA's 4 consumer warps do not keep an SM's share of HBM in flight.
+// 14.6 us per layer: one CTA's 4 consumer warps do not keep an SM's share of HBM in flight.  A
+// variant with 8 consumer warps, 128-key stages and one CTA per SM (clusters of 6: 96 CTAs, 192 KiB
+// in flight per SM) measured 14.42 against 14.38 us per layer for F16 and 16.3 against 14.1 for
+// Q8_0, so neither the CTA layout nor the SMs left idle limit the headline.
 int mma_nstage_forced() {
     static const int ns = [] {
         const char * e = std::getenv("MM3FA_DECODE_NSTAGE");
