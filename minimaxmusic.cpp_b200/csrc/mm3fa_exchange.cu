@@ -108,7 +108,9 @@ __device__ __forceinline__ uint4 ld_volatile_v4(const char * a) {
 // epoch} of values 2j, 2j+1 of source rank r (r != self), polled until both epochs match (bounded),
 // then written to result at (d, r*hl + h_l, i, seq).  The last CTA to finish advances the slot's
 // epoch.  Launched with programmatic stream serialisation: griddepcontrol.wait first, so the
-// attention call before it (which read the epoch) has completed.
+// attention call before it (which read the epoch) has completed.  It lets the next kernel in the
+// stream launch at once (that kernel's own griddepcontrol.wait still waits for this grid's
+// completion), so the next layer's CTAs are resident and set up while this one polls.
 struct UnpackParams {
     const char * recv;     // this rank's receive buffer, slot base
     char *       result;   // this rank's whole result [Dv, H, n_q, n_seq]
@@ -124,6 +126,7 @@ struct UnpackParams {
 
 __global__ void __launch_bounds__(256) peer_unpack_kernel(const UnpackParams p) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint32_t e      = *p.epoch + 1u;
     const int64_t  pairs  = p.vals / 2;
     const int64_t  items  = pairs * (p.n_ranks - 1);
@@ -327,6 +330,15 @@ int mm3fa_peer_wait(const mm3fa_peers * peers, int slot, uint32_t * epochs, mm3f
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs                                          = attr;
     cfg.numAttrs                                       = 1;
+    // the next layer's attention CTAs become resident beside this kernel's (early trigger): the SMs
+    // this kernel runs on keep the largest shared-memory carve-out, so two of those CTAs still fit
+    static const cudaError_t carve = [] {
+        const cudaError_t e = cudaFuncSetAttribute(peer_unpack_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                                   (int) cudaSharedmemCarveoutMaxShared);
+        cudaGetLastError();
+        return e;
+    }();
+    (void) carve;
     return cuda_status(cudaLaunchKernelEx(&cfg, peer_unpack_kernel, p));
 }
 
