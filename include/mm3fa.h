@@ -386,7 +386,11 @@ MM3FA_API int mm3fa_flash_attn_ext_peers(const mm3fa_tensor * q, const mm3fa_ten
  * of that call (epoch epochs[slot] + 1) are in this rank's receive buffer, writes them into
  * `result` - this rank's whole result [Dv, n_head, n_q, n_seq] F32, rank i's slice being heads
  * [i*n_head/G, (i+1)*n_head/G) - and advances epochs[slot].  Kernels enqueued after it read the
- * whole result.  Each wait is bounded (MM3FA_WAIT_TIMEOUT_MS, 2 s by default); on expiry it sets
+ * whole result.  It lets the next kernel in the stream launch as soon as it starts (programmatic
+ * dependent launch): a kernel launched with programmatic stream serialisation reads the result
+ * only after its own griddepcontrol.wait (cudaGridDependencySynchronize), as programmatic
+ * launch requires; other kernels are ordered as usual.  Each wait is bounded
+ * (MM3FA_WAIT_TIMEOUT_MS, 2 s by default); on expiry it sets
  * the workspace status word (mm3fa_workspace_status reports MM3FA_ERR_TIMEOUT) and returns.
  * Replaces: nothing in the reference (see above).
  */
