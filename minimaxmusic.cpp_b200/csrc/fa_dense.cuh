@@ -37,7 +37,12 @@ struct DenseParams {
     int          m_ne2, m_ne3;
     float        scale, softcap, max_bias, m0, m1;
     int          n_head_log2;
-    int          n_qt, n_kt;              // 128-row query tiles, 128-key tiles
+    int          n_qt, n_kt;              // query blocks (256 rows, or 128 with pair), 128-key tiles
+    // head pair mode (GQA with a mask shared by all heads): a work item is 128 query rows of two
+    // query heads of one kv group, Q tile t holding head 2 hp + t - both tiles see the same
+    // causal extent and share every K/V tile; otherwise 256 rows of one head (tile t = rows
+    // 128 t ..)
+    int          pair;
     const uint32_t * blocks;              // [plane][n_qt][n_kt] block flags (BLKF_*), null without mask
     // [plane][row][3]: max(n_kv - first -inf column), max(last zero column + 1), any other value;
     // a row is a step row (zeros, then -inf from column lim = n_kv - [0] on) when [2] == 0 and

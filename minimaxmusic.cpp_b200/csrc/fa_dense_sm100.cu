@@ -430,11 +430,12 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
     }
     // without a mask every item has the same length: query blocks vary fastest, so the CTAs in
     // flight share few (head, sequence) K/V slabs and those stay in L2
-    const int hs    = p.n_head * p.n_seq;
-    const int cq    = p.mask ? p.n_qt - 1 - item / hs : item % p.n_qt;  // 256-row query block
+    const int hunits = p.pair ? p.n_head / 2 : p.n_head;  // heads, or head pairs
+    const int hs    = hunits * p.n_seq;
+    const int cq    = p.mask ? p.n_qt - 1 - item / hs : item % p.n_qt;  // query block
     const int hsi   = p.mask ? item % hs : item / p.n_qt;
-    const int h     = hsi % p.n_head;
-    const int sq    = hsi / p.n_head;
+    const int h     = (hsi % hunits) * (p.pair ? 2 : 1);  // the item's (first) query head
+    const int sq    = hsi / hunits;
     const int g     = h / p.ratio;
     const int ks3   = sq / p.rk3;
     const int plane = (sq % p.m_ne3) * p.m_ne2 + (h % p.m_ne2);
@@ -624,15 +625,17 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
         regs_inc<DN_REGS_SOFTMAX>();
         // ======================================================= softmax warpgroups 1, 2
         const int      t     = wg - 1;            // Q tile
+        const int      ht    = p.pair ? h + t : h;                              // its query head
+        const int      rbase = p.pair ? cq * DN_M : cq * DN_ROWS + t * DN_M;   // its first query row
         const int      quad  = warp & 3;          // TMEM lane quadrant this warp may access
         const int      r     = quad * 32 + lane;  // row in the tile (= TMEM lane)
         const uint32_t tl    = (uint32_t) (quad * 32) << 16;
         const uint32_t s_col = tmem + tl + (uint32_t) (t * DN_N);
         const uint32_t o_col = tmem + tl + 256u + (uint32_t) (t * D);
-        const int      row   = cq * DN_ROWS + t * DN_M + r;
+        const int      row   = rbase + r;
         const bool     valid = row < p.n_q;
         const int      qi    = valid ? row : 0;
-        const float    slope = alibi_slope(h, p.max_bias, p.n_head_log2, p.m0, p.m1);
+        const float    slope = alibi_slope(ht, p.max_bias, p.n_head_log2, p.m0, p.m1);
         // step rows (the mask is 0 before column lim and -inf from it on, as in causal masks):
         // their mixed tiles take the fast path with a column bound instead of mask values
         int lim = p.n_kv, ri0 = 0, ri1 = 0, ri2 = 0;
@@ -645,7 +648,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
 
         // ---- stage Q row r into the swizzled K-major tile t, rounded to K's type
         {
-            const char * qrow = p.q + (int64_t) qi * p.q_nb1 + (int64_t) h * p.q_nb2 + (int64_t) sq * p.q_nb3;
+            const char * qrow = p.q + (int64_t) qi * p.q_nb1 + (int64_t) ht * p.q_nb2 + (int64_t) sq * p.q_nb3;
             char *       qs   = smem + L::OFF_Q + t * L::QT;
             if (p.q_type == KV_F32 && p.q_vec) {
                 // coalesced: the lanes of a warp load whole rows (LPR lanes x 16 bytes per row) of this
@@ -658,10 +661,10 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
 #pragma unroll
                 for (int it = 0; it < NLD; it++) {
                     const int rr  = quad * 32 + it * RPI + lane / LPR;  // row in the tile
-                    const int row = cq * DN_ROWS + t * DN_M + rr;
+                    const int row = rbase + rr;
                     x[it]         = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (row < p.n_q) {
-                        x[it] = reinterpret_cast<const float4 *>(p.q + (int64_t) row * p.q_nb1 + (int64_t) h * p.q_nb2 +
+                        x[it] = reinterpret_cast<const float4 *>(p.q + (int64_t) row * p.q_nb1 + (int64_t) ht * p.q_nb2 +
                                                                  (int64_t) sq * p.q_nb3)[lane % LPR];
                     }
                 }
@@ -700,7 +703,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
         }
 
         const __half * mrow = p.mask ? reinterpret_cast<const __half *>(
-                                           p.mask + (int64_t) qi * p.m_nb1 + (int64_t) (h % p.m_ne2) * p.m_nb2 +
+                                           p.mask + (int64_t) qi * p.m_nb1 + (int64_t) (ht % p.m_ne2) * p.m_nb2 +
                                            (int64_t) (sq % p.m_ne3) * p.m_nb3)
                                      : nullptr;
         const float sc    = p.softcap != 0.0f ? p.scale / p.softcap : p.scale;
@@ -1011,16 +1014,16 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                     fence_proxy_async_smem();
                     dn_named_barrier(1 + t, 128);
                     if (quad == 0 && lane == 0) {
-                        const int q0t = cq * DN_ROWS + t * DN_M;
+                        const int q0t = rbase;
 #pragma unroll
                         for (int c = 0; c < D / 32; c++) {
-                            dn_tma_store_4d(&tmo, stage + c * (DN_M * 128), c * 32, h, q0t, sq);
+                            dn_tma_store_4d(&tmo, stage + c * (DN_M * 128), c * 32, ht, q0t, sq);
                         }
                         asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                         asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
                     }
                 } else if (valid) {
-                    float * out = reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 + (int64_t) qi * p.d_nb2 +
+                    float * out = reinterpret_cast<float *>(p.dst + (int64_t) ht * p.d_nb1 + (int64_t) qi * p.d_nb2 +
                                                             (int64_t) sq * p.d_nb3);
 #pragma unroll
                     for (int c = 0; c < D / 32; c++) {
@@ -1067,17 +1070,17 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             fence_proxy_async_smem();
             dn_named_barrier(1 + t, 128);
             if (quad == 0 && lane == 0) {
-                const int q0t = cq * DN_ROWS + t * DN_M;
+                const int q0t = rbase;
 #pragma unroll
                 for (int c = 0; c < D / 32; c++) {
-                    dn_tma_store_4d(&tmo, stage + c * (DN_M * 128), c * 32, h, q0t, sq);
+                    dn_tma_store_4d(&tmo, stage + c * (DN_M * 128), c * 32, ht, q0t, sq);
                 }
                 asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                 asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
             }
         } else {
         float * out =
-            reinterpret_cast<float *>(p.dst + (int64_t) h * p.d_nb1 + (int64_t) qi * p.d_nb2 + (int64_t) sq * p.d_nb3);
+            reinterpret_cast<float *>(p.dst + (int64_t) ht * p.d_nb1 + (int64_t) qi * p.d_nb2 + (int64_t) sq * p.d_nb3);
 #pragma unroll
         for (int c = 0; c < D / 32; c++) {
             uint32_t o[32];
@@ -1134,7 +1137,7 @@ constexpr int MASK_ROWS          = MASK_CLASS_THREADS / (DN_N / 8);  // 32
 
 __global__ void __launch_bounds__(MASK_CLASS_THREADS)
     mask_block_class_kernel(const char * mask, int64_t nb1, int64_t nb2, int64_t nb3, int m_ne2, int n_q, int n_kv,
-                            int n_qt, int n_kt, int vec, uint32_t * bflags, int * rowinfo) {
+                            int n_qt, int n_kt, int qrows, int vec, uint32_t * bflags, int * rowinfo) {
     const int    kt = blockIdx.x, plane = blockIdx.z;
     const int    i2 = plane % m_ne2, i3 = plane / m_ne2;
     const int    r0 = blockIdx.y * MASK_ROWS, c0 = kt * DN_N;
@@ -1208,7 +1211,7 @@ __global__ void __launch_bounds__(MASK_CLASS_THREADS)
     if (threadIdx.x == 0) {
         const uint32_t f = (finite ? BLKF_FINITE : 0u) | (nonzero ? BLKF_NONZERO : 0u);
         if (f) {
-            atomicOr(&bflags[((int64_t) plane * n_qt + r0 / DN_ROWS) * n_kt + kt], f);
+            atomicOr(&bflags[((int64_t) plane * n_qt + r0 / qrows) * n_kt + kt], f);
         }
     }
 }
@@ -1252,7 +1255,7 @@ bool dense_eligible(int D, int kvt) {
 }
 
 size_t dense_workspace_bytes(int64_t n_q, int64_t n_kv, int64_t planes) {
-    const int64_t n_qt = (n_q + DN_ROWS - 1) / DN_ROWS, n_kt = (n_kv + DN_N - 1) / DN_N;
+    const int64_t n_qt = (n_q + DN_M - 1) / DN_M, n_kt = (n_kv + DN_N - 1) / DN_N;  // 128-row blocks at most
     return WS_STATUS_BYTES + (size_t) ((planes * n_qt * n_kt * 4 + 255) / 256 * 256) +
            (size_t) ((planes * n_q * 12 + 255) / 256 * 256);
 }
@@ -1294,7 +1297,10 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
     }
     char * ws = static_cast<char *>(workspace);
     p.status  = reinterpret_cast<uint32_t *>(ws);
-    p.n_qt    = (int) ((p.n_q + DN_ROWS - 1) / DN_ROWS);
+    // head pairs: GQA (an even number of query heads per kv head) with one mask plane for all heads
+    p.pair          = (p.mask && p.ratio % 2 == 0 && p.m_ne2 == 1) ? 1 : 0;
+    const int qrows = p.pair ? DN_M : DN_ROWS;
+    p.n_qt    = (int) ((p.n_q + qrows - 1) / qrows);
     p.n_kt    = (int) ((p.n_kv + DN_N - 1) / DN_N);
     p.blocks  = nullptr;
     p.rowinfo = nullptr;
@@ -1310,7 +1316,7 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
         const unsigned rgroups = (unsigned) ((p.n_q + MASK_ROWS - 1) / MASK_ROWS);
         mask_block_class_kernel<<<dim3((unsigned) p.n_kt, rgroups, (unsigned) planes), MASK_CLASS_THREADS, 0,
                                   stream>>>(p.mask, p.m_nb1, p.m_nb2, p.m_nb3, p.m_ne2, p.n_q, p.n_kv, p.n_qt, p.n_kt,
-                                            p.mask_vec, blocks, rinfo);
+                                            qrows, p.mask_vec, blocks, rinfo);
         e = cudaGetLastError();
         if (e != cudaSuccess) {
             return e;
@@ -1327,7 +1333,7 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
     // item's K/V range (all items, when there are at most half as many items as SMs)
     p.n_head          = (int) n_head;
     p.n_seq           = (int) n_seq;
-    const int n_items = p.n_qt * p.n_head * p.n_seq;
+    const int n_items = p.n_qt * (p.pair ? p.n_head / 2 : p.n_head) * p.n_seq;
     int       sms     = 148;
     int       dev     = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) {

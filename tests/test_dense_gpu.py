@@ -85,6 +85,37 @@ def test_prefill_causal(dense, cuda_device, S, kv_pos):
     check(workloads.prefill_case(n_seq=2, S=S, n_head=8, n_head_kv=2, kv_pos=kv_pos, seed=300 + S), cuda_device)
 
 
+@pytest.mark.parametrize("H,HKV", [(4, 4), (6, 2), (4, 2), (16, 2)])
+def test_prefill_head_layouts(dense, cuda_device, H, HKV):
+    """GQA ratios that take the head-pair work items (2, 8: two query heads of one kv group per
+    CTA, same rows) and those that do not (1: MHA, 3: odd), over several query blocks."""
+    check(workloads.prefill_case(n_seq=2, S=300, n_head=H, n_head_kv=HKV, kv_pos=20, seed=340 + 10 * H + HKV),
+          cuda_device)
+
+
+def test_prefill_pair_alibi(dense, cuda_device):
+    """ALiBi on head-pair items: each Q tile of a CTA takes its own head's slope."""
+    c = workloads.prefill_case(n_seq=1, S=256, n_head=8, n_head_kv=2, kv_pos=8, seed=351)
+    c.max_bias = 8.0
+    check(c, cuda_device)
+
+
+def test_prefill_per_head_mask(dense, cuda_device):
+    """A mask plane per query head (m_ne2 = n_head) keeps one head per CTA: the causal mask with a
+    finite per-head bias on the first column (so the diagonal and first tiles are general mixed
+    tiles, not step rows)."""
+    c = workloads.prefill_case(n_seq=1, S=260, n_head=8, n_head_kv=2, kv_pos=0, seed=352)
+    m = c.mask.storage  # [S, n_kv_pad]
+    S, nkv = m.shape
+    H = 8
+    mh = np.repeat(m[None], H, axis=0).copy()  # [H, S, n_kv_pad]
+    for h in range(H):
+        mh[h, :, 0] = np.float16(-0.5 * (h % 3))
+    c.mask = workloads.Operand(mh, ggml.GGML_TYPE_F16, [nkv, S, H, 1],
+                               ggml.contiguous_nb(ggml.GGML_TYPE_F16, [nkv, S, H, 1]))
+    check(c, cuda_device)
+
+
 def test_prefill_config4_full(dense, cuda_device):
     """benchmark config 4 at full size (2 x 1024 tokens, 32q/8kv, D=128, causal): 256 work items,
     more than one wave, every output row checked."""
