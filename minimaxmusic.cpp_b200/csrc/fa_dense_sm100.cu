@@ -468,20 +468,29 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
         }
         return kt;
     };
-    // this CTA's share of them: positions [pos_lo, pos_lo + n_mine) of the list
-    int n_all = 0;
-    for (int kt = next_tile(0); kt < p.n_kt; kt = next_tile(kt + 1)) {
-        n_all++;
-    }
-    const int pos_lo = half == 1 ? (n_all + 1) / 2 : 0;
-    const int n_mine = half == 0 ? (n_all + 1) / 2 : n_all - pos_lo;
-    int       kt_lo  = next_tile(0);
-    for (int k = 0; k < pos_lo; k++) {
-        kt_lo = next_tile(kt_lo + 1);
-    }
+    // this CTA's share of them: positions [pos_lo, pos_lo + n_mine) of the list.  The block
+    // classes and row summaries come from the mask pre-pass, which lets this kernel launch while
+    // it runs (masked calls are launched with programmatic stream serialisation; everything
+    // before the pre-pass has completed when it starts): each role reads them only after
+    // griddepcontrol.wait, and the softmax warpgroups stage Q before that.
+    int  n_mine = 0, kt_lo = 0;
+    auto tile_share = [&]() {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        int n_all = 0;
+        for (int kt = next_tile(0); kt < p.n_kt; kt = next_tile(kt + 1)) {
+            n_all++;
+        }
+        const int pos_lo = half == 1 ? (n_all + 1) / 2 : 0;
+        n_mine           = half == 0 ? (n_all + 1) / 2 : n_all - pos_lo;
+        kt_lo            = next_tile(0);
+        for (int k = 0; k < pos_lo; k++) {
+            kt_lo = next_tile(kt_lo + 1);
+        }
+    };
 
     if (wg == 0) {
         regs_dec<DN_REGS_OTHER>();
+        tile_share();
         if (warp == 0 && lane == 0) {
             // ======================================================= TMA producer
             int  nk_ld = 0, nv_ld = 0;  // K and V tile loads issued (stage = load index % NS)
@@ -636,16 +645,6 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
         const bool     valid = row < p.n_q;
         const int      qi    = valid ? row : 0;
         const float    slope = alibi_slope(ht, p.max_bias, p.n_head_log2, p.m0, p.m1);
-        // step rows (the mask is 0 before column lim and -inf from it on, as in causal masks):
-        // their mixed tiles take the fast path with a column bound instead of mask values
-        int lim = p.n_kv, ri0 = 0, ri1 = 0, ri2 = 0;
-        if (p.rowinfo && valid) {
-            const int * ri = p.rowinfo + ((int64_t) plane * p.n_q + qi) * 3;
-            ri0            = ri[0];
-            ri1            = ri[1];
-            ri2            = ri[2];
-        }
-
         // ---- stage Q row r into the swizzled K-major tile t, rounded to K's type
         {
             const char * qrow = p.q + (int64_t) qi * p.q_nb1 + (int64_t) ht * p.q_nb2 + (int64_t) sq * p.q_nb3;
@@ -700,6 +699,16 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             }
             fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
             dn_mbar_arrive(&bar[B_QREADY + t]);
+        }
+        tile_share();
+        // step rows (the mask is 0 before column lim and -inf from it on, as in causal masks):
+        // their mixed tiles take the fast path with a column bound instead of mask values
+        int lim = p.n_kv, ri0 = 0, ri1 = 0, ri2 = 0;
+        if (p.rowinfo && valid) {
+            const int * ri = p.rowinfo + ((int64_t) plane * p.n_q + qi) * 3;
+            ri0            = ri[0];
+            ri1            = ri[1];
+            ri2            = ri[2];
         }
 
         const __half * mrow = p.mask ? reinterpret_cast<const __half *>(
@@ -1138,6 +1147,9 @@ constexpr int MASK_ROWS          = MASK_CLASS_THREADS / (DN_N / 8);  // 32
 __global__ void __launch_bounds__(MASK_CLASS_THREADS)
     mask_block_class_kernel(const char * mask, int64_t nb1, int64_t nb2, int64_t nb3, int m_ne2, int n_q, int n_kv,
                             int n_qt, int n_kt, int qrows, int vec, uint32_t * bflags, int * rowinfo) {
+    // the attention kernel may launch at once: it reads nothing this kernel writes before its
+    // griddepcontrol.wait
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int    kt = blockIdx.x, plane = blockIdx.z;
     const int    i2 = plane % m_ne2, i3 = plane / m_ne2;
     const int    r0 = blockIdx.y * MASK_ROWS, c0 = kt * DN_N;
@@ -1314,6 +1326,16 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
             return e;
         }
         const unsigned rgroups = (unsigned) ((p.n_q + MASK_ROWS - 1) / MASK_ROWS);
+        // the attention's CTAs become resident beside this kernel's: its SMs keep the largest
+        // shared-memory carve-out
+        static const cudaError_t carve = [] {
+            const cudaError_t c = cudaFuncSetAttribute(mask_block_class_kernel,
+                                                       cudaFuncAttributePreferredSharedMemoryCarveout,
+                                                       (int) cudaSharedmemCarveoutMaxShared);
+            cudaGetLastError();
+            return c;
+        }();
+        (void) carve;
         mask_block_class_kernel<<<dim3((unsigned) p.n_kt, rgroups, (unsigned) planes), MASK_CLASS_THREADS, 0,
                                   stream>>>(p.mask, p.m_nb1, p.m_nb2, p.m_nb3, p.m_ne2, p.n_q, p.n_kv, p.n_qt, p.n_kt,
                                             qrows, p.mask_vec, blocks, rinfo);
@@ -1357,19 +1379,29 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
     p.n_regular   = n_items - n_split;
     void * args[] = { &tmk, &tmv, &tmo, &p };
     cudaLaunchConfig_t  cfg{};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     cfg.gridDim          = dim3((unsigned) (p.n_regular + 2 * n_split));
     cfg.blockDim         = dim3(DN_THREADS);
     cfg.dynamicSmemBytes = (size_t) smem;
     cfg.stream           = stream;
+    cfg.attrs            = attr;
     cfg.numAttrs         = 0;
     if (n_split > 0) {
-        attr[0].id               = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs                = attr;
-        cfg.numAttrs             = 1;
+        attr[cfg.numAttrs].id               = cudaLaunchAttributeClusterDimension;
+        attr[cfg.numAttrs].val.clusterDim.x = 2;
+        attr[cfg.numAttrs].val.clusterDim.y = 1;
+        attr[cfg.numAttrs].val.clusterDim.z = 1;
+        cfg.numAttrs++;
+    }
+    // masked calls: programmatic launch after the pre-pass (MM3FA_PDL=0 turns it off)
+    static const bool pdl = [] {
+        const char * e = std::getenv("MM3FA_PDL");
+        return !(e && std::atoi(e) == 0);
+    }();
+    if (p.mask && pdl) {
+        attr[cfg.numAttrs].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs++;
     }
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
