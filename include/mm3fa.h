@@ -397,6 +397,48 @@ MM3FA_API int mm3fa_flash_attn_ext_peers(const mm3fa_tensor * q, const mm3fa_ten
 MM3FA_API int mm3fa_peer_wait(const mm3fa_peers * peers, int slot, uint32_t * epochs, mm3fa_tensor * result,
                               void * workspace, void * stream);
 
+/*
+ * Dense attention (causal prefill, DiT) on this rank's shard with the exchange of the result fused
+ * into the kernel: computes exactly what mm3fa_flash_attn_ext computes into dst, and stores every
+ * finished result row, at the same byte offset, into each other rank's whole result as well (the
+ * row leaves from the epilogue with plain 16-byte stores over NVLink while later tiles are still
+ * computed; no permute, no collective library).
+ *   results->recv[r]       base of rank r's whole result buffer for this call (the caller's own
+ *                          at r = rank; the others mapped with mm3fa_ipc_open), each
+ *                          results->recv_slot_bytes long
+ *   dst                    this rank's slice: a view inside recv[rank] (e.g. its heads of the
+ *                          [Dv, n_head, n_q, n_seq] result, or its sequences)
+ * The other ranks' rows are complete only after mm3fa_gather_signal_wait on every rank.  A rank
+ * may write into a buffer that another rank is still reading, so the caller alternates at least
+ * two result buffers (slots) between calls, each followed by its mm3fa_gather_signal_wait.
+ * Only for operands that take the tensor-core prefill/DiT kernel (many query rows, keys present,
+ * dst rows 16-byte aligned, strides that its TMA store takes); other shapes and max_bias != 0
+ * return MM3FA_ERR_UNSUPPORTED and enqueue nothing.
+ * Replaces: the attention node of src/qwen3-lm.h:432-436 (prefill) or src/dit.h:218-222 (DiT) plus
+ *           the all-gather of the head-concatenated result that a sharded run needs before the
+ *           output projection (src/qwen3-lm.h:439, src/dit.h:226); the reference runs on one GPU.
+ */
+MM3FA_API int mm3fa_flash_attn_ext_gather(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                                          const mm3fa_tensor * mask, float scale, float max_bias,
+                                          float logit_softcap, int prec, mm3fa_tensor * dst, void * workspace,
+                                          size_t workspace_bytes, const mm3fa_peers * results, void * stream);
+
+/*
+ * Completion of the exchange of mm3fa_flash_attn_ext_gather, enqueued on `stream` after this rank's
+ * call: publishes this rank's rows to every other rank (a system-scope fence, then the call's
+ * epoch - epochs[slot] + 1 - stored into each rank's flag word [slot][this rank]) and waits on the
+ * device until every other rank's epoch is in this rank's words [slot][*]; then advances
+ * epochs[slot].  Kernels enqueued after it read the whole result.
+ *   flags->recv[r]          rank r's flag array: uint32 [n_slots][n_ranks], zero-filled before the
+ *                           first call, mapped like the results; recv_slot_bytes = its size
+ *   epochs                  this rank's device uint32 [n_slots], zero-filled before the first call
+ * Every rank calls it with the same slot sequence.  The wait is bounded (MM3FA_WAIT_TIMEOUT_MS);
+ * on expiry the workspace status word reports MM3FA_ERR_TIMEOUT.
+ * Replaces: nothing in the reference (see above).
+ */
+MM3FA_API int mm3fa_gather_signal_wait(const mm3fa_peers * flags, int slot, uint32_t * epochs, void * workspace,
+                                       void * stream);
+
 /* CUDA IPC handle of a device buffer: the allocation's handle plus the buffer's offset in it. */
 typedef struct mm3fa_ipc_handle {
     unsigned char handle[64];

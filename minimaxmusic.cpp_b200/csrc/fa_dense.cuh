@@ -43,6 +43,12 @@ struct DenseParams {
     // causal extent and share every K/V tile; otherwise 256 rows of one head (tile t = rows
     // 128 t ..)
     int          pair;
+    // fused head exchange (TMA-store epilogue only): each finished result row is also stored at
+    // the same byte offset from its dst address plus peer_off[i] - the same position in the other
+    // ranks' whole results, mapped by CUDA IPC - with 16-byte stores (no fence: the exchange's
+    // signal kernel, after this one in the stream, publishes the rows)
+    int          n_peers;
+    int64_t      peer_off[7];
     const uint32_t * blocks;              // [plane][n_qt][n_kt] block flags (BLKF_*), null without mask
     // [plane][row][3]: max(n_kv - first -inf column), max(last zero column + 1), any other value;
     // a row is a step row (zeros, then -inf from column lim = n_kv - [0] on) when [2] == 0 and

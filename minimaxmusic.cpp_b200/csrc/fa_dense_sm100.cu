@@ -1069,11 +1069,23 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                     }
                 }
                 char * tile = stage + c * (DN_M * 128);
+                // this row's place in the result (the other ranks' results hold it at peer_off)
+                char * prow = p.dst + (int64_t) ht * p.d_nb1 + (int64_t) qi * p.d_nb2 + (int64_t) sq * p.d_nb3 +
+                              (int64_t) c * 128;
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
-                    *reinterpret_cast<float4 *>(tile + sw128_off(r, j)) =
-                        make_float4(__uint_as_float(o[4 * j]) * inv, __uint_as_float(o[4 * j + 1]) * inv,
-                                    __uint_as_float(o[4 * j + 2]) * inv, __uint_as_float(o[4 * j + 3]) * inv);
+                    const float4 val = make_float4(__uint_as_float(o[4 * j]) * inv, __uint_as_float(o[4 * j + 1]) * inv,
+                                                   __uint_as_float(o[4 * j + 2]) * inv,
+                                                   __uint_as_float(o[4 * j + 3]) * inv);
+                    *reinterpret_cast<float4 *>(tile + sw128_off(r, j)) = val;
+                    if (p.n_peers > 0 && valid) {
+#pragma unroll
+                        for (int pp = 0; pp < 7; pp++) {
+                            if (pp < p.n_peers) {
+                                *reinterpret_cast<float4 *>(prow + p.peer_off[pp] + 16 * j) = val;
+                            }
+                        }
+                    }
                 }
             }
             fence_proxy_async_smem();
@@ -1307,6 +1319,9 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
         }
     }
+    if (p.n_peers > 0 && !p.tma_store) {
+        return cudaErrorNotSupported;  // the fused exchange lives in the TMA-store epilogue
+    }
     char * ws = static_cast<char *>(workspace);
     p.status  = reinterpret_cast<uint32_t *>(ws);
     // head pairs: GQA (an even number of query heads per kv head) with one mask plane for all heads
@@ -1365,7 +1380,7 @@ cudaError_t launch_dense(DenseParams p, int D, int kvt, int64_t n_head_kv, int64
     const char * env    = std::getenv("MM3FA_DENSE_SPLIT");
     // a half item has its own Q staging, epilogue and merge: only items of at least 16 K/V tiles
     // gain from halving
-    if (!(env && env[0] == '0') && p.n_kt >= 16) {
+    if (!(env && env[0] == '0') && p.n_kt >= 16 && p.n_peers == 0) {  // (split halves: no fused exchange)
         if (2 * n_items <= sms) {
             n_split = n_items;
         } else {

@@ -329,7 +329,8 @@ bool rows_vec16(const mm3fa_tensor * t) {
 
 int run_dense(const OpShape & s, const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
               const mm3fa_tensor * mask, float scale, float max_bias, float softcap, mm3fa_tensor * dst,
-              void * workspace, size_t workspace_bytes, uint64_t timeout_ns, cudaStream_t cs) {
+              void * workspace, size_t workspace_bytes, uint64_t timeout_ns, cudaStream_t cs,
+              const int64_t * peer_off = nullptr, int n_peers = 0) {
     const int64_t planes = mask ? mask->ne[2] * mask->ne[3] : 1;
     if (!workspace || workspace_bytes < dense_workspace_bytes(s.n_q, s.n_kv, planes)) {
         return MM3FA_ERR_WORKSPACE;
@@ -373,7 +374,15 @@ int run_dense(const OpShape & s, const mm3fa_tensor * q, const mm3fa_tensor * k,
     p.m0          = std::pow(2.0f, -max_bias / (float) n_head_log2);
     p.m1          = std::pow(2.0f, -max_bias / 2.0f / (float) n_head_log2);
     p.timeout_ns  = timeout_ns;
-    return record_cuda(launch_dense(p, (int) s.D, s.kvt, s.n_head_kv, s.n_seq_k, s.n_head, s.n_seq, workspace, cs));
+    p.n_peers     = n_peers;
+    for (int i = 0; i < n_peers; i++) {
+        p.peer_off[i] = peer_off[i];
+    }
+    const cudaError_t e = launch_dense(p, (int) s.D, s.kvt, s.n_head_kv, s.n_seq_k, s.n_head, s.n_seq, workspace, cs);
+    if (e == cudaErrorNotSupported) {
+        return MM3FA_ERR_UNSUPPORTED;
+    }
+    return record_cuda(e);
 }
 
 __global__ void zero_rows_kernel(char * dst, int64_t dv, int64_t n1, int64_t n2, int64_t n3, int64_t nb1,
@@ -695,6 +704,71 @@ int mm3fa_flash_attn_ext_peers(const mm3fa_tensor * q, const mm3fa_tensor * k, c
     }
     return flash_attn_impl(q, k, v, mask, kv_len, scale, max_bias, logit_softcap, prec, dst, workspace,
                            workspace_bytes, stream, peers, slot, epochs);
+}
+
+int mm3fa_flash_attn_ext_gather(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,
+                                const mm3fa_tensor * mask, float scale, float max_bias, float logit_softcap, int prec,
+                                mm3fa_tensor * dst, void * workspace, size_t workspace_bytes,
+                                const mm3fa_peers * results, void * stream) {
+    if (!results || !dst || !dst->data) {
+        return MM3FA_ERR_NULL;
+    }
+    const int G = results->n_ranks, me = results->rank;
+    if (G < 2 || G > MM3FA_MAX_RANKS || me < 0 || me >= G) {
+        return MM3FA_ERR_SHAPE;
+    }
+    for (int r = 0; r < G; r++) {
+        if (!results->recv[r]) {
+            return MM3FA_ERR_NULL;
+        }
+        if (!aligned(results->recv[r], 16)) {
+            return MM3FA_ERR_ALIGN;
+        }
+    }
+    // dst lies inside this rank's whole result [recv[me], recv[me] + recv_slot_bytes)
+    const char * base = static_cast<const char *>(results->recv[me]);
+    const char * d0   = static_cast<const char *>(dst->data);
+    if (d0 < base) {
+        return MM3FA_ERR_SHAPE;
+    }
+    const uint64_t last = (uint64_t) (d0 - base) + (uint64_t) ((dst->ne[1] - 1) * dst->nb[1] +
+                                                               (dst->ne[2] - 1) * dst->nb[2] +
+                                                               (dst->ne[3] - 1) * dst->nb[3]) +
+                          (uint64_t) dst->ne[0] * 4;
+    if (dst->ne[1] < 1 || dst->ne[2] < 1 || dst->ne[3] < 1 || last > results->recv_slot_bytes) {
+        return MM3FA_ERR_SHAPE;
+    }
+    // ALiBi slopes depend on the global head index, which a shard's descriptors do not carry
+    if (max_bias != 0.0f) {
+        return MM3FA_ERR_UNSUPPORTED;
+    }
+    if (prec != MM3FA_PREC_DEFAULT && prec != MM3FA_PREC_F32) {
+        return MM3FA_ERR_UNSUPPORTED;
+    }
+    OpShape s{};
+    int     st = check_op(q, k, v, mask, max_bias, logit_softcap, dst, true, s);
+    if (st != MM3FA_OK) {
+        return st;
+    }
+    if (device_info().major != 10) {
+        return MM3FA_ERR_DEVICE;
+    }
+    if (s.n_q == 0 || s.n_head == 0 || s.n_seq == 0 || s.DV == 0) {
+        return MM3FA_OK;
+    }
+    // the exchange lives in the tensor-core kernel's TMA-store epilogue: many query rows, keys present
+    if (s.n_kv == 0 || !use_dense(s, mask) || !rows_vec16(dst)) {
+        return MM3FA_ERR_UNSUPPORTED;
+    }
+    int64_t off[MM3FA_MAX_RANKS - 1];
+    int     n = 0;
+    for (int r = 0; r < G; r++) {
+        if (r != me) {
+            off[n++] = (int64_t) (static_cast<const char *>(results->recv[r]) - base);
+        }
+    }
+    return run_dense(s, q, k, v, mask, scale, max_bias, logit_softcap, dst, workspace, workspace_bytes,
+                     wait_timeout_ns(), static_cast<cudaStream_t>(stream), off, n);
 }
 
 int mm3fa_flash_attn_ext_kvlen(const mm3fa_tensor * q, const mm3fa_tensor * k, const mm3fa_tensor * v,

@@ -211,6 +211,60 @@ bool allocation_base(const void * p, char ** base) {
     return true;
 }
 
+// Completion step of the fused dense exchange (mm3fa_flash_attn_ext_gather): launched after that
+// rank's attention kernel in stream order, so the kernel's stores into the other ranks' results have
+// been performed.  Lane 0 fences at system scope and stores the call's epoch into every other
+// rank's flag word [slot][this rank] with release semantics; lane s (s != this rank) polls this
+// rank's word [slot][s] with acquire loads, bounded by the global timer, until rank s's epoch of the
+// call is there.  The epoch is the slot's call count + 1, advanced here.
+struct SignalParams {
+    uint32_t * flags[MM3FA_MAX_RANKS];  // every rank's flag array [n_slots][n_ranks]
+    int        n_ranks, rank, slot;
+    uint32_t * epoch;   // &epochs[slot]
+    uint32_t * status;  // workspace status word
+    uint64_t   timeout_ns;
+};
+
+__global__ void __launch_bounds__(32) gather_signal_wait_kernel(const SignalParams p) {
+    const int      lane = threadIdx.x;
+    const uint32_t e    = *p.epoch + 1u;
+    if (lane == 0) {
+        asm volatile("fence.sc.sys;" ::: "memory");
+        for (int r = 0; r < p.n_ranks; r++) {
+            if (r != p.rank) {
+                uint32_t * f = p.flags[r] + (int64_t) p.slot * p.n_ranks + p.rank;
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
+            }
+        }
+    }
+    bool failed = false;
+    if (lane < p.n_ranks && lane != p.rank) {
+        const uint32_t * f  = p.flags[p.rank] + (int64_t) p.slot * p.n_ranks + lane;
+        const uint64_t   dl = mm3fa::global_timer_ns() + p.timeout_ns;
+        uint32_t         spins = 0;
+        for (;;) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+            if ((int32_t) (v - e) >= 0) {
+                break;
+            }
+            if ((++spins & 63u) == 0 && mm3fa::global_timer_ns() > dl) {
+                failed = true;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    if (failed) {
+        atomicOr(&p.status[0], mm3fa::ST_TIMEOUT);
+        atomicExch(&p.status[1], 0xfffffff1u);  // where: the dense exchange's wait
+    }
+    __syncwarp();
+    if (lane == 0) {
+        *p.epoch = e;
+    }
+}
+
 }  // namespace
 
 extern "C" {
@@ -340,6 +394,41 @@ int mm3fa_peer_wait(const mm3fa_peers * peers, int slot, uint32_t * epochs, mm3f
     }();
     (void) carve;
     return cuda_status(cudaLaunchKernelEx(&cfg, peer_unpack_kernel, p));
+}
+
+int mm3fa_gather_signal_wait(const mm3fa_peers * flags, int slot, uint32_t * epochs, void * workspace, void * stream) {
+    if (!flags || !epochs || !workspace) {
+        return MM3FA_ERR_NULL;
+    }
+    if (flags->n_ranks < 2 || flags->n_ranks > MM3FA_MAX_RANKS || flags->rank < 0 ||
+        flags->rank >= flags->n_ranks || slot < 0) {
+        return MM3FA_ERR_SHAPE;
+    }
+    // recv_slot_bytes: the bytes of each rank's flag array, which holds [n_slots][n_ranks] words
+    if ((uint64_t) (slot + 1) * (uint64_t) flags->n_ranks * 4u > flags->recv_slot_bytes) {
+        return MM3FA_ERR_SHAPE;
+    }
+    SignalParams p{};
+    for (int r = 0; r < flags->n_ranks; r++) {
+        if (!flags->recv[r]) {
+            return MM3FA_ERR_NULL;
+        }
+        if (!aligned(flags->recv[r], 4)) {
+            return MM3FA_ERR_ALIGN;
+        }
+        p.flags[r] = static_cast<uint32_t *>(flags->recv[r]);
+    }
+    if (!aligned(epochs, 4)) {
+        return MM3FA_ERR_ALIGN;
+    }
+    p.n_ranks    = flags->n_ranks;
+    p.rank       = flags->rank;
+    p.slot       = slot;
+    p.epoch      = epochs + slot;
+    p.status     = static_cast<uint32_t *>(workspace);
+    p.timeout_ns = wait_timeout_ns();
+    gather_signal_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    return cuda_status(cudaGetLastError());
 }
 
 int mm3fa_ipc_export(const void * dev_ptr, mm3fa_ipc_handle * out) {

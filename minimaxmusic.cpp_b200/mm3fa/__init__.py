@@ -124,6 +124,11 @@ def lib():
         L.mm3fa_flash_attn_ext_peers.restype = ctypes.c_int
         L.mm3fa_peer_wait.argtypes = [ctypes.POINTER(Peers), ctypes.c_int, vp, P, vp, vp]
         L.mm3fa_peer_wait.restype = ctypes.c_int
+        L.mm3fa_flash_attn_ext_gather.argtypes = [P, P, P, P, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                                  ctypes.c_int, P, vp, ctypes.c_size_t, ctypes.POINTER(Peers), vp]
+        L.mm3fa_flash_attn_ext_gather.restype = ctypes.c_int
+        L.mm3fa_gather_signal_wait.argtypes = [ctypes.POINTER(Peers), ctypes.c_int, vp, vp, vp]
+        L.mm3fa_gather_signal_wait.restype = ctypes.c_int
         L.mm3fa_ipc_export.argtypes = [vp, ctypes.POINTER(IpcHandle)]
         L.mm3fa_ipc_export.restype = ctypes.c_int
         L.mm3fa_ipc_open.argtypes = [ctypes.POINTER(IpcHandle), ctypes.POINTER(ctypes.c_void_p)]
@@ -332,6 +337,27 @@ def peer_wait(peers: Peers, slot: int, epochs_ptr: int, result: Tensor, workspac
                                ctypes.c_void_p(workspace or None), ctypes.c_void_p(stream or None))
     if st != OK:
         raise MM3FAError(st, "mm3fa_peer_wait")
+
+
+def flash_attn_ext_gather(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None, scale: float, dst: Tensor,
+                          workspace: int, workspace_bytes: int, results: Peers, stream: int = 0,
+                          max_bias: float = 0.0, logit_softcap: float = 0.0, prec: int = GGML_PREC_F32) -> None:
+    """Dense attention on this rank's shard whose result rows also go straight into every other
+    rank's whole result (results.recv[r]; dst is this rank's slice inside results.recv[rank])."""
+    st = lib().mm3fa_flash_attn_ext_gather(_ref(q), _ref(k), _ref(v), _ref(mask), scale, max_bias, logit_softcap,
+                                           prec, _ref(dst), ctypes.c_void_p(workspace or None), workspace_bytes,
+                                           ctypes.byref(results), ctypes.c_void_p(stream or None))
+    if st != OK:
+        raise MM3FAError(st, "mm3fa_flash_attn_ext_gather")
+
+
+def gather_signal_wait(flags: Peers, slot: int, epochs_ptr: int, workspace: int, stream: int = 0) -> None:
+    """Publishes this rank's rows of the last mm3fa_flash_attn_ext_gather call on `slot` and waits
+    (on the device, bounded) for every other rank's; advances epochs[slot]."""
+    st = lib().mm3fa_gather_signal_wait(ctypes.byref(flags), slot, ctypes.c_void_p(epochs_ptr or None),
+                                        ctypes.c_void_p(workspace or None), ctypes.c_void_p(stream or None))
+    if st != OK:
+        raise MM3FAError(st, "mm3fa_gather_signal_wait")
 
 
 def ipc_export(ptr: int) -> bytes:

@@ -157,8 +157,8 @@ def test_prologue_entry_points_reject_before_touching_the_device():
 
 
 def test_exchange_entry_points_reject_before_touching_the_device():
-    """mm3fa_allgather_heads / _flash_attn_ext_peers / _peer_wait / IPC helpers: argument checks
-    that need neither a GPU nor NCCL."""
+    """mm3fa_allgather_heads / _flash_attn_ext_peers / _peer_wait / _flash_attn_ext_gather /
+    _gather_signal_wait / IPC helpers: argument checks that need neither a GPU nor NCCL."""
     L = mm3fa.lib()
     vp = ctypes.c_void_p
     # allgather: null pointers, bad split, null communicator
@@ -209,6 +209,42 @@ def test_exchange_entry_points_reject_before_touching_the_device():
     peers.recv_slot_bytes = 1024  # smaller than 2 ranks x 2 parities x the slice's words
     assert L.mm3fa_peer_wait(ctypes.byref(peers), 0, vp(0x7000), ctypes.byref(res), vp(0x8000), None) == \
         mm3fa.ERR_WORKSPACE
+    # fused dense exchange: results table, dst placement, ALiBi; the signal-wait's table and slot
+    res = mm3fa.Peers()
+    res.n_ranks, res.rank = 2, 0
+    base = 0x400000
+    dd = ggml.make(ggml.GGML_TYPE_F32, [128, 32, 1, 2], base + 4096)
+    g = lambda pr, dst=dd, mb=0.0: L.mm3fa_flash_attn_ext_gather(ctypes.byref(q4), ctypes.byref(k4), ctypes.byref(v4),
+                                                                  ctypes.byref(m4), 0.1, mb, 0.0, 10, ctypes.byref(dst),
+                                                                  vp(0x8000), 4096, pr, None)
+    assert g(None) == mm3fa.ERR_NULL
+    assert g(ctypes.byref(res)) == mm3fa.ERR_NULL  # result buffers missing
+    res.recv[0], res.recv[1] = base, base + 0x100000
+    res.recv_slot_bytes = 0x10000
+    res.n_ranks = 9
+    assert g(ctypes.byref(res)) == mm3fa.ERR_SHAPE
+    res.n_ranks = 2
+    res.recv[1] = base + 0x100004
+    assert g(ctypes.byref(res)) == mm3fa.ERR_ALIGN
+    res.recv[1] = base + 0x100000
+    below = ggml.make(ggml.GGML_TYPE_F32, [128, 32, 1, 2], base - 512)  # dst starts before the rank's result
+    assert g(ctypes.byref(res), below) == mm3fa.ERR_SHAPE
+    res.recv_slot_bytes = 4096 + 128 * 32 * 2 * 4 - 4  # dst's last row ends past the result
+    assert g(ctypes.byref(res)) == mm3fa.ERR_SHAPE
+    res.recv_slot_bytes = 0x10000
+    assert g(ctypes.byref(res), mb=8.0) == mm3fa.ERR_UNSUPPORTED
+    fl = mm3fa.Peers()
+    fl.n_ranks, fl.rank = 2, 1
+    fl.recv[0], fl.recv[1] = 0x500000, 0x600000
+    fl.recv_slot_bytes = 2 * 2 * 4  # two slots of two ranks' words
+    sw = lambda pr, slot=0, ep=0x7000, ws=0x8000: L.mm3fa_gather_signal_wait(pr, slot, vp(ep), vp(ws), None)
+    assert sw(None) == mm3fa.ERR_NULL
+    assert sw(ctypes.byref(fl), ep=0) == mm3fa.ERR_NULL
+    assert sw(ctypes.byref(fl), slot=2) == mm3fa.ERR_SHAPE  # past the flag array
+    assert sw(ctypes.byref(fl), slot=-1) == mm3fa.ERR_SHAPE
+    assert sw(ctypes.byref(fl), ep=0x7002) == mm3fa.ERR_ALIGN
+    fl.recv[0] = 0x500002
+    assert sw(ctypes.byref(fl)) == mm3fa.ERR_ALIGN
     # IPC helpers
     h = mm3fa.IpcHandle()
     assert L.mm3fa_ipc_export(None, ctypes.byref(h)) == mm3fa.ERR_NULL

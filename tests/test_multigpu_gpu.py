@@ -6,6 +6,9 @@ Each rank computes its shard of a CFG decode call (kv heads [8r/G, 8(r+1)/G)) an
   * mm3fa_flash_attn_ext_peers + mm3fa_peer_wait (the decode kernel stores its values as
     {value, epoch} words into every other rank's receive buffer over NVLink, the consumer's
     kernel waits for them and unpacks them), over several slots and both epoch parities.
+  * mm3fa_flash_attn_ext_gather + mm3fa_gather_signal_wait (DiT and causal prefill shards: the
+    dense kernel's epilogue stores each result row into every rank's whole result, a signal
+    kernel publishes them), over both result slots.
 The exchanged result must equal, bit for bit, the slices computed one by one on rank 0's GPU
 with the plain entry point (the exchange is a copy), and match the oracle at the north-star
 bound.  Runs on MM3FA_TEST_GPUS ranks (2 by default; 4 and 8 split the heads further); skipped on
@@ -134,7 +137,56 @@ def _rank_main(rank, world, port, out_dir):
             mm3fa.run(q_, k_, v_, None, mm3fa.dst_desc(q_, v_, o.data_ptr()), cd.scale, ws=ws)
             parts.append(o.cpu().numpy())
         out["dit_ref"] = sharding.allgather_scatter_np(np.stack(parts), ss)
+    # DiT through the fused dense exchange: the slice goes into every rank's whole result from the
+    # kernel's epilogue; calls on slots 0, 1, 0, each into a NaN-filled result
+    gb = exchange.GatherBuffers(torch, dist, dev, B * S * Hd * Dd * 4, 2)
+    wsd = torch.zeros(1 << 20, dtype=torch.uint8, device=dev)
+    s0, s1, h0, h1, _ = sharding.unit_slice(B, Hd, rank, world)
+
+    def fused(case_q, case_k, case_v, case_m, scale, nbytes, view_of):
+        res = []
+        for slot in (0, 1, 0):
+            gb.result(slot)[:nbytes].view(torch.float32).fill_(float("nan"))
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            dv = view_of(gb.result_ptr(slot))
+            mm3fa.flash_attn_ext_gather(case_q, case_k, case_v, case_m, scale, dv, wsd.data_ptr(), wsd.numel(),
+                                        gb.results(slot), s.cuda_stream)
+            mm3fa.gather_signal_wait(gb.flags, slot, gb.epochs.data_ptr(), wsd.data_ptr(), s.cuda_stream)
+            torch.cuda.synchronize(dev)
+            res.append(gb.result(slot)[:nbytes].view(torch.float32).cpu().numpy().copy())
+        return np.stack(res)
+
+    out["dit_fused"] = fused(qv, kv, vv, None, cd.scale, B * S * Hd * Dd * 4,
+                             lambda base: ggml.make(F32, [Dd, h1 - h0, S, s1 - s0], base + (s0 * S * Hd + h0) * Dd * 4,
+                                                    [4, 4 * Dd, 4 * Dd * Hd, 4 * Dd * Hd * S]))
+    # causal prefill (32q / 8kv, head pairs) by kv-head shard, fused and through NCCL
+    cp = workloads.prefill_case(n_seq=2, S=300, n_head=32, n_head_kv=8, kv_pos=20, seed=902)
+    dp = _descs(torch, ggml, cp, dev, keep)
+    Dp, Sp, Hp, nsp = 128, 300, 32, 2
+    hlp = Hp // world
+    pq, pk, pv, pm = sharding.shard_operands(dp["q"], dp["k"], dp["v"], dp["mask"], rank, world)
+    pbytes = nsp * Sp * Hp * Dp * 4
+    gb2 = gb if pbytes <= gb.slot_bytes else exchange.GatherBuffers(torch, dist, dev, pbytes, 2)
+    gb_saved, gb = gb, gb2
+    out["prefill_fused"] = fused(pq, pk, pv, pm, cp.scale, pbytes,
+                                 lambda base: ggml.make(F32, [Dp, hlp, Sp, nsp], base + rank * hlp * Dp * 4,
+                                                        [4, 4 * Dp, 4 * Dp * Hp, 4 * Dp * Hp * Sp]))
+    gp = torch.full((world, nsp, Sp, hlp, Dp), float("nan"), device=dev)
+    fullp = torch.full((nsp, Sp, Hp, Dp), float("nan"), device=dev)
+    mm3fa.run(pq, pk, pv, pm, ggml.make(F32, [Dp, hlp, Sp, nsp], gp[rank].data_ptr()), cp.scale, ws=ws)
+    mm3fa.allgather_heads(gp[rank].data_ptr(), gp.data_ptr(), fullp.data_ptr(), Dp, Hp, Sp, nsp, 1, comm, s.cuda_stream)
+    torch.cuda.synchronize(dev)
+    out["prefill_nccl"] = fullp.cpu().numpy()
+    st2, raw2 = mm3fa.workspace_status(wsd.data_ptr(), s.cuda_stream)
+    out["fused_status"] = np.array([st2, raw2])
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **out)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    gb = gb_saved
+    if gb2 is not gb:
+        gb2.close()
+    gb.close()
     torch.cuda.synchronize(dev)
     dist.barrier()
     pb.close()
@@ -170,6 +222,18 @@ def test_fused_peer_exchange_is_the_shards_bit_for_bit(exchange_results):
             assert np.array_equal(res["decode_peer"][k], ref), f"rank {r}: peer exchange call {k} differs"
 
 
+def test_fused_dense_exchange_is_the_all_gather_bit_for_bit(exchange_results):
+    import mm3fa
+
+    for r, res in enumerate(exchange_results):
+        assert tuple(res["fused_status"]) == (mm3fa.OK, 0), f"rank {r}: a dense exchange wait expired"
+        for k in range(3):
+            ref = exchange_results[0]["dit_ref"].reshape(res["dit_fused"][k].shape)
+            assert np.array_equal(res["dit_fused"][k], ref), f"rank {r}: fused DiT exchange call {k} differs"
+            got = res["prefill_fused"][k].reshape(res["prefill_nccl"].shape)
+            assert np.array_equal(got, res["prefill_nccl"]), f"rank {r}: fused prefill exchange call {k} differs"
+
+
 def test_exchanged_results_match_the_oracle(exchange_results):
     from gpu_util import check_three_ways
     from mm3fa import workloads
@@ -177,3 +241,5 @@ def test_exchanged_results_match_the_oracle(exchange_results):
     check_three_ways(exchange_results[0]["decode_nccl"], workloads.decode_case(n_seq=4, n_kv=2048, max_seq=2304,
                                                                                seed=900))
     check_three_ways(exchange_results[1]["dit_nccl"], workloads.dit_case(B=2, S=300, H=8, D=64, seed=901))
+    check_three_ways(exchange_results[-1]["prefill_nccl"],
+                     workloads.prefill_case(n_seq=2, S=300, n_head=32, n_head_kv=8, kv_pos=20, seed=902))
