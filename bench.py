@@ -23,8 +23,9 @@ reads its inputs from HBM; "dit_real" the same at the real model's shape (B=2 x 
 D=64, 8 operand sets cycled); "prefill" times config 4 (2 x 1024-token causal prefill, 32q/8kv,
 D=128, F16 causal mask over the 256-padded cache view).  At N GPUs the jobs grow with N: the DiT
 by CFG pairs (every head of a pair on one rank: no exchange needed; "dit_strong" splits the B=2
-job's heads over the ranks and all-gathers after every call), the prefill by sequences split by kv
-head, all-gathered after every call.  "q8_decode" is config 3, "decode_step" the fused prologue +
+job's heads over the ranks and exchanges the result after every call), the prefill by sequences
+split by kv head, exchanged after every call - the kernel's epilogue stores each result row into
+every rank's result (mm3fa_flash_attn_ext_gather), the NCCL all-gather is timed beside it.  "q8_decode" is config 3, "decode_step" the fused prologue +
 attention, "depth" the depth decoder's F32 attention of one frame.
 
 Printed JSON: value = whole-job algorithmic GB/s of the timed steps (device time, max over
@@ -248,9 +249,11 @@ def bench_dense(torch, dist, mm3fa, ggml, dev, stream, steps: int, warmup: int, 
 
     N GPUs: the DiT job grows to N CFG pairs (B = 2N) and rank r computes pair r, all 16 heads
     (weak scaling, no exchange needed); a second line keeps the B = 2 job and splits its 32
-    (batch x head) units over the ranks (strong scaling), each call followed by
-    mm3fa_allgather_heads (NCCL), as to_out needs every head of its rows.  The prefill job grows to
-    2N sequences, split by kv head, with the same all-gather after the call (o_proj)."""
+    (batch x head) units over the ranks (strong scaling), each call followed by the exchange of the
+    result, as to_out needs every head of its rows.  The prefill job grows to 2N sequences, split by
+    kv head, with the same exchange after the call (o_proj).  The exchange the lines report is the
+    fused one (the kernel stores its rows into every rank's result, then a signal-and-wait kernel);
+    mm3fa_allgather_heads (NCCL + permute) is timed beside it."""
     from mm3fa import exchange as xch, sharding
 
     g = torch.Generator(device=dev)
@@ -294,6 +297,36 @@ def bench_dense(torch, dist, mm3fa, ggml, dev, stream, steps: int, warmup: int, 
             us_call = ms * 1e3 / n_calls_per_step
             res[tag] = (us_call, flops_per_call / (us_call * 1e-6) / 1e12, clk.summary())
         return res
+
+    def timed_fused(calls, result_bytes, flops_per_call, ws):
+        """The fused exchange: calls [(q, k, v, mask, scale, view_of)] where view_of(base) is this rank's
+        dst slice inside a whole result at `base`; call i runs on result slot i % 2 through
+        mm3fa_flash_attn_ext_gather (rows stored into every rank's result from the kernel) and is
+        followed by mm3fa_gather_signal_wait.  Returns (us per call, TFLOP/s, clocks, status)."""
+        gb = xch.GatherBuffers(torch, dist, dev, result_bytes, 2)
+
+        def step():
+            for i, (qd_, kd_, vd_, md_, sc_, view_of) in enumerate(calls):
+                slot = i % 2
+                mm3fa.flash_attn_ext_gather(qd_, kd_, vd_, md_, sc_, view_of(gb.result_ptr(slot)), ws.data_ptr(),
+                                            ws.numel(), gb.results(slot), stream.cuda_stream)
+                mm3fa.gather_signal_wait(gb.flags, slot, gb.epochs.data_ptr(), ws.data_ptr(), stream.cuda_stream)
+
+        with torch.cuda.stream(stream):
+            step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        with ClockSampler(local) as clk:
+            ms = timed_replays(torch, dist, graph, stream, steps, warmup, world)
+        del graph
+        torch.cuda.synchronize()
+        st, raw = mm3fa.workspace_status(ws.data_ptr(), stream.cuda_stream)
+        dist.barrier()
+        gb.close()
+        us_call = ms * 1e3 / len(calls)
+        return us_call, flops_per_call / (us_call * 1e-6) / 1e12, clk.summary(), int(st)
 
     burst, sustained, src = measured_tensor_peaks()
     out = {}
@@ -345,10 +378,22 @@ def bench_dense(torch, dist, mm3fa, ggml, dev, stream, steps: int, warmup: int, 
             calls2.append(((view(qd), view(kd), view(vd), None, dd2), 1.0 / math.sqrt(Dh)))
         ex2 = lambda s_: mm3fa.allgather_heads(sptr, 0 if direct else gath.data_ptr(), full2.data_ptr(), Dh, H, S, B,
                                                ss, comm, s_.cuda_stream)
-        r2 = timed(calls2, ex2, 24, fl, torch.zeros(1 << 20, dtype=torch.uint8, device=dev))
-        out["dit_strong"] = {"tflops_job": round(r2["with_exchange"][1], 1), "us_per_call": round(r2["with_exchange"][0], 2),
+        ws2 = torch.zeros(1 << 20, dtype=torch.uint8, device=dev)
+        r2 = timed(calls2, ex2, 24, fl, ws2)
+        # the fused exchange: each rank's slice of the job's [Dh, H, S, B] result, stored by the kernel
+        fcalls = [(c[0][0], c[0][1], c[0][2], None, c[1],
+                   lambda base: ggml.make(F32, [Dh, hl, S, sl], base + (s0 * S * H + h0) * Dh * 4,
+                                          [4, 4 * Dh, 4 * Dh * H, 4 * Dh * H * S])) for c in calls2]
+        fu, ftf, fclk, fst = timed_fused(fcalls, B * S * H * Dh * 4, fl, ws2)
+        out["dit_strong"] = {"tflops_job": round(ftf, 1), "us_per_call": round(fu, 2),
+                             "exchange": "fused: rows stored into every rank's result from the kernel "
+                                         "(mm3fa_flash_attn_ext_gather + mm3fa_gather_signal_wait)",
+                             "exchange_status": fst,
+                             "nccl_us_per_call": round(r2["with_exchange"][0], 2),
+                             "nccl_tflops_job": round(r2["with_exchange"][1], 1),
                              "attention_only_us_per_call": round(r2["attention_only"][0], 2),
                              "attention_only_tflops_job": round(r2["attention_only"][1], 1),
+                             "clocks": fclk,
                              "units_per_gpu": sl * hl, "config": {"global_batch": B, "heads": H, "seq": S,
                                                                   "seq_split": ss, "scaling": "strong"}}
         del full2, gath, calls2
@@ -383,15 +428,29 @@ def bench_dense(torch, dist, mm3fa, ggml, dev, stream, steps: int, warmup: int, 
     r = timed([((qd, kd, vd, md, ddp), 1.0 / math.sqrt(Dh))], exp_, 1, flp, ws)
     us, tf, clocks = r["with_exchange"]
     tf_k = r.get("attention_only", r["with_exchange"])[1]
+    fused_info = None
+    if world > 1:
+        # the fused exchange (the line's figure): this rank's heads of the job's [Dh, 32, Sp, 2N] result,
+        # stored by the kernel into every rank's result; two calls per step, one per result slot
+        pview = lambda base: ggml.make(F32, [Dh, Hq, Sp, nsp], base + rank * Hq * Dh * 4,
+                                       [4, 4 * Dh, 4 * Dh * N_HEAD, 4 * Dh * N_HEAD * Sp])
+        nccl_us = us
+        us, tf, clocks, fst = timed_fused([(qd, kd, vd, md, 1.0 / math.sqrt(Dh), pview)] * 2,
+                                          nsp * Sp * N_HEAD * Dh * 4, flp, ws)
+        fused_info = {"exchange": "fused: rows stored into every rank's result from the kernel "
+                                  "(mm3fa_flash_attn_ext_gather + mm3fa_gather_signal_wait)",
+                      "exchange_status": fst, "nccl_us_per_call": round(nccl_us, 2)}
     out["prefill"] = {"tflops": round(tf * world, 1), "tflops_per_gpu": round(tf, 1), "us_per_call": round(us, 2),
                       "frac_of_burst": round(tf_k / burst, 4), "frac_of_sustained": round(tf_k / sustained, 4),
                       "clocks": clocks,
                       "config": {"workload": "causal LM prefill, benchmark config 4", "n_seq": nsp, "tokens": Sp,
                                  "n_head": N_HEAD, "n_head_kv": N_HEAD_KV, "head_dim": Dh, "n_kv_view": n_kv,
                                  "parallelism": f"kv-head shard x{world}"
-                                                + (", all-gather after the call" if world > 1 else "")}}
+                                                + (", head exchange after the call" if world > 1 else "")}}
     if "attention_only" in r:
         out["prefill"]["attention_only_us_per_call"] = round(r["attention_only"][0], 2)
+    if fused_info:
+        out["prefill"].update(fused_info)
     return out
 
 

@@ -1069,27 +1069,39 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                     }
                 }
                 char * tile = stage + c * (DN_M * 128);
-                // this row's place in the result (the other ranks' results hold it at peer_off)
-                char * prow = p.dst + (int64_t) ht * p.d_nb1 + (int64_t) qi * p.d_nb2 + (int64_t) sq * p.d_nb3 +
-                              (int64_t) c * 128;
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
-                    const float4 val = make_float4(__uint_as_float(o[4 * j]) * inv, __uint_as_float(o[4 * j + 1]) * inv,
-                                                   __uint_as_float(o[4 * j + 2]) * inv,
-                                                   __uint_as_float(o[4 * j + 3]) * inv);
-                    *reinterpret_cast<float4 *>(tile + sw128_off(r, j)) = val;
-                    if (p.n_peers > 0 && valid) {
+                    *reinterpret_cast<float4 *>(tile + sw128_off(r, j)) =
+                        make_float4(__uint_as_float(o[4 * j]) * inv, __uint_as_float(o[4 * j + 1]) * inv,
+                                    __uint_as_float(o[4 * j + 2]) * inv, __uint_as_float(o[4 * j + 3]) * inv);
+                }
+            }
+            fence_proxy_async_smem();
+            dn_named_barrier(1 + t, 128);
+            if (p.n_peers > 0) {
+                // fused exchange: the staged rows to the other ranks' results (the same place there,
+                // at peer_off), a warp per 32 rows, each store instruction covering whole rows
+                // (D / 4 lanes x 16 contiguous bytes per row), so that NVLink carries full lines
+                constexpr int F4  = D / 4;    // 16-byte pieces of a row
+                constexpr int RPW = 32 / F4;  // rows per warp instruction
+                const int     c   = (lane % F4) / 8;
+                const int     jj  = (lane % F4) % 8;
+                for (int i = lane / F4; i < 32; i += RPW) {
+                    const int rr = quad * 32 + i;
+                    const int rw = rbase + rr;
+                    if (rw < p.n_q) {
+                        const float4 val = *reinterpret_cast<const float4 *>(stage + c * (DN_M * 128) + sw128_off(rr, jj));
+                        char * prow = p.dst + (int64_t) ht * p.d_nb1 + (int64_t) rw * p.d_nb2 + (int64_t) sq * p.d_nb3 +
+                                      c * 128 + jj * 16;
 #pragma unroll
                         for (int pp = 0; pp < 7; pp++) {
                             if (pp < p.n_peers) {
-                                *reinterpret_cast<float4 *>(prow + p.peer_off[pp] + 16 * j) = val;
+                                *reinterpret_cast<float4 *>(prow + p.peer_off[pp]) = val;
                             }
                         }
                     }
                 }
             }
-            fence_proxy_async_smem();
-            dn_named_barrier(1 + t, 128);
             if (quad == 0 && lane == 0) {
                 const int q0t = rbase;
 #pragma unroll
